@@ -1,0 +1,196 @@
+/*
+ * molten_cuda.h -- C ABI of the B200 (sm_100a) quantized MoE matmul path.
+ *
+ * Drop-in boundary for the op-level surface that Molten's
+ * src/kernels/{lfm,quant,elementwise}.rs expose to src/lfm.rs. Every entry
+ * point below names the reference function it replaces (paths inside the
+ * reference project). A Rust `src/cuda.rs` binds these with `extern "C"`
+ * (see INTEGRATION.md); tests and bench.py bind them with ctypes.
+ *
+ * Conventions
+ *  - All pointers are DEVICE pointers owned by the caller; no entry point
+ *    allocates device memory (scratch is passed in, as the reference's
+ *    `Scratch` is preallocated by the caller, lfm.rs:557-626).
+ *  - bf16 values travel as uint16_t bit patterns.
+ *  - Work is enqueued on the context's stream and is asynchronous, like
+ *    `ComputePass::dispatch_at` (metal.rs:326-355); mc_sync is `commit_wait`.
+ *  - Return 0 on success or a negative MC_E* code; the message is in
+ *    mc_last_error() (thread-local). Argument checks run before anything is
+ *    enqueued, so a rejected call leaves nothing half-issued, like the
+ *    reference's `ensure!`s before encoding (quant.rs:42-66).
+ *  - One context per thread and device; calls are not re-entrant.
+ *  - Q4 = MLX affine 4-bit, group 64: codes u32[out][in/8], low nibble first;
+ *    Q6 = 4 codes per 3 bytes (little-endian 6-bit stream), codes u32 words
+ *    [out][in*6/32]; scales/biases bf16[out][in/64]; w = s*q + b
+ *    (weights.rs:7-20).
+ */
+#ifndef MOLTEN_CUDA_H
+#define MOLTEN_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define MC_OK 0
+#define MC_EINVAL (-1)       /* bad shape, dtype, alignment or pointer */
+#define MC_ECUDA (-2)        /* CUDA runtime error */
+#define MC_EUNSUPPORTED (-3) /* shape this build does not instantiate */
+#define MC_ENCCL (-4)        /* NCCL error (expert parallelism) */
+#define MC_ETIMEOUT (-5)     /* a bounded wait ran out */
+
+#define MC_ROUTE_SOFTMAX_RENORM 0 /* BASELINE: softmax over E, top-4, renormalise */
+#define MC_ROUTE_SIGMOID_BIAS 1   /* reference model: sigmoid + expert_bias selection */
+
+#define MC_DTYPE_BF16 0
+#define MC_DTYPE_F32 1
+
+typedef struct mc_ctx mc_ctx;
+
+/* QuantWeights (weights.rs:11-30). Device pointers, caller-owned. */
+typedef struct mc_qweights {
+  const uint32_t* codes;
+  const uint16_t* scales;
+  const uint16_t* biases;
+  int32_t out_features;
+  int32_t in_features;
+  int32_t group_size;
+  int32_t bits;
+} mc_qweights;
+
+/* ---------------------------------------------------------------- context */
+
+/* MetalContext::new (metal.rs:91-147): binds `device`; `stream` is a
+ * cudaStream_t to enqueue on, or NULL to create a private one. */
+int mc_create(int device, void* stream, mc_ctx** out);
+int mc_destroy(mc_ctx* ctx);
+/* Switches the stream later calls enqueue on (NULL = the private stream). */
+int mc_set_stream(mc_ctx* ctx, void* stream);
+/* ComputePass::commit_wait (metal.rs:383-399): waits for all enqueued work
+ * and reports any asynchronous CUDA error. */
+int mc_sync(mc_ctx* ctx);
+const char* mc_last_error(void);
+/* Library build id, e.g. "molten_cuda sm_100a". */
+const char* mc_version(void);
+
+/* check_quant (quant.rs:42-66): validates a weight descriptor without a GPU
+ * call. Returns 0 or MC_EINVAL with the reason in mc_last_error(). */
+int mc_check_quant(const mc_qweights* w);
+
+/* ------------------------------------------------------------ decode path */
+
+/* gemv_quant (kernels/lfm.rs:112-149 -> lfm_gemv_q4_bf16_k2048
+ * lfm.metal:161-183, lfm_gemv_q6_bf16_x4 :245-297): y[b] = W . x[b] for
+ * `batch` independent bf16 rows x[batch][in] -> y[batch][out]. bits 4 or 6. */
+int mc_gemv_quant(mc_ctx* ctx, const mc_qweights* w, const uint16_t* x, uint16_t* y,
+                  int batch);
+
+/* gemv_head_argmax (kernels/lfm.rs:826-844 -> lfm_gemv_q6_bf16_x4_argmax
+ * lfm.metal:1215-1282): fused head GEMV + argmax over bf16-rounded logits,
+ * folded into keys[b] by 64-bit atomic max. keys[batch] must be zero on entry
+ * (mc_token_tail clears them). */
+int mc_gemv_head_argmax(mc_ctx* ctx, const mc_qweights* w, const uint16_t* x,
+                        unsigned long long* keys, int batch);
+
+/* token_tail (kernels/lfm.rs:850-888 -> lfm_token_tail lfm.metal:1291-1386):
+ * reads and clears keys[b], writes out_tok[b]; when `embed` is non-NULL also
+ * writes the next input row x_next[b] = embed[tok] (bf16 table [vocab][hidden])
+ * and its RMSNorm normed_next[b] with gain norm_w. */
+int mc_token_tail(mc_ctx* ctx, unsigned long long* keys, uint32_t* out_tok,
+                  const uint16_t* embed, int vocab, const uint16_t* norm_w,
+                  uint16_t* x_next, uint16_t* normed_next, int hidden, float eps,
+                  int batch);
+
+/* argmax_bf16 (kernels/lfm.rs:794-820 -> lfm.metal:1126-1192): argmax over
+ * stored bf16 logits[batch][n], ties to the lowest index. */
+int mc_argmax_bf16(mc_ctx* ctx, const uint16_t* logits, int n, uint32_t* out, int batch);
+
+/* add_rmsnorm_bf16 (norm.metal:63-136, via lfm_norm_row_v8_tg
+ * lfm.metal:306-366): hout = bf16(h + b) (b may be NULL), nout =
+ * RMSNorm(hout) * w. hidden = 2048. */
+int mc_add_rmsnorm(mc_ctx* ctx, const uint16_t* h, const uint16_t* b, const uint16_t* w,
+                   uint16_t* hout, uint16_t* nout, int hidden, float eps, int batch);
+
+/* router_addnorm_route (kernels/lfm.rs:266-311 -> lfm_router_addnorm_route_f32
+ * lfm.metal:773-854): residual add + RMSNorm + router GEMV + top-4 in one
+ * launch. router_w is [E][hidden] in router_dtype (MC_DTYPE_BF16 for the
+ * BASELINE router, MC_DTYPE_F32 for the reference model's). expert_bias
+ * (f32[E], nullable) is used by MC_ROUTE_SIGMOID_BIAS. counter: u32[batch]
+ * zeroed words the kernel leaves zeroed. E = 64, hidden = 2048. */
+int mc_router_addnorm_route(mc_ctx* ctx, const uint16_t* h, const uint16_t* b,
+                            const uint16_t* norm_w, uint16_t* h_out, uint16_t* normed,
+                            const void* router_w, int router_dtype, const float* expert_bias,
+                            int route_mode, float* logits, uint32_t* ids, uint16_t* weights,
+                            uint32_t* counter, int n_experts, int hidden, float eps,
+                            float route_eps, int batch);
+
+/* gemv_f32 (kernels/lfm.rs:314-335 -> lfm.metal:417-428): unfused router
+ * logits[batch][E] = W . x[batch] (prompt-final row). */
+int mc_gemv_router(mc_ctx* ctx, const void* router_w, int router_dtype, const uint16_t* x,
+                   float* logits, int n_experts, int hidden, int batch);
+
+/* route_token (kernels/lfm.rs:391-417 -> lfm_route_warp_f32 lfm.metal:686-703):
+ * top-4 ids and bf16 weights from logits[batch][E]. */
+int mc_route_token(mc_ctx* ctx, const float* logits, int n_experts, int route_mode,
+                   const float* expert_bias, float route_eps, uint32_t* ids,
+                   uint16_t* weights, int batch);
+
+/* gemv_gather_act (kernels/lfm.rs:421-460 -> lfm_gemv_q4_gather_act_bf16
+ * lfm.metal:1392-1445): act[b][r][i] = silu(gate row)*up row for the four
+ * selected experts ids[b][r]; gate/up stacked [E*I][H] Q4. */
+int mc_gemv_gather_act(mc_ctx* ctx, const mc_qweights* gate, const mc_qweights* up,
+                       const uint16_t* x, const uint32_t* ids, uint16_t* act, int n_experts,
+                       int batch);
+
+/* gemv_gather_down_combine4 (kernels/lfm.rs:499-533 ->
+ * lfm_gemv_q4_gather_down_combine4_bf16 lfm.metal:1503-1554): down GEMVs of
+ * the four selected experts (stacked [E*H][I] Q4) with the weighted combine. */
+int mc_gemv_gather_down_combine4(mc_ctx* ctx, const mc_qweights* down, const uint16_t* act,
+                                 const uint32_t* ids, const uint16_t* weights, uint16_t* out,
+                                 int n_experts, int batch);
+
+/* ----------------------------------------------------------- prefill path */
+
+/* moe_route_batch (kernels/lfm.rs:536-555 -> lfm.metal:1558-1602): per-token
+ * top-4 ids[m][4] and bf16 gate weights gw[m][4] from logits[m][E]. */
+int mc_moe_route_batch(mc_ctx* ctx, const float* logits, int m, int n_experts,
+                       int route_mode, const float* expert_bias, float route_eps,
+                       uint32_t* ids, uint16_t* gw);
+
+/* moe_zero_counts .. moe_blocks (kernels/lfm.rs:557-697 -> lfm.metal:1604-1770)
+ * in two launches: counts[E], offsets[E] (exclusive scan), the stable
+ * token-major, rank-major scatter ids_sorted[m*4] / slotpos[m*4], and the
+ * row-tile list tiles[max_tiles] of uint4 {m0, m_end, expert, 0} with its
+ * length in *n_tiles (device u32). bm is the tile height (128);
+ * max_tiles >= ceil(m*4/bm) + E. */
+int mc_moe_sort_map(mc_ctx* ctx, const uint32_t* ids, int m, int n_experts, int bm,
+                    uint32_t* counts, uint32_t* offsets, uint32_t* ids_sorted,
+                    uint32_t* slotpos, uint32_t* tiles, uint32_t* n_tiles, int max_tiles);
+
+/* gather_rows_bf16 (elementwise.rs:59-104 -> elementwise.metal:41-52):
+ * out[i] = table[ids[i]] for bf16 rows of width hidden. */
+int mc_gather_rows_bf16(mc_ctx* ctx, const uint16_t* table, const uint32_t* ids, int rows,
+                        int hidden, uint16_t* out);
+
+/* silu_mul_bf16 (elementwise.rs:48-56 -> elementwise.metal:7-15). */
+int mc_silu_mul_bf16(mc_ctx* ctx, const uint16_t* gate, const uint16_t* up, uint16_t* out,
+                     size_t n);
+
+/* moe_combine_rows (kernels/lfm.rs:701-756 -> lfm_moe_combine_rows_bf16_v16
+ * lfm.metal:915-940): out[t] = bf16(sum_r bf16(gw[t][r] * ed[slotpos[t][r]])). */
+int mc_moe_combine_rows(mc_ctx* ctx, const uint16_t* ed, const uint32_t* slotpos,
+                        const uint16_t* gw, uint16_t* out, int m, int topk, int hidden);
+
+/* -------------------------------------------------------------- test aid */
+
+/* Evaluates the library's device math on x[n] into y[n]: op 0 = mc_exp,
+ * 1 = SiLU, 2 = sigmoid, 3 = bf16 rounding. Lets tests check the device
+ * functions bit for bit against the CPU restatement. */
+int mc_eval_math(mc_ctx* ctx, int op, const float* x, float* y, int n);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* MOLTEN_CUDA_H */

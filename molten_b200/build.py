@@ -1,0 +1,57 @@
+"""Builds the sm_100a C-ABI library ``molten_b200/libmolten_cuda.so`` in-tree.
+
+One nvcc invocation compiles every ``csrc/*.cu`` for ``sm_100a`` (nvcc
+cross-compiles; no GPU is needed). ``--fmad=false`` keeps nvcc from fusing
+multiply-adds on its own: every fused multiply-add in the kernels is written
+out explicitly, because the decode path's reduction order is part of its
+contract (bit-identical ids and tokens).
+"""
+from __future__ import annotations
+
+import os
+import subprocess
+import sys
+from pathlib import Path
+
+HERE = Path(__file__).resolve().parent
+CSRC = HERE / "csrc"
+LIB = HERE / "libmolten_cuda.so"
+NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
+
+NVCC_FLAGS = [
+    "-gencode", "arch=compute_100a,code=sm_100a",
+    "-O3", "-lineinfo", "--fmad=false", "-std=c++17",
+    "-Xcompiler", "-fPIC,-O2",
+    "--expt-relaxed-constexpr",
+]
+
+
+def sources() -> list[Path]:
+    return sorted(CSRC.glob("*.cu"))
+
+
+def needs_build() -> bool:
+    if not LIB.exists():
+        return True
+    t = LIB.stat().st_mtime
+    deps = list(CSRC.glob("*")) + [HERE.parent / "include" / "molten_cuda.h", Path(__file__)]
+    return any(p.stat().st_mtime > t for p in deps if p.exists())
+
+
+def build(force: bool = False, verbose: bool = False) -> Path:
+    if not force and not needs_build():
+        return LIB
+    tmp = LIB.with_suffix(".so.tmp")
+    cmd = [NVCC, *NVCC_FLAGS, "-shared", "-o", str(tmp), *map(str, sources()),
+           "-ldl"]
+    if verbose:
+        print(" ".join(cmd), file=sys.stderr)
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    if r.returncode != 0:
+        raise RuntimeError(f"nvcc failed ({r.returncode}):\n{r.stdout}\n{r.stderr}")
+    os.replace(tmp, LIB)
+    return LIB
+
+
+if __name__ == "__main__":
+    print(build(force="--force" in sys.argv, verbose=True))

@@ -1,0 +1,133 @@
+// Context, errors and weight validation for the C ABI (include/molten_cuda.h).
+#include "mc_internal.cuh"
+#include <stdlib.h>
+#include <string.h>
+
+static thread_local char g_err[512] = "";
+
+int mc_fail(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_err, sizeof g_err, fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+int mc_after_launch(const char* what) {
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return mc_fail(MC_ECUDA, "%s launch failed: %s", what, cudaGetErrorString(e));
+  return MC_OK;
+}
+
+// check_quant (quant.rs:42-66) for the decode GEMVs: group 64, 4- or 6-bit,
+// in_features a multiple of 64, codes 16-byte aligned (rows are read as
+// 16-byte vectors), rows in range.
+int mc_check_gemv_weights(const mc_qweights* w, const char* what) {
+  if (!w) return mc_fail(MC_EINVAL, "%s: null weights", what);
+  if (w->bits != 4 && w->bits != 6)
+    return mc_fail(MC_EUNSUPPORTED, "%s: unsupported bit width %d", what, w->bits);
+  if (w->group_size != 64)
+    return mc_fail(MC_EUNSUPPORTED, "%s: group size %d (only 64 is built)", what, w->group_size);
+  if (w->in_features <= 0 || w->in_features % 64 != 0 || w->in_features > 4096)
+    return mc_fail(MC_EINVAL, "%s: in_features %d must be a positive multiple of 64 <= 4096",
+                   what, w->in_features);
+  if (w->out_features <= 0)
+    return mc_fail(MC_EINVAL, "%s: out_features %d", what, w->out_features);
+  if (!w->codes || !w->scales || !w->biases)
+    return mc_fail(MC_EINVAL, "%s: null codes/scales/biases", what);
+  if (!mc_aligned(w->codes, 16))
+    return mc_fail(MC_EINVAL, "%s: codes not 16-byte aligned; the kernels read codes as 16-byte vectors",
+                   what);
+  if (!mc_aligned(w->scales, 2) || !mc_aligned(w->biases, 2))
+    return mc_fail(MC_EINVAL, "%s: scales/biases not 2-byte aligned", what);
+  return MC_OK;
+}
+
+extern "C" int mc_check_quant(const mc_qweights* w) {
+  if (!w) return mc_fail(MC_EINVAL, "check_quant: null weights");
+  if (w->bits != 4 && w->bits != 6 && w->bits != 8)
+    return mc_fail(MC_EINVAL, "unsupported bit width %d", w->bits);
+  if (w->group_size <= 0 || w->in_features <= 0 || w->out_features <= 0)
+    return mc_fail(MC_EINVAL, "check_quant: non-positive shape");
+  // A 16-byte code block must not cross a quantization group (quant.rs:46-53).
+  const int per_block = 128 / w->bits;
+  if (w->in_features % w->group_size != 0 || (w->bits != 6 && w->group_size % per_block != 0))
+    return mc_fail(MC_EINVAL, "in_features %d / group size %d not block-packable at %d bits",
+                   w->in_features, w->group_size, w->bits);
+  if (w->bits == 6 && w->group_size % 64 != 0)
+    return mc_fail(MC_EINVAL, "6-bit group size %d must be a multiple of 64", w->group_size);
+  if (!mc_aligned(w->codes, 16))
+    return mc_fail(MC_EINVAL, "codes address not 16-aligned; the kernels read codes as 16-byte vectors");
+  return MC_OK;
+}
+
+extern "C" const char* mc_last_error(void) { return g_err; }
+
+extern "C" const char* mc_version(void) { return "molten_cuda 0.1 sm_100a"; }
+
+extern "C" int mc_create(int device, void* stream, mc_ctx** out) {
+  if (!out) return mc_fail(MC_EINVAL, "mc_create: null out");
+  *out = nullptr;
+  int n = 0;
+  MC_CUDA(cudaGetDeviceCount(&n));
+  if (device < 0 || device >= n) return mc_fail(MC_EINVAL, "mc_create: device %d of %d", device, n);
+  MC_CUDA(cudaSetDevice(device));
+  cudaDeviceProp prop;
+  MC_CUDA(cudaGetDeviceProperties(&prop, device));
+  if (prop.major != 10)
+    return mc_fail(MC_EUNSUPPORTED, "mc_create: device %d is sm_%d%d; this library is built for sm_100a",
+                   device, prop.major, prop.minor);
+  mc_ctx* c = (mc_ctx*)calloc(1, sizeof(mc_ctx));
+  if (!c) return mc_fail(MC_EINVAL, "mc_create: out of host memory");
+  c->device = device;
+  c->num_sms = prop.multiProcessorCount;
+  c->l2_bytes = prop.l2CacheSize;
+  int optin = 0;
+  cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, device);
+  c->max_smem_optin = optin;
+  if (stream) {
+    c->stream = (cudaStream_t)stream;
+  } else {
+    cudaError_t e = cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking);
+    if (e != cudaSuccess) {
+      free(c);
+      return mc_fail(MC_ECUDA, "mc_create: cudaStreamCreate: %s", cudaGetErrorString(e));
+    }
+    c->owns_stream = 1;
+  }
+  *out = c;
+  return MC_OK;
+}
+
+extern "C" int mc_set_stream(mc_ctx* ctx, void* stream) {
+  if (!ctx) return mc_fail(MC_EINVAL, "mc_set_stream: null context");
+  if (stream) {
+    if (ctx->owns_stream) {
+      cudaStreamDestroy(ctx->stream);
+      ctx->owns_stream = 0;
+    }
+    ctx->stream = (cudaStream_t)stream;
+    return MC_OK;
+  }
+  if (!ctx->owns_stream) {
+    MC_CUDA(cudaStreamCreateWithFlags(&ctx->stream, cudaStreamNonBlocking));
+    ctx->owns_stream = 1;
+  }
+  return MC_OK;
+}
+
+extern "C" int mc_sync(mc_ctx* ctx) {
+  if (!ctx) return mc_fail(MC_EINVAL, "mc_sync: null context");
+  MC_CUDA(cudaStreamSynchronize(ctx->stream));
+  MC_CUDA(cudaGetLastError());
+  return MC_OK;
+}
+
+int mc_ep_teardown(mc_ctx* ctx);
+
+extern "C" int mc_destroy(mc_ctx* ctx) {
+  if (!ctx) return MC_OK;
+  if (ctx->owns_stream) cudaStreamDestroy(ctx->stream);
+  free(ctx);
+  return MC_OK;
+}

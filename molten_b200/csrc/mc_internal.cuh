@@ -1,0 +1,65 @@
+// Internal plumbing shared by the kernel files: the context, the thread-local
+// error message, argument checks and small device helpers.
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+#include <stdarg.h>
+#include <stdio.h>
+#include "../../include/molten_cuda.h"
+#include "mc_numerics.cuh"
+
+struct mc_ctx {
+  int device;
+  cudaStream_t stream;
+  int owns_stream;
+  int num_sms;
+  int max_smem_optin;
+  int l2_bytes;
+  void* nccl_comm;   // ncclComm_t when expert parallelism is initialised
+  int ep_rank;
+  int ep_size;
+  int ep_timeout_ms;
+};
+
+// Records a formatted message for mc_last_error() and returns `code`.
+int mc_fail(int code, const char* fmt, ...);
+
+#define MC_REQUIRE(cond, ...)                                  \
+  do {                                                         \
+    if (!(cond)) return mc_fail(MC_EINVAL, __VA_ARGS__);       \
+  } while (0)
+
+#define MC_CUDA(call)                                                            \
+  do {                                                                           \
+    cudaError_t _e = (call);                                                     \
+    if (_e != cudaSuccess)                                                       \
+      return mc_fail(MC_ECUDA, "%s failed: %s", #call, cudaGetErrorString(_e));  \
+  } while (0)
+
+// Checks the launch that was just issued.
+int mc_after_launch(const char* what);
+
+static inline bool mc_aligned(const void* p, size_t a) { return ((uintptr_t)p % a) == 0; }
+
+// ------------------------------------------------------------ device helpers
+
+// Streaming 16-byte load that skips L1 (weights are read exactly once).
+__device__ __forceinline__ uint4 mc_ldg_stream(const void* p) {
+  uint4 r;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "l"(p));
+  return r;
+}
+
+__device__ __forceinline__ float mc_warp_butterfly(float v) {
+#pragma unroll
+  for (int m = 16; m >= 1; m >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, m));
+  return v;
+}
+
+// 2^-e as a float constant (e in 0..23).
+__device__ __forceinline__ float mc_pow2_neg(int e) { return __uint_as_float((uint32_t)(127 - e) << 23); }
+
+#define MC_MAGIC 0x4B000000u
+#define MC_MAGIC_F 8388608.0f

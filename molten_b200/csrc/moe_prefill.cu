@@ -1,0 +1,229 @@
+// Prefill MoE dispatch around the grouped GEMM: the deterministic counting
+// sort + row-tile list (lfm.metal:1604-1770), the row gather
+// (elementwise.metal:41-52), SwiGLU (elementwise.metal:7-15) and the weighted
+// combine (lfm.metal:915-940).
+//
+// Sort: two launches, one CTA per expert each. Launch 1 counts the expert's
+// pairs (no atomics: every CTA scans the whole id list, 64 x 64 KB from L2 at
+// the 4096-token chunk, so counts are deterministic). Launch 2 derives the
+// expert's offset and tile offset from the 64 counts, scans its pairs in
+// token-major, rank-major order (each thread a contiguous token range, block
+// exclusive scan), and writes ids_sorted / slotpos and its row tiles.
+#include "mc_internal.cuh"
+
+namespace {
+
+__global__ void __launch_bounds__(256)
+sort_count_kernel(const uint32_t* __restrict__ ids, int S, uint32_t* __restrict__ counts) {
+  __shared__ uint32_t red[8];
+  const uint32_t e = blockIdx.x;
+  uint32_t c = 0;
+  for (int i = threadIdx.x; i < S; i += 256) c += (__ldg(ids + i) == e);
+#pragma unroll
+  for (int m = 16; m >= 1; m >>= 1) c += __shfl_xor_sync(0xffffffffu, c, m);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = c;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    uint32_t t = 0;
+    for (int w = 0; w < 8; ++w) t += red[w];
+    counts[e] = t;
+  }
+}
+
+__global__ void __launch_bounds__(256)
+sort_scatter_kernel(const uint32_t* __restrict__ ids, int m, int E, int bm,
+                    const uint32_t* __restrict__ counts, uint32_t* __restrict__ offsets,
+                    uint32_t* __restrict__ ids_sorted, uint32_t* __restrict__ slotpos,
+                    uint4* __restrict__ tiles, uint32_t* __restrict__ n_tiles, int max_tiles) {
+  __shared__ uint32_t warp_tot[8];
+  __shared__ uint32_t base_s[2];
+  const uint32_t e = blockIdx.x;
+  const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
+  if (t == 0) {
+    uint32_t off = 0, toff = 0, all_tiles = 0;
+    for (int j = 0; j < E; ++j) {
+      const uint32_t c = counts[j];
+      const uint32_t nt = (c + bm - 1) / bm;
+      if ((uint32_t)j < e) {
+        off += c;
+        toff += nt;
+      }
+      all_tiles += nt;
+    }
+    base_s[0] = off;
+    base_s[1] = toff;
+    offsets[e] = off;
+    if (e == 0) *n_tiles = all_tiles;
+  }
+  // contiguous token range per thread
+  const int per = (m + 255) / 256;
+  const int t0 = min(m, t * per), t1 = min(m, t0 + per);
+  uint32_t c = 0;
+  for (int tok = t0; tok < t1; ++tok)
+#pragma unroll
+    for (int r = 0; r < 4; ++r) c += (__ldg(ids + 4 * (size_t)tok + r) == e);
+  // block exclusive scan of c
+  uint32_t incl = c;
+#pragma unroll
+  for (int d = 1; d < 32; d <<= 1) {
+    const uint32_t v = __shfl_up_sync(0xffffffffu, incl, d);
+    if (lane >= d) incl += v;
+  }
+  if (lane == 31) warp_tot[warp] = incl;
+  __syncthreads();
+  uint32_t wbase = 0;
+  for (int w = 0; w < warp; ++w) wbase += warp_tot[w];
+  uint32_t pos = base_s[0] + wbase + incl - c;
+  for (int tok = t0; tok < t1; ++tok)
+#pragma unroll
+    for (int r = 0; r < 4; ++r)
+      if (__ldg(ids + 4 * (size_t)tok + r) == e) {
+        ids_sorted[pos] = (uint32_t)tok;
+        slotpos[4 * (size_t)tok + r] = pos;
+        ++pos;
+      }
+  // row tiles of this expert
+  const uint32_t n = counts[e];
+  const uint32_t nt = (n + bm - 1) / bm;
+  for (uint32_t j = t; j < nt; j += 256) {
+    const uint32_t slot = base_s[1] + j;
+    if (slot < (uint32_t)max_tiles) {
+      const uint32_t m0 = base_s[0] + j * bm;
+      tiles[slot] = make_uint4(m0, min(m0 + (uint32_t)bm, base_s[0] + n), e, 0u);
+    }
+  }
+}
+
+__global__ void __launch_bounds__(256)
+gather_rows_kernel(const uint4* __restrict__ table, const uint32_t* __restrict__ ids, int rows,
+                   int h16, uint4* __restrict__ out) {
+  const size_t i = (size_t)blockIdx.x * 256 + threadIdx.x;
+  const size_t total = (size_t)rows * h16;
+  if (i >= total) return;
+  const size_t r = i / h16, c = i % h16;
+  out[i] = __ldg(table + (size_t)__ldg(ids + r) * h16 + c);
+}
+
+__global__ void __launch_bounds__(256)
+silu_mul_kernel(const uint4* __restrict__ g, const uint4* __restrict__ u, uint4* __restrict__ out,
+                size_t n8) {
+  const size_t i = (size_t)blockIdx.x * 256 + threadIdx.x;
+  if (i >= n8) return;
+  const uint4 gv = __ldg(g + i), uv = __ldg(u + i);
+  const uint32_t gw[4] = {gv.x, gv.y, gv.z, gv.w}, uw[4] = {uv.x, uv.y, uv.z, uv.w};
+  uint32_t ow[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    uint32_t o = 0;
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const float gf = mc_bf16_to_f32((uint16_t)(gw[j] >> (16 * h)));
+      const float uf = mc_bf16_to_f32((uint16_t)(uw[j] >> (16 * h)));
+      const float s = mc_round_bf16(mc_silu(gf));
+      o |= (uint32_t)mc_f32_to_bf16(__fmul_rn(s, uf)) << (16 * h);
+    }
+    ow[j] = o;
+  }
+  out[i] = make_uint4(ow[0], ow[1], ow[2], ow[3]);
+}
+
+// out[t][h] = bf16(sum_r bf16(gw[t][r] * ed[slotpos[t][r]][h])), rank order
+// from +0; thread = 8 consecutive h.
+__global__ void __launch_bounds__(256)
+combine_kernel(const uint16_t* __restrict__ ed, const uint32_t* __restrict__ slotpos,
+               const uint16_t* __restrict__ gw, uint16_t* __restrict__ out, int m, int topk,
+               int h8) {
+  const size_t i = (size_t)blockIdx.x * 256 + threadIdx.x;
+  if (i >= (size_t)m * h8) return;
+  const size_t t = i / h8, c = i % h8;
+  float s[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) s[j] = 0.0f;
+  for (int r = 0; r < topk; ++r) {
+    const uint32_t p = __ldg(slotpos + t * topk + r);
+    const float w = mc_bf16_to_f32(__ldg(gw + t * topk + r));
+    const uint4 v = __ldg(reinterpret_cast<const uint4*>(ed + (size_t)p * h8 * 8) + c);
+    const uint32_t vw[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      s[j] = __fadd_rn(s[j], mc_round_bf16(__fmul_rn(
+                                 w, mc_bf16_to_f32((uint16_t)(vw[j >> 1] >> (16 * (j & 1)))))));
+  }
+  uint4 o;
+  o.x = (uint32_t)mc_f32_to_bf16(s[0]) | ((uint32_t)mc_f32_to_bf16(s[1]) << 16);
+  o.y = (uint32_t)mc_f32_to_bf16(s[2]) | ((uint32_t)mc_f32_to_bf16(s[3]) << 16);
+  o.z = (uint32_t)mc_f32_to_bf16(s[4]) | ((uint32_t)mc_f32_to_bf16(s[5]) << 16);
+  o.w = (uint32_t)mc_f32_to_bf16(s[6]) | ((uint32_t)mc_f32_to_bf16(s[7]) << 16);
+  reinterpret_cast<uint4*>(out)[i] = o;
+}
+
+}  // namespace
+
+extern "C" int mc_moe_sort_map(mc_ctx* ctx, const uint32_t* ids, int m, int n_experts, int bm,
+                               uint32_t* counts, uint32_t* offsets, uint32_t* ids_sorted,
+                               uint32_t* slotpos, uint32_t* tiles, uint32_t* n_tiles,
+                               int max_tiles) {
+  MC_REQUIRE(ctx, "moe_sort_map: null context");
+  MC_REQUIRE(m >= 1 && m <= (1 << 22), "moe_sort_map: m %d out of range", m);
+  MC_REQUIRE(n_experts >= 1 && n_experts <= 1024, "moe_sort_map: n_experts %d", n_experts);
+  MC_REQUIRE(bm >= 1 && bm <= 4096, "moe_sort_map: bm %d", bm);
+  MC_REQUIRE(ids && counts && offsets && ids_sorted && slotpos && tiles && n_tiles,
+             "moe_sort_map: null pointer");
+  MC_REQUIRE(mc_aligned(tiles, 16), "moe_sort_map: tiles must be 16-byte aligned");
+  const long need = ((long)m * 4 + bm - 1) / bm + n_experts;
+  MC_REQUIRE(max_tiles >= need, "moe_sort_map: max_tiles %d < %ld", max_tiles, need);
+  sort_count_kernel<<<n_experts, 256, 0, ctx->stream>>>(ids, m * 4, counts);
+  int rc = mc_after_launch("sort_count_kernel");
+  if (rc) return rc;
+  sort_scatter_kernel<<<n_experts, 256, 0, ctx->stream>>>(ids, m, n_experts, bm, counts, offsets,
+                                                          ids_sorted, slotpos,
+                                                          reinterpret_cast<uint4*>(tiles), n_tiles,
+                                                          max_tiles);
+  return mc_after_launch("sort_scatter_kernel");
+}
+
+extern "C" int mc_gather_rows_bf16(mc_ctx* ctx, const uint16_t* table, const uint32_t* ids,
+                                   int rows, int hidden, uint16_t* out) {
+  MC_REQUIRE(ctx, "gather_rows_bf16: null context");
+  MC_REQUIRE(table && ids && out, "gather_rows_bf16: null pointer");
+  MC_REQUIRE(hidden % 8 == 0 && hidden > 0, "gather_rows_bf16: hidden %d must be a multiple of 8",
+             hidden);
+  MC_REQUIRE(mc_aligned(table, 16) && mc_aligned(out, 16), "gather_rows_bf16: 16-byte alignment");
+  MC_REQUIRE(rows >= 0, "gather_rows_bf16: rows %d", rows);
+  if (rows == 0) return MC_OK;
+  const size_t total = (size_t)rows * (hidden / 8);
+  gather_rows_kernel<<<(unsigned)((total + 255) / 256), 256, 0, ctx->stream>>>(
+      reinterpret_cast<const uint4*>(table), ids, rows, hidden / 8, reinterpret_cast<uint4*>(out));
+  return mc_after_launch("gather_rows_kernel");
+}
+
+extern "C" int mc_silu_mul_bf16(mc_ctx* ctx, const uint16_t* gate, const uint16_t* up,
+                                uint16_t* out, size_t n) {
+  MC_REQUIRE(ctx, "silu_mul_bf16: null context");
+  MC_REQUIRE(gate && up && out, "silu_mul_bf16: null pointer");
+  MC_REQUIRE(n % 8 == 0, "silu_mul_bf16: n %zu must be a multiple of 8", n);
+  MC_REQUIRE(mc_aligned(gate, 16) && mc_aligned(up, 16) && mc_aligned(out, 16),
+             "silu_mul_bf16: 16-byte alignment");
+  if (n == 0) return MC_OK;
+  const size_t n8 = n / 8;
+  silu_mul_kernel<<<(unsigned)((n8 + 255) / 256), 256, 0, ctx->stream>>>(
+      reinterpret_cast<const uint4*>(gate), reinterpret_cast<const uint4*>(up),
+      reinterpret_cast<uint4*>(out), n8);
+  return mc_after_launch("silu_mul_kernel");
+}
+
+extern "C" int mc_moe_combine_rows(mc_ctx* ctx, const uint16_t* ed, const uint32_t* slotpos,
+                                   const uint16_t* gw, uint16_t* out, int m, int topk,
+                                   int hidden) {
+  MC_REQUIRE(ctx, "moe_combine_rows: null context");
+  MC_REQUIRE(ed && slotpos && gw && out, "moe_combine_rows: null pointer");
+  MC_REQUIRE(hidden % 8 == 0 && hidden > 0, "moe_combine_rows: hidden %d", hidden);
+  MC_REQUIRE(topk >= 1 && topk <= 8, "moe_combine_rows: topk %d", topk);
+  MC_REQUIRE(mc_aligned(ed, 16) && mc_aligned(out, 16), "moe_combine_rows: 16-byte alignment");
+  MC_REQUIRE(m >= 0, "moe_combine_rows: m %d", m);
+  if (m == 0) return MC_OK;
+  const size_t total = (size_t)m * (hidden / 8);
+  combine_kernel<<<(unsigned)((total + 255) / 256), 256, 0, ctx->stream>>>(ed, slotpos, gw, out, m,
+                                                                           topk, hidden / 8);
+  return mc_after_launch("combine_kernel");
+}

@@ -1,0 +1,283 @@
+"""Op-level mirror of Molten's ``src/kernels/lfm.rs`` / ``elementwise.rs`` over the
+CUDA C ABI.
+
+Each function keeps the reference wrapper's name, argument meaning and
+``ensure!``-style validation (raising ValueError before anything is
+enqueued), then enqueues the sm_100a kernel on the context's stream. Tensors
+are CUDA tensors owned by the caller; nothing here allocates device memory.
+u32 buffers (ids, tokens, counters, codes) are int32 tensors holding the bit
+patterns; the argmax key is an int64 tensor.
+"""
+from __future__ import annotations
+
+import torch
+
+from . import _lib
+from .quant import QuantWeights, check_quant
+
+ARGMAX_GROUPS = 64
+FIXED_HIDDEN = 2048
+FIXED_MOE_INTER = 1536
+ROUTE_SOFTMAX_RENORM = _lib.ROUTE_SOFTMAX_RENORM
+ROUTE_SIGMOID_BIAS = _lib.ROUTE_SIGMOID_BIAS
+
+
+def ensure(cond: bool, msg: str) -> None:
+    if not cond:
+        raise ValueError(msg)
+
+
+def _p(t: torch.Tensor | None) -> int | None:
+    if t is None:
+        return None
+    ensure(t.is_cuda, "tensors must be on the GPU")
+    ensure(t.is_contiguous(), "tensors must be contiguous")
+    return t.data_ptr()
+
+
+class Context:
+    """MetalContext + ComputePass stand-in: one device and stream (metal.rs:91-400).
+
+    By default work goes on torch's current stream of ``device`` at call time,
+    so torch ops and these kernels interleave in order.
+    """
+
+    def __init__(self, device: int | torch.device = 0, stream: torch.cuda.Stream | None = None):
+        dev = torch.device("cuda", device) if isinstance(device, int) else torch.device(device)
+        self.device = dev
+        self._fixed_stream = stream
+        h = _lib.C.c_void_p()
+        s = (stream or torch.cuda.current_stream(dev)).cuda_stream
+        _lib.check(_lib.lib().mc_create(dev.index or 0, s, _lib.C.byref(h)))
+        self.h = h
+
+    @property
+    def handle(self):
+        s = (self._fixed_stream or torch.cuda.current_stream(self.device)).cuda_stream
+        _lib.check(_lib.lib().mc_set_stream(self.h, s))
+        return self.h
+
+    def commit_wait(self) -> None:
+        _lib.check(_lib.lib().mc_sync(self.h))
+
+    def close(self) -> None:
+        if self.h:
+            _lib.lib().mc_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def _bf16(*ts):
+    for t in ts:
+        if t is not None:
+            ensure(t.dtype == torch.bfloat16, "expects BF16")
+
+
+def _u32(*ts):
+    for t in ts:
+        if t is not None:
+            ensure(t.dtype == torch.int32, "expects U32 (int32 storage)")
+
+
+# ----------------------------------------------------------------- decode ops
+
+def gemv_quant(ctx: Context, w: QuantWeights, x: torch.Tensor, y: torch.Tensor) -> None:
+    """gemv_quant (kernels/lfm.rs:112-149): y = W x for rows of x [batch, in]."""
+    n, k = check_quant(w)
+    ensure(x.shape[-1] == k and y.shape[-1] == n, "gemv shape mismatch")
+    batch = x.numel() // k
+    ensure(y.numel() == batch * n, "gemv shape mismatch")
+    _bf16(x, y)
+    _lib.call("mc_gemv_quant", ctx.handle, _lib.C.byref(w.qw()), _p(x), _p(y), batch)
+
+
+def gemv_head_argmax(ctx: Context, w: QuantWeights, x: torch.Tensor, best: torch.Tensor) -> None:
+    """gemv_head_argmax (kernels/lfm.rs:826-844): argmax keys folded into ``best``
+    (int64 [batch], zero before the call)."""
+    n, k = check_quant(w)
+    batch = x.numel() // k
+    ensure(x.numel() == batch * k and best.numel() >= batch and best.dtype == torch.int64,
+           "head argmax input/key")
+    _bf16(x)
+    _lib.call("mc_gemv_head_argmax", ctx.handle, _lib.C.byref(w.qw()), _p(x), _p(best), batch)
+
+
+def token_tail(ctx: Context, best: torch.Tensor, out_tok: torch.Tensor,
+               next: tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor] | None = None,
+               eps: float = 1e-5) -> None:
+    """token_tail (kernels/lfm.rs:850-888). ``next = (embed, norm_w, x, normed)``
+    with a bf16 embedding table [vocab, 2048]."""
+    _u32(out_tok)
+    batch = out_tok.numel()
+    ensure(best.dtype == torch.int64 and best.numel() >= batch, "token tail key")
+    if next is None:
+        _lib.call("mc_token_tail", ctx.handle, _p(best), _p(out_tok), None, 0, None, None, None,
+                  FIXED_HIDDEN, eps, batch)
+        return
+    embed, norm_w, x, normed = next
+    _bf16(embed, norm_w, x, normed)
+    ensure(embed.shape[-1] == FIXED_HIDDEN, "token tail embedding width")
+    for t in (x, normed):
+        ensure(t.numel() == batch * FIXED_HIDDEN, "token tail rows")
+    _lib.call("mc_token_tail", ctx.handle, _p(best), _p(out_tok), _p(embed), embed.shape[0],
+              _p(norm_w), _p(x), _p(normed), FIXED_HIDDEN, eps, batch)
+
+
+def argmax_bf16(ctx: Context, x: torch.Tensor, out: torch.Tensor) -> None:
+    """argmax_bf16 (kernels/lfm.rs:794-820) over rows of bf16 logits."""
+    _bf16(x)
+    _u32(out)
+    n = x.shape[-1]
+    batch = x.numel() // n
+    ensure(out.numel() >= batch, "argmax output")
+    _lib.call("mc_argmax_bf16", ctx.handle, _p(x), n, _p(out), batch)
+
+
+def add_rmsnorm(ctx: Context, h: torch.Tensor, b: torch.Tensor | None, w: torch.Tensor,
+                hout: torch.Tensor | None, out: torch.Tensor, eps: float = 1e-5) -> None:
+    """add_rmsnorm_bf16 (norm.metal:63-136) for hidden 2048."""
+    _bf16(h, b, w, hout, out)
+    batch = h.numel() // FIXED_HIDDEN
+    ensure(h.numel() == batch * FIXED_HIDDEN and out.numel() == h.numel(), "add_rmsnorm shapes")
+    _lib.call("mc_add_rmsnorm", ctx.handle, _p(h), _p(b), _p(w), _p(hout), _p(out),
+              FIXED_HIDDEN, eps, batch)
+
+
+def router_addnorm_route(ctx: Context, h, b, nw, hout, normed, w, logits, bias, ids, weights,
+                         counter, eps: float = 1e-5, route_mode: int = ROUTE_SOFTMAX_RENORM,
+                         route_eps: float = 1e-6) -> None:
+    """router_addnorm_route (kernels/lfm.rs:266-311). ``w`` is the [E, H] router
+    in bf16 (BASELINE) or f32 (reference model); ``bias`` the f32 expert bias
+    (used by the sigmoid mode, may be None)."""
+    e, k = w.shape
+    ensure(e <= 64 and k == FIXED_HIDDEN, "fused router route requires E<=64, H=2048")
+    ensure(w.dtype in (torch.bfloat16, torch.float32), "router dtype")
+    batch = h.numel() // k
+    ensure(logits.numel() == batch * e and logits.dtype == torch.float32, "router logits shape")
+    ensure(bias is None or (bias.numel() == e and bias.dtype == torch.float32), "router bias")
+    for t in (h, b, hout, normed):
+        ensure(t is None or t.numel() == batch * k, "router norm shapes")
+    _bf16(h, b, nw, hout, normed, weights)
+    _u32(ids, counter)
+    ensure(ids.numel() == 4 * batch and weights.numel() == 4 * batch, "route outputs")
+    ensure(counter.numel() >= batch, "route counter shape")
+    dt = _lib.DTYPE_BF16 if w.dtype == torch.bfloat16 else _lib.DTYPE_F32
+    _lib.call("mc_router_addnorm_route", ctx.handle, _p(h), _p(b), _p(nw), _p(hout), _p(normed),
+              _p(w), dt, _p(bias), route_mode, _p(logits), _p(ids), _p(weights), _p(counter), e,
+              k, eps, route_eps, batch)
+
+
+def gemv_f32(ctx: Context, w: torch.Tensor, x: torch.Tensor, y: torch.Tensor) -> None:
+    """gemv_f32 (kernels/lfm.rs:314-335): router logits y = W x (f32 out)."""
+    e, k = w.shape
+    batch = x.numel() // k
+    ensure(y.numel() == batch * e and y.dtype == torch.float32, "gemv_f32 output F32")
+    _bf16(x)
+    dt = _lib.DTYPE_BF16 if w.dtype == torch.bfloat16 else _lib.DTYPE_F32
+    _lib.call("mc_gemv_router", ctx.handle, _p(w), dt, _p(x), _p(y), e, k, batch)
+
+
+def route_token(ctx: Context, logits, bias, ids, weights,
+                route_mode: int = ROUTE_SOFTMAX_RENORM, route_eps: float = 1e-6) -> None:
+    """route_token (kernels/lfm.rs:391-417)."""
+    _u32(ids)
+    _bf16(weights)
+    batch = ids.numel() // 4
+    e = logits.numel() // batch
+    ensure(e <= 64 and logits.dtype == torch.float32, "router logits")
+    _lib.call("mc_route_token", ctx.handle, _p(logits), e, route_mode, _p(bias), route_eps,
+              _p(ids), _p(weights), batch)
+
+
+def gemv_gather_act(ctx: Context, gate: QuantWeights, up: QuantWeights, x: torch.Tensor,
+                    ids: torch.Tensor, act: torch.Tensor, n_experts: int = 64) -> None:
+    """gemv_gather_act (kernels/lfm.rs:421-460)."""
+    check_quant(gate)
+    check_quant(up)
+    k = x.shape[-1]
+    batch = x.numel() // k
+    n = gate.out_features // n_experts
+    ensure(act.numel() == batch * 4 * n, "act shape")
+    ensure(k == FIXED_HIDDEN and gate.in_features == k and up.in_features == k,
+           "gather act is the compile-time expert shape")
+    _bf16(x, act)
+    _u32(ids)
+    _lib.call("mc_gemv_gather_act", ctx.handle, _lib.C.byref(gate.qw()), _lib.C.byref(up.qw()),
+              _p(x), _p(ids), _p(act), n_experts, batch)
+
+
+def gemv_gather_down_combine4(ctx: Context, down: QuantWeights, act: torch.Tensor,
+                              ids: torch.Tensor, weights: torch.Tensor, out: torch.Tensor,
+                              n_experts: int = 64) -> None:
+    """gemv_gather_down_combine4 (kernels/lfm.rs:499-533)."""
+    check_quant(down)
+    k = down.in_features
+    n = down.out_features // n_experts
+    batch = out.numel() // n
+    ensure(act.numel() == batch * 4 * k and weights.numel() == batch * 4, "combine shapes")
+    _bf16(act, weights, out)
+    _u32(ids)
+    _lib.call("mc_gemv_gather_down_combine4", ctx.handle, _lib.C.byref(down.qw()), _p(act),
+              _p(ids), _p(weights), _p(out), n_experts, batch)
+
+
+# ---------------------------------------------------------------- prefill ops
+
+def moe_route_batch(ctx: Context, logits, bias, ids, gw, m: int,
+                    route_mode: int = ROUTE_SOFTMAX_RENORM, route_eps: float = 1e-6) -> None:
+    """moe_route_batch (kernels/lfm.rs:536-555)."""
+    e = logits.numel() // m
+    ensure(ids.numel() == m * 4 and gw.numel() == m * 4, "route batch shapes")
+    _u32(ids)
+    _bf16(gw)
+    _lib.call("mc_moe_route_batch", ctx.handle, _p(logits), m, e, route_mode, _p(bias),
+              route_eps, _p(ids), _p(gw))
+
+
+def moe_sort_map(ctx: Context, ids, counts, offsets, ids_sorted, slotpos, tiles, n_tiles,
+                 m: int, bm: int = 128) -> None:
+    """moe_zero_counts .. moe_blocks (kernels/lfm.rs:557-697) in two launches."""
+    e = counts.numel()
+    _u32(ids, counts, offsets, ids_sorted, slotpos, tiles, n_tiles)
+    ensure(tiles.numel() % 4 == 0, "tile list is uint4 entries")
+    _lib.call("mc_moe_sort_map", ctx.handle, _p(ids), m, e, bm, _p(counts), _p(offsets),
+              _p(ids_sorted), _p(slotpos), _p(tiles), _p(n_tiles), tiles.numel() // 4)
+
+
+def gather_rows_bf16(ctx: Context, table: torch.Tensor, ids: torch.Tensor,
+                     out: torch.Tensor) -> None:
+    """gather_rows_bf16 (elementwise.rs:59-104)."""
+    _bf16(table, out)
+    _u32(ids)
+    h = table.shape[-1]
+    ensure(out.numel() == ids.numel() * h, "gather out shape")
+    _lib.call("mc_gather_rows_bf16", ctx.handle, _p(table), _p(ids), ids.numel(), h, _p(out))
+
+
+def silu_mul_bf16(ctx: Context, gate: torch.Tensor, up: torch.Tensor, out: torch.Tensor) -> None:
+    """silu_mul_bf16 (elementwise.rs:48-56)."""
+    _bf16(gate, up, out)
+    ensure(gate.numel() == up.numel() == out.numel(), "size mismatch in silu_mul_bf16")
+    _lib.call("mc_silu_mul_bf16", ctx.handle, _p(gate), _p(up), _p(out), gate.numel())
+
+
+def moe_combine_rows(ctx: Context, sorted_rows, slotpos, weights, out, topk: int = 4) -> None:
+    """moe_combine_rows (kernels/lfm.rs:701-756)."""
+    m, h = out.shape
+    ensure(sorted_rows.shape[-1] == h and sorted_rows.numel() >= m * topk * h,
+           "combine sorted shape")
+    _bf16(sorted_rows, weights, out)
+    _u32(slotpos)
+    _lib.call("mc_moe_combine_rows", ctx.handle, _p(sorted_rows), _p(slotpos), _p(weights),
+              _p(out), m, topk, h)
+
+
+def eval_math(ctx: Context, op: int, x: torch.Tensor, y: torch.Tensor) -> None:
+    """Device math probe (0 exp, 1 silu, 2 sigmoid, 3 bf16 rounding)."""
+    ensure(x.dtype == torch.float32 and y.dtype == torch.float32, "f32 only")
+    _lib.call("mc_eval_math", ctx.handle, op, _p(x), _p(y), x.numel())

@@ -1,0 +1,548 @@
+/*
+ * TEST INFRASTRUCTURE ONLY -- the CPU oracle for the quantized MoE matmul path.
+ *
+ * Only tests/, __graft_entry__.smoke() and bench.py's cpu_baseline /
+ * --impl reference leg may load this library, and only as the checker or the
+ * timed CPU baseline. The product (molten_b200/) never calls it.
+ *
+ * PARITY UNPINNED: the reference (zhangshuibai/molten) is Rust + Metal and
+ * cannot run on this machine, and it ships no tests, fixtures or golden
+ * vectors for this path. This file restates the reference's arithmetic from
+ * its Metal sources (file:line cited per function, paths inside the
+ * reference project) and fixes every fp32 reduction order so that the CUDA
+ * kernels can be checked bit for bit. Where the reference's order is that of
+ * Apple's simd_sum (unspecified), the canonical order below is this
+ * project's choice, shared with the CUDA kernels and documented in
+ * DESIGN.md. It is pinned by hand-computable known answers in
+ * tests/test_oracle.py and by the committed fixtures in tests/golden/.
+ *
+ * Build: oracle/build.py (gcc -O2 -ffp-contract=off; fmaf only where named).
+ *
+ * Conventions (weights.rs:7-20, quant.rs:1-3, lfm.metal:185-199):
+ *   Q4: codes u32[N][K/8], 8 codes per word, low nibble first.
+ *   Q6: codes are a little-endian bit stream, code k at bits 6k..6k+5
+ *       (MLX's 4-codes-in-3-bytes packing).
+ *   scales, biases: bf16[N][K/64]; w = s*q + b.
+ *   Activations bf16; accumulation fp32.
+ */
+#include <math.h>
+#include <stdint.h>
+#include <stdlib.h>
+#include <string.h>
+
+/* ------------------------------------------------------------ numerics */
+
+static float f_of(uint32_t u) { float f; memcpy(&f, &u, 4); return f; }
+static uint32_t u_of(float f) { uint32_t u; memcpy(&u, &f, 4); return u; }
+
+float or_bf16_to_f32(uint16_t h) { return f_of(((uint32_t)h) << 16); }
+
+/* round to nearest even; NaN -> quiet NaN (MLX bfloat cast). */
+uint16_t or_f32_to_bf16(float f) {
+  uint32_t u = u_of(f);
+  if ((u & 0x7fffffffu) > 0x7f800000u) return (uint16_t)((u >> 16) | 0x0040u);
+  u += 0x7fffu + ((u >> 16) & 1u);
+  return (uint16_t)(u >> 16);
+}
+
+static float rb(float f) { return or_bf16_to_f32(or_f32_to_bf16(f)); }
+static float bf(uint16_t h) { return or_bf16_to_f32(h); }
+
+/* exp(x): Cody-Waite reduction by ln2 (LN2_HI = 22713/2^15), degree-7 Taylor
+ * polynomial in Horner form, 2^n applied as two power-of-two factors. The
+ * same steps as the CUDA side's mc_exp, written again here. */
+float or_exp(float x) {
+  const float LOG2E = 1.44269502162933349609375f;
+  const float LN2_HI = 0.693145751953125f;
+  const float LN2_LO = 1.42860682030941723212e-06f;
+  if (x != x) return x;
+  if (x > 88.8f) return f_of(0x7f800000u);
+  if (x < -104.0f) return 0.0f;
+  float n = rintf(x * LOG2E);
+  float r = fmaf(-n, LN2_HI, x);
+  r = fmaf(-n, LN2_LO, r);
+  float p = 1.98412698412698412698e-04f;
+  p = fmaf(p, r, 1.38888888888888888889e-03f);
+  p = fmaf(p, r, 8.33333333333333333333e-03f);
+  p = fmaf(p, r, 4.16666666666666666667e-02f);
+  p = fmaf(p, r, 1.66666666666666666667e-01f);
+  p = fmaf(p, r, 0.5f);
+  p = fmaf(p, r, 1.0f);
+  p = fmaf(p, r, 1.0f);
+  int ni = (int)n;
+  int n1 = ni / 2;
+  int n2 = ni - n1;
+  float s1 = f_of((uint32_t)(n1 + 127) << 23);
+  float s2 = f_of((uint32_t)(n2 + 127) << 23);
+  return (p * s1) * s2;
+}
+
+/* elementwise.metal:11-13 / lfm.metal:1442-1443: g / (1 + exp(-g)). */
+float or_silu(float g) { return g / (1.0f + or_exp(-g)); }
+/* lfm.metal:629-630. */
+float or_sigmoid(float z) { return 1.0f / (1.0f + or_exp(-z)); }
+
+/* lfm.metal:1200-1207. */
+uint64_t or_argmax_key(float v, uint32_t i) {
+  uint32_t u = u_of(v);
+  if ((u << 1) == 0u) u = 0u;
+  uint32_t o = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+  return ((uint64_t)o << 32) | (uint64_t)(~i);
+}
+
+/* lfm.metal:1119-1124. */
+static int better(float v, uint32_t i, float bv, uint32_t bi) {
+  return v > bv || (v == bv && i < bi);
+}
+
+/* 32-lane xor butterfly (masks 16, 8, 4, 2, 1); every lane ends with the
+ * same bits because fp32 addition is commutative. */
+static float butterfly32(float* v) {
+  for (int m = 16; m >= 1; m >>= 1) {
+    float t[32];
+    for (int l = 0; l < 32; ++l) t[l] = v[l] + v[l ^ m];
+    memcpy(v, t, sizeof t);
+  }
+  return v[0];
+}
+
+/* ------------------------------------------------------ quantized GEMV row
+ *
+ * Reference: dot_word_q4 + GEMV_Q4_BODY, lfm.metal:102-139 (per 8-code word
+ * s*(q.x) + b*(sum x)); decode_q6/_reg lfm.metal:186-243.
+ * Canonical order (this project's; Apple's simd_sum order is unspecified):
+ *   - lane l (0..31) owns groups g = l, l+32, ... and keeps acc_l, starting
+ *     at +0.0f;
+ *   - per group (64 codes): two chains cE (even k) and cO (odd k), each
+ *     cX = fmaf(q_k * 2^e_k, x_k * 2^-e_k, cX) in increasing k, where e_k is
+ *     the bit position the GPU leaves code k at (E4 / E6 below; the product
+ *     is exact, the power-of-two pre-scaling of x is what the GPU reads);
+ *     qx = cE + cO;
+ *   - xg_g = x_{64g} + x_{64g+1} + ... (left to right) -- shared by all rows;
+ *   - term = fmaf(s_g, qx, b_g * xg_g); acc_l = acc_l + term;
+ *   - row sum = 32-lane xor butterfly of acc_l.
+ */
+static const int E4[8] = {0, 4, 8, 12, 16, 20, 16, 20};
+static const int E6[4] = {0, 6, 12, 10};
+
+static void prescale(const float* x, int K, int bits, float* xs, float* xg) {
+  for (int k = 0; k < K; ++k) {
+    int e = bits == 4 ? E4[k & 7] : E6[k & 3];
+    xs[k] = x[k] * ldexpf(1.0f, -e);
+  }
+  for (int g = 0; g < K / 64; ++g) {
+    float s = x[64 * g];
+    for (int i = 1; i < 64; ++i) s = s + x[64 * g + i];
+    xg[g] = s;
+  }
+}
+
+static inline uint32_t code_at(const uint8_t* row, int bits, int k) {
+  if (bits == 4) {
+    uint32_t w;
+    memcpy(&w, row + 4 * (k >> 3), 4);
+    return (w >> (4 * (k & 7))) & 15u;
+  }
+  /* 6-bit little-endian stream */
+  int bit = 6 * k;
+  uint32_t lo = row[bit >> 3];
+  /* a code at bit offset 0 or 2 of its byte does not reach the next byte
+   * (and for the last code of a row that byte is outside the row) */
+  uint32_t hi = (bit & 7) > 2 ? row[(bit >> 3) + 1] : 0;
+  uint32_t v = lo | (hi << 8);
+  return (v >> (bit & 7)) & 63u;
+}
+
+static float row_dot(const uint8_t* row, const uint16_t* s, const uint16_t* b,
+                     int bits, int K, const float* xs, const float* xg) {
+  float acc[32];
+  for (int l = 0; l < 32; ++l) acc[l] = 0.0f;
+  const int G = K / 64;
+  for (int g = 0; g < G; ++g) {
+    float cE = 0.0f, cO = 0.0f;
+    for (int i = 0; i < 64; ++i) {
+      int k = 64 * g + i;
+      uint32_t q = code_at(row, bits, k);
+      int e = bits == 4 ? E4[k & 7] : E6[k & 3];
+      float qf = (float)(q << e);
+      if (k & 1) cO = fmaf(qf, xs[k], cO);
+      else cE = fmaf(qf, xs[k], cE);
+    }
+    float qx = cE + cO;
+    float term = fmaf(bf(s[g]), qx, bf(b[g]) * xg[g]);
+    acc[g & 31] = acc[g & 31] + term;
+  }
+  return butterfly32(acc);
+}
+
+static size_t row_bytes(int bits, int K) { return (size_t)K * bits / 8; }
+
+/* gemv_quant (kernels/lfm.rs:112-149): y[b][n] = bf16(row_dot). acc_out
+ * (nullable) receives the fp32 sums. x: bf16 [B][K]. */
+void or_gemv_quant(const void* codes, const uint16_t* scales, const uint16_t* biases,
+                   int bits, int N, int K, const uint16_t* x, int B,
+                   uint16_t* y, float* acc_out) {
+  float* xf = (float*)malloc(sizeof(float) * K);
+  float* xs = (float*)malloc(sizeof(float) * K);
+  float* xg = (float*)malloc(sizeof(float) * (K / 64));
+  const int G = K / 64;
+  for (int bb = 0; bb < B; ++bb) {
+    for (int k = 0; k < K; ++k) xf[k] = bf(x[(size_t)bb * K + k]);
+    prescale(xf, K, bits, xs, xg);
+    for (int n = 0; n < N; ++n) {
+      const uint8_t* row = (const uint8_t*)codes + (size_t)n * row_bytes(bits, K);
+      float v = row_dot(row, scales + (size_t)n * G, biases + (size_t)n * G, bits, K, xs, xg);
+      if (acc_out) acc_out[(size_t)bb * N + n] = v;
+      if (y) y[(size_t)bb * N + n] = or_f32_to_bf16(v);
+    }
+  }
+  free(xf); free(xs); free(xg);
+}
+
+/* gemv_head_argmax + token_tail (kernels/lfm.rs:826-888; lfm.metal:1215-1291):
+ * logits are bf16-rounded, the winner is "value desc, index asc" (ties to the
+ * lowest token id), reported as the 64-bit key and the token. */
+void or_head_argmax(const void* codes, const uint16_t* scales, const uint16_t* biases,
+                    int bits, int N, int K, const uint16_t* x, int B,
+                    uint64_t* keys, uint32_t* tokens) {
+  float* xf = (float*)malloc(sizeof(float) * K);
+  float* xs = (float*)malloc(sizeof(float) * K);
+  float* xg = (float*)malloc(sizeof(float) * (K / 64));
+  const int G = K / 64;
+  for (int bb = 0; bb < B; ++bb) {
+    for (int k = 0; k < K; ++k) xf[k] = bf(x[(size_t)bb * K + k]);
+    prescale(xf, K, bits, xs, xg);
+    float bv = -INFINITY;
+    uint32_t bi = 0;
+    for (int n = 0; n < N; ++n) {
+      const uint8_t* row = (const uint8_t*)codes + (size_t)n * row_bytes(bits, K);
+      float v = rb(row_dot(row, scales + (size_t)n * G, biases + (size_t)n * G, bits, K, xs, xg));
+      if (better(v, (uint32_t)n, bv, bi)) { bv = v; bi = (uint32_t)n; }
+    }
+    if (keys) keys[bb] = or_argmax_key(bv, bi);
+    if (tokens) tokens[bb] = bi;
+  }
+  free(xf); free(xs); free(xg);
+}
+
+/* argmax_bf16 (kernels/lfm.rs:794-820; lfm.metal:1126-1192): ties to the
+ * lowest index; the result does not depend on the partition. */
+void or_argmax_bf16(const uint16_t* logits, int n, int B, uint32_t* out) {
+  for (int bb = 0; bb < B; ++bb) {
+    float bv = -INFINITY;
+    uint32_t bi = 0;
+    for (int i = 0; i < n; ++i) {
+      float v = bf(logits[(size_t)bb * n + i]);
+      if (better(v, (uint32_t)i, bv, bi)) { bv = v; bi = (uint32_t)i; }
+    }
+    out[bb] = bi;
+  }
+}
+
+/* ------------------------------------------------------- add + RMSNorm
+ * lfm_norm_row_v8_tg lfm.metal:306-366 (bf16 residual add, fp32 sum of
+ * squares, total/H + eps, bf16 output). Canonical order: 256 partials, partial
+ * t = fmaf chain over k = 8t..8t+7; 8 warps of 32 partials each reduced by the
+ * xor butterfly; total = ((p0 + p1) + p2) ... + p7; inv = 1/sqrtf(total/H +
+ * eps) (IEEE sqrt and divide); n_k = bf16((h'_k * inv) * w_k). H = 2048.
+ * b (the residual addend) may be NULL (treated as all zeros, h' = h). */
+void or_add_rmsnorm(const uint16_t* h, const uint16_t* b, const uint16_t* w, int H,
+                    float eps, uint16_t* hout, uint16_t* nout) {
+  float* hp = (float*)malloc(sizeof(float) * H);
+  for (int k = 0; k < H; ++k) {
+    float v = b ? bf(h[k]) + bf(b[k]) : bf(h[k]);
+    hp[k] = rb(v);
+    if (hout) hout[k] = or_f32_to_bf16(v);
+  }
+  const int T = 256, per = H / 256;
+  float part[256];
+  for (int t = 0; t < T; ++t) {
+    float a = 0.0f;
+    for (int i = 0; i < per; ++i) { float v = hp[per * t + i]; a = fmaf(v, v, a); }
+    part[t] = a;
+  }
+  float total = 0.0f;
+  for (int wp = 0; wp < 8; ++wp) total = total + butterfly32(part + 32 * wp);
+  float inv = 1.0f / sqrtf(total / (float)H + eps);
+  for (int k = 0; k < H; ++k) nout[k] = or_f32_to_bf16((hp[k] * inv) * bf(w[k]));
+  free(hp);
+}
+
+/* --------------------------------------------------------- router GEMV
+ * lfm_router_lane_sum_tg_fixed lfm.metal:728-771 (lane-strided fp32 dot,
+ * simd_sum). Canonical order: lane l owns k = 256j + 8l + i (j outer, i
+ * inner), acc = fmaf(W_k, n_k, acc) from +0; 32-lane xor butterfly.
+ * w_dtype 0 = bf16 router (BASELINE cfg1), 1 = f32 router (reference model).
+ * K must be a multiple of 256. */
+void or_router_logits(const uint16_t* normed, const void* W, int w_dtype, int E, int K,
+                      float* logits) {
+  for (int e = 0; e < E; ++e) {
+    float acc[32];
+    for (int l = 0; l < 32; ++l) {
+      float a = 0.0f;
+      for (int j = 0; j < K / 256; ++j)
+        for (int i = 0; i < 8; ++i) {
+          int k = 256 * j + 8 * l + i;
+          float wv = w_dtype == 0 ? bf(((const uint16_t*)W)[(size_t)e * K + k])
+                                  : ((const float*)W)[(size_t)e * K + k];
+          a = fmaf(wv, bf(normed[k]), a);
+        }
+      acc[l] = a;
+    }
+    logits[e] = butterfly32(acc);
+  }
+}
+
+/* --------------------------------------------------------------- top-4
+ * Selection: lfm_topk_warp_b lfm.metal:619-675 and lfm_moe_route_batch
+ * :1558-1602 -- repeat TOPK times: the unused candidate with the greatest
+ * value, an exact tie to the lower expert id.
+ * mode 0 (softmax_renorm, BASELINE cfg1/cfg3): value = raw logit (softmax is
+ *   monotone); weights = softmax over all experts renormalised over the
+ *   selected ones, computed as e_r = exp(z_r - z_top1), den = ((e0+e1)+e2)+e3,
+ *   w_r = bf16(e_r / den) (the full-softmax denominator cancels).
+ * mode 1 (sigmoid_bias, the reference model): s = sigmoid(z); value = s +
+ *   bias; den = eps; den += s_r in rank order; w_r = bf16(s_r / den). */
+void or_route_topk(const float* z, int E, int topk, int mode, const float* bias,
+                   float eps, uint32_t* ids, uint16_t* wts) {
+  float val[256], s[256];
+  int used[256];
+  for (int e = 0; e < E; ++e) {
+    used[e] = 0;
+    if (mode == 0) { s[e] = z[e]; val[e] = z[e]; }
+    else { s[e] = or_sigmoid(z[e]); val[e] = s[e] + (bias ? bias[e] : 0.0f); }
+  }
+  uint32_t ch[8];
+  for (int r = 0; r < topk; ++r) {
+    float bv = -INFINITY; uint32_t bi = 0xffffffffu;
+    for (int e = 0; e < E; ++e) {
+      if (used[e]) continue;
+      if (better(val[e], (uint32_t)e, bv, bi)) { bv = val[e]; bi = (uint32_t)e; }
+    }
+    if (bi == 0xffffffffu) bi = 0;
+    ch[r] = bi; used[bi] = 1;
+  }
+  if (mode == 0) {
+    float ex[8], den = 0.0f;
+    for (int r = 0; r < topk; ++r) { ex[r] = or_exp(z[ch[r]] - z[ch[0]]); den = den + ex[r]; }
+    for (int r = 0; r < topk; ++r) { ids[r] = ch[r]; wts[r] = or_f32_to_bf16(ex[r] / den); }
+  } else {
+    float den = eps;
+    for (int r = 0; r < topk; ++r) den = den + s[ch[r]];
+    for (int r = 0; r < topk; ++r) { ids[r] = ch[r]; wts[r] = or_f32_to_bf16(s[ch[r]] / den); }
+  }
+}
+
+/* router_addnorm_route (kernels/lfm.rs:266-311; lfm.metal:773-854), batch B
+ * independent rows. h, b (nullable), out rows bf16 [B][H]; logits f32 [B][E];
+ * ids u32 [B][4]; wts bf16 [B][4]. */
+void or_router_addnorm_route(const uint16_t* h, const uint16_t* b, const uint16_t* norm_w,
+                             const void* W, int w_dtype, const float* ebias, int mode,
+                             int E, int H, float eps, float route_eps, int B,
+                             uint16_t* hout, uint16_t* normed, float* logits,
+                             uint32_t* ids, uint16_t* wts) {
+  for (int bb = 0; bb < B; ++bb) {
+    const size_t o = (size_t)bb * H;
+    or_add_rmsnorm(h + o, b ? b + o : NULL, norm_w, H, eps, hout + o, normed + o);
+    or_router_logits(normed + o, W, w_dtype, E, H, logits + (size_t)bb * E);
+    or_route_topk(logits + (size_t)bb * E, E, 4, mode, ebias, route_eps, ids + 4 * bb,
+                  wts + 4 * bb);
+  }
+}
+
+/* gemv_gather_act (kernels/lfm.rs:421-460; lfm.metal:1392-1445): for slot r
+ * and row i, rows ids[r]*I + i of the stacked [E*I, H] gate/up weights;
+ * act = bf16(bf16(silu(bf16(gate))) * bf16(up)). x: bf16 [B][H];
+ * ids [B][4]; act bf16 [B][4][I]. */
+void or_gemv_gather_act(const void* gc, const uint16_t* gs, const uint16_t* gb,
+                        const void* uc, const uint16_t* us, const uint16_t* ub,
+                        int I, int H, const uint16_t* x, const uint32_t* ids, int B,
+                        uint16_t* act) {
+  float* xf = (float*)malloc(sizeof(float) * H);
+  float* xs = (float*)malloc(sizeof(float) * H);
+  float* xg = (float*)malloc(sizeof(float) * (H / 64));
+  const int G = H / 64;
+  const size_t rb_ = row_bytes(4, H);
+  for (int bb = 0; bb < B; ++bb) {
+    for (int k = 0; k < H; ++k) xf[k] = bf(x[(size_t)bb * H + k]);
+    prescale(xf, H, 4, xs, xg);
+    for (int r = 0; r < 4; ++r) {
+      const size_t e = ids[4 * bb + r];
+      for (int i = 0; i < I; ++i) {
+        const size_t row = e * I + i;
+        float g = row_dot((const uint8_t*)gc + row * rb_, gs + row * G, gb + row * G, 4, H, xs, xg);
+        float u = row_dot((const uint8_t*)uc + row * rb_, us + row * G, ub + row * G, 4, H, xs, xg);
+        float sl = rb(or_silu(rb(g)));
+        act[((size_t)bb * 4 + r) * I + i] = or_f32_to_bf16(sl * rb(u));
+      }
+    }
+  }
+  free(xf); free(xs); free(xg);
+}
+
+/* gemv_gather_down_combine4 (kernels/lfm.rs:499-533; lfm.metal:1503-1554):
+ * p_r = bf16(row_dot(down row ids[r]*H + i, act_r)); out = bf16(sum over r in
+ * rank order, from 0, of bf16(w_r * p_r)). act bf16 [B][4][I]; out [B][H]. */
+void or_gemv_gather_down_combine4(const void* dc, const uint16_t* ds, const uint16_t* db,
+                                  int H, int I, const uint16_t* act, const uint32_t* ids,
+                                  const uint16_t* wts, int B, uint16_t* out) {
+  float* xf = (float*)malloc(sizeof(float) * 4 * I);
+  float* xs = (float*)malloc(sizeof(float) * 4 * I);
+  float* xg = (float*)malloc(sizeof(float) * 4 * (I / 64));
+  const int G = I / 64;
+  const size_t rb_ = row_bytes(4, I);
+  for (int bb = 0; bb < B; ++bb) {
+    for (int r = 0; r < 4; ++r) {
+      for (int k = 0; k < I; ++k) xf[r * I + k] = bf(act[((size_t)bb * 4 + r) * I + k]);
+      prescale(xf + r * I, I, 4, xs + r * I, xg + r * G);
+    }
+    for (int i = 0; i < H; ++i) {
+      float tot = 0.0f;
+      for (int r = 0; r < 4; ++r) {
+        const size_t row = (size_t)ids[4 * bb + r] * H + i;
+        float p = rb(row_dot((const uint8_t*)dc + row * rb_, ds + row * G, db + row * G, 4, I,
+                             xs + r * I, xg + r * G));
+        tot = tot + rb(bf(wts[4 * bb + r]) * p);
+      }
+      out[(size_t)bb * H + i] = or_f32_to_bf16(tot);
+    }
+  }
+  free(xf); free(xs); free(xg);
+}
+
+/* ------------------------------------------------------------- prefill */
+
+/* moe_route_batch (kernels/lfm.rs:536-555; lfm.metal:1558-1602). */
+void or_moe_route_batch(const float* logits, int m, int E, int mode, const float* bias,
+                        float eps, uint32_t* ids, uint16_t* gw) {
+  for (int t = 0; t < m; ++t)
+    or_route_topk(logits + (size_t)t * E, E, 4, mode, bias, eps, ids + 4 * (size_t)t,
+                  gw + 4 * (size_t)t);
+}
+
+/* moe_count_slots / moe_offsets / moe_sorted (lfm.metal:1604-1686): per-expert
+ * counts, exclusive scan, and the stable token-major, rank-major scatter:
+ * ids_sorted[pos] = t, slotpos[t*topk + r] = pos. */
+void or_moe_sort(const uint32_t* ids, int m, int topk, int E, uint32_t* counts,
+                 uint32_t* offsets, uint32_t* ids_sorted, uint32_t* slotpos) {
+  for (int e = 0; e < E; ++e) counts[e] = 0;
+  for (size_t i = 0; i < (size_t)m * topk; ++i) counts[ids[i]]++;
+  uint32_t acc = 0;
+  for (int e = 0; e < E; ++e) { offsets[e] = acc; acc += counts[e]; }
+  uint32_t* pos = (uint32_t*)malloc(sizeof(uint32_t) * E);
+  memcpy(pos, offsets, sizeof(uint32_t) * E);
+  for (int t = 0; t < m; ++t)
+    for (int r = 0; r < topk; ++r) {
+      uint32_t e = ids[(size_t)t * topk + r];
+      uint32_t p = pos[e]++;
+      ids_sorted[p] = (uint32_t)t;
+      slotpos[(size_t)t * topk + r] = p;
+    }
+  free(pos);
+}
+
+/* dequantize<bfloat16, 8, 4> quant_nax.metal:2947-2953: w = bf16(s*q + b)
+ * (s*q is exact in fp32, so the one rounding is of the sum). out bf16 [N][K]. */
+void or_dequant_q4(const uint32_t* codes, const uint16_t* scales, const uint16_t* biases,
+                   int N, int K, uint16_t* out) {
+  const int G = K / 64;
+  for (int n = 0; n < N; ++n)
+    for (int k = 0; k < K; ++k) {
+      uint32_t w = codes[(size_t)n * (K / 8) + k / 8];
+      float q = (float)((w >> (4 * (k & 7))) & 15u);
+      float s = bf(scales[(size_t)n * G + k / 64]), b = bf(biases[(size_t)n * G + k / 64]);
+      out[(size_t)n * K + k] = or_f32_to_bf16(fmaf(s, q, b));
+    }
+}
+
+/* Grouped Q4 GEMM reference (quant.rs:228-266 -> lfm_qmm_t_body
+ * quant_nax.metal:4091-4234): for sorted row i of expert e,
+ * C[i][n] = bf16(sum_k A[i][k] * Wdeq[e*N + n][k]) with fp32 accumulation in
+ * increasing k (the tensor-op order on the GPU differs, hence a tolerance).
+ * A rows are given already in sorted order (gx / act). */
+void or_gemm_q4_grouped(const uint16_t* A, int S, int K, const uint32_t* codes,
+                        const uint16_t* scales, const uint16_t* biases, int N,
+                        const uint32_t* counts, const uint32_t* offsets, int E,
+                        uint16_t* C, float* Cacc) {
+  uint16_t* wd = (uint16_t*)malloc(sizeof(uint16_t) * (size_t)N * K);
+  float* af = (float*)malloc(sizeof(float) * K);
+  float* wf = (float*)malloc(sizeof(float) * (size_t)N * K);
+  for (int e = 0; e < E; ++e) {
+    if (counts[e] == 0) continue;
+    or_dequant_q4(codes + (size_t)e * N * (K / 8), scales + (size_t)e * N * (K / 64),
+                  biases + (size_t)e * N * (K / 64), N, K, wd);
+    for (size_t j = 0; j < (size_t)N * K; ++j) wf[j] = bf(wd[j]);
+    for (uint32_t i = offsets[e]; i < offsets[e] + counts[e]; ++i) {
+      for (int k = 0; k < K; ++k) af[k] = bf(A[(size_t)i * K + k]);
+      for (int n = 0; n < N; ++n) {
+        const float* wr = wf + (size_t)n * K;
+        float a = 0.0f;
+        for (int k = 0; k < K; ++k) a = a + af[k] * wr[k];
+        if (Cacc) Cacc[(size_t)i * N + n] = a;
+        C[(size_t)i * N + n] = or_f32_to_bf16(a);
+      }
+    }
+  }
+  (void)S;
+  free(wd); free(af); free(wf);
+}
+
+/* silu_mul_bf16 (elementwise.metal:7-15). */
+void or_silu_mul(const uint16_t* g, const uint16_t* u, size_t n, uint16_t* out) {
+  for (size_t i = 0; i < n; ++i)
+    out[i] = or_f32_to_bf16(rb(or_silu(bf(g[i]))) * bf(u[i]));
+}
+
+/* gather_rows_bf16 (elementwise.metal:19-52). */
+void or_gather_rows(const uint16_t* table, const uint32_t* ids, int rows, int H,
+                    uint16_t* out) {
+  for (int r = 0; r < rows; ++r)
+    memcpy(out + (size_t)r * H, table + (size_t)ids[r] * H, sizeof(uint16_t) * H);
+}
+
+/* moe_combine_rows (kernels/lfm.rs:701-756; lfm.metal:859-940):
+ * out[t][h] = bf16(sum_r (from 0, rank order) bf16(gw[t][r] * ed[slotpos][h])). */
+void or_moe_combine(const uint16_t* ed, const uint32_t* slotpos, const uint16_t* gw, int m,
+                    int topk, int H, uint16_t* out) {
+  for (int t = 0; t < m; ++t)
+    for (int h = 0; h < H; ++h) {
+      float s = 0.0f;
+      for (int r = 0; r < topk; ++r) {
+        uint32_t p = slotpos[(size_t)t * topk + r];
+        s = s + rb(bf(gw[(size_t)t * topk + r]) * bf(ed[(size_t)p * H + h]));
+      }
+      out[(size_t)t * H + h] = or_f32_to_bf16(s);
+    }
+}
+
+/* Whole prefill MoE FFN for a chunk (moe_prefill lfm.rs:847-965, without the
+ * router GEMV: the logits are an input, as in BASELINE cfg3). x: bf16 [m][H];
+ * logits f32 [m][E]; weights stacked [E*I][H] (gate, up) and [E*H][I] (down).
+ * Outputs: ids/gw [m][4]; out bf16 [m][H]. Intermediates optional (NULL). */
+void or_moe_prefill(const uint16_t* x, const float* logits, int m, int E, int H, int I,
+                    int mode, const float* bias,
+                    const uint32_t* gc, const uint16_t* gs, const uint16_t* gb,
+                    const uint32_t* uc, const uint16_t* us, const uint16_t* ub,
+                    const uint32_t* dc, const uint16_t* ds, const uint16_t* db,
+                    uint32_t* ids, uint16_t* gw, uint32_t* ids_sorted, uint32_t* slotpos,
+                    uint16_t* act_out, uint16_t* ed_out, uint16_t* out) {
+  const size_t S = (size_t)m * 4;
+  uint32_t* counts = (uint32_t*)malloc(sizeof(uint32_t) * E);
+  uint32_t* offsets = (uint32_t*)malloc(sizeof(uint32_t) * E);
+  uint16_t* gx = (uint16_t*)malloc(sizeof(uint16_t) * S * H);
+  uint16_t* g = (uint16_t*)malloc(sizeof(uint16_t) * S * I);
+  uint16_t* u = (uint16_t*)malloc(sizeof(uint16_t) * S * I);
+  uint16_t* act = (uint16_t*)malloc(sizeof(uint16_t) * S * I);
+  uint16_t* ed = (uint16_t*)malloc(sizeof(uint16_t) * S * H);
+  or_moe_route_batch(logits, m, E, mode, bias, 1e-6f, ids, gw);
+  or_moe_sort(ids, m, 4, E, counts, offsets, ids_sorted, slotpos);
+  or_gather_rows(x, ids_sorted, (int)S, H, gx);
+  or_gemm_q4_grouped(gx, (int)S, H, gc, gs, gb, I, counts, offsets, E, g, NULL);
+  or_gemm_q4_grouped(gx, (int)S, H, uc, us, ub, I, counts, offsets, E, u, NULL);
+  or_silu_mul(g, u, S * I, act);
+  or_gemm_q4_grouped(act, (int)S, I, dc, ds, db, H, counts, offsets, E, ed, NULL);
+  or_moe_combine(ed, slotpos, gw, m, 4, H, out);
+  if (act_out) memcpy(act_out, act, sizeof(uint16_t) * S * I);
+  if (ed_out) memcpy(ed_out, ed, sizeof(uint16_t) * S * H);
+  free(counts); free(offsets); free(gx); free(g); free(u); free(act); free(ed);
+}
