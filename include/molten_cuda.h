@@ -62,11 +62,11 @@ typedef struct mc_qweights {
 
 /* ---------------------------------------------------------------- context */
 
-/* MetalContext::new (metal.rs:91-147): binds `device`; `stream` is a
- * cudaStream_t to enqueue on, or NULL to create a private one. */
+/* MetalContext::new (metal.rs:91-147): binds `device`; `stream` is the
+ * cudaStream_t to enqueue on (NULL = the default stream). */
 int mc_create(int device, void* stream, mc_ctx** out);
 int mc_destroy(mc_ctx* ctx);
-/* Switches the stream later calls enqueue on (NULL = the private stream). */
+/* Switches the stream later calls enqueue on (NULL = the default stream). */
 int mc_set_stream(mc_ctx* ctx, void* stream);
 /* ComputePass::commit_wait (metal.rs:383-399): waits for all enqueued work
  * and reports any asynchronous CUDA error. */
@@ -151,6 +151,25 @@ int mc_gemv_gather_down_combine4(mc_ctx* ctx, const mc_qweights* down, const uin
                                  const uint32_t* ids, const uint16_t* weights, uint16_t* out,
                                  int n_experts, int batch);
 
+/* moe_decode (lfm.rs:967-1011) behind the fused router (lfm.rs:1154-1169):
+ * one persistent launch does router_addnorm_route + gemv_gather_act +
+ * gemv_gather_down_combine4 for ONE token (batch 1), bit-identical to the
+ * three separate calls. `workspace` holds mc_moe_decode_workspace_words(I)
+ * u32 words, zeroed once before the first call and then owned by one chain
+ * of calls (it keeps an epoch and tagged intermediate values between calls;
+ * workspace[2] != 0 after a call reports a bounded wait that gave up (1) or
+ * an expert id out of range (2); the act rows are the bf16 values
+ * ((uint16_t*)(workspace + 132))[r*I + i]). All row buffers, the weights'
+ * scales/biases and the workspace 16-byte aligned. */
+size_t mc_moe_decode_workspace_words(int moe_inter);
+int mc_moe_decode_layer(mc_ctx* ctx, const uint16_t* h, const uint16_t* b,
+                        const uint16_t* norm_w, uint16_t* h_out, uint16_t* normed,
+                        const void* router_w, int router_dtype, const float* expert_bias,
+                        int route_mode, float* logits, uint32_t* ids, uint16_t* weights,
+                        const mc_qweights* gate, const mc_qweights* up,
+                        const mc_qweights* down, int n_experts, uint16_t* out,
+                        uint32_t* workspace, size_t ws_words, float eps, float route_eps);
+
 /* ----------------------------------------------------------- prefill path */
 
 /* moe_route_batch (kernels/lfm.rs:536-555 -> lfm.metal:1558-1602): per-token
@@ -184,6 +203,14 @@ int mc_moe_combine_rows(mc_ctx* ctx, const uint16_t* ed, const uint32_t* slotpos
                         const uint16_t* gw, uint16_t* out, int m, int topk, int hidden);
 
 /* -------------------------------------------------------------- test aid */
+
+/* Profiling aid: when buf (device, n u64 words) is set, the persistent
+ * kernels record %globaltimer at their phase boundaries, 16 words per CTA
+ * (mc_moe_decode_layer: 0 start, 1 norm, 2 logits published, 3 top-4 known,
+ * 13 copies issued, 8/9 first/last gate-up chunk landed, 4 gate/up done,
+ * 5 act published, 10 act loaded, 11 down rows landed, 12 down computed,
+ * 6 combine, 7 exit). NULL switches it off (the default). */
+int mc_set_trace(mc_ctx* ctx, unsigned long long* buf, int n);
 
 /* Evaluates the library's device math on x[n] into y[n]: op 0 = mc_exp,
  * 1 = SiLU, 2 = sigmoid, 3 = bf16 rounding. Lets tests check the device

@@ -68,12 +68,16 @@ SIGNATURES: dict[str, tuple] = {
     "mc_route_token": (I, [P, P, I, I, P, F, P, P, I]),
     "mc_gemv_gather_act": (I, [P, QP, QP, P, P, P, I, I]),
     "mc_gemv_gather_down_combine4": (I, [P, QP, P, P, P, P, I, I]),
+    "mc_moe_decode_layer": (I, [P, P, P, P, P, P, P, I, P, I, P, P, P, QP, QP, QP, I, P, P,
+                                C.c_size_t, F, F]),
+    "mc_moe_decode_workspace_words": (C.c_size_t, [I]),
     "mc_moe_route_batch": (I, [P, P, I, I, I, P, F, P, P]),
     "mc_moe_sort_map": (I, [P, P, I, I, I, P, P, P, P, P, P, I]),
     "mc_gather_rows_bf16": (I, [P, P, P, I, I, P]),
     "mc_silu_mul_bf16": (I, [P, P, P, P, C.c_size_t]),
     "mc_moe_combine_rows": (I, [P, P, P, P, P, I, I, I]),
     "mc_eval_math": (I, [P, I, P, P, I]),
+    "mc_set_trace": (I, [P, P, I]),
 }
 
 _lib: C.CDLL | None = None

@@ -217,13 +217,11 @@ int dispatch_gemv(mc_ctx* ctx, const mc_qweights* w, const uint16_t* x, uint16_t
     if (G <= 32) return launch_gemv<4, 1, 4, MODE>(ctx, w, x, y, keys, batch);
     return launch_gemv<4, 2, 2, MODE>(ctx, w, x, y, keys, batch);
   }
-  if (G <= 32) return launch_gemv<6, 1, 4, MODE>(ctx, w, x, y, keys, batch);
-  return launch_gemv<6, 2, 2, MODE>(ctx, w, x, y, keys, batch);
+  if (G <= 32) return launch_gemv<6, 1, 2, MODE>(ctx, w, x, y, keys, batch);
+  return launch_gemv<6, 2, 1, MODE>(ctx, w, x, y, keys, batch);
 }
 
 }  // namespace
-
-int mc_check_gemv_weights(const mc_qweights* w, const char* what);
 
 extern "C" int mc_gemv_quant(mc_ctx* ctx, const mc_qweights* w, const uint16_t* x, uint16_t* y,
                              int batch) {

@@ -3,8 +3,9 @@
 //
 // Canonical row order (mirrored by oracle/mc_oracle.c row_dot):
 //   lane l of a warp owns the 64-code groups g = l, l+32, ...; per group two
-//   chains, even codes and odd codes, each acc = fma(q*2^e, x*2^-e, acc) in
-//   increasing k; qx = even + odd; term = fma(s, qx, b * xg) with xg the
+//   chains each acc = fma(q*2^e, x*2^-e, acc) in increasing k -- for Q4 the
+//   codes of even words (bit 3 of k clear) and of odd words; for Q6 even and
+//   odd k -- ; qx = chain0 + chain1; term = fma(s, qx, b * xg) with xg the
 //   left-to-right sum of the group's 64 activations; the lane's terms are
 //   added in increasing g starting from +0; the row sum is the 32-lane xor
 //   butterfly. (Reference arithmetic: dot_word_q4 / GEMV_Q4_BODY,
@@ -17,40 +18,45 @@
 #pragma once
 #include "mc_internal.cuh"
 
-// 8 codes of one Q4 word against 4 activation pairs (x pre-scaled by E4).
-__device__ __forceinline__ void q4_word_fma(uint32_t w, float2 x0, float2 x1, float2 x2,
-                                            float2 x3, float2& acc) {
+__device__ __forceinline__ float2 mc_u64_as_float2(uint64_t v) {
+  float2 f;
+  f.x = __uint_as_float((uint32_t)v);
+  f.y = __uint_as_float((uint32_t)(v >> 32));
+  return f;
+}
+
+// 16 codes of two adjacent Q4 words (wa = word 2m, wb = word 2m+1 of a group)
+// against 8 activation pairs xs[j] = (x[16m+j], x[16m+8+j]) pre-scaled by E4.
+// The two words sit in an aligned register pair (they come from one 16-byte
+// load), so each 64-bit mask-and-OR yields a float2 of codes directly; chain
+// .x takes word 2m's codes, chain .y word 2m+1's, each in increasing k.
+__device__ __forceinline__ void q4_wordpair_fma(uint32_t wa, uint32_t wb, const float2* xs,
+                                                float2& acc) {
   const float2 neg = make_float2(-MC_MAGIC_F, -MC_MAGIC_F);
-  const uint32_t w8 = w >> 8;
-  float2 q01 = make_float2(__uint_as_float((w & 0x0000000Fu) | MC_MAGIC),
-                           __uint_as_float((w & 0x000000F0u) | MC_MAGIC));
-  float2 q23 = make_float2(__uint_as_float((w & 0x00000F00u) | MC_MAGIC),
-                           __uint_as_float((w & 0x0000F000u) | MC_MAGIC));
-  float2 q45 = make_float2(__uint_as_float((w & 0x000F0000u) | MC_MAGIC),
-                           __uint_as_float((w & 0x00F00000u) | MC_MAGIC));
-  float2 q67 = make_float2(__uint_as_float((w8 & 0x000F0000u) | MC_MAGIC),
-                           __uint_as_float((w8 & 0x00F00000u) | MC_MAGIC));
-  q01 = __fadd2_rn(q01, neg);
-  q23 = __fadd2_rn(q23, neg);
-  q45 = __fadd2_rn(q45, neg);
-  q67 = __fadd2_rn(q67, neg);
-  acc = __ffma2_rn(q01, x0, acc);
-  acc = __ffma2_rn(q23, x1, acc);
-  acc = __ffma2_rn(q45, x2, acc);
-  acc = __ffma2_rn(q67, x3, acc);
+  const uint64_t MAG = 0x4B0000004B000000ull;
+  const uint64_t W = ((uint64_t)wb << 32) | wa;
+  // codes 5..7 (bits 20..31) would reach the exponent: take them from w >> 12
+  const uint64_t S = ((uint64_t)(wb >> 12) << 32) | (wa >> 12);
+  float2 q[8];
+  q[0] = mc_u64_as_float2((W & 0x0000000F0000000Full) | MAG);
+  q[1] = mc_u64_as_float2((W & 0x000000F0000000F0ull) | MAG);
+  q[2] = mc_u64_as_float2((W & 0x00000F0000000F00ull) | MAG);
+  q[3] = mc_u64_as_float2((W & 0x0000F0000000F000ull) | MAG);
+  q[4] = mc_u64_as_float2((W & 0x000F0000000F0000ull) | MAG);
+  q[5] = mc_u64_as_float2((S & 0x00000F0000000F00ull) | MAG);
+  q[6] = mc_u64_as_float2((S & 0x0000F0000000F000ull) | MAG);
+  q[7] = mc_u64_as_float2((S & 0x000F0000000F0000ull) | MAG);
+#pragma unroll
+  for (int j = 0; j < 8; ++j) acc = __ffma2_rn(__fadd2_rn(q[j], neg), xs[j], acc);
 }
 
 // One Q4 group: 8 words (two uint4) against 32 pre-scaled activation pairs.
 __device__ __forceinline__ float q4_group_qx(uint4 a, uint4 b, const float2* xs) {
   float2 acc = make_float2(0.0f, 0.0f);
-  q4_word_fma(a.x, xs[0], xs[1], xs[2], xs[3], acc);
-  q4_word_fma(a.y, xs[4], xs[5], xs[6], xs[7], acc);
-  q4_word_fma(a.z, xs[8], xs[9], xs[10], xs[11], acc);
-  q4_word_fma(a.w, xs[12], xs[13], xs[14], xs[15], acc);
-  q4_word_fma(b.x, xs[16], xs[17], xs[18], xs[19], acc);
-  q4_word_fma(b.y, xs[20], xs[21], xs[22], xs[23], acc);
-  q4_word_fma(b.z, xs[24], xs[25], xs[26], xs[27], acc);
-  q4_word_fma(b.w, xs[28], xs[29], xs[30], xs[31], acc);
+  q4_wordpair_fma(a.x, a.y, xs + 0, acc);
+  q4_wordpair_fma(a.z, a.w, xs + 8, acc);
+  q4_wordpair_fma(b.x, b.y, xs + 16, acc);
+  q4_wordpair_fma(b.z, b.w, xs + 24, acc);
   return __fadd_rn(acc.x, acc.y);
 }
 
@@ -97,35 +103,57 @@ template <int BITS>
 __device__ __forceinline__ int code_shift(int k) {
   if (BITS == 4) {
     const int j = k & 7;
-    return j < 6 ? 4 * j : (j == 6 ? 16 : 20);
+    return j < 5 ? 4 * j : 4 * (j - 3);
   } else {
     const int j = k & 3;
     return j == 0 ? 0 : (j == 1 ? 6 : (j == 2 ? 12 : 10));
   }
 }
 
+// Pre-scales one group's 64 activations into the pair layout the code
+// kernels consume and returns the group's left-to-right activation sum.
+// Q4: xs[8m + j] = (x[16m+j], x[16m+8+j]) * 2^-E4[j]; Q6: xs[i] =
+// (x[2i], x[2i+1]) * 2^-E6.
+template <int BITS>
+__device__ __forceinline__ float prescale_group_x(const float* xv, float2* xs) {
+  float sum = xv[0];
+#pragma unroll
+  for (int k = 1; k < 64; ++k) sum = __fadd_rn(sum, xv[k]);
+  if (BITS == 4) {
+#pragma unroll
+    for (int m = 0; m < 4; ++m)
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        xs[8 * m + j] = make_float2(__fmul_rn(xv[16 * m + j], mc_pow2_neg(code_shift<4>(j))),
+                                    __fmul_rn(xv[16 * m + 8 + j], mc_pow2_neg(code_shift<4>(j))));
+  } else {
+#pragma unroll
+    for (int i = 0; i < 32; ++i)
+      xs[i] = make_float2(__fmul_rn(xv[2 * i], mc_pow2_neg(code_shift<6>(2 * i))),
+                          __fmul_rn(xv[2 * i + 1], mc_pow2_neg(code_shift<6>(2 * i + 1))));
+  }
+  return sum;
+}
+
 // Loads one group's 64 bf16 activations (128 bytes at x + 64*g), writes the
 // pre-scaled pairs and returns the group's left-to-right activation sum.
-template <int BITS>
+// SRC 0: read-only global (__ldg); 1: global written earlier in the same
+// kernel by other CTAs (__ldcg, L2); 2: generic pointer (shared memory).
+template <int BITS, int SRC = 0>
 __device__ __forceinline__ float load_group_x(const uint16_t* __restrict__ x, int g, float2* xs) {
   const uint4* src = reinterpret_cast<const uint4*>(x + 64 * g);
-  float sum = 0.0f;
+  float xv[64];
 #pragma unroll
   for (int c = 0; c < 8; ++c) {
-    const uint4 v = __ldg(src + c);
+    const uint4 v = SRC == 0 ? __ldg(src + c) : (SRC == 1 ? __ldcg(src + c) : src[c]);
     const uint32_t wds[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
     for (int h = 0; h < 4; ++h) {
-      const int k0 = 8 * c + 2 * h;
-      const float lo = __uint_as_float(wds[h] << 16);
-      const float hi = __uint_as_float(wds[h] & 0xffff0000u);
-      sum = (k0 == 0) ? lo : __fadd_rn(sum, lo);
-      sum = __fadd_rn(sum, hi);
-      xs[k0 / 2] = make_float2(__fmul_rn(lo, mc_pow2_neg(code_shift<BITS>(k0))),
-                               __fmul_rn(hi, mc_pow2_neg(code_shift<BITS>(k0 + 1))));
+      xv[8 * c + 2 * h] = __uint_as_float(wds[h] << 16);
+      xv[8 * c + 2 * h + 1] = __uint_as_float(wds[h] & 0xffff0000u);
     }
   }
-  return sum;
+  return prescale_group_x<BITS>(xv, xs);
 }
 
 // Per-group code bytes.
@@ -188,3 +216,31 @@ __device__ __forceinline__ void rows_dot(const uint8_t* const* rows, const uint1
   for (int r = 0; r < R; ++r) out[r] = mc_warp_butterfly(acc[r]);
 }
 
+
+// R Q4 rows staged in shared memory (codes, scales, biases contiguous per
+// row); one group per lane (K <= 2048); same canonical order as rows_dot.
+template <int R>
+__device__ __forceinline__ void smem_rows_dot_q4(const uint8_t* const* rows,
+                                                 const uint16_t* const* sc,
+                                                 const uint16_t* const* bi, int G, int lane,
+                                                 const float2* xs, float xg, float* out) {
+  uint4 a[R], b[R];
+  float s[R], bb[R];
+  const bool on = lane < G;
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    if (on) {
+      const uint4* p = reinterpret_cast<const uint4*>(rows[r] + 32 * lane);
+      a[r] = p[0];
+      b[r] = p[1];
+      s[r] = mc_bf16_to_f32(sc[r][lane]);
+      bb[r] = mc_bf16_to_f32(bi[r][lane]);
+    }
+  }
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    float acc = 0.0f;
+    if (on) acc = __fadd_rn(acc, __fmaf_rn(s[r], q4_group_qx(a[r], b[r], xs), __fmul_rn(bb[r], xg)));
+    out[r] = mc_warp_butterfly(acc);
+  }
+}

@@ -85,34 +85,24 @@ extern "C" int mc_create(int device, void* stream, mc_ctx** out) {
   int optin = 0;
   cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, device);
   c->max_smem_optin = optin;
-  if (stream) {
-    c->stream = (cudaStream_t)stream;
-  } else {
-    cudaError_t e = cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking);
-    if (e != cudaSuccess) {
-      free(c);
-      return mc_fail(MC_ECUDA, "mc_create: cudaStreamCreate: %s", cudaGetErrorString(e));
-    }
-    c->owns_stream = 1;
-  }
+  // NULL is CUDA's default stream, as everywhere in the runtime API.
+  c->stream = (cudaStream_t)stream;
+  c->owns_stream = 0;
   *out = c;
   return MC_OK;
 }
 
 extern "C" int mc_set_stream(mc_ctx* ctx, void* stream) {
   if (!ctx) return mc_fail(MC_EINVAL, "mc_set_stream: null context");
-  if (stream) {
-    if (ctx->owns_stream) {
-      cudaStreamDestroy(ctx->stream);
-      ctx->owns_stream = 0;
-    }
-    ctx->stream = (cudaStream_t)stream;
-    return MC_OK;
-  }
-  if (!ctx->owns_stream) {
-    MC_CUDA(cudaStreamCreateWithFlags(&ctx->stream, cudaStreamNonBlocking));
-    ctx->owns_stream = 1;
-  }
+  ctx->stream = (cudaStream_t)stream;
+  return MC_OK;
+}
+
+extern "C" int mc_set_trace(mc_ctx* ctx, unsigned long long* buf, int n) {
+  if (!ctx) return mc_fail(MC_EINVAL, "mc_set_trace: null context");
+  if (buf && n < 0) return mc_fail(MC_EINVAL, "mc_set_trace: n %d", n);
+  ctx->trace = buf;
+  ctx->trace_len = buf ? n : 0;
   return MC_OK;
 }
 

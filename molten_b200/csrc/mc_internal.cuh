@@ -19,7 +19,15 @@ struct mc_ctx {
   int ep_rank;
   int ep_size;
   int ep_timeout_ms;
+  unsigned long long* trace;  // optional per-CTA phase timestamps (mc_set_trace)
+  int trace_len;
 };
+
+__device__ __forceinline__ unsigned long long mc_globaltimer() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
 
 // Records a formatted message for mc_last_error() and returns `code`.
 int mc_fail(int code, const char* fmt, ...);
@@ -35,6 +43,9 @@ int mc_fail(int code, const char* fmt, ...);
     if (_e != cudaSuccess)                                                       \
       return mc_fail(MC_ECUDA, "%s failed: %s", #call, cudaGetErrorString(_e));  \
   } while (0)
+
+// check_quant for the GEMV kernels (mc_api.cu).
+int mc_check_gemv_weights(const mc_qweights* w, const char* what);
 
 // Checks the launch that was just issued.
 int mc_after_launch(const char* what);

@@ -138,9 +138,9 @@ MC_HD bool mc_better(float v, uint32_t i, float bv, uint32_t bi) {
 #define MC_E4_2 8
 #define MC_E4_3 12
 #define MC_E4_4 16
-#define MC_E4_5 20
-#define MC_E4_6 16
-#define MC_E4_7 20
+#define MC_E4_5 8
+#define MC_E4_6 12
+#define MC_E4_7 16
 // 6-bit codes: position within the 4-code (3-byte) packet.
 #define MC_E6_0 0
 #define MC_E6_1 6

@@ -115,8 +115,6 @@ down_combine_kernel(const uint32_t* __restrict__ dc, const uint16_t* __restrict_
 
 }  // namespace
 
-int mc_check_gemv_weights(const mc_qweights* w, const char* what);
-
 extern "C" int mc_gemv_gather_act(mc_ctx* ctx, const mc_qweights* gate, const mc_qweights* up,
                                   const uint16_t* x, const uint32_t* ids, uint16_t* act,
                                   int n_experts, int batch) {

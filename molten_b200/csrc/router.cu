@@ -11,146 +11,9 @@
 // counter -- the reference's last-finisher pattern, with no inter-CTA wait.
 #include "mc_internal.cuh"
 #include "rownorm.cuh"
+#include "route_common.cuh"
 
 namespace {
-
-// Router logit of one expert row (canonical order, oracle or_router_logits):
-// lane l owns k = 256j + 8l + i (j outer, i inner), fma chain from +0, then
-// the 32-lane butterfly. n: the normalized row as floats.
-template <int DT>
-struct RouterRow;
-
-template <>
-struct RouterRow<MC_DTYPE_BF16> {
-  uint4 w[8];
-  __device__ __forceinline__ void load(const void* W, int e, int lane) {
-    const uint4* row = reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(W) +
-                                                      (size_t)e * 2048);
-#pragma unroll
-    for (int j = 0; j < 8; ++j) w[j] = __ldg(row + 32 * j + lane);
-  }
-  __device__ __forceinline__ float dot(const float* n, int lane) const {
-    float acc = 0.0f;
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const uint32_t ww[4] = {w[j].x, w[j].y, w[j].z, w[j].w};
-      const float4 n0 = *reinterpret_cast<const float4*>(n + 256 * j + 8 * lane);
-      const float4 n1 = *reinterpret_cast<const float4*>(n + 256 * j + 8 * lane + 4);
-      const float nv[8] = {n0.x, n0.y, n0.z, n0.w, n1.x, n1.y, n1.z, n1.w};
-#pragma unroll
-      for (int i = 0; i < 8; ++i)
-        acc = __fmaf_rn(mc_bf16_to_f32((uint16_t)(ww[i >> 1] >> (16 * (i & 1)))), nv[i], acc);
-    }
-    return mc_warp_butterfly(acc);
-  }
-};
-
-template <>
-struct RouterRow<MC_DTYPE_F32> {
-  float4 w[16];
-  __device__ __forceinline__ void load(const void* W, int e, int lane) {
-    const float4* row =
-        reinterpret_cast<const float4*>(reinterpret_cast<const float*>(W) + (size_t)e * 2048);
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      w[2 * j] = __ldg(row + 64 * j + 2 * lane);
-      w[2 * j + 1] = __ldg(row + 64 * j + 2 * lane + 1);
-    }
-  }
-  __device__ __forceinline__ float dot(const float* n, int lane) const {
-    float acc = 0.0f;
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const float4 n0 = *reinterpret_cast<const float4*>(n + 256 * j + 8 * lane);
-      const float4 n1 = *reinterpret_cast<const float4*>(n + 256 * j + 8 * lane + 4);
-      const float4 a = w[2 * j], b = w[2 * j + 1];
-      acc = __fmaf_rn(a.x, n0.x, acc);
-      acc = __fmaf_rn(a.y, n0.y, acc);
-      acc = __fmaf_rn(a.z, n0.z, acc);
-      acc = __fmaf_rn(a.w, n0.w, acc);
-      acc = __fmaf_rn(b.x, n1.x, acc);
-      acc = __fmaf_rn(b.y, n1.y, acc);
-      acc = __fmaf_rn(b.z, n1.z, acc);
-      acc = __fmaf_rn(b.w, n1.w, acc);
-    }
-    return mc_warp_butterfly(acc);
-  }
-};
-
-// Warp top-4 over E <= 64 logits (lane owns experts lane and lane+32), the
-// selection and weight rules of oracle or_route_topk. Results valid in lane 0.
-__device__ __forceinline__ void warp_top4(const float* z, int E, int mode, const float* bias,
-                                          float route_eps, uint32_t* ids_out,
-                                          uint16_t* w_out) {
-  const int lane = threadIdx.x & 31;
-  float s0 = -INFINITY, s1 = -INFINITY, v0 = -INFINITY, v1 = -INFINITY;
-  bool u0 = lane >= E, u1 = lane + 32 >= E;
-  if (!u0) {
-    const float zz = z[lane];
-    s0 = mode == MC_ROUTE_SOFTMAX_RENORM ? zz : mc_sigmoid(zz);
-    v0 = mode == MC_ROUTE_SOFTMAX_RENORM ? zz : __fadd_rn(s0, bias ? bias[lane] : 0.0f);
-  }
-  if (!u1) {
-    const float zz = z[lane + 32];
-    s1 = mode == MC_ROUTE_SOFTMAX_RENORM ? zz : mc_sigmoid(zz);
-    v1 = mode == MC_ROUTE_SOFTMAX_RENORM ? zz : __fadd_rn(s1, bias ? bias[lane + 32] : 0.0f);
-  }
-  uint32_t ch[4];
-  float raw[4];
-#pragma unroll
-  for (int r = 0; r < 4; ++r) {
-    float bv = -INFINITY;
-    uint32_t bi = 0xffffffffu;
-    if (!u0 && mc_better(v0, (uint32_t)lane, bv, bi)) {
-      bv = v0;
-      bi = (uint32_t)lane;
-    }
-    if (!u1 && mc_better(v1, (uint32_t)(lane + 32), bv, bi)) {
-      bv = v1;
-      bi = (uint32_t)(lane + 32);
-    }
-#pragma unroll
-    for (int m = 16; m >= 1; m >>= 1) {
-      const float ov = __shfl_xor_sync(0xffffffffu, bv, m);
-      const uint32_t oi = __shfl_xor_sync(0xffffffffu, bi, m);
-      if (mc_better(ov, oi, bv, bi)) {
-        bv = ov;
-        bi = oi;
-      }
-    }
-    uint32_t pick = bi == 0xffffffffu ? 0u : bi;
-    if ((uint32_t)lane == pick) u0 = true;
-    if ((uint32_t)lane + 32 == pick) u1 = true;
-    const float ps0 = __shfl_sync(0xffffffffu, s0, pick & 31);
-    const float ps1 = __shfl_sync(0xffffffffu, s1, pick & 31);
-    ch[r] = pick;
-    raw[r] = pick < 32 ? ps0 : ps1;
-  }
-  if (lane == 0) {
-    if (mode == MC_ROUTE_SOFTMAX_RENORM) {
-      float ex[4], den = 0.0f;
-#pragma unroll
-      for (int r = 0; r < 4; ++r) {
-        ex[r] = mc_exp(__fadd_rn(raw[r], -raw[0]));
-        den = __fadd_rn(den, ex[r]);
-      }
-#pragma unroll
-      for (int r = 0; r < 4; ++r) {
-        ids_out[r] = ch[r];
-        w_out[r] = mc_f32_to_bf16(__fdiv_rn(ex[r], den));
-      }
-    } else {
-      float den = route_eps;
-#pragma unroll
-      for (int r = 0; r < 4; ++r) den = __fadd_rn(den, raw[r]);
-#pragma unroll
-      for (int r = 0; r < 4; ++r) {
-        ids_out[r] = ch[r];
-        w_out[r] = mc_f32_to_bf16(__fdiv_rn(raw[r], den));
-      }
-    }
-  }
-}
 
 template <int DT>
 __global__ void __launch_bounds__(256)

@@ -226,6 +226,38 @@ def gemv_gather_down_combine4(ctx: Context, down: QuantWeights, act: torch.Tenso
               _p(ids), _p(weights), _p(out), n_experts, batch)
 
 
+def moe_decode_workspace_words(moe_inter: int = FIXED_MOE_INTER) -> int:
+    """u32 words of workspace moe_decode_layer needs (zero it once)."""
+    return int(_lib.lib().mc_moe_decode_workspace_words(moe_inter))
+
+
+def moe_decode_layer(ctx: Context, h, b, nw, hout, normed, router, logits, bias, ids, weights,
+                     gate: QuantWeights, up: QuantWeights, down: QuantWeights, out, workspace,
+                     eps: float = 1e-5, route_mode: int = ROUTE_SOFTMAX_RENORM,
+                     route_eps: float = 1e-6, n_experts: int = 64) -> None:
+    """moe_decode (lfm.rs:967-1011) with the fused router, one persistent launch
+    for one token. ``workspace``: int32 [moe_decode_workspace_words(I)], zeroed
+    once, then reused by one chain of calls (it carries an epoch)."""
+    for w in (gate, up, down):
+        check_quant(w)
+    e, k = router.shape
+    ensure(e == n_experts and k == FIXED_HIDDEN, "router shape")
+    ensure(h.numel() == k and out.numel() == k, "moe_decode_layer is batch 1")
+    _bf16(h, b, nw, hout, normed, weights, out)
+    _u32(ids, workspace)
+    dt = _lib.DTYPE_BF16 if router.dtype == torch.bfloat16 else _lib.DTYPE_F32
+    _lib.call("mc_moe_decode_layer", ctx.handle, _p(h), _p(b), _p(nw), _p(hout), _p(normed),
+              _p(router), dt, _p(bias), route_mode, _p(logits), _p(ids), _p(weights),
+              _lib.C.byref(gate.qw()), _lib.C.byref(up.qw()), _lib.C.byref(down.qw()),
+              n_experts, _p(out), _p(workspace), workspace.numel(), eps, route_eps)
+
+
+def decode_workspace_act(workspace: torch.Tensor, moe_inter: int = FIXED_MOE_INTER):
+    """The act rows (bf16 [4, I]) held in a moe_decode_layer workspace."""
+    w = workspace[132:132 + 2 * moe_inter].contiguous()
+    return w.view(torch.bfloat16).reshape(4, moe_inter)
+
+
 # ---------------------------------------------------------------- prefill ops
 
 def moe_route_batch(ctx: Context, logits, bias, ids, gw, m: int,

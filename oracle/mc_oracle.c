@@ -113,7 +113,8 @@ static float butterfly32(float* v) {
  * Canonical order (this project's; Apple's simd_sum order is unspecified):
  *   - lane l (0..31) owns groups g = l, l+32, ... and keeps acc_l, starting
  *     at +0.0f;
- *   - per group (64 codes): two chains cE (even k) and cO (odd k), each
+ *   - per group (64 codes): two chains cE and cO -- Q4: codes of even and
+ *     odd 32-bit words (bit 3 of k), Q6: even and odd k -- each
  *     cX = fmaf(q_k * 2^e_k, x_k * 2^-e_k, cX) in increasing k, where e_k is
  *     the bit position the GPU leaves code k at (E4 / E6 below; the product
  *     is exact, the power-of-two pre-scaling of x is what the GPU reads);
@@ -122,7 +123,7 @@ static float butterfly32(float* v) {
  *   - term = fmaf(s_g, qx, b_g * xg_g); acc_l = acc_l + term;
  *   - row sum = 32-lane xor butterfly of acc_l.
  */
-static const int E4[8] = {0, 4, 8, 12, 16, 20, 16, 20};
+static const int E4[8] = {0, 4, 8, 12, 16, 8, 12, 16};
 static const int E6[4] = {0, 6, 12, 10};
 
 static void prescale(const float* x, int K, int bits, float* xs, float* xg) {
@@ -165,7 +166,9 @@ static float row_dot(const uint8_t* row, const uint16_t* s, const uint16_t* b,
       uint32_t q = code_at(row, bits, k);
       int e = bits == 4 ? E4[k & 7] : E6[k & 3];
       float qf = (float)(q << e);
-      if (k & 1) cO = fmaf(qf, xs[k], cO);
+      /* Q4: chain by word parity (bit 3 of k); Q6: by code parity */
+      int odd = bits == 4 ? (k >> 3) & 1 : k & 1;
+      if (odd) cO = fmaf(qf, xs[k], cO);
       else cE = fmaf(qf, xs[k], cE);
     }
     float qx = cE + cO;

@@ -1,0 +1,180 @@
+/*
+ * TEST INFRASTRUCTURE ONLY -- the timed CPU baseline of the quantized MoE path.
+ *
+ * The reference has no CPU implementation of this path (it is Metal-only) and
+ * the MLX CPU backend BASELINE.json names is not in the reference tree, so
+ * the CPU baseline is this port of the same arithmetic (oracle/mc_oracle.c),
+ * written for speed: OpenMP over output rows, vectorisable inner loops,
+ * -O3 -ffast-math (sums may be reassociated, so results agree with the exact
+ * oracle only within tolerance). Only bench.py's cpu_baseline and
+ * --impl reference legs call it.
+ *
+ * Algorithm per Q4 row (dot_word_q4 / GEMV_Q4_BODY, lfm.metal:102-139):
+ *   y = sum_g s_g * (sum_{k in g} q_k x_k) + b_g * (sum_{k in g} x_k).
+ */
+#include <math.h>
+#include <omp.h>
+#include <stdint.h>
+#include <stdlib.h>
+#include <string.h>
+
+static inline float bf(uint16_t h) {
+  union { uint32_t u; float f; } v; v.u = (uint32_t)h << 16; return v.f;
+}
+static inline uint16_t tobf(float f) {
+  union { uint32_t u; float f; } v; v.f = f;
+  uint32_t u = v.u;
+  if ((u & 0x7fffffffu) > 0x7f800000u) return (uint16_t)((u >> 16) | 0x40u);
+  u += 0x7fffu + ((u >> 16) & 1u);
+  return (uint16_t)(u >> 16);
+}
+static inline float rbf(float f) { return bf(tobf(f)); }
+
+int of_threads(void) { return omp_get_max_threads(); }
+void of_set_threads(int n) { if (n > 0) omp_set_num_threads(n); }
+
+/* one Q4 row against x (float, K), xg (group sums) */
+static inline float q4_row(const uint32_t* codes, const uint16_t* s, const uint16_t* b, int K,
+                           const float* x, const float* xg) {
+  const int G = K / 64;
+  float acc = 0.0f;
+  for (int g = 0; g < G; ++g) {
+    const uint32_t* w = codes + 8 * g;
+    const float* xx = x + 64 * g;
+    float qx = 0.0f;
+    for (int i = 0; i < 8; ++i) {
+      uint32_t v = w[i];
+      for (int j = 0; j < 8; ++j) qx += (float)((v >> (4 * j)) & 15u) * xx[8 * i + j];
+    }
+    acc += bf(s[g]) * qx + bf(b[g]) * xg[g];
+  }
+  return acc;
+}
+
+static void prep_x(const uint16_t* xb, int K, float* x, float* xg) {
+  for (int k = 0; k < K; ++k) x[k] = bf(xb[k]);
+  for (int g = 0; g < K / 64; ++g) {
+    float s = 0.0f;
+    for (int i = 0; i < 64; ++i) s += x[64 * g + i];
+    xg[g] = s;
+  }
+}
+
+void of_gemv_q4(const uint32_t* codes, const uint16_t* s, const uint16_t* b, int N, int K,
+                const uint16_t* xb, uint16_t* y) {
+  float* x = (float*)malloc(sizeof(float) * K);
+  float* xg = (float*)malloc(sizeof(float) * (K / 64));
+  prep_x(xb, K, x, xg);
+#pragma omp parallel for schedule(static)
+  for (int n = 0; n < N; ++n)
+    y[n] = tobf(q4_row(codes + (size_t)n * (K / 8), s + (size_t)n * (K / 64),
+                       b + (size_t)n * (K / 64), K, x, xg));
+  free(x); free(xg);
+}
+
+/* One BASELINE cfg1 decode layer for one token: add + RMSNorm, bf16 router,
+ * softmax-renorm top-4, gate/up/SiLU, down + combine. */
+void of_moe_decode_layer(const uint16_t* h, const uint16_t* badd, const uint16_t* norm_w,
+                         const uint16_t* router, const uint32_t* gc, const uint16_t* gs,
+                         const uint16_t* gb, const uint32_t* uc, const uint16_t* us,
+                         const uint16_t* ub, const uint32_t* dc, const uint16_t* ds,
+                         const uint16_t* db, int E, int H, int I, float eps,
+                         uint16_t* hout, uint32_t* ids, uint16_t* wts, uint16_t* out) {
+  float* n = (float*)malloc(sizeof(float) * H);
+  float* ng = (float*)malloc(sizeof(float) * (H / 64));
+  float* z = (float*)malloc(sizeof(float) * E);
+  float* act = (float*)malloc(sizeof(float) * 4 * I);
+  float* ag = (float*)malloc(sizeof(float) * 4 * (I / 64));
+  float ss = 0.0f;
+  for (int k = 0; k < H; ++k) {
+    float v = rbf(bf(h[k]) + (badd ? bf(badd[k]) : 0.0f));
+    hout[k] = tobf(v);
+    n[k] = v;
+    ss += v * v;
+  }
+  float inv = 1.0f / sqrtf(ss / (float)H + eps);
+  for (int k = 0; k < H; ++k) n[k] = rbf(n[k] * inv * bf(norm_w[k]));
+  for (int g = 0; g < H / 64; ++g) {
+    float s = 0.0f;
+    for (int i = 0; i < 64; ++i) s += n[64 * g + i];
+    ng[g] = s;
+  }
+#pragma omp parallel for schedule(static)
+  for (int e = 0; e < E; ++e) {
+    float a = 0.0f;
+    const uint16_t* r = router + (size_t)e * H;
+    for (int k = 0; k < H; ++k) a += bf(r[k]) * n[k];
+    z[e] = a;
+  }
+  int used[256] = {0};
+  uint32_t ch[4];
+  for (int r = 0; r < 4; ++r) {
+    float bv = -INFINITY; int bi = 0;
+    for (int e = 0; e < E; ++e)
+      if (!used[e] && z[e] > bv) { bv = z[e]; bi = e; }
+    ch[r] = (uint32_t)bi; used[bi] = 1;
+  }
+  float ex[4], den = 0.0f;
+  for (int r = 0; r < 4; ++r) { ex[r] = expf(z[ch[r]] - z[ch[0]]); den += ex[r]; }
+  for (int r = 0; r < 4; ++r) { ids[r] = ch[r]; wts[r] = tobf(ex[r] / den); }
+  const int Gh = H / 64, Gi = I / 64;
+#pragma omp parallel for schedule(static)
+  for (int t = 0; t < 4 * I; ++t) {
+    const int r = t / I, i = t % I;
+    const size_t row = (size_t)ch[r] * I + i;
+    float g = rbf(q4_row(gc + row * (H / 8), gs + row * Gh, gb + row * Gh, H, n, ng));
+    float u = rbf(q4_row(uc + row * (H / 8), us + row * Gh, ub + row * Gh, H, n, ng));
+    act[t] = rbf(rbf(g / (1.0f + expf(-g))) * u);
+  }
+  for (int r = 0; r < 4; ++r)
+    for (int g = 0; g < Gi; ++g) {
+      float s = 0.0f;
+      for (int i = 0; i < 64; ++i) s += act[r * I + 64 * g + i];
+      ag[r * Gi + g] = s;
+    }
+#pragma omp parallel for schedule(static)
+  for (int i = 0; i < H; ++i) {
+    float tot = 0.0f;
+    for (int r = 0; r < 4; ++r) {
+      const size_t row = (size_t)ch[r] * H + i;
+      float p = rbf(q4_row(dc + row * (I / 8), ds + row * Gi, db + row * Gi, I, act + r * I,
+                           ag + r * Gi));
+      tot += rbf(bf(wts[r]) * p);
+    }
+    out[i] = tobf(tot);
+  }
+  free(n); free(ng); free(z); free(act); free(ag);
+}
+
+/* Grouped Q4 GEMM over sorted rows (prefill baseline): C[i] = A[i] . Wdeq[e]^T,
+ * dequantising each expert once into a float panel. */
+void of_gemm_q4_grouped(const uint16_t* A, int K, const uint32_t* codes, const uint16_t* scales,
+                        const uint16_t* biases, int N, const uint32_t* counts,
+                        const uint32_t* offsets, int E, uint16_t* C) {
+  float* wd = (float*)malloc(sizeof(float) * (size_t)N * K);
+  const int G = K / 64;
+  for (int e = 0; e < E; ++e) {
+    if (!counts[e]) continue;
+#pragma omp parallel for schedule(static)
+    for (int n = 0; n < N; ++n) {
+      const size_t row = (size_t)e * N + n;
+      for (int k = 0; k < K; ++k) {
+        uint32_t w = codes[row * (K / 8) + k / 8];
+        float q = (float)((w >> (4 * (k & 7))) & 15u);
+        wd[(size_t)n * K + k] = rbf(bf(scales[row * G + k / 64]) * q + bf(biases[row * G + k / 64]));
+      }
+    }
+#pragma omp parallel for schedule(static)
+    for (uint32_t i = offsets[e]; i < offsets[e] + counts[e]; ++i) {
+      float a[4096];
+      for (int k = 0; k < K; ++k) a[k] = bf(A[(size_t)i * K + k]);
+      for (int n = 0; n < N; ++n) {
+        const float* w = wd + (size_t)n * K;
+        float s = 0.0f;
+        for (int k = 0; k < K; ++k) s += a[k] * w[k];
+        C[(size_t)i * N + n] = tobf(s);
+      }
+    }
+  }
+  free(wd);
+}

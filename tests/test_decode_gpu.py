@@ -219,3 +219,38 @@ def test_rejects_bad_arguments(cuda_ctx):
     bad.bits = 3
     with pytest.raises(ValueError):
         lfm.gemv_quant(cuda_ctx, bad, empty_bf16(2048), empty_bf16(64))
+
+
+@pytest.mark.parametrize("mode,seed", [(0, 0), (0, 1), (0, 2), (1, 3), (0, 4)])
+def test_fused_moe_decode_layer(cuda_ctx, moe_layer, mode, seed):
+    """The one-launch layer equals the oracle (and so the three-kernel path)
+    bit for bit on consecutive calls sharing one workspace, and reports no
+    error status."""
+    g = synth.rng(2000 + seed)
+    D = moe_layer["dev"]
+    ebias = g.normal(0, 0.1, 64).astype(np.float32)
+    ws = zeros_u32(lfm.moe_decode_workspace_words())
+    hout, normed = empty_bf16(1, 2048), empty_bf16(1, 2048)
+    logits = torch.empty((1, 64), dtype=torch.float32, device="cuda")
+    ids, wts = zeros_u32(1, 4), empty_bf16(1, 4)
+    out = empty_bf16(1, 2048)
+    for it in range(3):
+        h = synth.activations_np(g, 1, 2048)
+        badd = synth.activations_np(g, 1, 2048)
+        lfm.moe_decode_layer(cuda_ctx, dev_bf16(h), dev_bf16(badd), D["norm_w"], hout, normed,
+                             D["router"], logits, dev_f32(ebias), ids, wts, D["gate"], D["up"],
+                             D["down"], out, ws, route_mode=mode)
+        torch.cuda.synchronize()
+        ctl = host_u32(ws[:4])
+        assert ctl[0] == it + 1 and ctl[1] == 0 and ctl[2] == 0 and ctl[3] == 0, ctl
+        ho, no, lo, io, wo = oracle.router_addnorm_route(h, badd, moe_layer["norm_w"],
+                                                         moe_layer["router"], 0, ebias, mode)
+        assert np.array_equal(host_u32(ids), io), "top-4 ids"
+        assert_bits_equal(host_bits(wts), wo, "weights")
+        assert_bits_equal(host_bits(hout), ho, "h_out")
+        assert_bits_equal(host_bits(normed), no, "normed")
+        assert np.array_equal(logits.cpu().numpy().view(np.uint32), lo.view(np.uint32))
+        act_o = oracle.gemv_gather_act(moe_layer["gate"], moe_layer["up"], no, io)
+        assert_bits_equal(host_bits(lfm.decode_workspace_act(ws)), act_o.reshape(4, 1536), "act")
+        out_o = oracle.gemv_gather_down_combine4(moe_layer["down"], act_o, io, wo)
+        assert_bits_equal(host_bits(out), out_o, "out")
