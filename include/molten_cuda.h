@@ -193,6 +193,26 @@ int mc_moe_sort_map(mc_ctx* ctx, const uint32_t* ids, int m, int n_experts, int 
 int mc_gather_rows_bf16(mc_ctx* ctx, const uint16_t* table, const uint32_t* ids, int rows,
                         int hidden, uint16_t* out);
 
+/* gemm_q4_grouped_mlx (quant.rs:228-266 -> lfm_qmm_t_body
+ * quant_nax.metal:4091-4234): C[i][n] = sum_k A[i][k] * bf16(s*q+b)[e*N+n][k]
+ * for the rows i of each tile's expert e; A bf16 [rows][K] (expert-sorted),
+ * C bf16 [rows][N]; w stacked [E*N][K] Q4; tiles/n_tiles from
+ * mc_moe_sort_map with bm = 128. tcgen05 tensor-core kernel (fp32
+ * accumulation). status: nullable u32 word, bit 0 = a bounded wait gave up,
+ * bit 1 = a malformed tile was skipped. N % 128 == 0, K % 64 == 0. */
+int mc_gemm_q4_grouped(mc_ctx* ctx, const uint16_t* a, int rows, const mc_qweights* w,
+                       int n_experts, uint16_t* c, const uint32_t* tiles,
+                       const uint32_t* n_tiles, int max_tiles, uint32_t* status);
+
+/* gemm_q4_grouped_mlx_gu + silu_mul_bf16 (quant.rs:146-199,
+ * elementwise.metal:7-15): the gate and up grouped GEMMs of a tile share the
+ * A tile and the epilogue writes act = bf16(bf16(silu(g)) * u) with g, u the
+ * bf16-rounded GEMM outputs. */
+int mc_gemm_q4_grouped_gu(mc_ctx* ctx, const uint16_t* a, int rows, const mc_qweights* gate,
+                          const mc_qweights* up, int n_experts, uint16_t* act,
+                          const uint32_t* tiles, const uint32_t* n_tiles, int max_tiles,
+                          uint32_t* status);
+
 /* silu_mul_bf16 (elementwise.rs:48-56 -> elementwise.metal:7-15). */
 int mc_silu_mul_bf16(mc_ctx* ctx, const uint16_t* gate, const uint16_t* up, uint16_t* out,
                      size_t n);

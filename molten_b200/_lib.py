@@ -74,6 +74,8 @@ SIGNATURES: dict[str, tuple] = {
     "mc_moe_route_batch": (I, [P, P, I, I, I, P, F, P, P]),
     "mc_moe_sort_map": (I, [P, P, I, I, I, P, P, P, P, P, P, I]),
     "mc_gather_rows_bf16": (I, [P, P, P, I, I, P]),
+    "mc_gemm_q4_grouped": (I, [P, P, I, QP, I, P, P, P, I, P]),
+    "mc_gemm_q4_grouped_gu": (I, [P, P, I, QP, QP, I, P, P, P, I, P]),
     "mc_silu_mul_bf16": (I, [P, P, P, P, C.c_size_t]),
     "mc_moe_combine_rows": (I, [P, P, P, P, P, I, I, I]),
     "mc_eval_math": (I, [P, I, P, P, I]),

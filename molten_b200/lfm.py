@@ -291,6 +291,36 @@ def gather_rows_bf16(ctx: Context, table: torch.Tensor, ids: torch.Tensor,
     _lib.call("mc_gather_rows_bf16", ctx.handle, _p(table), _p(ids), ids.numel(), h, _p(out))
 
 
+def gemm_q4_grouped(ctx: Context, a: torch.Tensor, w: QuantWeights, c: torch.Tensor,
+                    tiles: torch.Tensor, n_tiles: torch.Tensor, n_experts: int = 64,
+                    status: torch.Tensor | None = None) -> None:
+    """gemm_q4_grouped_mlx (quant.rs:228-266): tcgen05 grouped Q4 GEMM over the
+    row tiles of moe_sort_map (bm = 128)."""
+    check_quant(w)
+    rows, k = a.shape
+    ensure(k == w.in_features and c.shape[0] == rows, "grouped GEMM shapes")
+    _bf16(a, c)
+    _u32(tiles, n_tiles, status)
+    _lib.call("mc_gemm_q4_grouped", ctx.handle, _p(a), rows, _lib.C.byref(w.qw()), n_experts,
+              _p(c), _p(tiles), _p(n_tiles), tiles.numel() // 4, _p(status))
+
+
+def gemm_q4_grouped_gu(ctx: Context, a: torch.Tensor, gate: QuantWeights, up: QuantWeights,
+                       act: torch.Tensor, tiles: torch.Tensor, n_tiles: torch.Tensor,
+                       n_experts: int = 64, status: torch.Tensor | None = None) -> None:
+    """gemm_q4_grouped_mlx_gu + silu_mul_bf16 (quant.rs:146-199): gate and up
+    grouped GEMMs sharing the A tile, SwiGLU in the epilogue."""
+    check_quant(gate)
+    check_quant(up)
+    rows, k = a.shape
+    ensure(k == gate.in_features and act.shape[0] == rows, "grouped gate/up shapes")
+    _bf16(a, act)
+    _u32(tiles, n_tiles, status)
+    _lib.call("mc_gemm_q4_grouped_gu", ctx.handle, _p(a), rows, _lib.C.byref(gate.qw()),
+              _lib.C.byref(up.qw()), n_experts, _p(act), _p(tiles), _p(n_tiles),
+              tiles.numel() // 4, _p(status))
+
+
 def silu_mul_bf16(ctx: Context, gate: torch.Tensor, up: torch.Tensor, out: torch.Tensor) -> None:
     """silu_mul_bf16 (elementwise.rs:48-56)."""
     _bf16(gate, up, out)
