@@ -54,7 +54,8 @@ def parse():
     p.add_argument("--steps", type=int, default=20000)
     p.add_argument("--warmup", type=int, default=200)
     p.add_argument("--impl", choices=["molten", "reference"], default="molten")
-    p.add_argument("--workload", choices=["cfg0", "cfg1", "cfg2"], default="cfg1")
+    p.add_argument("--workload", choices=["cfg0", "cfg1", "cfg2", "cfg3"], default="cfg1")
+    p.add_argument("--tokens", type=int, default=4096, help="cfg3 prefill chunk")
     p.add_argument("--seed", type=int, default=0)
     p.add_argument("--sets", type=int, default=16, help="rotated weight sets (cfg1)")
     p.add_argument("--decode-path", choices=["fused", "split"], default="fused",
@@ -505,6 +506,140 @@ def bench_gemv(args, torch, ws, rank, local, head: bool):
     }
 
 
+# ------------------------------------------------------------------ cfg3
+
+def zipf_logits_torch(torch, gen, m, e=E, s=1.0, device="cuda"):
+    """log(Zipf_s(rank(pi(e)))) + Gumbel(0, 1): top-4 is a Plackett-Luce draw."""
+    perm = torch.randperm(e, generator=gen, device=device).to(torch.float32)
+    base = -s * torch.log(perm + 1.0)
+    u = torch.rand((m, e), generator=gen, device=device).clamp_(1e-20, 1.0)
+    return (base[None, :] - torch.log(-torch.log(u))).contiguous()
+
+
+def prefill_flops(S):
+    return 2.0 * S * (2 * I * H + H * I)  # gate + up + down, padding excluded
+
+
+def cpu_baseline_prefill(torch, layer, x, logits, seconds):
+    import ctypes as C
+    import numpy as np
+    from oracle import build as obuild
+    _, fast = obuild.build()
+    L = C.CDLL(str(fast))
+    L.of_set_threads(os.cpu_count() or 1)
+    nthreads = L.of_threads()
+    host = lambda t: np.ascontiguousarray(t.detach().cpu().contiguous().view(torch.int16).numpy()
+                                          if t.dtype == torch.bfloat16 else t.detach().cpu().numpy())
+    arr = []
+    for k in ("gate", "up", "down"):
+        q = layer[k]
+        arr += [host(q.codes), host(q.scales), host(q.biases)]
+    ms = 64
+    xs, ls = host(x[:ms]), host(logits[:ms])
+    out = np.zeros((ms, H), np.uint16)
+    P = lambda a: a.ctypes.data_as(C.c_void_p)
+    def one():
+        L.of_moe_prefill(P(xs), P(ls), ms, E, H, I, *(P(a) for a in arr), P(out))
+    t0 = time.perf_counter()
+    n = 0
+    while n == 0 or time.perf_counter() - t0 < seconds:
+        one()
+        n += 1
+    dt = time.perf_counter() - t0
+    return {"value": round(ms * n / dt, 1), "unit": "tokens/s", "cores": nthreads, "kind": "port",
+            "sample": f"{n} x {ms}-token chunks of the cfg3 FFN ({dt:.1f} s), "
+                      "oracle/mc_oracle_fast.c -O3 OpenMP (dequantises every routed expert)"}
+
+
+def bench_cfg3(args, torch, ws, rank, local):
+    from molten_b200 import lfm, synth
+    ctx = lfm.Context(local)
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(args.seed * 1000 + rank + 3)
+    m = args.tokens
+    layer = synth.moe_layer_torch(gen, "cuda")
+    x = torch.randn((m, H), generator=gen, device="cuda").to(torch.bfloat16)
+    logits = zipf_logits_torch(torch, gen, m)
+    wsb = torch.zeros(lfm.moe_prefill_workspace_size(m), dtype=torch.uint8, device="cuda")
+    out = torch.empty((m, H), dtype=torch.bfloat16, device="cuda")
+    step = lambda: lfm.moe_prefill(ctx, x, logits, layer["gate"], layer["up"], layer["down"],
+                                   wsb, out)
+    K, W = args.steps, max(args.warmup, 3)
+    gw_, gt = build_graphs(torch, step, W), build_graphs(torch, step, K)
+    run_graph_steps(torch, gw_, W)
+    torch.cuda.synchronize()
+    view = lfm.prefill_workspace_view(wsb, m)
+    status = int(view["status"].cpu()[0])
+    if status:
+        raise RuntimeError(f"grouped GEMM status {status}")
+    barrier(ws)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        a.record()
+        run_graph_steps(torch, gt, K)
+        b.record()
+        torch.cuda.synchronize()
+    ms_ = max_over_ranks(ws, a.elapsed_time(b))
+    value = ws * m * K / (ms_ * 1e-3)
+    # per-kernel: the two grouped GEMMs on the step's own workspace
+    S = 4 * m
+    v = lfm.prefill_workspace_view(wsb, m)
+    tiles, ntl, gx, act, ed = v["tiles"], v["n_tiles"], v["gx"], v["act"], v["ed"]
+    gu_ms = time_kernel(torch, lambda: lfm.gemm_q4_grouped_gu(ctx, gx, layer["gate"], layer["up"],
+                                                              act, tiles, ntl), 20)
+    dn_ms = time_kernel(torch, lambda: lfm.gemm_q4_grouped(ctx, act, layer["down"], ed, tiles,
+                                                           ntl), 20)
+    n_tiles = int(ntl.cpu()[0])
+    _, bf16_peak, src = peaks()
+    gu_flops = 2.0 * S * 2 * I * H
+    achieved = gu_flops / (gu_ms * 1e-3) / 1e12
+    # e2e through the public call with host buffers
+    hx = x.cpu().pin_memory()
+    hl = logits.cpu().pin_memory()
+    hout = torch.empty((m, H), dtype=torch.bfloat16).pin_memory()
+    n_e2e = min(K, 20)
+    for _ in range(2):
+        x.copy_(hx, non_blocking=True); logits.copy_(hl, non_blocking=True); step()
+        hout.copy_(out, non_blocking=True)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0 = time.perf_counter()
+    e0.record()
+    for _ in range(n_e2e):
+        x.copy_(hx, non_blocking=True)
+        logits.copy_(hl, non_blocking=True)
+        step()
+        hout.copy_(out, non_blocking=True)
+    e1.record()
+    torch.cuda.synchronize()
+    e2e_ms = max_over_ranks(ws, max(e0.elapsed_time(e1), (time.perf_counter() - t0) * 1e3))
+    res = {
+        "metric": "prefill grouped-GEMM tokens/s (cfg3: 4096-token MoE FFN, Zipf routing)",
+        "value": round(value, 1), "unit": "tokens/s", "n_gpus": ws, "steps": K, "warmup": W,
+        "ms_per_step": round(ms_ / K, 4), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "q4 weights dequantised to bf16, bf16 x bf16 -> fp32 tcgen05",
+        "data": "synthetic (seeded; Zipf(s=1) + Gumbel router logits, random-init weights)",
+        "config": {"workload": f"cfg3: {m} tokens x 2048, E=64 top-4, SwiGLU 2048->1536->2048 Q4",
+                   "pairs": S, "row_tiles": n_tiles, "useful_gflop_per_step": prefill_flops(S) / 1e9,
+                   "l2": "expert weights 340 MB > L2, streamed every step"},
+        "e2e": {"value": round(ws * m * n_e2e / (e2e_ms * 1e-3), 1), "unit": "tokens/s",
+                "h2d_bytes_per_step": m * H * 2 + m * E * 4, "d2h_bytes_per_step": m * H * 2},
+        "roofline": {"bound": "tensor", "kernel": "grouped_gemm_kernel<gate/up>",
+                     "achieved": round(achieved, 1), "peak": bf16_peak, "unit": "TFLOP/s",
+                     "frac": round(achieved / bf16_peak, 4),
+                     "peak_source": f"{src} bf16_tflops (burst)",
+                     "traffic": ncu_traffic("grouped_gemm_kernel", "cfg3"),
+                     "per_kernel_us": {"gemm_gate_up": round(gu_ms * 1e3, 1),
+                                       "gemm_down": round(dn_ms * 1e3, 1)},
+                     "down_tflops": round(2.0 * S * H * I / (dn_ms * 1e-3) / 1e12, 1)},
+        "gpu_launches": 7 * K,
+        "clocks": clk.summary(),
+    }
+    if rank == 0 and ws == 1 and not args.no_cpu_baseline:
+        res["cpu_baseline"] = cpu_baseline_prefill(torch, layer, x, logits, args.cpu_seconds)
+    return res
+
+
 # ------------------------------------------------------------------ reference arm
 
 def bench_reference(args, ws, rank):
@@ -551,6 +686,8 @@ def main():
     try:
         if args.workload == "cfg1":
             res = bench_cfg1(args, torch, ws, rank, local)
+        elif args.workload == "cfg3":
+            res = bench_cfg3(args, torch, ws, rank, local)
         else:
             res = bench_gemv(args, torch, ws, rank, local, head=args.workload == "cfg2")
         if rank == 0:

@@ -222,6 +222,19 @@ int mc_silu_mul_bf16(mc_ctx* ctx, const uint16_t* gate, const uint16_t* up, uint
 int mc_moe_combine_rows(mc_ctx* ctx, const uint16_t* ed, const uint32_t* slotpos,
                         const uint16_t* gw, uint16_t* out, int m, int topk, int hidden);
 
+/* moe_prefill (lfm.rs:847-965) from router logits on: route, sort + tile
+ * map, gather, grouped gate/up + SwiGLU, grouped down, combine (seven
+ * launches, no host round trip). x bf16 [m][H], logits f32 [m][E]; gate/up
+ * stacked [E*I][H], down [E*H][I] Q4; out bf16 [m][H]. workspace: device
+ * bytes >= mc_moe_prefill_workspace_size(m, E, H, I), 256-byte aligned; it
+ * holds the intermediates (ids, gate weights, sorted order, tiles, gx, act,
+ * ed) and the GEMM status word. */
+size_t mc_moe_prefill_workspace_size(int m, int n_experts, int hidden, int moe_inter);
+int mc_moe_prefill(mc_ctx* ctx, const uint16_t* x, const float* logits, int m,
+                   const mc_qweights* gate, const mc_qweights* up, const mc_qweights* down,
+                   int n_experts, int route_mode, const float* expert_bias, void* workspace,
+                   size_t ws_bytes, uint16_t* out);
+
 /* -------------------------------------------------------------- test aid */
 
 /* Profiling aid: when buf (device, n u64 words) is set, the persistent

@@ -76,6 +76,8 @@ SIGNATURES: dict[str, tuple] = {
     "mc_gather_rows_bf16": (I, [P, P, P, I, I, P]),
     "mc_gemm_q4_grouped": (I, [P, P, I, QP, I, P, P, P, I, P]),
     "mc_gemm_q4_grouped_gu": (I, [P, P, I, QP, QP, I, P, P, P, I, P]),
+    "mc_moe_prefill_workspace_size": (C.c_size_t, [I, I, I, I]),
+    "mc_moe_prefill": (I, [P, P, P, I, QP, QP, QP, I, I, P, P, C.c_size_t, P]),
     "mc_silu_mul_bf16": (I, [P, P, P, P, C.c_size_t]),
     "mc_moe_combine_rows": (I, [P, P, P, P, P, I, I, I]),
     "mc_eval_math": (I, [P, I, P, P, I]),

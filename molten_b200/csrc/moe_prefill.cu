@@ -227,3 +227,81 @@ extern "C" int mc_moe_combine_rows(mc_ctx* ctx, const uint16_t* ed, const uint32
                                                                            topk, hidden / 8);
   return mc_after_launch("combine_kernel");
 }
+
+// ---------------------------------------------------------------- orchestration
+// moe_prefill (lfm.rs:847-965) from router logits on. Workspace carve-up
+// (every piece 256-byte aligned): ids u32[4m], gw bf16[4m], counts/offsets
+// u32[E], ids_sorted/slotpos u32[4m], tiles uint4[max_tiles], n_tiles +
+// status u32, gx bf16[4m][H], act bf16[4m][I], ed bf16[4m][H].
+namespace {
+struct PrefillWs {
+  size_t ids, gw, counts, offsets, ids_sorted, slotpos, tiles, ctl, gx, act, ed, total;
+  int max_tiles;
+};
+PrefillWs prefill_layout(int m, int E, int H, int I) {
+  auto al = [](size_t v) { return (v + 255) & ~size_t(255); };
+  const size_t S = (size_t)m * 4;
+  PrefillWs w;
+  w.max_tiles = (int)((S + 127) / 128 + E);
+  size_t o = 0;
+  w.ids = o; o = al(o + S * 4);
+  w.gw = o; o = al(o + S * 2);
+  w.counts = o; o = al(o + (size_t)E * 4);
+  w.offsets = o; o = al(o + (size_t)E * 4);
+  w.ids_sorted = o; o = al(o + S * 4);
+  w.slotpos = o; o = al(o + S * 4);
+  w.tiles = o; o = al(o + (size_t)w.max_tiles * 16);
+  w.ctl = o; o = al(o + 8);
+  w.gx = o; o = al(o + S * H * 2);
+  w.act = o; o = al(o + S * I * 2);
+  w.ed = o; o = al(o + S * H * 2);
+  w.total = o;
+  return w;
+}
+}  // namespace
+
+extern "C" size_t mc_moe_prefill_workspace_size(int m, int n_experts, int hidden, int moe_inter) {
+  if (m < 1 || n_experts < 1 || hidden < 1 || moe_inter < 1) return 0;
+  return prefill_layout(m, n_experts, hidden, moe_inter).total;
+}
+
+extern "C" int mc_moe_prefill(mc_ctx* ctx, const uint16_t* x, const float* logits, int m,
+                              const mc_qweights* gate, const mc_qweights* up,
+                              const mc_qweights* down, int n_experts, int route_mode,
+                              const float* expert_bias, void* workspace, size_t ws_bytes,
+                              uint16_t* out) {
+  MC_REQUIRE(ctx, "moe_prefill: null context");
+  MC_REQUIRE(gate && up && down && x && logits && workspace && out, "moe_prefill: null pointer");
+  MC_REQUIRE(n_experts >= 4 && n_experts <= 64, "moe_prefill: n_experts %d", n_experts);
+  MC_REQUIRE(m >= 1, "moe_prefill: m %d", m);
+  const int H = gate->in_features;
+  MC_REQUIRE(gate->out_features % n_experts == 0, "moe_prefill: stacked gate rows");
+  const int I = gate->out_features / n_experts;
+  MC_REQUIRE(down->in_features == I && down->out_features == n_experts * H,
+             "moe_prefill: down shape [%d][%d] does not match E*H x I", down->out_features,
+             down->in_features);
+  const PrefillWs w = prefill_layout(m, n_experts, H, I);
+  MC_REQUIRE(ws_bytes >= w.total, "moe_prefill: workspace %zu < %zu bytes", ws_bytes, w.total);
+  MC_REQUIRE(mc_aligned(workspace, 256), "moe_prefill: workspace must be 256-byte aligned");
+  uint8_t* base = static_cast<uint8_t*>(workspace);
+  auto U32 = [&](size_t off) { return reinterpret_cast<uint32_t*>(base + off); };
+  auto B16 = [&](size_t off) { return reinterpret_cast<uint16_t*>(base + off); };
+  const int S = 4 * m;
+  int rc;
+  if ((rc = mc_moe_route_batch(ctx, logits, m, n_experts, route_mode, expert_bias, 1e-6f,
+                               U32(w.ids), B16(w.gw))))
+    return rc;
+  if ((rc = mc_moe_sort_map(ctx, U32(w.ids), m, n_experts, 128, U32(w.counts), U32(w.offsets),
+                            U32(w.ids_sorted), U32(w.slotpos), U32(w.tiles), U32(w.ctl),
+                            w.max_tiles)))
+    return rc;
+  MC_CUDA(cudaMemsetAsync(U32(w.ctl) + 1, 0, 4, ctx->stream));
+  if ((rc = mc_gather_rows_bf16(ctx, x, U32(w.ids_sorted), S, H, B16(w.gx)))) return rc;
+  if ((rc = mc_gemm_q4_grouped_gu(ctx, B16(w.gx), S, gate, up, n_experts, B16(w.act), U32(w.tiles),
+                                  U32(w.ctl), w.max_tiles, U32(w.ctl) + 1)))
+    return rc;
+  if ((rc = mc_gemm_q4_grouped(ctx, B16(w.act), S, down, n_experts, B16(w.ed), U32(w.tiles),
+                               U32(w.ctl), w.max_tiles, U32(w.ctl) + 1)))
+    return rc;
+  return mc_moe_combine_rows(ctx, B16(w.ed), U32(w.slotpos), B16(w.gw), out, m, 4, H);
+}

@@ -343,3 +343,48 @@ def eval_math(ctx: Context, op: int, x: torch.Tensor, y: torch.Tensor) -> None:
     """Device math probe (0 exp, 1 silu, 2 sigmoid, 3 bf16 rounding)."""
     ensure(x.dtype == torch.float32 and y.dtype == torch.float32, "f32 only")
     _lib.call("mc_eval_math", ctx.handle, op, _p(x), _p(y), x.numel())
+
+
+def moe_prefill_workspace_size(m: int, n_experts: int = 64, hidden: int = FIXED_HIDDEN,
+                               moe_inter: int = FIXED_MOE_INTER) -> int:
+    return int(_lib.lib().mc_moe_prefill_workspace_size(m, n_experts, hidden, moe_inter))
+
+
+def moe_prefill(ctx: Context, x: torch.Tensor, logits: torch.Tensor, gate: QuantWeights,
+                up: QuantWeights, down: QuantWeights, workspace: torch.Tensor, out: torch.Tensor,
+                n_experts: int = 64, route_mode: int = ROUTE_SOFTMAX_RENORM,
+                bias: torch.Tensor | None = None) -> None:
+    """moe_prefill (lfm.rs:847-965) from the router logits on, all on device."""
+    for w in (gate, up, down):
+        check_quant(w)
+    m, h = x.shape
+    ensure(logits.shape == (m, n_experts) and logits.dtype == torch.float32, "prefill logits")
+    ensure(out.shape == (m, h), "prefill out shape")
+    _bf16(x, out)
+    ensure(workspace.dtype == torch.uint8, "workspace is a byte tensor")
+    _lib.call("mc_moe_prefill", ctx.handle, _p(x), _p(logits), m, _lib.C.byref(gate.qw()),
+              _lib.C.byref(up.qw()), _lib.C.byref(down.qw()), n_experts, route_mode, _p(bias),
+              _p(workspace), workspace.numel(), _p(out))
+
+
+def prefill_workspace_view(workspace: torch.Tensor, m: int, n_experts: int = 64,
+                           hidden: int = FIXED_HIDDEN, moe_inter: int = FIXED_MOE_INTER) -> dict:
+    """Named views of a moe_prefill workspace (layout of moe_prefill.cu)."""
+    S = 4 * m
+    al = lambda v: (v + 255) & ~255
+    offs, o = {}, 0
+    max_tiles = (S + 127) // 128 + n_experts
+    for name, nbytes in (("ids", S * 4), ("gw", S * 2), ("counts", n_experts * 4),
+                         ("offsets", n_experts * 4), ("ids_sorted", S * 4), ("slotpos", S * 4),
+                         ("tiles", max_tiles * 16), ("ctl", 8), ("gx", S * hidden * 2),
+                         ("act", S * moe_inter * 2), ("ed", S * hidden * 2)):
+        offs[name] = (o, nbytes)
+        o = al(o + nbytes)
+    v = {k: workspace[a:a + n] for k, (a, n) in offs.items()}
+    u32 = lambda t: t.view(torch.int32)
+    b16 = lambda t: t.view(torch.bfloat16)
+    return dict(ids=u32(v["ids"]).view(m, 4), gw=b16(v["gw"]).view(m, 4),
+                ids_sorted=u32(v["ids_sorted"]), slotpos=u32(v["slotpos"]),
+                status=u32(v["ctl"])[1:2], n_tiles=u32(v["ctl"])[0:1],
+                tiles=u32(v["tiles"]).view(max_tiles, 4), gx=b16(v["gx"]).view(S, hidden),
+                act=b16(v["act"]).view(S, moe_inter), ed=b16(v["ed"]).view(S, hidden))

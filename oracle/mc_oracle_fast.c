@@ -178,3 +178,59 @@ void of_gemm_q4_grouped(const uint16_t* A, int K, const uint32_t* codes, const u
   }
   free(wd);
 }
+
+/* Whole prefill MoE FFN (softmax-renorm top-4, sort, grouped gate/up/SwiGLU,
+ * grouped down, combine) for m tokens: the CPU baseline of BASELINE cfg3. */
+void of_moe_prefill(const uint16_t* x, const float* logits, int m, int E, int H, int I,
+                    const uint32_t* gc, const uint16_t* gs, const uint16_t* gb,
+                    const uint32_t* uc, const uint16_t* us, const uint16_t* ub,
+                    const uint32_t* dc, const uint16_t* ds, const uint16_t* db, uint16_t* out) {
+  const int S = 4 * m;
+  uint32_t* ids = (uint32_t*)malloc(sizeof(uint32_t) * S);
+  float* w = (float*)malloc(sizeof(float) * S);
+  uint32_t* counts = (uint32_t*)calloc(E, sizeof(uint32_t));
+  uint32_t* offsets = (uint32_t*)malloc(sizeof(uint32_t) * E);
+  uint32_t* sorted = (uint32_t*)malloc(sizeof(uint32_t) * S);
+  uint32_t* slot = (uint32_t*)malloc(sizeof(uint32_t) * S);
+  uint16_t* gx = (uint16_t*)malloc(sizeof(uint16_t) * (size_t)S * H);
+  uint16_t* g = (uint16_t*)malloc(sizeof(uint16_t) * (size_t)S * I);
+  uint16_t* u = (uint16_t*)malloc(sizeof(uint16_t) * (size_t)S * I);
+  uint16_t* ed = (uint16_t*)malloc(sizeof(uint16_t) * (size_t)S * H);
+  for (int t = 0; t < m; ++t) {
+    const float* z = logits + (size_t)t * E;
+    int used[256] = {0};
+    float ex[4], den = 0.0f;
+    for (int r = 0; r < 4; ++r) {
+      float bv = -INFINITY; int bi = 0;
+      for (int e = 0; e < E; ++e) if (!used[e] && z[e] > bv) { bv = z[e]; bi = e; }
+      used[bi] = 1; ids[4 * t + r] = (uint32_t)bi;
+      ex[r] = expf(z[bi] - z[ids[4 * t]]); den += ex[r];
+    }
+    for (int r = 0; r < 4; ++r) w[4 * t + r] = rbf(ex[r] / den);
+  }
+  for (int i = 0; i < S; ++i) counts[ids[i]]++;
+  uint32_t acc = 0;
+  for (int e = 0; e < E; ++e) { offsets[e] = acc; acc += counts[e]; }
+  uint32_t* pos = (uint32_t*)malloc(sizeof(uint32_t) * E);
+  memcpy(pos, offsets, sizeof(uint32_t) * E);
+  for (int i = 0; i < S; ++i) { uint32_t p = pos[ids[i]]++; sorted[p] = (uint32_t)(i / 4); slot[i] = p; }
+#pragma omp parallel for schedule(static)
+  for (int i = 0; i < S; ++i) memcpy(gx + (size_t)i * H, x + (size_t)sorted[i] * H, 2 * (size_t)H);
+  of_gemm_q4_grouped(gx, H, gc, gs, gb, I, counts, offsets, E, g);
+  of_gemm_q4_grouped(gx, H, uc, us, ub, I, counts, offsets, E, u);
+#pragma omp parallel for schedule(static)
+  for (size_t i = 0; i < (size_t)S * I; ++i) {
+    float gv = bf(g[i]);
+    g[i] = tobf(rbf(gv / (1.0f + expf(-gv))) * bf(u[i]));
+  }
+  of_gemm_q4_grouped(g, I, dc, ds, db, H, counts, offsets, E, ed);
+#pragma omp parallel for schedule(static)
+  for (int t = 0; t < m; ++t)
+    for (int h = 0; h < H; ++h) {
+      float s = 0.0f;
+      for (int r = 0; r < 4; ++r) s += rbf(w[4 * t + r] * bf(ed[(size_t)slot[4 * t + r] * H + h]));
+      out[(size_t)t * H + h] = tobf(s);
+    }
+  free(ids); free(w); free(counts); free(offsets); free(sorted); free(slot); free(gx);
+  free(g); free(u); free(ed); free(pos);
+}

@@ -114,3 +114,33 @@ def test_grouped_gemm_single_matrix_exactness_structure(cuda_ctx):
     want = oracle.gemm_q4_grouped(a, (codes, s, b), np.array([rows], np.uint32),
                                   np.array([0], np.uint32), E)
     assert_close_bf16(host_bits(c), want, "single tile", min_equal=0.8)
+
+
+def test_moe_prefill_entry_point(cuda_ctx):
+    """mc_moe_prefill (all seven launches behind one call) against the oracle."""
+    E, H, I, m = 8, 2048, 256, 160
+    x, logits, gate, up, down = prefill_case(11, m, E, H, I)
+    ws = torch.zeros(lfm.moe_prefill_workspace_size(m, E, H, I), dtype=torch.uint8, device="cuda")
+    out = empty_bf16(m, H)
+    lfm.moe_prefill(cuda_ctx, dev_bf16(x), dev_f32(logits), dev_qw(*gate), dev_qw(*up),
+                    dev_qw(*down), ws, out, n_experts=E)
+    torch.cuda.synchronize()
+    v = lfm.prefill_workspace_view(ws, m, E, H, I)
+    assert int(host_u32(v["status"])[0]) == 0
+    want = oracle.moe_prefill(x, logits, gate, up, down, n_experts=E)
+    assert np.array_equal(host_u32(v["ids"]), want["ids"])
+    assert_close_bf16(host_bits(v["act"]), want["act"], "act")
+    # combine is a fixed-order sum: bit-exact on the GPU's own expert rows
+    ed = host_bits(v["ed"])
+    gw = host_bits(v["gw"])
+    slot = host_u32(v["slotpos"])
+    assert_bits_equal(host_bits(out), oracle.moe_combine(ed, slot, gw, m, H), "combine")
+    # end to end: out is a sum of four bf16-rounded terms that can cancel, so the
+    # relative part of the tolerance is taken on sum_r |w_r * ed_r|, not on |out|
+    f = lambda b: synth.bf16_bits_to_f32(np.asarray(b)).astype(np.float64)
+    terms = np.abs(f(want["gw"]).reshape(m, 4, 1) *
+                   f(want["ed"])[want["slotpos"].reshape(m, 4)])
+    got_o, want_o = f(host_bits(out)), f(want["out"])
+    rms = np.sqrt(np.mean(want_o ** 2))
+    bad = np.abs(got_o - want_o) > RTOL * terms.sum(axis=1) + ATOL_RMS * rms
+    assert not bad.any(), f"out: {bad.sum()} outside tolerance"
