@@ -170,6 +170,29 @@ int mc_moe_decode_layer(mc_ctx* ctx, const uint16_t* h, const uint16_t* b,
                         const mc_qweights* down, int n_experts, uint16_t* out,
                         uint32_t* workspace, size_t ws_words, float eps, float route_eps);
 
+/* mc_moe_decode_layer with no workspace argument and no allocation: the
+ * scratch is a fixed 33,296-byte array inside this library (one per device),
+ * for callers that cannot lend device memory (an engine whose allocator is
+ * frozen after start-up, a plugin barred from allocating on the serving
+ * path). It has no counterpart in the reference, whose Metal kernels take
+ * every buffer from the caller. Limits and duties:
+ *  - expert width I = gate->out_features / n_experts at most 2048, else
+ *    MC_EINVAL before any launch;
+ *  - the first call on each device is the set-up: it looks up the array's
+ *    address with that device current and zeroes it on ctx's stream, waiting
+ *    for that, so it blocks and must come before any stream capture;
+ *  - the scratch is shared by every context and stream of the process on a
+ *    device, so calls whose kernels could overlap race: order them;
+ *  - `status` (device u32, may be NULL) receives this call's status word,
+ *    the codes mc_moe_decode_layer leaves in workspace[2]. */
+int mc_moe_decode_layer_noalloc(mc_ctx* ctx, const uint16_t* h, const uint16_t* b,
+                                const uint16_t* norm_w, uint16_t* h_out, uint16_t* normed,
+                                const void* router_w, int router_dtype,
+                                const float* expert_bias, int route_mode, float* logits,
+                                uint32_t* ids, uint16_t* weights, const mc_qweights* gate,
+                                const mc_qweights* up, const mc_qweights* down, int n_experts,
+                                uint16_t* out, uint32_t* status, float eps, float route_eps);
+
 /* ----------------------------------------------------------- prefill path */
 
 /* moe_route_batch (kernels/lfm.rs:536-555 -> lfm.metal:1558-1602): per-token

@@ -71,6 +71,8 @@ SIGNATURES: dict[str, tuple] = {
     "mc_moe_decode_layer": (I, [P, P, P, P, P, P, P, I, P, I, P, P, P, QP, QP, QP, I, P, P,
                                 C.c_size_t, F, F]),
     "mc_moe_decode_workspace_words": (C.c_size_t, [I]),
+    "mc_moe_decode_layer_noalloc": (I, [P, P, P, P, P, P, P, I, P, I, P, P, P, QP, QP, QP, I, P,
+                                        P, F, F]),
     "mc_moe_route_batch": (I, [P, P, I, I, I, P, F, P, P]),
     "mc_moe_sort_map": (I, [P, P, I, I, I, P, P, P, P, P, P, I]),
     "mc_gather_rows_bf16": (I, [P, P, P, I, I, P]),

@@ -252,6 +252,29 @@ def moe_decode_layer(ctx: Context, h, b, nw, hout, normed, router, logits, bias,
               n_experts, _p(out), _p(workspace), workspace.numel(), eps, route_eps)
 
 
+def moe_decode_layer_noalloc(ctx: Context, h, b, nw, hout, normed, router, logits, bias, ids,
+                             weights, gate: QuantWeights, up: QuantWeights, down: QuantWeights,
+                             out, status=None, eps: float = 1e-5,
+                             route_mode: int = ROUTE_SOFTMAX_RENORM, route_eps: float = 1e-6,
+                             n_experts: int = 64) -> None:
+    """moe_decode_layer with the library's built-in per-device scratch instead
+    of a caller workspace (expert width <= 2048). The first call per device
+    sets the scratch up and blocks; calls that could overlap on one device
+    race. ``status``: optional int32 [1] receiving this call's status word."""
+    for w in (gate, up, down):
+        check_quant(w)
+    e, k = router.shape
+    ensure(e == n_experts and k == FIXED_HIDDEN, "router shape")
+    ensure(h.numel() == k and out.numel() == k, "moe_decode_layer_noalloc is batch 1")
+    _bf16(h, b, nw, hout, normed, weights, out)
+    _u32(ids, status)
+    dt = _lib.DTYPE_BF16 if router.dtype == torch.bfloat16 else _lib.DTYPE_F32
+    _lib.call("mc_moe_decode_layer_noalloc", ctx.handle, _p(h), _p(b), _p(nw), _p(hout),
+              _p(normed), _p(router), dt, _p(bias), route_mode, _p(logits), _p(ids), _p(weights),
+              _lib.C.byref(gate.qw()), _lib.C.byref(up.qw()), _lib.C.byref(down.qw()),
+              n_experts, _p(out), _p(status), eps, route_eps)
+
+
 def decode_workspace_act(workspace: torch.Tensor, moe_inter: int = FIXED_MOE_INTER):
     """The act rows (bf16 [4, I]) held in a moe_decode_layer workspace."""
     w = workspace[132:132 + 2 * moe_inter].contiguous()
