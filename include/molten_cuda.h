@@ -160,7 +160,8 @@ int mc_gemv_gather_down_combine4(mc_ctx* ctx, const mc_qweights* down, const uin
  * workspace[2] != 0 after a call reports a bounded wait that gave up (1) or
  * an expert id out of range (2); the act rows are the bf16 values
  * ((uint16_t*)(workspace + 132))[r*I + i]). All row buffers, the weights'
- * scales/biases and the workspace 16-byte aligned. */
+ * scales/biases and the workspace 16-byte aligned; the expert width I is a
+ * multiple of 512 and at most 2048 (each row's scales are one bulk copy). */
 size_t mc_moe_decode_workspace_words(int moe_inter);
 int mc_moe_decode_layer(mc_ctx* ctx, const uint16_t* h, const uint16_t* b,
                         const uint16_t* norm_w, uint16_t* h_out, uint16_t* normed,
@@ -205,8 +206,8 @@ int mc_moe_route_batch(mc_ctx* ctx, const float* logits, int m, int n_experts,
  * in two launches: counts[E], offsets[E] (exclusive scan), the stable
  * token-major, rank-major scatter ids_sorted[m*4] / slotpos[m*4], and the
  * row-tile list tiles[max_tiles] of uint4 {m0, m_end, expert, 0} with its
- * length in *n_tiles (device u32). bm is the tile height (128);
- * max_tiles >= ceil(m*4/bm) + E. */
+ * length in *n_tiles (device u32). bm is the tile height (256 for the
+ * grouped GEMMs, at most 256 there); max_tiles >= ceil(m*4/bm) + E. */
 int mc_moe_sort_map(mc_ctx* ctx, const uint32_t* ids, int m, int n_experts, int bm,
                     uint32_t* counts, uint32_t* offsets, uint32_t* ids_sorted,
                     uint32_t* slotpos, uint32_t* tiles, uint32_t* n_tiles, int max_tiles);
@@ -220,9 +221,10 @@ int mc_gather_rows_bf16(mc_ctx* ctx, const uint16_t* table, const uint32_t* ids,
  * quant_nax.metal:4091-4234): C[i][n] = sum_k A[i][k] * bf16(s*q+b)[e*N+n][k]
  * for the rows i of each tile's expert e; A bf16 [rows][K] (expert-sorted),
  * C bf16 [rows][N]; w stacked [E*N][K] Q4; tiles/n_tiles from
- * mc_moe_sort_map with bm = 128. tcgen05 tensor-core kernel (fp32
- * accumulation). status: nullable u32 word, bit 0 = a bounded wait gave up,
- * bit 1 = a malformed tile was skipped. N % 128 == 0, K % 64 == 0. */
+ * mc_moe_sort_map with bm <= 256 (a tile taller than 256 rows is malformed).
+ * tcgen05 tensor-core kernel (fp32 accumulation). status: nullable u32 word,
+ * bit 0 = a bounded wait gave up, bit 1 = a malformed tile was skipped.
+ * N % 128 == 0, K % 64 == 0. */
 int mc_gemm_q4_grouped(mc_ctx* ctx, const uint16_t* a, int rows, const mc_qweights* w,
                        int n_experts, uint16_t* c, const uint32_t* tiles,
                        const uint32_t* n_tiles, int max_tiles, uint32_t* status);

@@ -4,22 +4,30 @@
 //
 //   C[i][n] = sum_k A[i][k] * bf16(s*q + b)[e*N + n][k]
 //
-// for the sorted rows i of each row tile (m0, m_end, expert e); A bf16
+// for the sorted rows i of each row chunk (m0, m_end, expert e); A bf16
 // [rows][K] (the expert-sorted activations), W the stacked [E*N][K] MLX Q4
-// matrix. The gate/up variant computes both GEMMs of a tile against the same
-// A tile and writes act = bf16(bf16(silu(bf16(g))) * bf16(u)) in the
+// matrix. The gate/up variant computes both GEMMs of a chunk against the same
+// A rows and writes act = bf16(bf16(silu(bf16(g))) * bf16(u)) in the
 // epilogue (silu_mul_bf16, elementwise.metal:7-15).
 //
-// Persistent kernel, one CTA per SM, work items = (row tile, 128-column
-// block) in tile-major order so neighbouring CTAs share the A tile in L2.
-// Warp roles (192 threads):
-//   warp 0      TMA: 128x64 bf16 A tiles, 128-byte swizzle, into the stage ring
-//   warp 1      TMEM allocation; lane 0 issues tcgen05.mma (M=128, N=128,
-//               K=16, bf16 x bf16 -> fp32) and tcgen05.commit
-//   warps 2..5  dequantise the B tile(s) straight into the UMMA K-major
+// The MMA runs "weights x tokens": the dequantised 128-feature weight block
+// is the M = 128 operand and the chunk's token rows are the N operand, with
+// N = the chunk height rounded up to 16 (at most 256), so one dequantised
+// weight tile serves up to 256 tokens and small experts do not pay for
+// padding rows. D (TMEM) is [128 features][N tokens] fp32.
+//
+// Persistent kernel, one CTA per SM, work items = (row chunk, 128-feature
+// block) in chunk-major order so neighbouring CTAs share a chunk's token rows
+// in L2. Warp roles (320 threads):
+//   warp 0      TMA: 64-row x 64-K bf16 boxes of the chunk's token rows,
+//               128-byte swizzle, into the stage ring
+//   warp 1      TMEM allocation (512 columns); lane 0 issues tcgen05.mma
+//               (M=128, N=chunk, K=16, bf16 x bf16 -> fp32) and commits
+//   warps 2..9  dequantise the weight tiles straight into the UMMA K-major
 //               128-byte-swizzled layout (w = bf16(fma(s, q, b)), MLX's
-//               dequantize), then run the epilogue from TMEM (tcgen05.ld)
-// Stage s: full[s] (TMA tx + 128 dequant arrivals), empty[s] (tcgen05.commit).
+//               dequantize): gate/up: warps 2-5 gate, 6-9 up; down: warps
+//               2-5 even K steps, 6-9 odd ones. Then the epilogue from TMEM.
+// Stage s: full[s] (TMA tx + dequant arrivals), empty[s] (tcgen05.commit).
 // Every wait is bounded by a %globaltimer deadline; on timeout the kernel
 // records status bit 1, stops issuing and still drains what it issued before
 // freeing TMEM.
@@ -31,19 +39,27 @@
 
 namespace {
 
-constexpr int BM = 128, BN = 128, BK = 64;
-constexpr int kThreads = 192;
+constexpr int BF = 128;    // weight features per item (the MMA's M)
+constexpr int BK = 64;     // K per stage
+constexpr int MAXN = 256;  // token rows per chunk (the MMA's N, rounded up to 16)
+constexpr int BOX_ROWS = 64;
+constexpr int BOX_BYTES = BOX_ROWS * BK * 2;  // 8 KB token box
+constexpr int kDeqThreads = 256;
+constexpr int kThreads = 64 + kDeqThreads;
 constexpr unsigned long long kTimeoutNs = 1000000000ull;  // 1 s per wait
 
 template <bool GU>
 struct Cfg {
-  static constexpr int STAGES = GU ? 4 : 6;
-  static constexpr int A_BYTES = BM * BK * 2;  // 16 KB
-  static constexpr int B_BYTES = BN * BK * 2;  // 16 KB per weight matrix
   static constexpr int NMAT = GU ? 2 : 1;
-  static constexpr int STAGE_BYTES = A_BYTES + NMAT * B_BYTES;
-  static constexpr int TMEM_COLS = GU ? 256 : 128;
+  static constexpr int B_BYTES = MAXN * BK * 2;  // 32 KB of token rows
+  static constexpr int A_BYTES = BF * BK * 2;    // 16 KB per weight matrix
+  static constexpr int STAGE_BYTES = B_BYTES + NMAT * A_BYTES;
+  static constexpr int STAGES = GU ? 3 : 4;
   static constexpr int SMEM = STAGES * STAGE_BYTES + 1024;
+  static constexpr int TMEM_COLS = 512;
+  static constexpr int NBUF = GU ? 1 : 2;  // accumulator buffers (gate+up fill TMEM)
+  // dequant arrivals per stage: gate/up both groups, down one group
+  static constexpr uint32_t DEQ_ARRIVALS = GU ? 256u : 128u;
 };
 
 struct GemmParams {
@@ -54,6 +70,28 @@ struct GemmParams {
   uint32_t* status;
   int N, K, rows, max_tiles, n_experts;
 };
+
+// One work item: token rows [m0, mend) of expert e against feature block nb.
+struct Item {
+  uint32_t m0, mend, e;
+  int nb, n;  // n = MMA N (rows rounded up to 16)
+  bool ok;
+};
+
+__device__ __forceinline__ Item item_info(const GemmParams& P, int item, int nblk) {
+  const uint4 tile = P.tiles[item / nblk];
+  Item it;
+  it.nb = item % nblk;
+  it.ok = tile.z < (uint32_t)P.n_experts && tile.x < tile.y && tile.y <= (uint32_t)P.rows &&
+          tile.y - tile.x <= (uint32_t)MAXN;
+  // a malformed tile still runs through the pipeline (every role sees the same
+  // shape) on row 0 of expert 0, and its results are not stored
+  it.m0 = it.ok ? tile.x : 0u;
+  it.mend = it.ok ? tile.y : 1u;
+  it.e = it.ok ? tile.z : 0u;
+  it.n = (int)((it.mend - it.m0 + 15u) & ~15u);
+  return it;
+}
 
 // ---- PTX wrappers -----------------------------------------------------------
 
@@ -73,17 +111,17 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
          ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
 }
 
-// Instruction descriptor: D f32, A/B bf16, both K-major, N = BN, M = BM.
-constexpr uint32_t kIdesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) |
-                            ((uint32_t)(BM >> 4) << 24);
+// Instruction descriptor: D f32, A/B bf16, both K-major, M = BF; N per item.
+constexpr uint32_t kIdescBase = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BF >> 4) << 24);
+__device__ __forceinline__ uint32_t idesc_for(int n) { return kIdescBase | ((uint32_t)(n >> 3) << 17); }
 
 __device__ __forceinline__ void umma_bf16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc,
-                                          uint32_t accumulate) {
+                                          uint32_t idesc, uint32_t accumulate) {
   asm volatile(
       "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
       " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n}\n" ::"r"(
           tmem_d),
-      "l"(adesc), "l"(bdesc), "r"(kIdesc), "r"(accumulate), "r"(0), "r"(0), "r"(0), "r"(0)
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(0), "r"(0), "r"(0), "r"(0)
       : "memory");
 }
 
@@ -175,23 +213,24 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const GemmParams P)
   using C = Cfg<GU>;
   extern __shared__ uint8_t smem_raw[];
   __shared__ __align__(8) uint64_t full[C::STAGES], empty[C::STAGES];
-  __shared__ __align__(8) uint64_t acc_full, acc_empty;
+  __shared__ __align__(8) uint64_t acc_full[2], acc_empty[2], drain_bar;
   __shared__ uint32_t tmem_base_s;
   __shared__ volatile uint32_t abort_s;
-  __shared__ uint32_t acc_commits_s;  // commits the MMA thread made to acc_full
 
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
   const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
-  const unsigned long long t_start = mc_globaltimer();
 
   if (t == 0) {
     for (int s = 0; s < C::STAGES; ++s) {
-      mc_mbar_init(&full[s], 1 + 128);
+      mc_mbar_init(&full[s], 1 + C::DEQ_ARRIVALS);
       mc_mbar_init(&empty[s], 1);
     }
-    mc_mbar_init(&acc_full, 1);
-    mc_mbar_init(&acc_empty, 128);
+    for (int b = 0; b < 2; ++b) {
+      mc_mbar_init(&acc_full[b], 1);
+      mc_mbar_init(&acc_empty[b], kDeqThreads);
+    }
+    mc_mbar_init(&drain_bar, 1);
     mc_fence_barrier_init();
     abort_s = 0;
   }
@@ -207,7 +246,7 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const GemmParams P)
   tc_fence_after();
   const uint32_t tmem = tmem_base_s;
 
-  const int nblk = P.N / BN;
+  const int nblk = P.N / BF;
   const int ksteps = P.K / BK;
   int ntiles = (int)*P.n_tiles;
   if (ntiles > P.max_tiles) ntiles = P.max_tiles;
@@ -218,7 +257,11 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const GemmParams P)
     if (lane == 0) {
       uint32_t it = 0;
       for (int item = blockIdx.x; item < total && !abort_s; item += gridDim.x) {
-        const uint4 tile = P.tiles[item / nblk];
+        const Item w = item_info(P, item, nblk);
+        int nbox = (w.n + BOX_ROWS - 1) / BOX_ROWS;
+        // boxes that start past the last row would only read fill values
+        const int rows_left = P.rows - (int)w.m0;
+        if (nbox * BOX_ROWS > rows_left + BOX_ROWS - 1) nbox = (rows_left + BOX_ROWS - 1) / BOX_ROWS;
         for (int kk = 0; kk < ksteps; ++kk, ++it) {
           const int s = it % C::STAGES;
           const uint32_t ph = (it / C::STAGES) & 1;
@@ -226,27 +269,33 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const GemmParams P)
             abort_s = 1;
             break;
           }
-          mc_mbar_expect_tx(&full[s], C::A_BYTES);
-          tma_load_2d(smem + s * C::STAGE_BYTES, &tmA, kk * BK, (int)tile.x, &full[s]);
+          mc_mbar_expect_tx(&full[s], (uint32_t)(nbox * BOX_BYTES));
+          for (int bx = 0; bx < nbox; ++bx)
+            tma_load_2d(smem + s * C::STAGE_BYTES + bx * BOX_BYTES, &tmA, kk * BK,
+                        (int)w.m0 + bx * BOX_ROWS, &full[s]);
         }
       }
-    }
-    if (lane == 0 && abort_s) {
-      // loads already issued finish within microseconds; give them a bounded
-      // time to land before the CTA may leave
-      for (int k = 0; k < 200; ++k) __nanosleep(1000);
+      if (abort_s) {
+        // loads already issued finish within microseconds; give them a bounded
+        // time to land before the CTA may leave
+        for (int k = 0; k < 200; ++k) __nanosleep(1000);
+      }
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       uint32_t it = 0, j = 0;
-      acc_commits_s = 0;
       for (int item = blockIdx.x; item < total && !abort_s; item += gridDim.x, ++j) {
-        if (!wait_bar(&acc_empty, (j & 1) ^ 1, &abort_s, mc_globaltimer() + kTimeoutNs)) {
+        const Item w = item_info(P, item, nblk);
+        const uint32_t idesc = idesc_for(w.n);
+        const int buf = (int)(j % C::NBUF);
+        const uint32_t use = j / C::NBUF;
+        if (!wait_bar(&acc_empty[buf], (use & 1) ^ 1, &abort_s, mc_globaltimer() + kTimeoutNs)) {
           abort_s = 1;
           break;
         }
         tc_fence_after();
+        const uint32_t d0 = tmem + (uint32_t)(buf * 256);
         bool ok = true;
         for (int kk = 0; kk < ksteps; ++kk, ++it) {
           const int s = it % C::STAGES;
@@ -257,121 +306,110 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const GemmParams P)
             break;
           }
           tc_fence_after();
-          const uint32_t a_addr = mc_smem_u32(smem + s * C::STAGE_BYTES);
-          const uint64_t adesc = sw128_desc(a_addr);
-          const uint64_t bdesc0 = sw128_desc(a_addr + C::A_BYTES);
-          const uint64_t bdesc1 = sw128_desc(a_addr + C::A_BYTES + C::B_BYTES);
+          const uint32_t base = mc_smem_u32(smem + s * C::STAGE_BYTES);
+          const uint64_t bdesc = sw128_desc(base);
+          const uint64_t adesc0 = sw128_desc(base + C::B_BYTES);
+          const uint64_t adesc1 = sw128_desc(base + C::B_BYTES + C::A_BYTES);
 #pragma unroll
           for (int k16 = 0; k16 < BK / 16; ++k16) {
             const uint32_t acc = (kk > 0 || k16 > 0) ? 1u : 0u;
-            umma_bf16(tmem, adesc + 2 * k16, bdesc0 + 2 * k16, acc);
-            if (GU) umma_bf16(tmem + BN, adesc + 2 * k16, bdesc1 + 2 * k16, acc);
+            umma_bf16(d0, adesc0 + 2 * k16, bdesc + 2 * k16, idesc, acc);
+            if (GU) umma_bf16(d0 + 256, adesc1 + 2 * k16, bdesc + 2 * k16, idesc, acc);
           }
           umma_commit(&empty[s]);  // stage free once these MMAs have read it
         }
         if (!ok) break;
-        umma_commit(&acc_full);
-        acc_commits_s = j + 1;
+        umma_commit(&acc_full[buf]);
       }
     }
     __syncwarp();
   } else {
     // ------------------------------------------ dequant producers + epilogue
-    const int d = t - 64;  // B-tile row (0..127)
-    const int q = warp & 3;  // TMEM lane quarter this warp may access
-    const int r_out = 32 * q + lane;  // accumulator row this thread reads
+    const int dt = t - 64;            // 0..255
+    const int grp = dt >> 7;          // gate/up: matrix; down: K-step parity
+    const int d = dt & 127;           // weight row within the feature block
+    const int q = warp & 3;           // TMEM lane quarter this warp may access
+    const uint32_t* wcodes = (GU && grp) ? P.w1.codes : P.w0.codes;
+    const uint16_t* wscales = (GU && grp) ? P.w1.scales : P.w0.scales;
+    const uint16_t* wbiases = (GU && grp) ? P.w1.biases : P.w0.biases;
     uint32_t it = 0, j = 0;
     for (int item = blockIdx.x; item < total && !abort_s; item += gridDim.x, ++j) {
-      const uint4 tile = P.tiles[item / nblk];
-      const int nb = item % nblk;
-      const uint32_t e = tile.z;
-      const bool tile_ok = e < (uint32_t)P.n_experts && tile.x < tile.y &&
-                           tile.y <= (uint32_t)P.rows && tile.y - tile.x <= (uint32_t)BM;
-      if (!tile_ok && t == 64 && P.status) atomicOr(P.status, 2u);
-      const size_t wrow = (size_t)(tile_ok ? e : 0) * P.N + (size_t)nb * BN + d;
-      const uint8_t* c0 = reinterpret_cast<const uint8_t*>(P.w0.codes) + wrow * (P.K / 2);
-      const uint16_t* s0 = P.w0.scales + wrow * (P.K / 64);
-      const uint16_t* b0 = P.w0.biases + wrow * (P.K / 64);
-      const uint8_t* c1 = GU ? reinterpret_cast<const uint8_t*>(P.w1.codes) + wrow * (P.K / 2) : c0;
-      const uint16_t* s1 = GU ? P.w1.scales + wrow * (P.K / 64) : s0;
-      const uint16_t* b1 = GU ? P.w1.biases + wrow * (P.K / 64) : b0;
+      const Item w = item_info(P, item, nblk);
+      if (!w.ok && dt == 0 && P.status) atomicOr(P.status, 2u);
+      const size_t wrow = (size_t)w.e * P.N + (size_t)w.nb * BF + d;
+      const uint8_t* crow = reinterpret_cast<const uint8_t*>(wcodes) + wrow * (P.K / 2);
+      const uint16_t* srow = wscales + wrow * (P.K / 64);
+      const uint16_t* brow = wbiases + wrow * (P.K / 64);
+      // K steps of this thread: all (gate/up) or every other one (down)
+      const int step = GU ? 1 : 2;
+      const int k0 = GU ? 0 : (int)((grp - it) & 1u);
       bool ok = true;
-      uint4 na0 = __ldg(reinterpret_cast<const uint4*>(c0));
-      uint4 nb0 = __ldg(reinterpret_cast<const uint4*>(c0) + 1);
-      uint4 na1 = na0, nb1 = nb0;
-      if (GU) {
-        na1 = __ldg(reinterpret_cast<const uint4*>(c1));
-        nb1 = __ldg(reinterpret_cast<const uint4*>(c1) + 1);
+      uint4 na = make_uint4(0, 0, 0, 0), nb = na;
+      float nsc = 0.0f, nbi = 0.0f;
+      if (k0 < ksteps) {
+        na = __ldg(reinterpret_cast<const uint4*>(crow + k0 * 32));
+        nb = __ldg(reinterpret_cast<const uint4*>(crow + k0 * 32) + 1);
+        nsc = mc_bf16_to_f32(__ldg(srow + k0));
+        nbi = mc_bf16_to_f32(__ldg(brow + k0));
       }
-      for (int kk = 0; kk < ksteps; ++kk, ++it) {
-        const uint4 a0 = na0, bq0 = nb0, a1 = na1, bq1 = nb1;
-        const float sc0 = mc_bf16_to_f32(__ldg(s0 + kk)), bi0 = mc_bf16_to_f32(__ldg(b0 + kk));
-        float sc1 = 0.0f, bi1 = 0.0f;
-        if (GU) {
-          sc1 = mc_bf16_to_f32(__ldg(s1 + kk));
-          bi1 = mc_bf16_to_f32(__ldg(b1 + kk));
+      for (int kk = k0; kk < ksteps; kk += step) {
+        const uint4 ca = na, cb = nb;
+        const float sc = nsc, bi = nbi;
+        const int kn = kk + step;
+        if (kn < ksteps) {  // prefetch this thread's next K slice
+          na = __ldg(reinterpret_cast<const uint4*>(crow + kn * 32));
+          nb = __ldg(reinterpret_cast<const uint4*>(crow + kn * 32) + 1);
+          nsc = mc_bf16_to_f32(__ldg(srow + kn));
+          nbi = mc_bf16_to_f32(__ldg(brow + kn));
         }
-        if (kk + 1 < ksteps) {  // prefetch the next K slice's codes
-          na0 = __ldg(reinterpret_cast<const uint4*>(c0 + (kk + 1) * 32));
-          nb0 = __ldg(reinterpret_cast<const uint4*>(c0 + (kk + 1) * 32) + 1);
-          if (GU) {
-            na1 = __ldg(reinterpret_cast<const uint4*>(c1 + (kk + 1) * 32));
-            nb1 = __ldg(reinterpret_cast<const uint4*>(c1 + (kk + 1) * 32) + 1);
-          }
-        }
-        const int s = it % C::STAGES;
-        const uint32_t ph = (it / C::STAGES) & 1;
+        const uint32_t itk = it + (uint32_t)kk;
+        const int s = itk % C::STAGES;
+        const uint32_t ph = (itk / C::STAGES) & 1;
         if (!wait_bar(&empty[s], ph ^ 1, &abort_s, mc_globaltimer() + kTimeoutNs)) {
           abort_s = 1;
           ok = false;
           break;
         }
-        uint8_t* bt = smem + s * C::STAGE_BYTES + C::A_BYTES;
-        dequant_row64(a0, bq0, sc0, bi0, bt + d * 128, d & 7);
-        if (GU) dequant_row64(a1, bq1, sc1, bi1, bt + C::B_BYTES + d * 128, d & 7);
+        uint8_t* at = smem + s * C::STAGE_BYTES + C::B_BYTES + (GU ? grp * C::A_BYTES : 0);
+        dequant_row64(ca, cb, sc, bi, at + d * 128, d & 7);
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         mc_mbar_arrive(&full[s]);
       }
+      it += (uint32_t)ksteps;
       if (!ok) break;
-      // ---- epilogue: TMEM -> registers -> bf16 rows
-      if (!wait_bar(&acc_full, j & 1, &abort_s, mc_globaltimer() + kTimeoutNs)) {
+      // ---- epilogue: TMEM [feature][token] -> bf16 out[token][feature]
+      const int buf = (int)(j % C::NBUF);
+      const uint32_t use = j / C::NBUF;
+      if (!wait_bar(&acc_full[buf], use & 1, &abort_s, mc_globaltimer() + kTimeoutNs)) {
         abort_s = 1;
         break;
       }
       tc_fence_after();
-      const uint32_t m0 = tile.x, mend = tile.y;
-      const bool live = tile_ok && m0 + r_out < mend;
-      uint16_t* orow = P.out + (size_t)(m0 + r_out) * P.N + (size_t)nb * BN;
+      const int f = 32 * q + lane;  // feature row of D this thread reads
+      const int n16 = w.n >> 4, split = (n16 + 1) >> 1;
+      const int c_lo = grp ? split : 0, c_hi = grp ? n16 : split;
+      const uint32_t lane_base = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(buf * 256);
+      uint16_t* ocol = P.out + (size_t)w.nb * BF + f;
 #pragma unroll 1
-      for (int c = 0; c < BN; c += 16) {
+      for (int c = c_lo; c < c_hi; ++c) {
         uint32_t g[16], u[16];
-        tmem_ld16(tmem + ((uint32_t)(32 * q) << 16) + c, g);
-        if (GU) tmem_ld16(tmem + ((uint32_t)(32 * q) << 16) + BN + c, u);
+        tmem_ld16(lane_base + 16 * c, g);
+        if (GU) tmem_ld16(lane_base + 256 + 16 * c, u);
         tmem_wait_ld();
-        uint32_t pk[8];
+        const uint32_t r0 = w.m0 + 16u * (uint32_t)c;
 #pragma unroll
-        for (int h = 0; h < 8; ++h) {
-          float o[2];
-#pragma unroll
-          for (int z = 0; z < 2; ++z) {
-            const float gv = mc_round_bf16(__uint_as_float(g[2 * h + z]));
-            if (GU) {
-              const float uv = mc_round_bf16(__uint_as_float(u[2 * h + z]));
-              o[z] = __fmul_rn(mc_round_bf16(mc_silu(gv)), uv);
-            } else {
-              o[z] = gv;
-            }
+        for (int i = 0; i < 16; ++i) {
+          const float gv = mc_round_bf16(__uint_as_float(g[i]));
+          float o = gv;
+          if (GU) {
+            const float uv = mc_round_bf16(__uint_as_float(u[i]));
+            o = __fmul_rn(mc_round_bf16(mc_silu(gv)), uv);
           }
-          pk[h] = (uint32_t)mc_f32_to_bf16(o[0]) | ((uint32_t)mc_f32_to_bf16(o[1]) << 16);
-        }
-        if (live) {
-          uint4* dst = reinterpret_cast<uint4*>(orow + c);
-          dst[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
-          dst[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+          if (w.ok && r0 + i < w.mend) ocol[(size_t)(r0 + i) * P.N] = mc_f32_to_bf16(o);
         }
       }
       tc_fence_before();
-      mc_mbar_arrive(&acc_empty);
+      mc_mbar_arrive(&acc_empty[buf]);
     }
   }
 
@@ -380,12 +418,11 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const GemmParams P)
   if (abort_s && t == 0 && P.status) atomicOr(P.status, 1u);
   if (warp == 1) {
     if (abort_s && lane == 0) {
-      // make sure no MMA is still writing TMEM before it is freed: one more
-      // commit completes acc_full's next phase once all issued MMAs are done
-      const uint32_t n = acc_commits_s;
-      umma_commit(&acc_full);
+      // no MMA may still write TMEM when it is freed: this commit arrives once
+      // every MMA issued before it has completed
+      umma_commit(&drain_bar);
       const unsigned long long dl = mc_globaltimer() + kTimeoutNs;
-      while (!mc_mbar_test_sleep(&acc_full, n & 1, 20000u))
+      while (!mc_mbar_test_sleep(&drain_bar, 0, 20000u))
         if (mc_globaltimer() > dl) break;
     }
     __syncwarp();
@@ -394,7 +431,6 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const GemmParams P)
                  "r"(C::TMEM_COLS)
                  : "memory");
   }
-  (void)t_start;
 }
 
 // ---- host side ---------------------------------------------------------------
@@ -417,7 +453,7 @@ int make_a_map(CUtensorMap* map, const uint16_t* a, int rows, int K) {
   if (!enc) return mc_fail(MC_ECUDA, "cuTensorMapEncodeTiled unavailable");
   const cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)rows};
   const cuuint64_t strides[1] = {(cuuint64_t)K * 2};
-  const cuuint32_t box[2] = {BK, BM};
+  const cuuint32_t box[2] = {BK, BOX_ROWS};
   const cuuint32_t estr[2] = {1, 1};
   CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<uint16_t*>(a), dims,
                    strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
@@ -453,7 +489,7 @@ int check_grouped(const uint16_t* a, int rows, const mc_qweights* w, int n_exper
              "%s: stacked rows %d not a multiple of n_experts %d", what, w->out_features,
              n_experts);
   const int N = w->out_features / n_experts;
-  MC_REQUIRE(N % BN == 0, "%s: expert width %d must be a multiple of %d", what, N, BN);
+  MC_REQUIRE(N % BF == 0, "%s: expert width %d must be a multiple of %d", what, N, BF);
   MC_REQUIRE(w->in_features % BK == 0, "%s: K %d must be a multiple of %d", what, w->in_features,
              BK);
   MC_REQUIRE(rows >= 1, "%s: rows %d", what, rows);

@@ -509,6 +509,8 @@ extern "C" int mc_moe_decode_layer(mc_ctx* ctx, const uint16_t* h, const uint16_
   MC_REQUIRE(I % 64 == 0 && I <= 2048 && 4 * I <= 4 * 2048 && down->in_features == I &&
                  down->out_features == n_experts * H,
              "moe_decode_layer: expert shapes (I=%d)", I);
+  // a down row's scales (I/64 bf16) are one bulk copy: 16-byte size and start
+  MC_REQUIRE(I % 512 == 0, "moe_decode_layer: expert width %d must be a multiple of 512", I);
   MC_REQUIRE(ws_words >= mc_moe_decode_workspace_words(I),
              "moe_decode_layer: workspace of %zu words < %zu", ws_words,
              mc_moe_decode_workspace_words(I));

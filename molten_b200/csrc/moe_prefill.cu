@@ -234,6 +234,9 @@ extern "C" int mc_moe_combine_rows(mc_ctx* ctx, const uint16_t* ed, const uint32
 // u32[E], ids_sorted/slotpos u32[4m], tiles uint4[max_tiles], n_tiles +
 // status u32, gx bf16[4m][H], act bf16[4m][I], ed bf16[4m][H].
 namespace {
+// token rows per grouped-GEMM chunk (the tcgen05 MMA's N is at most 256)
+constexpr int kPrefillChunk = 256;
+
 struct PrefillWs {
   size_t ids, gw, counts, offsets, ids_sorted, slotpos, tiles, ctl, gx, act, ed, total;
   int max_tiles;
@@ -242,7 +245,7 @@ PrefillWs prefill_layout(int m, int E, int H, int I) {
   auto al = [](size_t v) { return (v + 255) & ~size_t(255); };
   const size_t S = (size_t)m * 4;
   PrefillWs w;
-  w.max_tiles = (int)((S + 127) / 128 + E);
+  w.max_tiles = (int)((S + kPrefillChunk - 1) / kPrefillChunk + E);
   size_t o = 0;
   w.ids = o; o = al(o + S * 4);
   w.gw = o; o = al(o + S * 2);
@@ -291,7 +294,7 @@ extern "C" int mc_moe_prefill(mc_ctx* ctx, const uint16_t* x, const float* logit
   if ((rc = mc_moe_route_batch(ctx, logits, m, n_experts, route_mode, expert_bias, 1e-6f,
                                U32(w.ids), B16(w.gw))))
     return rc;
-  if ((rc = mc_moe_sort_map(ctx, U32(w.ids), m, n_experts, 128, U32(w.counts), U32(w.offsets),
+  if ((rc = mc_moe_sort_map(ctx, U32(w.ids), m, n_experts, kPrefillChunk, U32(w.counts), U32(w.offsets),
                             U32(w.ids_sorted), U32(w.slotpos), U32(w.tiles), U32(w.ctl),
                             w.max_tiles)))
     return rc;

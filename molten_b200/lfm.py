@@ -20,6 +20,7 @@ FIXED_HIDDEN = 2048
 FIXED_MOE_INTER = 1536
 ROUTE_SOFTMAX_RENORM = _lib.ROUTE_SOFTMAX_RENORM
 ROUTE_SIGMOID_BIAS = _lib.ROUTE_SIGMOID_BIAS
+PREFILL_CHUNK = 256  # token rows per grouped-GEMM chunk (mc_moe_prefill's sort_map bm)
 
 
 def ensure(cond: bool, msg: str) -> None:
@@ -396,7 +397,7 @@ def prefill_workspace_view(workspace: torch.Tensor, m: int, n_experts: int = 64,
     S = 4 * m
     al = lambda v: (v + 255) & ~255
     offs, o = {}, 0
-    max_tiles = (S + 127) // 128 + n_experts
+    max_tiles = (S + PREFILL_CHUNK - 1) // PREFILL_CHUNK + n_experts
     for name, nbytes in (("ids", S * 4), ("gw", S * 2), ("counts", n_experts * 4),
                          ("offsets", n_experts * 4), ("ids_sorted", S * 4), ("slotpos", S * 4),
                          ("tiles", max_tiles * 16), ("ctl", 8), ("gx", S * hidden * 2),

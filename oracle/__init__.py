@@ -151,7 +151,7 @@ def router_addnorm_route(h, b, norm_w, w, w_dtype, ebias, mode, eps=1e-5, route_
     return hout, normed, logits, ids, wts
 
 
-def gemv_gather_act(gate, up, x, ids):
+def gemv_gather_act(gate, up, x, ids, n_experts=64):
     """gate/up: (codes, scales, biases) stacked [E*I, H]; x [B, H]; ids [B, 4]."""
     gc, gs, gb = gate
     uc, us, ub = up
@@ -159,8 +159,7 @@ def gemv_gather_act(gate, up, x, ids):
     x = np.ascontiguousarray(x.reshape(-1, H))
     B = x.shape[0]
     ids = np.ascontiguousarray(ids.reshape(B, 4), dtype=np.uint32)
-    E = 64
-    I = gc.shape[0] // E
+    I = gc.shape[0] // n_experts
     act = np.zeros((B, 4, I), np.uint16)
     lib().or_gemv_gather_act(_ptr(gc), _ptr(gs), _ptr(gb), _ptr(uc), _ptr(us), _ptr(ub), I, H,
                              _ptr(x), _ptr(ids), B, _ptr(act))

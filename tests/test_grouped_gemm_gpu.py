@@ -43,17 +43,17 @@ def prefill_case(seed, m, E, H, I, hot=None):
     return x, logits, gate, up, down
 
 
-def run_gpu_chain(ctx, x, logits, gate, up, down, E):
+def run_gpu_chain(ctx, x, logits, gate, up, down, E, bm=128):
     m, H = x.shape
     I = gate[0].shape[0] // E
     S = 4 * m
     ids, gw = zeros_u32(m, 4), empty_bf16(m, 4)
     lfm.moe_route_batch(ctx, dev_f32(logits), None, ids, gw, m)
-    max_tiles = (S + 127) // 128 + E
+    max_tiles = (S + bm - 1) // bm + E
     counts, offsets = zeros_u32(E), zeros_u32(E)
     ids_sorted, slotpos = zeros_u32(S), zeros_u32(S)
     tiles, n_tiles = zeros_u32(max_tiles, 4), zeros_u32(1)
-    lfm.moe_sort_map(ctx, ids, counts, offsets, ids_sorted, slotpos, tiles, n_tiles, m, 128)
+    lfm.moe_sort_map(ctx, ids, counts, offsets, ids_sorted, slotpos, tiles, n_tiles, m, bm)
     gx = empty_bf16(S, H)
     lfm.gather_rows_bf16(ctx, dev_bf16(x), ids_sorted, gx)
     act = torch.zeros((S, I), dtype=torch.bfloat16, device="cuda")
@@ -71,12 +71,17 @@ def run_gpu_chain(ctx, x, logits, gate, up, down, E):
                 out=host_bits(out), gx=gx)
 
 
-@pytest.mark.parametrize("seed,m,E,I,hot", [(1, 96, 8, 256, None), (2, 300, 8, 384, None),
-                                            (3, 64, 64, 1536, 8)])
-def test_grouped_ffn_matches_oracle(cuda_ctx, seed, m, E, I, hot):
+@pytest.mark.parametrize("seed,m,E,I,hot,bm", [(1, 96, 8, 256, None, 128),
+                                               (2, 300, 8, 384, None, 256),
+                                               (3, 64, 64, 1536, 8, 256),
+                                               (4, 10, 8, 256, None, 256),
+                                               (5, 200, 4, 128, None, 64)])
+def test_grouped_ffn_matches_oracle(cuda_ctx, seed, m, E, I, hot, bm):
+    """bm 256: chunks up to the MMA's largest N; m=10: fewer rows (40) than one
+    64-row token box; bm 64: many short chunks per expert."""
     H = 2048
     x, logits, gate, up, down = prefill_case(seed, m, E, H, I, hot)
-    got = run_gpu_chain(cuda_ctx, x, logits, gate, up, down, E)
+    got = run_gpu_chain(cuda_ctx, x, logits, gate, up, down, E, bm)
     want = oracle.moe_prefill(x, logits, gate, up, down, n_experts=E)
     assert np.array_equal(got["ids"], want["ids"])
     assert_bits_equal(got["gw"], want["gw"], "gw")
@@ -144,3 +149,25 @@ def test_moe_prefill_entry_point(cuda_ctx):
     rms = np.sqrt(np.mean(want_o ** 2))
     bad = np.abs(got_o - want_o) > RTOL * terms.sum(axis=1) + ATOL_RMS * rms
     assert not bad.any(), f"out: {bad.sum()} outside tolerance"
+
+
+def test_grouped_gemm_flags_malformed_tile(cuda_ctx):
+    """A tile past the last row or taller than 256 rows is not computed into C:
+    status bit 1 is set and the good tile's rows are still right."""
+    E, H, N, rows = 2, 2048, 128, 100
+    g = synth.rng(6)
+    a = synth.activations_np(g, rows, H)
+    w = synth.quant_weights_np(g, E * N, H)
+    from tests.gpu_util import dev_u32
+    tiles = np.zeros((4, 4), np.uint32)
+    tiles[0] = [0, rows, 1, 0]
+    tiles[1] = [0, 400, 0, 0]  # m_end past rows and taller than 256
+    c = torch.zeros((rows, N), dtype=torch.bfloat16, device="cuda")
+    st = zeros_u32(1)
+    lfm.gemm_q4_grouped(cuda_ctx, dev_bf16(a), dev_qw(*w), c, dev_u32(tiles),
+                        dev_u32(np.array([2], np.uint32)), E, st)
+    torch.cuda.synchronize()
+    assert int(host_u32(st)[0]) == 2
+    want = oracle.gemm_q4_grouped(a, w, np.array([0, rows], np.uint32),
+                                  np.array([0, 0], np.uint32), E)
+    assert_close_bf16(host_bits(c), want, "good tile beside a malformed one", min_equal=0.8)
