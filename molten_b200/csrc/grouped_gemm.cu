@@ -27,7 +27,8 @@
 //               128-byte-swizzled layout (w = bf16(fma(s, q, b)), MLX's
 //               dequantize): gate/up: warps 2-5 gate, 6-9 up; down: warps
 //               2-5 even K steps, 6-9 odd ones. Then the epilogue from TMEM.
-// Stage s: full[s] (TMA tx + dequant arrivals), empty[s] (tcgen05.commit).
+// Two rings: token rows (bfull: TMA tx, bempty: tcgen05.commit) and weight
+// tiles (afull: dequant arrivals, aempty: tcgen05.commit).
 // Every wait is bounded by a %globaltimer deadline; on timeout the kernel
 // records status bit 1, stops issuing and still drains what it issued before
 // freeing TMEM.
@@ -51,16 +52,21 @@ constexpr unsigned long long kTimeoutNs = 1000000000ull;  // 1 s per wait
 template <bool GU>
 struct Cfg {
   static constexpr int NMAT = GU ? 2 : 1;
-  static constexpr int B_BYTES = MAXN * BK * 2;  // 32 KB of token rows
-  static constexpr int A_BYTES = BF * BK * 2;    // 16 KB per weight matrix
-  static constexpr int STAGE_BYTES = B_BYTES + NMAT * A_BYTES;
-  static constexpr int STAGES = GU ? 3 : 4;
-  static constexpr int SMEM = STAGES * STAGE_BYTES + 1024;
+  static constexpr int B_BYTES = MAXN * BK * 2;        // 32 KB of token rows per K step
+  static constexpr int A_BYTES = BF * BK * 2;          // 16 KB per weight matrix per K step
+  static constexpr int A_STAGE = NMAT * A_BYTES;
+  // Token rows come by TMA from L2/HBM (microseconds away): a deep ring. The
+  // weight tiles are produced on chip by the dequant warps: a short one.
+  static constexpr int BSTAGES = GU ? 3 : 4;
+  static constexpr int ASTAGES = GU ? 3 : 4;
+  static constexpr int SMEM = BSTAGES * B_BYTES + ASTAGES * A_STAGE + 1024;
   static constexpr int TMEM_COLS = 512;
   static constexpr int NBUF = GU ? 1 : 2;  // accumulator buffers (gate+up fill TMEM)
   // dequant arrivals per stage: gate/up both groups, down one group
   static constexpr uint32_t DEQ_ARRIVALS = GU ? 256u : 128u;
 };
+static_assert(Cfg<true>::SMEM + 512 <= 232448 && Cfg<false>::SMEM + 512 <= 232448,
+              "shared memory budget");
 
 struct GemmParams {
   mc_qweights w0, w1;
@@ -152,14 +158,43 @@ __device__ __forceinline__ void tmem_wait_ld() {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
-// Bounded mbarrier wait that also gives up when another role aborted.
-__device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t parity, volatile uint32_t* abort_f,
-                                         unsigned long long deadline) {
+// Bounded mbarrier wait that also gives up when another role aborted. The
+// clock is read only once the barrier was found incomplete.
+__device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t parity, volatile uint32_t* abort_f) {
+  if (mc_mbar_test_sleep(bar, parity, 20000u)) return true;
+  const unsigned long long deadline = mc_globaltimer() + kTimeoutNs;
   while (!mc_mbar_test_sleep(bar, parity, 20000u)) {
     if (*abort_f) return false;
     if (mc_globaltimer() > deadline) return false;
   }
   return true;
+}
+
+// ---- epilogue arithmetic ------------------------------------------------------
+// Single-value float->bf16 conversions and MUFU exp/rcp each issue at about
+// 16 per clock per SM, so the epilogue rounds with integer ops (round to
+// nearest even on the bit pattern; inputs are finite), takes one MUFU per
+// element for the sigmoid, and converts the outputs two at a time.
+__device__ __forceinline__ float bf16_round(float x) {
+  uint32_t u = __float_as_uint(x);
+  u += 0x7fffu + ((u >> 16) & 1u);
+  return __uint_as_float(u & 0xffff0000u);
+}
+__device__ __forceinline__ float tanh_approx(float x) {
+  float y;
+  asm("tanh.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+// silu(g) = g * sigmoid(g), sigmoid(g) = 0.5 + 0.5 * tanh(g / 2): the prefill
+// activations are compared within the bf16 tolerance (the tensor cores'
+// summation order is unspecified anyway), so the decode path's bit-exact
+// exponential is not needed here.
+__device__ __forceinline__ float silu_fast(float g) {
+  return __fmul_rn(g, __fmaf_rn(0.5f, tanh_approx(__fmul_rn(0.5f, g)), 0.5f));
+}
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+  const __nv_bfloat162 t = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t*>(&t);
 }
 
 // ---- dequantisation of one 64-wide K slice of one weight row ----------------
@@ -212,7 +247,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const GemmParams P) {
   using C = Cfg<GU>;
   extern __shared__ uint8_t smem_raw[];
-  __shared__ __align__(8) uint64_t full[C::STAGES], empty[C::STAGES];
+  __shared__ __align__(8) uint64_t bfull[C::BSTAGES], bempty[C::BSTAGES];
+  __shared__ __align__(8) uint64_t afull[C::ASTAGES], aempty[C::ASTAGES];
   __shared__ __align__(8) uint64_t acc_full[2], acc_empty[2], drain_bar;
   __shared__ uint32_t tmem_base_s;
   __shared__ volatile uint32_t abort_s;
@@ -222,9 +258,13 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const GemmParams P)
   const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
 
   if (t == 0) {
-    for (int s = 0; s < C::STAGES; ++s) {
-      mc_mbar_init(&full[s], 1 + C::DEQ_ARRIVALS);
-      mc_mbar_init(&empty[s], 1);
+    for (int s = 0; s < C::BSTAGES; ++s) {
+      mc_mbar_init(&bfull[s], 1);
+      mc_mbar_init(&bempty[s], 1);
+    }
+    for (int s = 0; s < C::ASTAGES; ++s) {
+      mc_mbar_init(&afull[s], C::DEQ_ARRIVALS);
+      mc_mbar_init(&aempty[s], 1);
     }
     for (int b = 0; b < 2; ++b) {
       mc_mbar_init(&acc_full[b], 1);
@@ -263,16 +303,16 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const GemmParams P)
         const int rows_left = P.rows - (int)w.m0;
         if (nbox * BOX_ROWS > rows_left + BOX_ROWS - 1) nbox = (rows_left + BOX_ROWS - 1) / BOX_ROWS;
         for (int kk = 0; kk < ksteps; ++kk, ++it) {
-          const int s = it % C::STAGES;
-          const uint32_t ph = (it / C::STAGES) & 1;
-          if (!wait_bar(&empty[s], ph ^ 1, &abort_s, mc_globaltimer() + kTimeoutNs)) {
+          const int s = it % C::BSTAGES;
+          const uint32_t ph = (it / C::BSTAGES) & 1;
+          if (!wait_bar(&bempty[s], ph ^ 1, &abort_s)) {
             abort_s = 1;
             break;
           }
-          mc_mbar_expect_tx(&full[s], (uint32_t)(nbox * BOX_BYTES));
+          mc_mbar_expect_tx(&bfull[s], (uint32_t)(nbox * BOX_BYTES));
           for (int bx = 0; bx < nbox; ++bx)
-            tma_load_2d(smem + s * C::STAGE_BYTES + bx * BOX_BYTES, &tmA, kk * BK,
-                        (int)w.m0 + bx * BOX_ROWS, &full[s]);
+            tma_load_2d(smem + s * C::B_BYTES + bx * BOX_BYTES, &tmA, kk * BK,
+                        (int)w.m0 + bx * BOX_ROWS, &bfull[s]);
         }
       }
       if (abort_s) {
@@ -290,7 +330,7 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const GemmParams P)
         const uint32_t idesc = idesc_for(w.n);
         const int buf = (int)(j % C::NBUF);
         const uint32_t use = j / C::NBUF;
-        if (!wait_bar(&acc_empty[buf], (use & 1) ^ 1, &abort_s, mc_globaltimer() + kTimeoutNs)) {
+        if (!wait_bar(&acc_empty[buf], (use & 1) ^ 1, &abort_s)) {
           abort_s = 1;
           break;
         }
@@ -298,25 +338,26 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const GemmParams P)
         const uint32_t d0 = tmem + (uint32_t)(buf * 256);
         bool ok = true;
         for (int kk = 0; kk < ksteps; ++kk, ++it) {
-          const int s = it % C::STAGES;
-          const uint32_t ph = (it / C::STAGES) & 1;
-          if (!wait_bar(&full[s], ph, &abort_s, mc_globaltimer() + kTimeoutNs)) {
+          const int sb = it % C::BSTAGES, sa = it % C::ASTAGES;
+          if (!wait_bar(&bfull[sb], (it / C::BSTAGES) & 1, &abort_s) ||
+              !wait_bar(&afull[sa], (it / C::ASTAGES) & 1, &abort_s)) {
             abort_s = 1;
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t base = mc_smem_u32(smem + s * C::STAGE_BYTES);
-          const uint64_t bdesc = sw128_desc(base);
-          const uint64_t adesc0 = sw128_desc(base + C::B_BYTES);
-          const uint64_t adesc1 = sw128_desc(base + C::B_BYTES + C::A_BYTES);
+          const uint64_t bdesc = sw128_desc(mc_smem_u32(smem + sb * C::B_BYTES));
+          const uint32_t abase = mc_smem_u32(smem + C::BSTAGES * C::B_BYTES + sa * C::A_STAGE);
+          const uint64_t adesc0 = sw128_desc(abase);
+          const uint64_t adesc1 = sw128_desc(abase + C::A_BYTES);
 #pragma unroll
           for (int k16 = 0; k16 < BK / 16; ++k16) {
             const uint32_t acc = (kk > 0 || k16 > 0) ? 1u : 0u;
             umma_bf16(d0, adesc0 + 2 * k16, bdesc + 2 * k16, idesc, acc);
             if (GU) umma_bf16(d0 + 256, adesc1 + 2 * k16, bdesc + 2 * k16, idesc, acc);
           }
-          umma_commit(&empty[s]);  // stage free once these MMAs have read it
+          umma_commit(&bempty[sb]);  // both stages free once these MMAs have read them
+          umma_commit(&aempty[sa]);
         }
         if (!ok) break;
         umma_commit(&acc_full[buf]);
@@ -332,80 +373,107 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const GemmParams P)
     const uint32_t* wcodes = (GU && grp) ? P.w1.codes : P.w0.codes;
     const uint16_t* wscales = (GU && grp) ? P.w1.scales : P.w0.scales;
     const uint16_t* wbiases = (GU && grp) ? P.w1.biases : P.w0.biases;
-    uint32_t it = 0, j = 0;
-    for (int item = blockIdx.x; item < total && !abort_s; item += gridDim.x, ++j) {
+    // K steps of this thread: all (gate/up) or every other one (down)
+    const int step = GU ? 1 : 2;
+    // two K slices in flight per thread: slot 0 holds the slice being
+    // dequantised while slot 1's loads are outstanding, then they swap; the
+    // next item's first two slices are requested before this item's epilogue
+    // (scale and bias stay raw bf16 until use: converting them at load time
+    // would make the thread wait for the load right there)
+    uint4 ca0 = make_uint4(0, 0, 0, 0), cb0 = ca0, ca1 = ca0, cb1 = ca0;
+    uint16_t sc0 = 0, bi0 = 0, sc1 = 0, bi1 = 0;
+    const uint8_t* crow = nullptr;
+    const uint16_t *srow = nullptr, *brow = nullptr;
+    auto load_slice = [&](int kk, uint4& ca, uint4& cb, uint16_t& sc, uint16_t& bi) {
+      if (kk < ksteps) {
+        ca = __ldg(reinterpret_cast<const uint4*>(crow + kk * 32));
+        cb = __ldg(reinterpret_cast<const uint4*>(crow + kk * 32) + 1);
+        sc = __ldg(srow + kk);
+        bi = __ldg(brow + kk);
+      }
+    };
+    // point at item `item`'s weight row and request its first two slices
+    auto start_item = [&](int item, uint32_t it_base) -> Item {
       const Item w = item_info(P, item, nblk);
-      if (!w.ok && dt == 0 && P.status) atomicOr(P.status, 2u);
       const size_t wrow = (size_t)w.e * P.N + (size_t)w.nb * BF + d;
-      const uint8_t* crow = reinterpret_cast<const uint8_t*>(wcodes) + wrow * (P.K / 2);
-      const uint16_t* srow = wscales + wrow * (P.K / 64);
-      const uint16_t* brow = wbiases + wrow * (P.K / 64);
-      // K steps of this thread: all (gate/up) or every other one (down)
-      const int step = GU ? 1 : 2;
+      crow = reinterpret_cast<const uint8_t*>(wcodes) + wrow * (P.K / 2);
+      srow = wscales + wrow * (P.K / 64);
+      brow = wbiases + wrow * (P.K / 64);
+      const int k0 = GU ? 0 : (int)((grp - it_base) & 1u);
+      load_slice(k0, ca0, cb0, sc0, bi0);
+      load_slice(k0 + step, ca1, cb1, sc1, bi1);
+      return w;
+    };
+    uint32_t it = 0, j = 0;
+    Item w = start_item(blockIdx.x < total ? blockIdx.x : 0, 0);
+    for (int item = blockIdx.x; item < total && !abort_s; item += gridDim.x, ++j) {
+      if (!w.ok && dt == 0 && P.status) atomicOr(P.status, 2u);
       const int k0 = GU ? 0 : (int)((grp - it) & 1u);
       bool ok = true;
-      uint4 na = make_uint4(0, 0, 0, 0), nb = na;
-      float nsc = 0.0f, nbi = 0.0f;
-      if (k0 < ksteps) {
-        na = __ldg(reinterpret_cast<const uint4*>(crow + k0 * 32));
-        nb = __ldg(reinterpret_cast<const uint4*>(crow + k0 * 32) + 1);
-        nsc = mc_bf16_to_f32(__ldg(srow + k0));
-        nbi = mc_bf16_to_f32(__ldg(brow + k0));
-      }
-      for (int kk = k0; kk < ksteps; kk += step) {
-        const uint4 ca = na, cb = nb;
-        const float sc = nsc, bi = nbi;
-        const int kn = kk + step;
-        if (kn < ksteps) {  // prefetch this thread's next K slice
-          na = __ldg(reinterpret_cast<const uint4*>(crow + kn * 32));
-          nb = __ldg(reinterpret_cast<const uint4*>(crow + kn * 32) + 1);
-          nsc = mc_bf16_to_f32(__ldg(srow + kn));
-          nbi = mc_bf16_to_f32(__ldg(brow + kn));
-        }
+      auto do_slice = [&](int kk, uint4& ca, uint4& cb, uint16_t& sc, uint16_t& bi) -> bool {
+        const uint4 xa = ca, xb = cb;
+        const uint16_t xs = sc, xbias = bi;
+        load_slice(kk + 2 * step, ca, cb, sc, bi);  // refill this slot two slices ahead
         const uint32_t itk = it + (uint32_t)kk;
-        const int s = itk % C::STAGES;
-        const uint32_t ph = (itk / C::STAGES) & 1;
-        if (!wait_bar(&empty[s], ph ^ 1, &abort_s, mc_globaltimer() + kTimeoutNs)) {
-          abort_s = 1;
+        const int s = itk % C::ASTAGES;
+        const uint32_t ph = (itk / C::ASTAGES) & 1;
+        if (!wait_bar(&aempty[s], ph ^ 1, &abort_s)) return false;
+        uint8_t* at = smem + C::BSTAGES * C::B_BYTES + s * C::A_STAGE + (GU ? grp * C::A_BYTES : 0);
+        dequant_row64(xa, xb, mc_bf16_to_f32(xs), mc_bf16_to_f32(xbias), at + d * 128, d & 7);
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        mc_mbar_arrive(&afull[s]);
+        return true;
+      };
+      for (int kk = k0; kk < ksteps; kk += 2 * step) {
+        if (!do_slice(kk, ca0, cb0, sc0, bi0)) {
           ok = false;
           break;
         }
-        uint8_t* at = smem + s * C::STAGE_BYTES + C::B_BYTES + (GU ? grp * C::A_BYTES : 0);
-        dequant_row64(ca, cb, sc, bi, at + d * 128, d & 7);
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-        mc_mbar_arrive(&full[s]);
+        if (kk + step < ksteps && !do_slice(kk + step, ca1, cb1, sc1, bi1)) {
+          ok = false;
+          break;
+        }
       }
+      if (!ok) abort_s = 1;
       it += (uint32_t)ksteps;
       if (!ok) break;
+      const Item cur = w;
+      if (item + (int)gridDim.x < total) w = start_item(item + gridDim.x, it);
       // ---- epilogue: TMEM [feature][token] -> bf16 out[token][feature]
       const int buf = (int)(j % C::NBUF);
       const uint32_t use = j / C::NBUF;
-      if (!wait_bar(&acc_full[buf], use & 1, &abort_s, mc_globaltimer() + kTimeoutNs)) {
+      if (!wait_bar(&acc_full[buf], use & 1, &abort_s)) {
         abort_s = 1;
         break;
       }
       tc_fence_after();
       const int f = 32 * q + lane;  // feature row of D this thread reads
-      const int n16 = w.n >> 4, split = (n16 + 1) >> 1;
+      const int n16 = cur.n >> 4, split = (n16 + 1) >> 1;
       const int c_lo = grp ? split : 0, c_hi = grp ? n16 : split;
       const uint32_t lane_base = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(buf * 256);
-      uint16_t* ocol = P.out + (size_t)w.nb * BF + f;
+      uint16_t* ocol = P.out + (size_t)cur.nb * BF + f;
 #pragma unroll 1
       for (int c = c_lo; c < c_hi; ++c) {
         uint32_t g[16], u[16];
         tmem_ld16(lane_base + 16 * c, g);
         if (GU) tmem_ld16(lane_base + 256 + 16 * c, u);
         tmem_wait_ld();
-        const uint32_t r0 = w.m0 + 16u * (uint32_t)c;
+        const uint32_t r0 = cur.m0 + 16u * (uint32_t)c;
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const float gv = mc_round_bf16(__uint_as_float(g[i]));
-          float o = gv;
+        for (int i = 0; i < 16; i += 2) {
+          float o0, o1;
           if (GU) {
-            const float uv = mc_round_bf16(__uint_as_float(u[i]));
-            o = __fmul_rn(mc_round_bf16(mc_silu(gv)), uv);
+            const float g0 = bf16_round(__uint_as_float(g[i])), g1 = bf16_round(__uint_as_float(g[i + 1]));
+            const float u0 = bf16_round(__uint_as_float(u[i])), u1 = bf16_round(__uint_as_float(u[i + 1]));
+            o0 = __fmul_rn(bf16_round(silu_fast(g0)), u0);
+            o1 = __fmul_rn(bf16_round(silu_fast(g1)), u1);
+          } else {
+            o0 = __uint_as_float(g[i]);
+            o1 = __uint_as_float(g[i + 1]);
           }
-          if (w.ok && r0 + i < w.mend) ocol[(size_t)(r0 + i) * P.N] = mc_f32_to_bf16(o);
+          const uint32_t pk = pack_bf16x2(o0, o1);
+          if (cur.ok && r0 + i < cur.mend) ocol[(size_t)(r0 + i) * P.N] = (uint16_t)pk;
+          if (cur.ok && r0 + i + 1 < cur.mend) ocol[(size_t)(r0 + i + 1) * P.N] = (uint16_t)(pk >> 16);
         }
       }
       tc_fence_before();

@@ -31,6 +31,18 @@ def assert_close_bf16(got_bits, want_bits, what, min_equal=0.5):
     assert eq >= min_equal, f"{what}: only {eq:.2%} bit-identical"
 
 
+def assert_out_close(got_bits, want, what="out"):
+    """out[t] is a sum of four bf16-rounded terms that can cancel, so the
+    relative part of the tolerance is taken on sum_r |w_r * ed_r|, not on |out|."""
+    f = lambda b: synth.bf16_bits_to_f32(np.asarray(b)).astype(np.float64)
+    m = want["out"].shape[0]
+    terms = np.abs(f(want["gw"]).reshape(m, 4, 1) * f(want["ed"])[want["slotpos"].reshape(m, 4)])
+    got_o, want_o = f(got_bits), f(want["out"])
+    rms = np.sqrt(np.mean(want_o ** 2))
+    bad = np.abs(got_o - want_o) > RTOL * terms.sum(axis=1) + ATOL_RMS * rms
+    assert not bad.any(), f"{what}: {bad.sum()} of {bad.size} outside tolerance"
+
+
 def prefill_case(seed, m, E, H, I, hot=None):
     g = synth.rng(seed)
     x = synth.activations_np(g, m, H)
@@ -92,7 +104,9 @@ def test_grouped_ffn_matches_oracle(cuda_ctx, seed, m, E, I, hot, bm):
     counts, offsets, _, _ = oracle.moe_sort(want["ids"], E)
     ed_ref = oracle.gemm_q4_grouped(got["act"], down, counts, offsets, E)
     assert_close_bf16(got["ed"], ed_ref, "ed (teacher-forced act)", min_equal=0.8)
-    assert_close_bf16(got["out"], want["out"], "out")
+    assert_bits_equal(got["out"], oracle.moe_combine(got["ed"], got["slotpos"], got["gw"], m, H),
+                      "combine (teacher-forced ed)")
+    assert_out_close(got["out"], want)
 
 
 def test_grouped_gemm_single_matrix_exactness_structure(cuda_ctx):
@@ -140,15 +154,7 @@ def test_moe_prefill_entry_point(cuda_ctx):
     gw = host_bits(v["gw"])
     slot = host_u32(v["slotpos"])
     assert_bits_equal(host_bits(out), oracle.moe_combine(ed, slot, gw, m, H), "combine")
-    # end to end: out is a sum of four bf16-rounded terms that can cancel, so the
-    # relative part of the tolerance is taken on sum_r |w_r * ed_r|, not on |out|
-    f = lambda b: synth.bf16_bits_to_f32(np.asarray(b)).astype(np.float64)
-    terms = np.abs(f(want["gw"]).reshape(m, 4, 1) *
-                   f(want["ed"])[want["slotpos"].reshape(m, 4)])
-    got_o, want_o = f(host_bits(out)), f(want["out"])
-    rms = np.sqrt(np.mean(want_o ** 2))
-    bad = np.abs(got_o - want_o) > RTOL * terms.sum(axis=1) + ATOL_RMS * rms
-    assert not bad.any(), f"out: {bad.sum()} outside tolerance"
+    assert_out_close(host_bits(out), want)
 
 
 def test_grouped_gemm_flags_malformed_tile(cuda_ctx):
