@@ -206,8 +206,10 @@ int mc_moe_route_batch(mc_ctx* ctx, const float* logits, int m, int n_experts,
  * in two launches: counts[E], offsets[E] (exclusive scan), the stable
  * token-major, rank-major scatter ids_sorted[m*4] / slotpos[m*4], and the
  * row-tile list tiles[max_tiles] of uint4 {m0, m_end, expert, 0} with its
- * length in *n_tiles (device u32). bm is the tile height (256 for the
- * grouped GEMMs, at most 256 there); max_tiles >= ceil(m*4/bm) + E. */
+ * length in *n_tiles (device u32): every full bm-row tile first, in expert
+ * order, then the partial tiles by decreasing height (ties: lower expert).
+ * bm is the tile height (256 for the grouped GEMMs, at most 256 there);
+ * max_tiles >= ceil(m*4/bm) + E. */
 int mc_moe_sort_map(mc_ctx* ctx, const uint32_t* ids, int m, int n_experts, int bm,
                     uint32_t* counts, uint32_t* offsets, uint32_t* ids_sorted,
                     uint32_t* slotpos, uint32_t* tiles, uint32_t* n_tiles, int max_tiles);
@@ -224,7 +226,7 @@ int mc_gather_rows_bf16(mc_ctx* ctx, const uint16_t* table, const uint32_t* ids,
  * mc_moe_sort_map with bm <= 256 (a tile taller than 256 rows is malformed).
  * tcgen05 tensor-core kernel (fp32 accumulation). status: nullable u32 word,
  * bit 0 = a bounded wait gave up, bit 1 = a malformed tile was skipped.
- * N % 128 == 0, K % 64 == 0. */
+ * N % 128 == 0, K % 128 == 0. */
 int mc_gemm_q4_grouped(mc_ctx* ctx, const uint16_t* a, int rows, const mc_qweights* w,
                        int n_experts, uint16_t* c, const uint32_t* tiles,
                        const uint32_t* n_tiles, int max_tiles, uint32_t* status);

@@ -14,19 +14,26 @@
 // is the M = 128 operand and the chunk's token rows are the N operand, with
 // N = the chunk height rounded up to 16 (at most 256), so one dequantised
 // weight tile serves up to 256 tokens and small experts do not pay for
-// padding rows. D (TMEM) is [128 features][N tokens] fp32.
+// padding rows. D (TMEM) is [128 features][N tokens] fp32: gate/up 2 x 256
+// columns (all of TMEM, one buffer), down 256 (two buffers, so the next
+// item's MMAs overlap this item's epilogue).
 //
-// Persistent kernel, one CTA per SM, work items = (row chunk, 128-feature
-// block) in chunk-major order so neighbouring CTAs share a chunk's token rows
-// in L2. Warp roles (320 threads):
-//   warp 0      TMA: 64-row x 64-K bf16 boxes of the chunk's token rows,
-//               128-byte swizzle, into the stage ring
+// A TMA copy takes about the same time whatever its size, so each K step's
+// token rows come as ONE box of 64, 128 or 256 rows (the smallest that covers
+// the chunk), several stages in flight.
+//
+// Persistent kernel, one CTA per SM. Work items = (row chunk, 128-feature
+// block), chunk-major, dealt to CTAs in snake order; with the tile list from
+// mc_moe_sort_map (full chunks first, then partial ones by decreasing
+// height) every CTA gets a similar share. Warp roles (320 threads):
+//   warp 0      TMA of the token rows (128-byte swizzle) into the token ring
 //   warp 1      TMEM allocation (512 columns); lane 0 issues tcgen05.mma
 //               (M=128, N=chunk, K=16, bf16 x bf16 -> fp32) and commits
 //   warps 2..9  dequantise the weight tiles straight into the UMMA K-major
 //               128-byte-swizzled layout (w = bf16(fma(s, q, b)), MLX's
-//               dequantize): gate/up: warps 2-5 gate, 6-9 up; down: warps
-//               2-5 even K steps, 6-9 odd ones. Then the epilogue from TMEM.
+//               dequantize): gate/up: warps 2-5 the gate tile, 6-9 the up
+//               tile; down: warps 2-5 the first 32 K of every row, 6-9 the
+//               second. Then the epilogue from TMEM, half the columns each.
 // Two rings: token rows (bfull: TMA tx, bempty: tcgen05.commit) and weight
 // tiles (afull: dequant arrivals, aempty: tcgen05.commit).
 // Every wait is bounded by a %globaltimer deadline; on timeout the kernel
@@ -40,30 +47,27 @@
 
 namespace {
 
-constexpr int BF = 128;    // weight features per item (the MMA's M)
+constexpr int BF = 128;    // weight features per work item (the MMA's M)
 constexpr int BK = 64;     // K per stage
 constexpr int MAXN = 256;  // token rows per chunk (the MMA's N, rounded up to 16)
-constexpr int BOX_ROWS = 64;
-constexpr int BOX_BYTES = BOX_ROWS * BK * 2;  // 8 KB token box
 constexpr int kDeqThreads = 256;
 constexpr int kThreads = 64 + kDeqThreads;
 constexpr unsigned long long kTimeoutNs = 1000000000ull;  // 1 s per wait
 
 template <bool GU>
 struct Cfg {
-  static constexpr int NMAT = GU ? 2 : 1;
+  static constexpr int NMAT = GU ? 2 : 1;              // weight tiles per K step
   static constexpr int B_BYTES = MAXN * BK * 2;        // 32 KB of token rows per K step
-  static constexpr int A_BYTES = BF * BK * 2;          // 16 KB per weight matrix per K step
+  static constexpr int A_BYTES = BF * BK * 2;          // 16 KB per weight tile
   static constexpr int A_STAGE = NMAT * A_BYTES;
-  // Token rows come by TMA from L2/HBM (microseconds away): a deep ring. The
-  // weight tiles are produced on chip by the dequant warps: a short one.
-  static constexpr int BSTAGES = GU ? 3 : 4;
-  static constexpr int ASTAGES = GU ? 3 : 4;
+  // Ring depths measured best on B200 (deeper token rings were slower: more
+  // TMA traffic in flight delays the dequant warps' weight loads in L2).
+  static constexpr int BSTAGES = GU ? 2 : 4;
+  static constexpr int ASTAGES = GU ? 2 : 4;
   static constexpr int SMEM = BSTAGES * B_BYTES + ASTAGES * A_STAGE + 1024;
   static constexpr int TMEM_COLS = 512;
-  static constexpr int NBUF = GU ? 1 : 2;  // accumulator buffers (gate+up fill TMEM)
-  // dequant arrivals per stage: gate/up both groups, down one group
-  static constexpr uint32_t DEQ_ARRIVALS = GU ? 256u : 128u;
+  static constexpr int ACC_COLS = NMAT * MAXN;         // accumulator columns per item
+  static constexpr int NBUF = TMEM_COLS / ACC_COLS;    // gate/up: 1, down: 2
 };
 static_assert(Cfg<true>::SMEM + 512 <= 232448 && Cfg<false>::SMEM + 512 <= 232448,
               "shared memory budget");
@@ -98,6 +102,21 @@ __device__ __forceinline__ Item item_info(const GemmParams& P, int item, int nbl
   it.n = (int)((it.mend - it.m0 + 15u) & ~15u);
   return it;
 }
+
+// The i-th work item of this CTA: items are dealt in snake order (0..G-1,
+// then G-1..0, ...) so that, with the tile list sorted by decreasing height,
+// every CTA gets a similar total.
+__device__ __forceinline__ int cta_item(int i) {
+  const int G = (int)gridDim.x, b = (int)blockIdx.x;
+  return i * G + ((i & 1) ? G - 1 - b : b);
+}
+
+// Token-row box for a chunk of n rows: one TMA copy of 64, 128 or 256 rows
+// (a TMA copy costs about the same time whatever its size, so one big box per
+// stage beats several small ones).
+struct TokenMaps {
+  CUtensorMap m64, m128, m256;
+};
 
 // ---- PTX wrappers -----------------------------------------------------------
 
@@ -173,43 +192,42 @@ __device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t parity, volatil
 // ---- epilogue arithmetic ------------------------------------------------------
 // Single-value float->bf16 conversions and MUFU exp/rcp each issue at about
 // 16 per clock per SM, so the epilogue rounds with integer ops (round to
-// nearest even on the bit pattern; inputs are finite), takes one MUFU per
-// element for the sigmoid, and converts the outputs two at a time.
+// nearest even on the bit pattern; inputs are finite) and converts the
+// outputs two at a time.
 __device__ __forceinline__ float bf16_round(float x) {
   uint32_t u = __float_as_uint(x);
   u += 0x7fffu + ((u >> 16) & 1u);
   return __uint_as_float(u & 0xffff0000u);
 }
-__device__ __forceinline__ float tanh_approx(float x) {
-  float y;
-  asm("tanh.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
-  return y;
-}
-// silu(g) = g * sigmoid(g), sigmoid(g) = 0.5 + 0.5 * tanh(g / 2): the prefill
-// activations are compared within the bf16 tolerance (the tensor cores'
-// summation order is unspecified anyway), so the decode path's bit-exact
-// exponential is not needed here.
-__device__ __forceinline__ float silu_fast(float g) {
-  return __fmul_rn(g, __fmaf_rn(0.5f, tanh_approx(__fmul_rn(0.5f, g)), 0.5f));
-}
+// silu(g) = g / (1 + e^-g) with the hardware exponential and a fast divide
+// (two MUFU ops; accurate in relative terms on both tails, unlike
+// 0.5 + 0.5 tanh(g/2) for g << 0): the prefill activations are compared
+// within the bf16 tolerance (the tensor cores' summation order is unspecified
+// anyway), so the decode path's bit-exact exponential is not needed here.
+__device__ __forceinline__ float silu_fast(float g) { return __fdividef(g, 1.0f + __expf(-g)); }
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   const __nv_bfloat162 t = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<const uint32_t*>(&t);
 }
 
-// ---- dequantisation of one 64-wide K slice of one weight row ----------------
-// 8 Q4 words (64 codes, k = 16m + j in the order of the word pairs) ->
-// 64 bf16 values in natural k order, stored as 8 16-byte chunks at
-// row_base + ((c ^ swz) * 16): the UMMA K-major 128B-swizzle layout.
-// w = bf16(fma(s, q, b)) with s*q exact (MLX dequantize, quant_nax.metal:2947).
-__device__ __forceinline__ void dequant_row64(uint4 a, uint4 b, float s, float bias,
-                                              uint8_t* row_base, int swz) {
-  const uint32_t W[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
-  float v[64];
+// ---- dequantisation of Q4 words into the UMMA layout -------------------------
+// NP word pairs (16 codes each, k = 16m + j in the order of the word pairs)
+// -> 16*NP bf16 values in natural k order, stored as 16-byte chunks
+// c0 + 2m, c0 + 2m + 1 at row_base + ((c ^ swz) * 16): the UMMA K-major
+// 128B-swizzle layout. w = bf16(fma(s, q, b)) with s*q exact (MLX
+// dequantize, quant_nax.metal:2947).
+template <int NP>
+__device__ __forceinline__ void dequant_words(const uint32_t* W, float s, float bias,
+                                              uint8_t* row_base, int swz, int c0) {
   const float2 neg = make_float2(-MC_MAGIC_F, -MC_MAGIC_F);
   const float2 bb = make_float2(bias, bias);
+  float se[8];
 #pragma unroll
-  for (int m = 0; m < 4; ++m) {
+  for (int j = 0; j < 8; ++j) se[j] = __fmul_rn(s, mc_pow2_neg(j < 5 ? 4 * j : 4 * (j - 3)));
+  // lane .x of pair j is k = 16m + j, lane .y is k = 16m + 8 + j, so each word
+  // pair completes two 16-byte chunks, stored at once
+#pragma unroll
+  for (int m = 0; m < NP; ++m) {
     const uint32_t wa = W[2 * m], wb = W[2 * m + 1];
     const uint64_t Wd = ((uint64_t)wb << 32) | wa;
     const uint64_t Sd = ((uint64_t)(wb >> 12) << 32) | (wa >> 12);
@@ -218,33 +236,32 @@ __device__ __forceinline__ void dequant_row64(uint4 a, uint4 b, float s, float b
                                 Wd & 0x00000F0000000F00ull, Wd & 0x0000F0000000F000ull,
                                 Wd & 0x000F0000000F0000ull, Sd & 0x00000F0000000F00ull,
                                 Sd & 0x0000F0000000F000ull, Sd & 0x000F0000000F0000ull};
+    float2 w[8];
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
-      const int e = j < 5 ? 4 * j : 4 * (j - 3);
-      const float se = __fmul_rn(s, mc_pow2_neg(e));  // exact for |s| >= 2^-110
       const uint64_t qb = masked[j] | MAG;
       float2 q = make_float2(__uint_as_float((uint32_t)qb), __uint_as_float((uint32_t)(qb >> 32)));
-      q = __fadd2_rn(q, neg);                              // (q_k, q_{k+8}) * 2^e, exact
-      const float2 w = __ffma2_rn(q, make_float2(se, se), bb);  // s*q + b, one rounding
-      v[16 * m + j] = w.x;
-      v[16 * m + 8 + j] = w.y;
+      q = __fadd2_rn(q, neg);                               // (q_k, q_{k+8}) * 2^e, exact
+      w[j] = __ffma2_rn(q, make_float2(se[j], se[j]), bb);  // s*q + b, one rounding
     }
-  }
-#pragma unroll
-  for (int c = 0; c < 8; ++c) {
-    uint32_t p[4];
+    uint32_t lo[4], hi[4];
 #pragma unroll
     for (int h = 0; h < 4; ++h) {
-      const __nv_bfloat162 t = __floats2bfloat162_rn(v[8 * c + 2 * h], v[8 * c + 2 * h + 1]);
-      p[h] = *reinterpret_cast<const uint32_t*>(&t);
+      const __nv_bfloat162 tl = __floats2bfloat162_rn(w[2 * h].x, w[2 * h + 1].x);
+      const __nv_bfloat162 th = __floats2bfloat162_rn(w[2 * h].y, w[2 * h + 1].y);
+      lo[h] = *reinterpret_cast<const uint32_t*>(&tl);
+      hi[h] = *reinterpret_cast<const uint32_t*>(&th);
     }
-    *reinterpret_cast<uint4*>(row_base + ((c ^ swz) << 4)) = make_uint4(p[0], p[1], p[2], p[3]);
+    const int c = c0 + 2 * m;
+    *reinterpret_cast<uint4*>(row_base + ((c ^ swz) << 4)) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+    *reinterpret_cast<uint4*>(row_base + (((c + 1) ^ swz) << 4)) =
+        make_uint4(hi[0], hi[1], hi[2], hi[3]);
   }
 }
 
 template <bool GU>
 __global__ void __launch_bounds__(kThreads, 1)
-grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const GemmParams P) {
+grouped_gemm_kernel(const __grid_constant__ TokenMaps tm, const GemmParams P) {
   using C = Cfg<GU>;
   extern __shared__ uint8_t smem_raw[];
   __shared__ __align__(8) uint64_t bfull[C::BSTAGES], bempty[C::BSTAGES];
@@ -255,6 +272,7 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const GemmParams P)
 
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
+  uint8_t* a_ring = smem + C::BSTAGES * C::B_BYTES;
   const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
 
   if (t == 0) {
@@ -263,7 +281,7 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const GemmParams P)
       mc_mbar_init(&bempty[s], 1);
     }
     for (int s = 0; s < C::ASTAGES; ++s) {
-      mc_mbar_init(&afull[s], C::DEQ_ARRIVALS);
+      mc_mbar_init(&afull[s], kDeqThreads);
       mc_mbar_init(&aempty[s], 1);
     }
     for (int b = 0; b < 2; ++b) {
@@ -296,12 +314,10 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const GemmParams P)
     // ------------------------------------------------------------ TMA producer
     if (lane == 0) {
       uint32_t it = 0;
-      for (int item = blockIdx.x; item < total && !abort_s; item += gridDim.x) {
+      for (int i = 0, item = cta_item(0); item < total && !abort_s; item = cta_item(++i)) {
         const Item w = item_info(P, item, nblk);
-        int nbox = (w.n + BOX_ROWS - 1) / BOX_ROWS;
-        // boxes that start past the last row would only read fill values
-        const int rows_left = P.rows - (int)w.m0;
-        if (nbox * BOX_ROWS > rows_left + BOX_ROWS - 1) nbox = (rows_left + BOX_ROWS - 1) / BOX_ROWS;
+        const CUtensorMap* map = w.n <= 64 ? &tm.m64 : (w.n <= 128 ? &tm.m128 : &tm.m256);
+        const uint32_t bytes = (uint32_t)(w.n <= 64 ? 64 : (w.n <= 128 ? 128 : 256)) * BK * 2;
         for (int kk = 0; kk < ksteps; ++kk, ++it) {
           const int s = it % C::BSTAGES;
           const uint32_t ph = (it / C::BSTAGES) & 1;
@@ -309,10 +325,8 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const GemmParams P)
             abort_s = 1;
             break;
           }
-          mc_mbar_expect_tx(&bfull[s], (uint32_t)(nbox * BOX_BYTES));
-          for (int bx = 0; bx < nbox; ++bx)
-            tma_load_2d(smem + s * C::B_BYTES + bx * BOX_BYTES, &tmA, kk * BK,
-                        (int)w.m0 + bx * BOX_ROWS, &bfull[s]);
+          mc_mbar_expect_tx(&bfull[s], bytes);
+          tma_load_2d(smem + s * C::B_BYTES, map, kk * BK, (int)w.m0, &bfull[s]);
         }
       }
       if (abort_s) {
@@ -325,7 +339,7 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const GemmParams P)
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       uint32_t it = 0, j = 0;
-      for (int item = blockIdx.x; item < total && !abort_s; item += gridDim.x, ++j) {
+      for (int i = 0, item = cta_item(0); item < total && !abort_s; item = cta_item(++i), ++j) {
         const Item w = item_info(P, item, nblk);
         const uint32_t idesc = idesc_for(w.n);
         const int buf = (int)(j % C::NBUF);
@@ -335,7 +349,7 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const GemmParams P)
           break;
         }
         tc_fence_after();
-        const uint32_t d0 = tmem + (uint32_t)(buf * 256);
+        const uint32_t d0 = tmem + (uint32_t)(buf * C::ACC_COLS);
         bool ok = true;
         for (int kk = 0; kk < ksteps; ++kk, ++it) {
           const int sb = it % C::BSTAGES, sa = it % C::ASTAGES;
@@ -347,14 +361,14 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const GemmParams P)
           }
           tc_fence_after();
           const uint64_t bdesc = sw128_desc(mc_smem_u32(smem + sb * C::B_BYTES));
-          const uint32_t abase = mc_smem_u32(smem + C::BSTAGES * C::B_BYTES + sa * C::A_STAGE);
-          const uint64_t adesc0 = sw128_desc(abase);
-          const uint64_t adesc1 = sw128_desc(abase + C::A_BYTES);
+          const uint32_t abase = mc_smem_u32(a_ring + sa * C::A_STAGE);
 #pragma unroll
-          for (int k16 = 0; k16 < BK / 16; ++k16) {
-            const uint32_t acc = (kk > 0 || k16 > 0) ? 1u : 0u;
-            umma_bf16(d0, adesc0 + 2 * k16, bdesc + 2 * k16, idesc, acc);
-            if (GU) umma_bf16(d0 + 256, adesc1 + 2 * k16, bdesc + 2 * k16, idesc, acc);
+          for (int ti = 0; ti < C::NMAT; ++ti) {
+            const uint64_t adesc = sw128_desc(abase + ti * C::A_BYTES);
+#pragma unroll
+            for (int k16 = 0; k16 < BK / 16; ++k16)
+              umma_bf16(d0 + ti * MAXN, adesc + 2 * k16, bdesc + 2 * k16, idesc,
+                        (kk > 0 || k16 > 0) ? 1u : 0u);
           }
           umma_commit(&bempty[sb]);  // both stages free once these MMAs have read them
           umma_commit(&aempty[sa]);
@@ -366,79 +380,101 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const GemmParams P)
     __syncwarp();
   } else {
     // ------------------------------------------ dequant producers + epilogue
+    // gate/up: group g = matrix, each thread one 64-code row slice per K
+    // step; down: group g = K half, each thread 32 codes of a row per K step.
+    constexpr int NU = GU ? 2 : 1;  // uint4 code loads per thread per K step
     const int dt = t - 64;            // 0..255
-    const int grp = dt >> 7;          // gate/up: matrix; down: K-step parity
+    const int grp = dt >> 7;
     const int d = dt & 127;           // weight row within the feature block
     const int q = warp & 3;           // TMEM lane quarter this warp may access
     const uint32_t* wcodes = (GU && grp) ? P.w1.codes : P.w0.codes;
     const uint16_t* wscales = (GU && grp) ? P.w1.scales : P.w0.scales;
     const uint16_t* wbiases = (GU && grp) ? P.w1.biases : P.w0.biases;
-    // K steps of this thread: all (gate/up) or every other one (down)
-    const int step = GU ? 1 : 2;
-    // two K slices in flight per thread: slot 0 holds the slice being
-    // dequantised while slot 1's loads are outstanding, then they swap; the
-    // next item's first two slices are requested before this item's epilogue
-    // (scale and bias stay raw bf16 until use: converting them at load time
-    // would make the thread wait for the load right there)
-    uint4 ca0 = make_uint4(0, 0, 0, 0), cb0 = ca0, ca1 = ca0, cb1 = ca0;
-    uint16_t sc0 = 0, bi0 = 0, sc1 = 0, bi1 = 0;
+    const int half_off = GU ? 0 : 16 * grp;  // byte offset of this thread's codes in a slice
+    // Code slices two K steps ahead in two slots (even / odd K step); the
+    // scale and bias of a K-step pair as one 32-bit word each, one pair ahead
+    // (raw until use: converting at load time would wait for the load there).
+    // The next item's first loads are issued before this item's epilogue.
+    uint4 c0[NU], c1[NU];
+    uint32_t sw_n = 0, bw_n = 0;
     const uint8_t* crow = nullptr;
-    const uint16_t *srow = nullptr, *brow = nullptr;
-    auto load_slice = [&](int kk, uint4& ca, uint4& cb, uint16_t& sc, uint16_t& bi) {
+    const uint32_t *srow = nullptr, *brow = nullptr;
+#pragma unroll
+    for (int u = 0; u < NU; ++u) c0[u] = c1[u] = make_uint4(0, 0, 0, 0);
+    auto load_codes = [&](uint4* c, int kk) {
       if (kk < ksteps) {
-        ca = __ldg(reinterpret_cast<const uint4*>(crow + kk * 32));
-        cb = __ldg(reinterpret_cast<const uint4*>(crow + kk * 32) + 1);
-        sc = __ldg(srow + kk);
-        bi = __ldg(brow + kk);
+#pragma unroll
+        for (int u = 0; u < NU; ++u) c[u] = mc_ldg_stream(crow + kk * 32 + half_off + 16 * u);
       }
     };
-    // point at item `item`'s weight row and request its first two slices
-    auto start_item = [&](int item, uint32_t it_base) -> Item {
+    auto load_sb = [&](int pair) {
+      if (2 * pair < ksteps) {
+        sw_n = __ldg(srow + pair);
+        bw_n = __ldg(brow + pair);
+      }
+    };
+    auto start_item = [&](int item) -> Item {
       const Item w = item_info(P, item, nblk);
       const size_t wrow = (size_t)w.e * P.N + (size_t)w.nb * BF + d;
       crow = reinterpret_cast<const uint8_t*>(wcodes) + wrow * (P.K / 2);
-      srow = wscales + wrow * (P.K / 64);
-      brow = wbiases + wrow * (P.K / 64);
-      const int k0 = GU ? 0 : (int)((grp - it_base) & 1u);
-      load_slice(k0, ca0, cb0, sc0, bi0);
-      load_slice(k0 + step, ca1, cb1, sc1, bi1);
+      srow = reinterpret_cast<const uint32_t*>(wscales + wrow * (P.K / 64));
+      brow = reinterpret_cast<const uint32_t*>(wbiases + wrow * (P.K / 64));
+      load_codes(c0, 0);
+      load_codes(c1, 1);
+      load_sb(0);
       return w;
     };
+    // dequantise the slice held in c (K step kk) into stage itk
+    auto do_slice = [&](const uint4* c, uint32_t itk, float sc, float bi) -> bool {
+      const int s = itk % C::ASTAGES;
+      const uint32_t ph = (itk / C::ASTAGES) & 1;
+      if (!wait_bar(&aempty[s], ph ^ 1, &abort_s)) return false;
+      uint8_t* row = a_ring + s * C::A_STAGE + (GU ? grp * C::A_BYTES : 0) + d * 128;
+      uint32_t W[4 * NU];
+#pragma unroll
+      for (int u = 0; u < NU; ++u) {
+        W[4 * u] = c[u].x;
+        W[4 * u + 1] = c[u].y;
+        W[4 * u + 2] = c[u].z;
+        W[4 * u + 3] = c[u].w;
+      }
+      dequant_words<2 * NU>(W, sc, bi, row, d & 7, GU ? 0 : 4 * grp);
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      mc_mbar_arrive(&afull[s]);
+      return true;
+    };
     uint32_t it = 0, j = 0;
-    Item w = start_item(blockIdx.x < total ? blockIdx.x : 0, 0);
-    for (int item = blockIdx.x; item < total && !abort_s; item += gridDim.x, ++j) {
+    Item w = start_item(cta_item(0) < total ? cta_item(0) : 0);
+    for (int i = 0, item = cta_item(0); item < total && !abort_s; item = cta_item(++i), ++j) {
       if (!w.ok && dt == 0 && P.status) atomicOr(P.status, 2u);
-      const int k0 = GU ? 0 : (int)((grp - it) & 1u);
       bool ok = true;
-      auto do_slice = [&](int kk, uint4& ca, uint4& cb, uint16_t& sc, uint16_t& bi) -> bool {
-        const uint4 xa = ca, xb = cb;
-        const uint16_t xs = sc, xbias = bi;
-        load_slice(kk + 2 * step, ca, cb, sc, bi);  // refill this slot two slices ahead
-        const uint32_t itk = it + (uint32_t)kk;
-        const int s = itk % C::ASTAGES;
-        const uint32_t ph = (itk / C::ASTAGES) & 1;
-        if (!wait_bar(&aempty[s], ph ^ 1, &abort_s)) return false;
-        uint8_t* at = smem + C::BSTAGES * C::B_BYTES + s * C::A_STAGE + (GU ? grp * C::A_BYTES : 0);
-        dequant_row64(xa, xb, mc_bf16_to_f32(xs), mc_bf16_to_f32(xbias), at + d * 128, d & 7);
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-        mc_mbar_arrive(&afull[s]);
-        return true;
-      };
-      for (int kk = k0; kk < ksteps; kk += 2 * step) {
-        if (!do_slice(kk, ca0, cb0, sc0, bi0)) {
+      for (int kk = 0; kk < ksteps; kk += 2) {
+        const uint32_t sw = sw_n, bw = bw_n;
+        load_sb(kk / 2 + 1);
+        uint4 x[NU];
+#pragma unroll
+        for (int u = 0; u < NU; ++u) x[u] = c0[u];
+        load_codes(c0, kk + 2);
+        if (!do_slice(x, it + kk, mc_bf16_to_f32((uint16_t)sw), mc_bf16_to_f32((uint16_t)bw))) {
           ok = false;
           break;
         }
-        if (kk + step < ksteps && !do_slice(kk + step, ca1, cb1, sc1, bi1)) {
+#pragma unroll
+        for (int u = 0; u < NU; ++u) x[u] = c1[u];
+        load_codes(c1, kk + 3);
+        if (!do_slice(x, it + kk + 1, mc_bf16_to_f32((uint16_t)(sw >> 16)),
+                      mc_bf16_to_f32((uint16_t)(bw >> 16)))) {
           ok = false;
           break;
         }
       }
-      if (!ok) abort_s = 1;
+      if (!ok) {
+        abort_s = 1;
+        break;
+      }
       it += (uint32_t)ksteps;
-      if (!ok) break;
       const Item cur = w;
-      if (item + (int)gridDim.x < total) w = start_item(item + gridDim.x, it);
+      if (cta_item(i + 1) < total) w = start_item(cta_item(i + 1));
       // ---- epilogue: TMEM [feature][token] -> bf16 out[token][feature]
       const int buf = (int)(j % C::NBUF);
       const uint32_t use = j / C::NBUF;
@@ -450,30 +486,33 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const GemmParams P)
       const int f = 32 * q + lane;  // feature row of D this thread reads
       const int n16 = cur.n >> 4, split = (n16 + 1) >> 1;
       const int c_lo = grp ? split : 0, c_hi = grp ? n16 : split;
-      const uint32_t lane_base = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(buf * 256);
+      const uint32_t lane_base = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(buf * C::ACC_COLS);
       uint16_t* ocol = P.out + (size_t)cur.nb * BF + f;
 #pragma unroll 1
       for (int c = c_lo; c < c_hi; ++c) {
         uint32_t g[16], u[16];
         tmem_ld16(lane_base + 16 * c, g);
-        if (GU) tmem_ld16(lane_base + 256 + 16 * c, u);
+        if (GU) tmem_ld16(lane_base + MAXN + 16 * c, u);
         tmem_wait_ld();
         const uint32_t r0 = cur.m0 + 16u * (uint32_t)c;
 #pragma unroll
-        for (int i = 0; i < 16; i += 2) {
+        for (int i2 = 0; i2 < 16; i2 += 2) {
           float o0, o1;
           if (GU) {
-            const float g0 = bf16_round(__uint_as_float(g[i])), g1 = bf16_round(__uint_as_float(g[i + 1]));
-            const float u0 = bf16_round(__uint_as_float(u[i])), u1 = bf16_round(__uint_as_float(u[i + 1]));
+            const float g0 = bf16_round(__uint_as_float(g[i2]));
+            const float g1 = bf16_round(__uint_as_float(g[i2 + 1]));
+            const float u0 = bf16_round(__uint_as_float(u[i2]));
+            const float u1 = bf16_round(__uint_as_float(u[i2 + 1]));
             o0 = __fmul_rn(bf16_round(silu_fast(g0)), u0);
             o1 = __fmul_rn(bf16_round(silu_fast(g1)), u1);
           } else {
-            o0 = __uint_as_float(g[i]);
-            o1 = __uint_as_float(g[i + 1]);
+            o0 = __uint_as_float(g[i2]);
+            o1 = __uint_as_float(g[i2 + 1]);
           }
           const uint32_t pk = pack_bf16x2(o0, o1);
-          if (cur.ok && r0 + i < cur.mend) ocol[(size_t)(r0 + i) * P.N] = (uint16_t)pk;
-          if (cur.ok && r0 + i + 1 < cur.mend) ocol[(size_t)(r0 + i + 1) * P.N] = (uint16_t)(pk >> 16);
+          if (cur.ok && r0 + i2 < cur.mend) ocol[(size_t)(r0 + i2) * P.N] = (uint16_t)pk;
+          if (cur.ok && r0 + i2 + 1 < cur.mend)
+            ocol[(size_t)(r0 + i2 + 1) * P.N] = (uint16_t)(pk >> 16);
         }
       }
       tc_fence_before();
@@ -516,12 +555,12 @@ PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
   return fn;
 }
 
-int make_a_map(CUtensorMap* map, const uint16_t* a, int rows, int K) {
+int make_a_map(CUtensorMap* map, const uint16_t* a, int rows, int K, int box_rows) {
   auto enc = get_encode();
   if (!enc) return mc_fail(MC_ECUDA, "cuTensorMapEncodeTiled unavailable");
   const cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)rows};
   const cuuint64_t strides[1] = {(cuuint64_t)K * 2};
-  const cuuint32_t box[2] = {BK, BOX_ROWS};
+  const cuuint32_t box[2] = {BK, (cuuint32_t)box_rows};
   const cuuint32_t estr[2] = {1, 1};
   CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<uint16_t*>(a), dims,
                    strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
@@ -536,14 +575,16 @@ int launch(mc_ctx* ctx, const uint16_t* a, int rows, const mc_qweights* w0, cons
            int max_tiles, uint32_t* status) {
   using C = Cfg<GU>;
   const int N = w0->out_features / n_experts, K = w0->in_features;
-  CUtensorMap map;
-  int rc = make_a_map(&map, a, rows, K);
-  if (rc) return rc;
+  TokenMaps tm;
+  int rc;
+  if ((rc = make_a_map(&tm.m64, a, rows, K, 64)) || (rc = make_a_map(&tm.m128, a, rows, K, 128)) ||
+      (rc = make_a_map(&tm.m256, a, rows, K, 256)))
+    return rc;
   GemmParams P{*w0, GU ? *w1 : *w0, out, reinterpret_cast<const uint4*>(tiles), n_tiles, status,
                N, K, rows, max_tiles, n_experts};
   MC_CUDA(cudaFuncSetAttribute(grouped_gemm_kernel<GU>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                C::SMEM));
-  grouped_gemm_kernel<GU><<<ctx->num_sms, kThreads, C::SMEM, ctx->stream>>>(map, P);
+  grouped_gemm_kernel<GU><<<ctx->num_sms, kThreads, C::SMEM, ctx->stream>>>(tm, P);
   return mc_after_launch("grouped_gemm_kernel");
 }
 
@@ -558,8 +599,11 @@ int check_grouped(const uint16_t* a, int rows, const mc_qweights* w, int n_exper
              n_experts);
   const int N = w->out_features / n_experts;
   MC_REQUIRE(N % BF == 0, "%s: expert width %d must be a multiple of %d", what, N, BF);
-  MC_REQUIRE(w->in_features % BK == 0, "%s: K %d must be a multiple of %d", what, w->in_features,
-             BK);
+  // K steps come in pairs whose scales (and biases) are read as one 32-bit word
+  MC_REQUIRE(w->in_features % (2 * BK) == 0, "%s: K %d must be a multiple of %d", what,
+             w->in_features, 2 * BK);
+  MC_REQUIRE(mc_aligned(w->scales, 4) && mc_aligned(w->biases, 4),
+             "%s: scales/biases must be 4-byte aligned", what);
   MC_REQUIRE(rows >= 1, "%s: rows %d", what, rows);
   MC_REQUIRE(a && out && tiles && n_tiles && max_tiles >= 1, "%s: null pointer", what);
   MC_REQUIRE(mc_aligned(a, 16) && mc_aligned(out, 16) && mc_aligned(tiles, 16),

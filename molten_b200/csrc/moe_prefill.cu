@@ -6,9 +6,10 @@
 // Sort: two launches, one CTA per expert each. Launch 1 counts the expert's
 // pairs (no atomics: every CTA scans the whole id list, 64 x 64 KB from L2 at
 // the 4096-token chunk, so counts are deterministic). Launch 2 derives the
-// expert's offset and tile offset from the 64 counts, scans its pairs in
+// expert's offset and tile slots from the 64 counts, scans its pairs in
 // token-major, rank-major order (each thread a contiguous token range, block
-// exclusive scan), and writes ids_sorted / slotpos and its row tiles.
+// exclusive scan), and writes ids_sorted / slotpos and its row tiles (full
+// tiles first in expert order, then partial tiles by decreasing height).
 #include "mc_internal.cuh"
 
 namespace {
@@ -36,24 +37,32 @@ sort_scatter_kernel(const uint32_t* __restrict__ ids, int m, int E, int bm,
                     uint32_t* __restrict__ ids_sorted, uint32_t* __restrict__ slotpos,
                     uint4* __restrict__ tiles, uint32_t* __restrict__ n_tiles, int max_tiles) {
   __shared__ uint32_t warp_tot[8];
-  __shared__ uint32_t base_s[2];
+  __shared__ uint32_t base_s[3];
   const uint32_t e = blockIdx.x;
   const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
   if (t == 0) {
-    uint32_t off = 0, toff = 0, all_tiles = 0;
+    // Tile list order: every full bm-row tile first (expert order), then the
+    // partial tiles by decreasing height (ties: lower expert first), so a
+    // consumer that deals tiles out in list order balances its workers.
+    const uint32_t ce = counts[e], pe = ce % (uint32_t)bm;
+    uint32_t off = 0, full_before = 0, full_all = 0, part_rank = 0, parts = 0;
     for (int j = 0; j < E; ++j) {
-      const uint32_t c = counts[j];
-      const uint32_t nt = (c + bm - 1) / bm;
+      const uint32_t c = counts[j], pj = c % (uint32_t)bm;
       if ((uint32_t)j < e) {
         off += c;
-        toff += nt;
+        full_before += c / bm;
       }
-      all_tiles += nt;
+      full_all += c / bm;
+      if (pj) {
+        ++parts;
+        if (pj > pe || (pj == pe && (uint32_t)j < e)) ++part_rank;
+      }
     }
     base_s[0] = off;
-    base_s[1] = toff;
+    base_s[1] = full_before;
+    base_s[2] = full_all + part_rank;  // slot of this expert's partial tile
     offsets[e] = off;
-    if (e == 0) *n_tiles = all_tiles;
+    if (e == 0) *n_tiles = full_all + parts;
   }
   // contiguous token range per thread
   const int per = (m + 255) / 256;
@@ -84,9 +93,9 @@ sort_scatter_kernel(const uint32_t* __restrict__ ids, int m, int E, int bm,
       }
   // row tiles of this expert
   const uint32_t n = counts[e];
-  const uint32_t nt = (n + bm - 1) / bm;
+  const uint32_t nt = (n + bm - 1) / bm, nfull = n / bm;
   for (uint32_t j = t; j < nt; j += 256) {
-    const uint32_t slot = base_s[1] + j;
+    const uint32_t slot = j < nfull ? base_s[1] + j : base_s[2];
     if (slot < (uint32_t)max_tiles) {
       const uint32_t m0 = base_s[0] + j * bm;
       tiles[slot] = make_uint4(m0, min(m0 + (uint32_t)bm, base_s[0] + n), e, 0u);
@@ -234,7 +243,7 @@ extern "C" int mc_moe_combine_rows(mc_ctx* ctx, const uint16_t* ed, const uint32
 // u32[E], ids_sorted/slotpos u32[4m], tiles uint4[max_tiles], n_tiles +
 // status u32, gx bf16[4m][H], act bf16[4m][I], ed bf16[4m][H].
 namespace {
-// token rows per grouped-GEMM chunk (the tcgen05 MMA's N is at most 256)
+// token rows per grouped-GEMM chunk (the kernel's MMA N is at most 256)
 constexpr int kPrefillChunk = 256;
 
 struct PrefillWs {

@@ -15,16 +15,25 @@ pytestmark = pytest.mark.gpu
 
 RTOL = 1e-2
 ATOL_RMS = 1e-2
+ACT_ULPS = 3
 
 
-def assert_close_bf16(got_bits, want_bits, what, min_equal=0.5):
+def bf16_ulp(v):
+    """Spacing of bf16 values at |v| (8 significant bits)."""
+    e = np.floor(np.log2(np.maximum(np.abs(v), 2.0 ** -126)))
+    return 2.0 ** (e - 7)
+
+
+def assert_close_bf16(got_bits, want_bits, what, min_equal=0.5, ulps=0):
+    """|got - want| <= 1e-2 |want| + 1e-2 rms(want) (+ `ulps` bf16 ulps of want
+    for values that went through several bf16 roundings)."""
     got = synth.bf16_bits_to_f32(np.asarray(got_bits)).astype(np.float64)
     want = synth.bf16_bits_to_f32(np.asarray(want_bits)).astype(np.float64)
     assert got.shape == want.shape, what
     assert np.all(np.isfinite(got)), f"{what}: non-finite output"
     rms = np.sqrt(np.mean(want ** 2)) if want.size else 0.0
     err = np.abs(got - want)
-    bad = err > RTOL * np.abs(want) + ATOL_RMS * rms
+    bad = err > RTOL * np.abs(want) + ATOL_RMS * rms + ulps * bf16_ulp(want)
     assert not bad.any(), (f"{what}: {bad.sum()} of {bad.size} outside tolerance, "
                            f"max err {err.max():.3g}, rms {rms:.3g}")
     eq = np.mean(np.asarray(got_bits) == np.asarray(want_bits))
@@ -87,10 +96,14 @@ def run_gpu_chain(ctx, x, logits, gate, up, down, E, bm=128):
                                                (2, 300, 8, 384, None, 256),
                                                (3, 64, 64, 1536, 8, 256),
                                                (4, 10, 8, 256, None, 256),
-                                               (5, 200, 4, 128, None, 64)])
+                                               (5, 200, 4, 128, None, 64),
+                                               (6, 300, 8, 640, None, 112),
+                                               (7, 700, 4, 256, None, 200)])
 def test_grouped_ffn_matches_oracle(cuda_ctx, seed, m, E, I, hot, bm):
-    """bm 256: chunks up to the MMA's largest N; m=10: fewer rows (40) than one
-    64-row token box; bm 64: many short chunks per expert."""
+    """bm 256: chunks up to the MMA's largest N (one 256-row token box); m=10:
+    fewer rows (40) than the smallest token box; bm 64/112/200: chunk heights
+    that pick each token-box size and are not multiples of 16; I=384/640: down
+    K not a multiple of 256."""
     H = 2048
     x, logits, gate, up, down = prefill_case(seed, m, E, H, I, hot)
     got = run_gpu_chain(cuda_ctx, x, logits, gate, up, down, E, bm)
@@ -99,7 +112,10 @@ def test_grouped_ffn_matches_oracle(cuda_ctx, seed, m, E, I, hot, bm):
     assert_bits_equal(got["gw"], want["gw"], "gw")
     assert np.array_equal(got["ids_sorted"], want["ids_sorted"])
     assert np.array_equal(got["slotpos"], want["slotpos"])
-    assert_close_bf16(got["act"], want["act"], "act")
+    # act = bf16(bf16(silu(bf16 g)) * bf16 u): a one-ulp flip of g or u (their
+    # fp32 sums run in another order on the tensor cores) and of silu(g) stack
+    # to about three bf16 ulps of act
+    assert_close_bf16(got["act"], want["act"], "act", ulps=ACT_ULPS)
     # the down GEMM on the GPU's own act isolates the GEMM from act rounding
     counts, offsets, _, _ = oracle.moe_sort(want["ids"], E)
     ed_ref = oracle.gemm_q4_grouped(got["act"], down, counts, offsets, E)
@@ -148,7 +164,7 @@ def test_moe_prefill_entry_point(cuda_ctx):
     assert int(host_u32(v["status"])[0]) == 0
     want = oracle.moe_prefill(x, logits, gate, up, down, n_experts=E)
     assert np.array_equal(host_u32(v["ids"]), want["ids"])
-    assert_close_bf16(host_bits(v["act"]), want["act"], "act")
+    assert_close_bf16(host_bits(v["act"]), want["act"], "act", ulps=ACT_ULPS)
     # combine is a fixed-order sum: bit-exact on the GPU's own expert rows
     ed = host_bits(v["ed"])
     gw = host_bits(v["gw"])
