@@ -508,9 +508,10 @@ def bench_gemv(args, torch, ws, rank, local, head: bool):
 
 # ------------------------------------------------------------------ cfg3
 
-def zipf_logits_torch(torch, gen, m, e=E, s=1.0, device="cuda"):
-    """log(Zipf_s(rank(pi(e)))) + Gumbel(0, 1): top-4 is a Plackett-Luce draw."""
-    perm = torch.randperm(e, generator=gen, device=device).to(torch.float32)
+def zipf_logits_torch(torch, gen, m, e=E, s=1.0, device="cuda", perm_gen=None):
+    """log(Zipf_s(rank(pi(e)))) + Gumbel(0, 1): top-4 is a Plackett-Luce draw.
+    `perm_gen` (optional) draws pi, so several ranks can share one popularity order."""
+    perm = torch.randperm(e, generator=perm_gen or gen, device=device).to(torch.float32)
     base = -s * torch.log(perm + 1.0)
     u = torch.rand((m, e), generator=gen, device=device).clamp_(1e-20, 1.0)
     return (base[None, :] - torch.log(-torch.log(u))).contiguous()
@@ -551,7 +552,94 @@ def cpu_baseline_prefill(torch, layer, x, logits, seconds):
                       "oracle/mc_oracle_fast.c -O3 OpenMP (dequantises every routed expert)"}
 
 
+def bench_cfg3_ep(args, torch, ws, rank, local):
+    """cfg3 expert-parallel over ws GPUs: each rank holds 64/ws experts and its
+    own 4096 tokens (weak scaling); rows cross NVLink by NCCL point-to-point
+    both ways every step (molten_b200.ep)."""
+    import torch.distributed as dist
+    from molten_b200 import ep, lfm, synth
+    ctx = lfm.Context(local)
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(args.seed * 1000 + 3)          # same expert weights on every rank
+    layer = synth.moe_layer_torch(gen, "cuda")
+    sl = {k: ep.expert_slice(layer[k], rank, ws, E) for k in ("gate", "up", "down")}
+    del layer
+    m = args.tokens
+    tg = torch.Generator(device="cuda")
+    tg.manual_seed(args.seed * 1000 + 100 + rank)  # each rank its own tokens
+    pg = torch.Generator(device="cuda")
+    pg.manual_seed(args.seed * 1000 + 7)           # one expert popularity order for all
+    x = torch.randn((m, H), generator=tg, device="cuda").to(torch.bfloat16)
+    logits = zipf_logits_torch(torch, tg, m, perm_gen=pg)
+    ops = ep.CudaOps(ctx, sl["gate"], sl["up"], sl["down"], E, rank, ws)
+    step = lambda: ep.moe_prefill_ep(ops, x, logits, rank, ws)
+    K, W = args.steps, max(args.warmup, 3)
+    for _ in range(W):
+        out, plan = step()
+    torch.cuda.synchronize()
+    if int(ops.status.cpu()[0]):
+        raise RuntimeError(f"grouped GEMM status {int(ops.status.cpu()[0])}")
+    barrier(ws)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        a.record()
+        for _ in range(K):
+            out, plan = step()
+        b.record()
+        torch.cuda.synchronize()
+    ms_ = max_over_ranks(ws, a.elapsed_time(b))
+    value = ws * m * K / (ms_ * 1e-3)
+    # rows this rank computed and rows that crossed NVLink (both directions), per step
+    remote = sum(n for peer, _, n in plan.send if peer != rank)
+    loads = torch.tensor([plan.recv_rows, remote], dtype=torch.float64, device="cuda")
+    lmax, lmin = loads.clone(), loads.clone()
+    dist.all_reduce(lmax, op=dist.ReduceOp.MAX)
+    dist.all_reduce(lmin, op=dist.ReduceOp.MIN)
+    # e2e: host rows in, host rows out, through the same call
+    hx, hl = x.cpu().pin_memory(), logits.cpu().pin_memory()
+    hout = torch.empty((m, H), dtype=torch.bfloat16).pin_memory()
+    n_e2e = min(K, 10)
+    barrier(ws)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(n_e2e):
+        x.copy_(hx, non_blocking=True)
+        logits.copy_(hl, non_blocking=True)
+        out, _ = step()
+        hout.copy_(out, non_blocking=True)
+    e1.record()
+    torch.cuda.synchronize()
+    e2e_ms = max_over_ranks(ws, e0.elapsed_time(e1))
+    _, bf16_peak, src = peaks()
+    useful = prefill_flops(4 * m)                   # per rank per step (weak scaling)
+    achieved = useful / (ms_ / K * 1e-3) / 1e12
+    return {
+        "metric": "prefill grouped-GEMM tokens/s (cfg3: 4096-token MoE FFN, Zipf routing)",
+        "value": round(value, 1), "unit": "tokens/s", "n_gpus": ws, "steps": K, "warmup": W,
+        "ms_per_step": round(ms_ / K, 4), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "q4 weights dequantised to bf16, bf16 x bf16 -> fp32 tcgen05",
+        "data": "synthetic (seeded; Zipf(s=1) + Gumbel router logits sharing one expert "
+                "popularity order across ranks, random-init weights)",
+        "config": {"workload": f"cfg3 expert-parallel: {m} tokens per rank x 2048, E=64 top-4 "
+                               f"({E // ws} experts per GPU), SwiGLU 2048->1536->2048 Q4",
+                   "parallelism": f"ep{ws}", "exchange": "NCCL point-to-point rows both ways",
+                   "rows_computed_per_rank_max_min": [int(lmax[0]), int(lmin[0])],
+                   "rows_sent_remote_per_rank_max": int(lmax[1]),
+                   "l2": "expert weights > L2, streamed every step"},
+        "e2e": {"value": round(ws * m * n_e2e / (e2e_ms * 1e-3), 1), "unit": "tokens/s",
+                "h2d_bytes_per_step": m * H * 2 + m * E * 4, "d2h_bytes_per_step": m * H * 2},
+        "roofline": {"bound": "tensor", "kernel": "whole EP step per GPU (grouped GEMMs + "
+                     "exchange + dispatch)", "achieved": round(achieved, 1), "peak": bf16_peak,
+                     "unit": "TFLOP/s", "frac": round(achieved / bf16_peak, 4),
+                     "peak_source": f"{src} bf16_tflops (burst)", "traffic": None},
+        "gpu_launches": 9 * K,
+        "clocks": clk.summary(),
+    }
+
+
 def bench_cfg3(args, torch, ws, rank, local):
+    if ws > 1:
+        return bench_cfg3_ep(args, torch, ws, rank, local)
     from molten_b200 import lfm, synth
     ctx = lfm.Context(local)
     gen = torch.Generator(device="cuda")
