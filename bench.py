@@ -56,6 +56,8 @@ def parse():
     p.add_argument("--impl", choices=["molten", "reference"], default="molten")
     p.add_argument("--workload", choices=["cfg0", "cfg1", "cfg2", "cfg3"], default="cfg1")
     p.add_argument("--tokens", type=int, default=4096, help="cfg3 prefill chunk")
+    p.add_argument("--ep-exchange", choices=["peer", "nccl"], default="peer",
+                   help="cfg3 on N>1 GPUs: rows over NVLink peer memory or NCCL point-to-point")
     p.add_argument("--seed", type=int, default=0)
     p.add_argument("--sets", type=int, default=16, help="rotated weight sets (cfg1)")
     p.add_argument("--decode-path", choices=["fused", "split"], default="fused",
@@ -556,6 +558,7 @@ def bench_cfg3_ep(args, torch, ws, rank, local):
     """cfg3 expert-parallel over ws GPUs: each rank holds 64/ws experts and its
     own 4096 tokens (weak scaling); rows cross NVLink by NCCL point-to-point
     both ways every step (molten_b200.ep)."""
+    import numpy as np
     import torch.distributed as dist
     from molten_b200 import ep, lfm, synth
     ctx = lfm.Context(local)
@@ -572,13 +575,19 @@ def bench_cfg3_ep(args, torch, ws, rank, local):
     x = torch.randn((m, H), generator=tg, device="cuda").to(torch.bfloat16)
     logits = zipf_logits_torch(torch, tg, m, perm_gen=pg)
     ops = ep.CudaOps(ctx, sl["gate"], sl["up"], sl["down"], E, rank, ws)
-    step = lambda: ep.moe_prefill_ep(ops, x, logits, rank, ws)
+    px = None
+    if args.ep_exchange == "peer":
+        px = ep.PeerExchange(ctx, rank, ws, m, H, I, E)
+        step = lambda: (ep.moe_prefill_ep_peer(ops, px, x, logits), None)
+    else:
+        step = lambda: ep.moe_prefill_ep(ops, x, logits, rank, ws)
     K, W = args.steps, max(args.warmup, 3)
     for _ in range(W):
         out, plan = step()
     torch.cuda.synchronize()
-    if int(ops.status.cpu()[0]):
-        raise RuntimeError(f"grouped GEMM status {int(ops.status.cpu()[0])}")
+    st = int(ops.status.cpu()[0]) | (int(px.status.cpu()[0]) if px else 0)
+    if st:
+        raise RuntimeError(f"exchange / grouped GEMM status {st}")
     barrier(ws)
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clk:
@@ -589,9 +598,16 @@ def bench_cfg3_ep(args, torch, ws, rank, local):
         torch.cuda.synchronize()
     ms_ = max_over_ranks(ws, a.elapsed_time(b))
     value = ws * m * K / (ms_ * 1e-3)
-    # rows this rank computed and rows that crossed NVLink (both directions), per step
-    remote = sum(n for peer, _, n in plan.send if peer != rank)
-    loads = torch.tensor([plan.recv_rows, remote], dtype=torch.float64, device="cuda")
+    # rows this rank computed and rows that crossed NVLink (each way), per step
+    if px is not None:
+        ca = px.counts_all.cpu().numpy().astype(np.int64)
+        per = E // ws
+        recv_rows = int(ca[:, rank * per:(rank + 1) * per].sum())
+        remote = int(ca[rank].sum() - ca[rank, rank * per:(rank + 1) * per].sum())
+    else:
+        recv_rows = plan.recv_rows
+        remote = sum(n for peer, _, n in plan.send if peer != rank)
+    loads = torch.tensor([recv_rows, remote], dtype=torch.float64, device="cuda")
     lmax, lmin = loads.clone(), loads.clone()
     dist.all_reduce(lmax, op=dist.ReduceOp.MAX)
     dist.all_reduce(lmin, op=dist.ReduceOp.MIN)
@@ -610,6 +626,8 @@ def bench_cfg3_ep(args, torch, ws, rank, local):
     e1.record()
     torch.cuda.synchronize()
     e2e_ms = max_over_ranks(ws, e0.elapsed_time(e1))
+    if px is not None:
+        px.close()
     _, bf16_peak, src = peaks()
     useful = prefill_flops(4 * m)                   # per rank per step (weak scaling)
     achieved = useful / (ms_ / K * 1e-3) / 1e12
@@ -622,7 +640,10 @@ def bench_cfg3_ep(args, torch, ws, rank, local):
                 "popularity order across ranks, random-init weights)",
         "config": {"workload": f"cfg3 expert-parallel: {m} tokens per rank x 2048, E=64 top-4 "
                                f"({E // ws} experts per GPU), SwiGLU 2048->1536->2048 Q4",
-                   "parallelism": f"ep{ws}", "exchange": "NCCL point-to-point rows both ways",
+                   "parallelism": f"ep{ws}",
+                   "exchange": ("rows copied into the owners' buffers over NVLink peer memory "
+                                "(CUDA IPC), in-stream NCCL barriers, no host sync"
+                                if px is not None else "NCCL point-to-point rows both ways"),
                    "rows_computed_per_rank_max_min": [int(lmax[0]), int(lmin[0])],
                    "rows_sent_remote_per_rank_max": int(lmax[1]),
                    "l2": "expert weights > L2, streamed every step"},
@@ -632,7 +653,7 @@ def bench_cfg3_ep(args, torch, ws, rank, local):
                      "exchange + dispatch)", "achieved": round(achieved, 1), "peak": bf16_peak,
                      "unit": "TFLOP/s", "frac": round(achieved / bf16_peak, 4),
                      "peak_source": f"{src} bf16_tflops (burst)", "traffic": None},
-        "gpu_launches": 9 * K,
+        "gpu_launches": (10 if args.ep_exchange == "peer" else 9) * K,
         "clocks": clk.summary(),
     }
 

@@ -262,6 +262,40 @@ int mc_moe_prefill(mc_ctx* ctx, const uint16_t* x, const float* logits, int m,
                    int n_experts, int route_mode, const float* expert_bias, void* workspace,
                    size_t ws_bytes, uint16_t* out);
 
+/* ------------------------------------------- expert-parallel prefill (new)
+ * No counterpart in the reference (its moe_prefill runs on one device). Rank
+ * r of `world` holds experts [r*E/world, (r+1)*E/world); every rank sorted its
+ * own pairs with mc_moe_sort_map and holds counts_all[world][E] (an
+ * all-gather of every rank's counts). Receive buffers are expert-major (rows
+ * of local expert j contiguous, sources in rank order); all ranks allocate
+ * buffers of equal capacity. The caller puts a cross-rank barrier after
+ * mc_ep_dispatch and after mc_ep_return (a receiver may read only once every
+ * sender's copy finished). status (nullable u32) bit 2: rows beyond a
+ * capacity were skipped (inconsistent counts). */
+
+/* Device memory whose base can be shared with other processes (cudaMalloc). */
+int mc_ep_alloc(mc_ctx* ctx, size_t bytes, void** out);
+int mc_ep_free(mc_ctx* ctx, void* ptr);
+/* CUDA IPC: 64-byte handle of an mc_ep_alloc base; open / close a peer's. */
+int mc_ipc_handle(mc_ctx* ctx, void* base, void* handle_out);
+int mc_ipc_open(mc_ctx* ctx, const void* handle, void** out);
+int mc_ipc_close(mc_ctx* ctx, void* ptr);
+/* Copies this rank's expert-sorted rows x[ids_sorted[i]] (bf16 [m][hidden])
+ * into the owners' receive buffers recv_bufs[world] (own and peer-mapped). */
+int mc_ep_dispatch(mc_ctx* ctx, const uint16_t* x, int m, int hidden,
+                   const uint32_t* ids_sorted, const uint32_t* counts_all, int rank, int world,
+                   int n_experts, void* const* recv_bufs, size_t recv_cap_rows, uint32_t* status);
+/* Row-chunk list (uint4 {m0, m_end, local expert, 0}, <= bm rows, full chunks
+ * first then partial by decreasing height) of this rank's receive buffer,
+ * its length in *n_tiles and the row count in *rows (nullable). */
+int mc_ep_tiles(mc_ctx* ctx, const uint32_t* counts_all, int rank, int world, int n_experts,
+                int bm, uint32_t* tiles, uint32_t* n_tiles, uint32_t* rows, int max_tiles);
+/* Copies the expert outputs ed (bf16 [ed_rows][hidden], receive order) back to
+ * the sources' slots in home_bufs[world] (their sorted order). */
+int mc_ep_return(mc_ctx* ctx, const uint16_t* ed, size_t ed_rows, int hidden,
+                 const uint32_t* counts_all, int rank, int world, int n_experts,
+                 void* const* home_bufs, size_t home_cap_rows, uint32_t* status);
+
 /* -------------------------------------------------------------- test aid */
 
 /* Profiling aid: when buf (device, n u64 words) is set, the persistent

@@ -71,6 +71,14 @@ SIGNATURES: dict[str, tuple] = {
     "mc_moe_decode_layer": (I, [P, P, P, P, P, P, P, I, P, I, P, P, P, QP, QP, QP, I, P, P,
                                 C.c_size_t, F, F]),
     "mc_moe_decode_workspace_words": (C.c_size_t, [I]),
+    "mc_ep_alloc": (I, [P, C.c_size_t, C.POINTER(C.c_void_p)]),
+    "mc_ep_free": (I, [P, P]),
+    "mc_ipc_handle": (I, [P, P, P]),
+    "mc_ipc_open": (I, [P, P, C.POINTER(C.c_void_p)]),
+    "mc_ipc_close": (I, [P, P]),
+    "mc_ep_dispatch": (I, [P, P, I, I, P, P, I, I, I, P, C.c_size_t, P]),
+    "mc_ep_tiles": (I, [P, P, I, I, I, I, P, P, P, I]),
+    "mc_ep_return": (I, [P, P, C.c_size_t, I, P, I, I, I, P, C.c_size_t, P]),
     "mc_moe_decode_layer_noalloc": (I, [P, P, P, P, P, P, P, I, P, I, P, P, P, QP, QP, QP, I, P,
                                         P, F, F]),
     "mc_moe_route_batch": (I, [P, P, I, I, I, P, F, P, P]),

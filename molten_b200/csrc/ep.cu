@@ -1,0 +1,258 @@
+// Expert-parallel prefill exchange over NVLink peer memory (no reference
+// counterpart: the reference's moe_prefill, lfm.rs:847-965, runs on one
+// device).
+//
+// Rank r of W holds experts [r*P, (r+1)*P), P = E/W. Every rank has sorted its
+// own pairs by expert (mc_moe_sort_map) and all ranks share the pair counts
+// counts_all[W][E] (an all-gather). From those counts alone every rank
+// derives the same layout, with no further messages:
+//   * receive buffer of owner r: expert-major -- the rows of its local expert
+//     j contiguous from base_r[j] = sum_{j'<j} total_r[j'], and within them
+//     the rows of source s from base_r[j] + sum_{s'<s} counts_all[s'][r*P+j];
+//   * the rows of source s, expert e sit in s's own sorted order at
+//     off_s[e] = sum_{e'<e} counts_all[s][e'].
+// dispatch copies each of this rank's sorted rows (gathered from the token
+// rows through ids_sorted) straight into the owner's receive buffer; return
+// copies each received row's expert output back to the source's slot. Both
+// move whole rows with 16-byte stores, local or through peer pointers (CUDA
+// IPC mappings of the other ranks' buffers). The caller orders them with the
+// GEMMs and puts a cross-rank barrier after each (the receiver may read only
+// once every sender's kernel has finished).
+#include <string.h>
+
+#include "mc_internal.cuh"
+
+namespace {
+
+constexpr int kMaxRanks = 8;
+constexpr int kMaxExperts = 256;
+
+struct PeerPtrs {
+  uint16_t* p[kMaxRanks];
+};
+
+// Segment starts for one expert e: where its rows from `src` land in the
+// owner's receive buffer, and where they sit in src's sorted order.
+__device__ __forceinline__ void segment_bases(const uint32_t* counts_all, int W, int E, int e,
+                                              int src, uint32_t* recv_row, uint32_t* src_row) {
+  const int P = E / W, owner = e / P, j0 = owner * P;
+  uint32_t base = 0;
+  for (int jj = j0; jj < e; ++jj)
+    for (int s = 0; s < W; ++s) base += counts_all[s * E + jj];
+  for (int s = 0; s < src; ++s) base += counts_all[s * E + e];
+  uint32_t off = 0;
+  for (int ee = 0; ee < e; ++ee) off += counts_all[src * E + ee];
+  *recv_row = base;
+  *src_row = off;
+}
+
+// Rows of expert e from this rank -> owner's receive buffer. grid (E, Y);
+// one warp per row, 16 bytes per lane per step.
+__global__ void __launch_bounds__(256)
+ep_dispatch_kernel(const uint4* __restrict__ x, int m, int h16,
+                   const uint32_t* __restrict__ ids_sorted, const uint32_t* __restrict__ counts_all,
+                   int rank, int W, int E, PeerPtrs recv, uint32_t cap, uint32_t* status) {
+  const int e = blockIdx.x;
+  __shared__ uint32_t dst0, src0, n;
+  if (threadIdx.x == 0) {
+    segment_bases(counts_all, W, E, e, rank, &dst0, &src0);
+    n = counts_all[rank * E + e];
+  }
+  __syncthreads();
+  const int owner = e / (E / W);
+  uint4* dst = reinterpret_cast<uint4*>(recv.p[owner]);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (uint32_t k = blockIdx.y * 8 + warp; k < n; k += gridDim.y * 8) {
+    const uint32_t tok = __ldg(ids_sorted + src0 + k);
+    if (dst0 + k >= cap || tok >= (uint32_t)m) {  // inconsistent counts: never write past a buffer
+      if (lane == 0 && status) atomicOr(status, 4u);
+      continue;
+    }
+    const uint4* row = x + (size_t)tok * h16;
+    uint4* out = dst + (size_t)(dst0 + k) * h16;
+    for (int c = lane; c < h16; c += 32) out[c] = __ldg(row + c);
+  }
+  __threadfence_system();
+}
+
+// Expert outputs of this rank's received rows -> each source's slot.
+// grid (W * P, Y): block x = (source, local expert).
+__global__ void __launch_bounds__(256)
+ep_return_kernel(const uint4* __restrict__ ed, uint32_t ed_rows, int h16,
+                 const uint32_t* __restrict__ counts_all, int rank, int W, int E, PeerPtrs home,
+                 uint32_t cap, uint32_t* status) {
+  const int P = E / W;
+  const int src = blockIdx.x / P, e = rank * P + blockIdx.x % P;
+  __shared__ uint32_t row0, slot0, n;
+  if (threadIdx.x == 0) {
+    segment_bases(counts_all, W, E, e, src, &row0, &slot0);
+    n = counts_all[src * E + e];
+  }
+  __syncthreads();
+  uint4* dst = reinterpret_cast<uint4*>(home.p[src]);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (uint32_t k = blockIdx.y * 8 + warp; k < n; k += gridDim.y * 8) {
+    if (slot0 + k >= cap || row0 + k >= ed_rows) {  // never write or read past a buffer
+      if (lane == 0 && status) atomicOr(status, 4u);
+      continue;
+    }
+    const uint4* row = ed + (size_t)(row0 + k) * h16;
+    uint4* out = dst + (size_t)(slot0 + k) * h16;
+    for (int c = lane; c < h16; c += 32) out[c] = __ldg(row + c);
+  }
+  __threadfence_system();
+}
+
+// Row chunks of this rank's receive buffer for the grouped GEMMs: full
+// bm-row chunks first (local expert order), then the partial ones by
+// decreasing height (ties: lower expert). One CTA; thread j = local expert j.
+__global__ void __launch_bounds__(256)
+ep_tiles_kernel(const uint32_t* __restrict__ counts_all, int rank, int W, int E, int bm,
+                uint4* __restrict__ tiles, uint32_t* __restrict__ n_tiles, uint32_t* __restrict__ rows,
+                int max_tiles) {
+  const int P = E / W;
+  __shared__ uint32_t total_s[kMaxExperts];
+  for (int j = threadIdx.x; j < P; j += blockDim.x) {
+    uint32_t t = 0;
+    for (int s = 0; s < W; ++s) t += counts_all[s * E + rank * P + j];
+    total_s[j] = t;
+  }
+  __syncthreads();
+  uint32_t full_all = 0, parts = 0, all_rows = 0;
+  for (int jj = 0; jj < P; ++jj) {
+    full_all += total_s[jj] / bm;
+    parts += (total_s[jj] % bm) != 0;
+    all_rows += total_s[jj];
+  }
+  if (threadIdx.x == 0) {
+    *n_tiles = full_all + parts;
+    if (rows) *rows = all_rows;
+  }
+  for (int j = threadIdx.x; j < P; j += blockDim.x) {
+    const uint32_t tj = total_s[j], pj = tj % bm;
+    uint32_t base = 0, full_before = 0, rank_p = 0;
+    for (int jj = 0; jj < P; ++jj) {
+      const uint32_t t = total_s[jj], p = t % bm;
+      if (jj < j) {
+        base += t;
+        full_before += t / bm;
+      }
+      if (p && (p > pj || (p == pj && jj < j))) ++rank_p;
+    }
+    const uint32_t nfull = tj / bm;
+    for (uint32_t c = 0; c < nfull; ++c) {
+      const uint32_t slot = full_before + c;
+      if (slot < (uint32_t)max_tiles)
+        tiles[slot] = make_uint4(base + c * bm, base + (c + 1) * bm, (uint32_t)j, 0u);
+    }
+    if (pj) {
+      const uint32_t slot = full_all + rank_p;
+      if (slot < (uint32_t)max_tiles)
+        tiles[slot] = make_uint4(base + nfull * bm, base + tj, (uint32_t)j, 0u);
+    }
+  }
+}
+
+int check_ranks(int rank, int W, int E, const char* what) {
+  MC_REQUIRE(W >= 1 && W <= kMaxRanks && rank >= 0 && rank < W, "%s: rank %d of %d", what, rank,
+             W);
+  MC_REQUIRE(E >= 1 && E <= kMaxExperts && E % W == 0, "%s: %d experts over %d ranks", what, E, W);
+  return MC_OK;
+}
+
+int fill_peers(PeerPtrs* pp, void* const* ptrs, int W, const char* what) {
+  MC_REQUIRE(ptrs, "%s: null peer pointer table", what);
+  for (int r = 0; r < kMaxRanks; ++r) pp->p[r] = nullptr;
+  for (int r = 0; r < W; ++r) {
+    MC_REQUIRE(ptrs[r] && mc_aligned(ptrs[r], 16), "%s: peer buffer %d null or not 16-byte aligned",
+               what, r);
+    pp->p[r] = static_cast<uint16_t*>(ptrs[r]);
+  }
+  return MC_OK;
+}
+
+}  // namespace
+
+extern "C" int mc_ep_alloc(mc_ctx* ctx, size_t bytes, void** out) {
+  MC_REQUIRE(ctx && out && bytes > 0, "ep_alloc: bad arguments");
+  MC_CUDA(cudaMalloc(out, bytes));
+  return MC_OK;
+}
+
+extern "C" int mc_ep_free(mc_ctx* ctx, void* ptr) {
+  MC_REQUIRE(ctx, "ep_free: null context");
+  if (ptr) MC_CUDA(cudaFree(ptr));
+  return MC_OK;
+}
+
+extern "C" int mc_ipc_handle(mc_ctx* ctx, void* base, void* handle_out) {
+  MC_REQUIRE(ctx && base && handle_out, "ipc_handle: bad arguments");
+  cudaIpcMemHandle_t h;
+  MC_CUDA(cudaIpcGetMemHandle(&h, base));
+  memcpy(handle_out, &h, sizeof(h));
+  return MC_OK;
+}
+
+extern "C" int mc_ipc_open(mc_ctx* ctx, const void* handle, void** out) {
+  MC_REQUIRE(ctx && handle && out, "ipc_open: bad arguments");
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof(h));
+  MC_CUDA(cudaIpcOpenMemHandle(out, h, cudaIpcMemLazyEnablePeerAccess));
+  return MC_OK;
+}
+
+extern "C" int mc_ipc_close(mc_ctx* ctx, void* ptr) {
+  MC_REQUIRE(ctx, "ipc_close: null context");
+  if (ptr) MC_CUDA(cudaIpcCloseMemHandle(ptr));
+  return MC_OK;
+}
+
+extern "C" int mc_ep_dispatch(mc_ctx* ctx, const uint16_t* x, int m, int hidden,
+                              const uint32_t* ids_sorted, const uint32_t* counts_all, int rank,
+                              int world, int n_experts, void* const* recv_bufs,
+                              size_t recv_cap_rows, uint32_t* status) {
+  MC_REQUIRE(ctx && x && ids_sorted && counts_all, "ep_dispatch: null pointer");
+  int rc;
+  if ((rc = check_ranks(rank, world, n_experts, "ep_dispatch"))) return rc;
+  MC_REQUIRE(hidden > 0 && hidden % 8 == 0 && mc_aligned(x, 16), "ep_dispatch: rows");
+  PeerPtrs pp;
+  if ((rc = fill_peers(&pp, recv_bufs, world, "ep_dispatch"))) return rc;
+  MC_REQUIRE(m >= 1 && recv_cap_rows >= 1 && recv_cap_rows <= 0xffffffffu,
+             "ep_dispatch: m %d / capacity %zu", m, recv_cap_rows);
+  ep_dispatch_kernel<<<dim3(n_experts, 8), 256, 0, ctx->stream>>>(
+      reinterpret_cast<const uint4*>(x), m, hidden / 8, ids_sorted, counts_all, rank, world,
+      n_experts, pp, (uint32_t)recv_cap_rows, status);
+  return mc_after_launch("ep_dispatch_kernel");
+}
+
+extern "C" int mc_ep_return(mc_ctx* ctx, const uint16_t* ed, size_t ed_rows, int hidden,
+                            const uint32_t* counts_all, int rank, int world, int n_experts,
+                            void* const* home_bufs, size_t home_cap_rows, uint32_t* status) {
+  MC_REQUIRE(ctx && ed && counts_all, "ep_return: null pointer");
+  int rc;
+  if ((rc = check_ranks(rank, world, n_experts, "ep_return"))) return rc;
+  MC_REQUIRE(hidden > 0 && hidden % 8 == 0 && mc_aligned(ed, 16), "ep_return: rows");
+  PeerPtrs pp;
+  if ((rc = fill_peers(&pp, home_bufs, world, "ep_return"))) return rc;
+  MC_REQUIRE(ed_rows >= 1 && ed_rows <= 0xffffffffu && home_cap_rows >= 1 &&
+                 home_cap_rows <= 0xffffffffu,
+             "ep_return: rows %zu / capacity %zu", ed_rows, home_cap_rows);
+  ep_return_kernel<<<dim3(n_experts, 8), 256, 0, ctx->stream>>>(
+      reinterpret_cast<const uint4*>(ed), (uint32_t)ed_rows, hidden / 8, counts_all, rank, world,
+      n_experts, pp, (uint32_t)home_cap_rows, status);
+  return mc_after_launch("ep_return_kernel");
+}
+
+extern "C" int mc_ep_tiles(mc_ctx* ctx, const uint32_t* counts_all, int rank, int world,
+                           int n_experts, int bm, uint32_t* tiles, uint32_t* n_tiles,
+                           uint32_t* rows, int max_tiles) {
+  MC_REQUIRE(ctx && counts_all && tiles && n_tiles, "ep_tiles: null pointer");
+  int rc;
+  if ((rc = check_ranks(rank, world, n_experts, "ep_tiles"))) return rc;
+  MC_REQUIRE(bm >= 1 && bm <= 4096 && max_tiles >= 1 && mc_aligned(tiles, 16),
+             "ep_tiles: bm %d / max_tiles %d", bm, max_tiles);
+  ep_tiles_kernel<<<1, 256, 0, ctx->stream>>>(counts_all, rank, world, n_experts, bm,
+                                              reinterpret_cast<uint4*>(tiles), n_tiles, rows,
+                                              max_tiles);
+  return mc_after_launch("ep_tiles_kernel");
+}

@@ -223,3 +223,167 @@ def expert_slice(w, rank: int, world: int, n_experts: int):
     rows = w.codes.shape[0] // n_experts
     r0, r1 = rank * per * rows, (rank + 1) * per * rows
     return QuantWeights(w.codes[r0:r1], w.scales[r0:r1], w.biases[r0:r1], w.group_size, w.bits)
+
+
+# ----------------------------------------------------------- peer-memory exchange
+# The rows move by the library's own copy kernels straight into the other
+# ranks' buffers over NVLink (CUDA IPC mappings); the counts, the receive
+# layout and the GEMM row chunks are derived on the device from the gathered
+# counts, so a step needs no host synchronisation.
+
+class _DevBuf:
+    def __init__(self, ptr: int, nbytes: int):
+        self.__cuda_array_interface__ = {"shape": (nbytes // 2,), "typestr": "<i2",
+                                         "data": (ptr, False), "version": 3, "strides": None}
+
+
+def _rows_view(ptr: int, rows: int, hidden: int) -> torch.Tensor:
+    t = torch.as_tensor(_DevBuf(ptr, rows * hidden * 2), device="cuda")
+    return t.view(torch.bfloat16).view(rows, hidden)
+
+
+def _ptr_table(ptrs):
+    import ctypes as C
+    return (C.c_void_p * len(ptrs))(*ptrs)
+
+
+class PeerExchange:
+    """Receive and home row buffers of every rank, mapped into this process.
+    All ranks use the same capacities: receive = world * 4 * m_max rows (the
+    case of every pair routed to one rank), home = 4 * m_max rows."""
+
+    def __init__(self, ctx, rank: int, world: int, m_max: int, hidden: int, moe_inter: int,
+                 n_experts: int, group=None):
+        import ctypes as C
+        from molten_b200 import _lib
+        self.lib, self.ctx, self.rank, self.world, self.group = _lib, ctx, rank, world, group
+        self.H, self.E, self.per = hidden, n_experts, n_experts // world
+        self.recv_cap, self.home_cap = world * 4 * m_max, 4 * m_max
+        own = []
+        for rows in (self.recv_cap, self.home_cap):
+            p = C.c_void_p()
+            _lib.call("mc_ep_alloc", ctx.handle, rows * hidden * 2, C.byref(p))
+            own.append(p.value)
+        self.own = own
+        handles = []
+        for p in own:
+            h = (C.c_char * 64)()
+            _lib.call("mc_ipc_handle", ctx.handle, p, h)
+            handles.append(bytes(h))
+        every = [None] * world
+        dist.all_gather_object(every, handles, group=group)
+        self.opened = []
+        self.recv_ptrs, self.home_ptrs = [], []
+        for r in range(world):
+            for k, table in enumerate((self.recv_ptrs, self.home_ptrs)):
+                if r == rank:
+                    table.append(own[k])
+                else:
+                    p = C.c_void_p()
+                    hb = (C.c_char * 64).from_buffer_copy(every[r][k])
+                    _lib.call("mc_ipc_open", ctx.handle, hb, C.byref(p))
+                    self.opened.append(p.value)
+                    table.append(p.value)
+        self.recv = _rows_view(own[0], self.recv_cap, hidden)
+        self.home = _rows_view(own[1], self.home_cap, hidden)
+        dev = "cuda"
+        self.act = torch.empty((self.recv_cap, moe_inter), dtype=torch.bfloat16, device=dev)
+        self.ed = torch.empty((self.recv_cap, hidden), dtype=torch.bfloat16, device=dev)
+        self.max_tiles = self.recv_cap // CHUNK + self.per + 1
+        self.tiles = torch.zeros((self.max_tiles, 4), dtype=torch.int32, device=dev)
+        self.n_tiles = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.rows = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.counts_all = torch.zeros((world, n_experts), dtype=torch.int32, device=dev)
+        self.status = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.flag = torch.zeros(1, dtype=torch.int32, device=dev)
+        self._recv_tab, self._home_tab = _ptr_table(self.recv_ptrs), _ptr_table(self.home_ptrs)
+
+    def barrier(self):
+        """In-stream cross-rank barrier: every rank's earlier kernels finished."""
+        dist.all_reduce(self.flag, group=self.group)
+
+    def close(self):
+        torch.cuda.synchronize()
+        dist.barrier(group=self.group)
+        for p in self.opened:
+            self.lib.call("mc_ipc_close", self.ctx.handle, p)
+        self.opened = []
+        dist.barrier(group=self.group)
+        for p in self.own:
+            self.lib.call("mc_ep_free", self.ctx.handle, p)
+        self.own = []
+
+
+def moe_prefill_ep_peer(ops: "CudaOps", px: PeerExchange, x: torch.Tensor,
+                        logits: torch.Tensor) -> torch.Tensor:
+    """One expert-parallel step with the peer-memory exchange (no host sync)."""
+    lib, h = px.lib, px.ctx.handle
+    m, H = x.shape
+    ids, gw = ops.route(logits)
+    counts, slotpos, ids_sorted = ops.sort(ids, m)
+    dist.all_gather_into_tensor(px.counts_all.view(-1), counts.view(-1), group=px.group)
+    lib.call("mc_ep_tiles", h, px.counts_all.data_ptr(), px.rank, px.world, px.E, CHUNK,
+             px.tiles.data_ptr(), px.n_tiles.data_ptr(), px.rows.data_ptr(), px.max_tiles)
+    lib.call("mc_ep_dispatch", h, x.data_ptr(), m, H, ids_sorted.data_ptr(),
+             px.counts_all.data_ptr(), px.rank, px.world, px.E, px._recv_tab, px.recv_cap,
+             px.status.data_ptr())
+    px.barrier()
+    ops.lfm.gemm_q4_grouped_gu(ops.ctx, px.recv, ops.gate, ops.up, px.act, px.tiles, px.n_tiles,
+                               px.per, px.status)
+    ops.lfm.gemm_q4_grouped(ops.ctx, px.act, ops.down, px.ed, px.tiles, px.n_tiles, px.per,
+                            px.status)
+    lib.call("mc_ep_return", h, px.ed.data_ptr(), px.recv_cap, H, px.counts_all.data_ptr(),
+             px.rank, px.world, px.E, px._home_tab, px.home_cap, px.status.data_ptr())
+    px.barrier()
+    return ops.combine(px.home[:4 * m], slotpos, gw, m)
+
+
+def moe_prefill_ep_emulated(ctx, xs, logits, gate, up, down, n_experts: int):
+    """`world = len(xs)` ranks emulated on ONE GPU with the same device code as
+    moe_prefill_ep_peer (dispatch, row chunks, grouped GEMMs on each rank's
+    expert slice, return, combine), the ranks' kernels run one after another
+    so stream order stands in for the barriers. Returns every rank's output."""
+    from molten_b200 import _lib, lfm
+    world = len(xs)
+    E, per = n_experts, n_experts // world
+    m_max = max(x.shape[0] for x in xs)
+    H = xs[0].shape[1]
+    I = gate.out_features // E
+    recv_cap, home_cap = world * 4 * m_max, 4 * m_max
+    recv = [torch.zeros((recv_cap, H), dtype=torch.bfloat16, device="cuda") for _ in range(world)]
+    home = [torch.zeros((home_cap, H), dtype=torch.bfloat16, device="cuda") for _ in range(world)]
+    recv_tab = _ptr_table([t.data_ptr() for t in recv])
+    home_tab = _ptr_table([t.data_ptr() for t in home])
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    ops = [CudaOps(ctx, expert_slice(gate, r, world, E), expert_slice(up, r, world, E),
+                   expert_slice(down, r, world, E), E, r, world) for r in range(world)]
+    st = []
+    for r in range(world):
+        ids, gw = ops[r].route(logits[r])
+        counts, slotpos, ids_sorted = ops[r].sort(ids, xs[r].shape[0])
+        st.append((gw, counts, slotpos, ids_sorted))
+    counts_all = torch.stack([s[1] for s in st]).contiguous()
+    max_tiles = recv_cap // CHUNK + per + 1
+    eds = []
+    for r in range(world):
+        _lib.call("mc_ep_dispatch", ctx.handle, xs[r].data_ptr(), xs[r].shape[0], H,
+                  st[r][3].data_ptr(), counts_all.data_ptr(), r, world, E, recv_tab, recv_cap,
+                  status.data_ptr())
+    for r in range(world):
+        tiles = torch.zeros((max_tiles, 4), dtype=torch.int32, device="cuda")
+        n_tiles = torch.zeros(1, dtype=torch.int32, device="cuda")
+        _lib.call("mc_ep_tiles", ctx.handle, counts_all.data_ptr(), r, world, E, CHUNK,
+                  tiles.data_ptr(), n_tiles.data_ptr(), None, max_tiles)
+        act = torch.empty((recv_cap, I), dtype=torch.bfloat16, device="cuda")
+        ed = torch.empty((recv_cap, H), dtype=torch.bfloat16, device="cuda")
+        lfm.gemm_q4_grouped_gu(ctx, recv[r], ops[r].gate, ops[r].up, act, tiles, n_tiles, per,
+                               status)
+        lfm.gemm_q4_grouped(ctx, act, ops[r].down, ed, tiles, n_tiles, per, status)
+        eds.append(ed)
+    for r in range(world):
+        _lib.call("mc_ep_return", ctx.handle, eds[r].data_ptr(), recv_cap, H, counts_all.data_ptr(),
+                  r, world, E, home_tab, home_cap, status.data_ptr())
+    outs = [ops[r].combine(home[r][:4 * xs[r].shape[0]], st[r][2], st[r][0], xs[r].shape[0])
+            for r in range(world)]
+    torch.cuda.synchronize()
+    return outs, int(status.cpu()[0])
