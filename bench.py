@@ -56,6 +56,8 @@ def parse():
     p.add_argument("--impl", choices=["molten", "reference"], default="molten")
     p.add_argument("--workload", choices=["cfg0", "cfg1", "cfg2", "cfg3"], default="cfg1")
     p.add_argument("--tokens", type=int, default=4096, help="cfg3 prefill chunk")
+    p.add_argument("--ep-placement", choices=["balanced", "contiguous"], default="balanced",
+                   help="cfg3 on N>1 GPUs: expert-to-GPU placement")
     p.add_argument("--ep-exchange", choices=["peer", "nccl"], default="peer",
                    help="cfg3 on N>1 GPUs: rows over NVLink peer memory or NCCL point-to-point")
     p.add_argument("--seed", type=int, default=0)
@@ -77,6 +79,8 @@ def dist_setup(n):
     if ws > 1:
         import datetime
         import torch.distributed as dist
+        if os.environ.get("NCCL_DEBUG", "VERSION").upper() == "VERSION":
+            os.environ["NCCL_DEBUG"] = "WARN"  # keep stdout to the one JSON line
         torch.cuda.set_device(local)
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local))
@@ -565,8 +569,6 @@ def bench_cfg3_ep(args, torch, ws, rank, local):
     gen = torch.Generator(device="cuda")
     gen.manual_seed(args.seed * 1000 + 3)          # same expert weights on every rank
     layer = synth.moe_layer_torch(gen, "cuda")
-    sl = {k: ep.expert_slice(layer[k], rank, ws, E) for k in ("gate", "up", "down")}
-    del layer
     m = args.tokens
     tg = torch.Generator(device="cuda")
     tg.manual_seed(args.seed * 1000 + 100 + rank)  # each rank its own tokens
@@ -574,7 +576,19 @@ def bench_cfg3_ep(args, torch, ws, rank, local):
     pg.manual_seed(args.seed * 1000 + 7)           # one expert popularity order for all
     x = torch.randn((m, H), generator=tg, device="cuda").to(torch.bfloat16)
     logits = zipf_logits_torch(torch, tg, m, perm_gen=pg)
-    ops = ep.CudaOps(ctx, sl["gate"], sl["up"], sl["down"], E, rank, ws)
+    if args.ep_placement == "balanced":
+        # one routing pass measures the expert load; the placement is fixed from then on
+        probe = ep.CudaOps(ctx, None, None, None, E, rank, ws)
+        ids, _ = probe.route(logits)
+        counts, _, _ = probe.sort(ids, m)
+        load = ep.gather_counts(counts, ws).sum(axis=0)
+        table, experts = ep.place_experts(load, ws)
+        sl = {k: ep.placed_slice(layer[k], experts[rank], E) for k in ("gate", "up", "down")}
+        ops = ep.CudaOps(ctx, sl["gate"], sl["up"], sl["down"], E, rank, ws, placement=table)
+    else:
+        sl = {k: ep.expert_slice(layer[k], rank, ws, E) for k in ("gate", "up", "down")}
+        ops = ep.CudaOps(ctx, sl["gate"], sl["up"], sl["down"], E, rank, ws)
+    del layer
     px = None
     if args.ep_exchange == "peer":
         px = ep.PeerExchange(ctx, rank, ws, m, H, I, E)
@@ -641,6 +655,8 @@ def bench_cfg3_ep(args, torch, ws, rank, local):
         "config": {"workload": f"cfg3 expert-parallel: {m} tokens per rank x 2048, E=64 top-4 "
                                f"({E // ws} experts per GPU), SwiGLU 2048->1536->2048 Q4",
                    "parallelism": f"ep{ws}",
+                   "placement": ("greedy by the expert load of one routing pass"
+                                 if args.ep_placement == "balanced" else "contiguous ranges"),
                    "exchange": ("rows copied into the owners' buffers over NVLink peer memory "
                                 "(CUDA IPC), in-stream NCCL barriers, no host sync"
                                 if px is not None else "NCCL point-to-point rows both ways"),

@@ -273,6 +273,11 @@ int mc_moe_prefill(mc_ctx* ctx, const uint16_t* x, const float* logits, int m,
  * sender's copy finished). status (nullable u32) bit 2: rows beyond a
  * capacity were skipped (inconsistent counts). */
 
+/* Relabels expert ids[n] in place through table[n_experts] (an expert
+ * placement: model expert -> position in the rank-contiguous order). Ids out
+ * of range stay and set status bit 1. */
+int mc_map_ids(mc_ctx* ctx, uint32_t* ids, size_t n, const uint32_t* table, int n_experts,
+               uint32_t* status);
 /* Device memory whose base can be shared with other processes (cudaMalloc). */
 int mc_ep_alloc(mc_ctx* ctx, size_t bytes, void** out);
 int mc_ep_free(mc_ctx* ctx, void* ptr);

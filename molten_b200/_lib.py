@@ -71,6 +71,7 @@ SIGNATURES: dict[str, tuple] = {
     "mc_moe_decode_layer": (I, [P, P, P, P, P, P, P, I, P, I, P, P, P, QP, QP, QP, I, P, P,
                                 C.c_size_t, F, F]),
     "mc_moe_decode_workspace_words": (C.c_size_t, [I]),
+    "mc_map_ids": (I, [P, P, C.c_size_t, P, I, P]),
     "mc_ep_alloc": (I, [P, C.c_size_t, C.POINTER(C.c_void_p)]),
     "mc_ep_free": (I, [P, P]),
     "mc_ipc_handle": (I, [P, P, P]),

@@ -317,3 +317,32 @@ extern "C" int mc_moe_prefill(mc_ctx* ctx, const uint16_t* x, const float* logit
     return rc;
   return mc_moe_combine_rows(ctx, B16(w.ed), U32(w.slotpos), B16(w.gw), out, m, 4, H);
 }
+
+namespace {
+__global__ void __launch_bounds__(256)
+map_ids_kernel(uint32_t* __restrict__ ids, size_t n, const uint32_t* __restrict__ table, int E,
+               uint32_t* __restrict__ status) {
+  for (size_t i = (size_t)blockIdx.x * 256 + threadIdx.x; i < n; i += (size_t)gridDim.x * 256) {
+    const uint32_t v = ids[i];
+    if (v < (uint32_t)E) {
+      ids[i] = __ldg(table + v);
+    } else if (status) {
+      atomicOr(status, 2u);
+    }
+  }
+}
+}  // namespace
+
+// Relabels expert ids in place through table[E] (an expert placement): the
+// expert-parallel path routes on the model's expert numbering and sorts by
+// the placement's, so any assignment of experts to ranks keeps each rank's
+// experts contiguous. Ids out of range are left as they are and flagged.
+extern "C" int mc_map_ids(mc_ctx* ctx, uint32_t* ids, size_t n, const uint32_t* table,
+                          int n_experts, uint32_t* status) {
+  MC_REQUIRE(ctx && ids && table && n_experts >= 1, "map_ids: bad arguments");
+  if (n == 0) return MC_OK;
+  const size_t blocks = (n + 255) / 256, cap = (size_t)ctx->num_sms * 4;
+  const int grid = (int)(blocks < cap ? blocks : cap);
+  map_ids_kernel<<<grid, 256, 0, ctx->stream>>>(ids, n, table, n_experts, status);
+  return mc_after_launch("map_ids_kernel");
+}

@@ -165,19 +165,28 @@ class CudaOps(Ops):
     """The CUDA kernels of molten_b200 (C ABI) on this rank's expert slice."""
 
     def __init__(self, ctx, gate, up, down, n_experts: int, rank: int, world: int,
-                 route_mode: int = 0, bias=None):
-        from molten_b200 import lfm
-        self.lfm, self.ctx = lfm, ctx
+                 route_mode: int = 0, bias=None, placement=None):
+        """gate/up/down: this rank's experts only (in placement order when a
+        placement table -- model expert -> position, see place_experts -- is
+        given; contiguous expert ranges otherwise)."""
+        from molten_b200 import _lib, lfm
+        self.lfm, self.lib, self.ctx = lfm, _lib, ctx
         self.E, self.per = n_experts, n_experts // world
-        self.gate, self.up, self.down = gate, up, down   # this rank's experts only
+        self.gate, self.up, self.down = gate, up, down
         self.route_mode, self.bias = route_mode, bias
         self.status = torch.zeros(1, dtype=torch.int32, device="cuda")
+        self.table = None
+        if placement is not None:
+            self.table = torch.from_numpy(np.asarray(placement, np.uint32).view(np.int32)).cuda()
 
     def route(self, logits):
         m = logits.shape[0]
         ids = torch.zeros((m, 4), dtype=torch.int32, device="cuda")
         gw = torch.empty((m, 4), dtype=torch.bfloat16, device="cuda")
         self.lfm.moe_route_batch(self.ctx, logits, self.bias, ids, gw, m, route_mode=self.route_mode)
+        if self.table is not None:  # route on model ids, sort by placement position
+            self.lib.call("mc_map_ids", self.ctx.handle, ids.data_ptr(), ids.numel(),
+                          self.table.data_ptr(), self.E, self.status.data_ptr())
         return ids, gw
 
     def sort(self, ids, m):
@@ -214,6 +223,40 @@ class CudaOps(Ops):
         out = torch.empty((m, ed.shape[1]), dtype=torch.bfloat16, device="cuda")
         self.lfm.moe_combine_rows(self.ctx, ed, slotpos, gw, out)
         return out
+
+
+def place_experts(load, world: int):
+    """Skew-aware expert placement: experts by decreasing measured load, each
+    to the rank with the least load so far among those with a free slot
+    (every rank gets E/world experts; ties go to the lower rank). Returns
+    (table[e] = position of model expert e in the rank-contiguous order,
+    experts[r] = the model experts of rank r in position order)."""
+    load = np.asarray(load, dtype=np.float64)
+    E = load.shape[0]
+    if E % world:
+        raise ValueError(f"{E} experts do not split over {world} ranks")
+    per = E // world
+    rank_load = np.zeros(world)
+    experts = [[] for _ in range(world)]
+    for e in np.argsort(-load, kind="stable"):
+        free = [r for r in range(world) if len(experts[r]) < per]
+        r = min(free, key=lambda q: (rank_load[q], q))
+        experts[r].append(int(e))
+        rank_load[r] += load[e]
+    table = np.zeros(E, np.uint32)
+    for r in range(world):
+        for j, e in enumerate(experts[r]):
+            table[e] = r * per + j
+    return table, experts
+
+
+def placed_slice(w, experts, n_experts: int):
+    """The stacked rows of `experts` (in that order) of a [E*N][K] QuantWeights
+    (a copy: a placement's experts need not be adjacent)."""
+    from molten_b200.quant import QuantWeights
+    rows = w.codes.shape[0] // n_experts
+    pick = lambda t: torch.cat([t[e * rows:(e + 1) * rows] for e in experts]).contiguous()
+    return QuantWeights(pick(w.codes), pick(w.scales), pick(w.biases), w.group_size, w.bits)
 
 
 def expert_slice(w, rank: int, world: int, n_experts: int):
@@ -338,7 +381,7 @@ def moe_prefill_ep_peer(ops: "CudaOps", px: PeerExchange, x: torch.Tensor,
     return ops.combine(px.home[:4 * m], slotpos, gw, m)
 
 
-def moe_prefill_ep_emulated(ctx, xs, logits, gate, up, down, n_experts: int):
+def moe_prefill_ep_emulated(ctx, xs, logits, gate, up, down, n_experts: int, placement=None):
     """`world = len(xs)` ranks emulated on ONE GPU with the same device code as
     moe_prefill_ep_peer (dispatch, row chunks, grouped GEMMs on each rank's
     expert slice, return, combine), the ranks' kernels run one after another
@@ -355,8 +398,14 @@ def moe_prefill_ep_emulated(ctx, xs, logits, gate, up, down, n_experts: int):
     recv_tab = _ptr_table([t.data_ptr() for t in recv])
     home_tab = _ptr_table([t.data_ptr() for t in home])
     status = torch.zeros(1, dtype=torch.int32, device="cuda")
-    ops = [CudaOps(ctx, expert_slice(gate, r, world, E), expert_slice(up, r, world, E),
-                   expert_slice(down, r, world, E), E, r, world) for r in range(world)]
+    if placement is None:
+        ops = [CudaOps(ctx, expert_slice(gate, r, world, E), expert_slice(up, r, world, E),
+                       expert_slice(down, r, world, E), E, r, world) for r in range(world)]
+    else:
+        table, experts = placement
+        ops = [CudaOps(ctx, placed_slice(gate, experts[r], E), placed_slice(up, experts[r], E),
+                       placed_slice(down, experts[r], E), E, r, world, placement=table)
+               for r in range(world)]
     st = []
     for r in range(world):
         ids, gw = ops[r].route(logits[r])
@@ -386,4 +435,6 @@ def moe_prefill_ep_emulated(ctx, xs, logits, gate, up, down, n_experts: int):
     outs = [ops[r].combine(home[r][:4 * xs[r].shape[0]], st[r][2], st[r][0], xs[r].shape[0])
             for r in range(world)]
     torch.cuda.synchronize()
+    for o in ops:
+        status |= o.status
     return outs, int(status.cpu()[0])

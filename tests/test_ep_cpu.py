@@ -141,3 +141,24 @@ def test_two_rank_gloo_matches_one_device_oracle():
         p.join(timeout=60)
     for rank, ok, info in sorted(results, key=lambda t: t[0]):
         assert ok, f"rank {rank}: {info}"
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_placement_balances_zipf_load(world):
+    """Greedy placement: every rank gets E/world distinct experts, and on a
+    Zipf load the heaviest rank carries less than with contiguous ranges."""
+    E = 64
+    g = synth.rng(700 + world)
+    load = 1.0 / (1 + g.permutation(E))            # Zipf(1) over a random order
+    table, experts = ep.place_experts(load, world)
+    assert sorted(table.tolist()) == list(range(E))
+    per = E // world
+    for r, ex in enumerate(experts):
+        assert len(ex) == per
+        for j, e in enumerate(ex):
+            assert table[e] == r * per + j
+    placed = max(load[ex].sum() for ex in experts)
+    contiguous = max(load[r * per:(r + 1) * per].sum() for r in range(world))
+    assert placed <= contiguous + 1e-12
+    # a bound of greedy packing: within the heaviest expert of the ideal share
+    assert placed <= load.sum() / world + load.max() + 1e-12

@@ -26,8 +26,11 @@ def _case(seed_w, seeds, ms, E, I, H=2048):
     return gate, up, down, toks
 
 
-@pytest.mark.parametrize("world,ms", [(2, (48, 30)), (4, (64, 17, 40, 5))])
-def test_ep_peer_kernels_emulated_on_one_gpu(cuda_ctx, world, ms):
+@pytest.mark.parametrize("world,ms,placed", [(2, (48, 30), False), (4, (64, 17, 40, 5), False),
+                                              (4, (64, 33, 20, 50), True)])
+def test_ep_peer_kernels_emulated_on_one_gpu(cuda_ctx, world, ms, placed):
+    """placed: a load-balanced expert placement (experts no longer in
+    contiguous ranges, ids relabelled on the device before sorting)."""
     import oracle
     from molten_b200 import ep, synth
     from tests.gpu_util import dev_qw
@@ -36,8 +39,16 @@ def test_ep_peer_kernels_emulated_on_one_gpu(cuda_ctx, world, ms):
     gate, up, down, toks = _case(950, [960 + r for r in range(world)], ms, E, I)
     xs = [synth.bf16_tensor(x).cuda() for x, _ in toks]
     lg = [torch.from_numpy(l).cuda() for _, l in toks]
+    placement = None
+    if placed:
+        load = np.zeros(E)
+        for _, l in toks:
+            ids, _ = oracle.moe_route_batch(l)
+            load += np.bincount(ids.ravel(), minlength=E)
+        placement = ep.place_experts(load, world)
+        assert placement[0].tolist() != list(range(E))
     outs, status = ep.moe_prefill_ep_emulated(cuda_ctx, xs, lg, dev_qw(*gate), dev_qw(*up),
-                                              dev_qw(*down), E)
+                                              dev_qw(*down), E, placement)
     assert status == 0
     for r, (x, l) in enumerate(toks):
         want = oracle.moe_prefill(x, l, gate, up, down, n_experts=E)
