@@ -54,7 +54,9 @@ def parse():
     p.add_argument("--steps", type=int, default=20000)
     p.add_argument("--warmup", type=int, default=200)
     p.add_argument("--impl", choices=["molten", "reference"], default="molten")
-    p.add_argument("--workload", choices=["cfg0", "cfg1", "cfg2", "cfg3"], default="cfg1")
+    p.add_argument("--workload", choices=["cfg0", "cfg1", "cfg2", "cfg3", "cfg4"], default="cfg1")
+    p.add_argument("--batch", type=int, default=1, help="cfg4 decode batch (1, 8, 32)")
+    p.add_argument("--layers", type=int, default=40, help="cfg4 stacked layers")
     p.add_argument("--tokens", type=int, default=4096, help="cfg3 prefill chunk")
     p.add_argument("--ep-placement", choices=["balanced", "contiguous"], default="balanced",
                    help="cfg3 on N>1 GPUs: expert-to-GPU placement")
@@ -765,6 +767,162 @@ def bench_cfg3(args, torch, ws, rank, local):
     return res
 
 
+# ------------------------------------------------------------------ cfg4
+
+VOCAB = 65536
+
+
+def cpu_baseline_cfg4(torch, layers, head, embed, n_layers, seconds):
+    """The CPU port on the same stack: per token, L x (Q4 projection + MoE
+    layer) + the Q6 head argmax, OpenMP on all host cores."""
+    import ctypes as C
+    import numpy as np
+    from oracle import build as obuild
+    _, fast = obuild.build()
+    Lb = C.CDLL(str(fast))
+    Lb.of_set_threads(os.cpu_count() or 1)
+    Lb.of_head_q6_argmax.restype = C.c_uint32
+    nthreads = Lb.of_threads()
+    host = lambda t: np.ascontiguousarray(t.detach().cpu().view(torch.int16).numpy()
+                                          if t.dtype == torch.bfloat16 else t.detach().cpu().numpy())
+    P = lambda a: a.ctypes.data_as(C.c_void_p)
+    hl = []
+    for l in layers[:2]:  # two layers' weights, reused round robin (bounded host memory)
+        hl.append({k: host(l[k]) for k in ("norm_w", "router")} |
+                  {k: (host(l[k].codes), host(l[k].scales), host(l[k].biases))
+                   for k in ("gate", "up", "down", "proj")})
+    hh = (host(head.codes), host(head.scales), host(head.biases))
+    emb = host(embed[:VOCAB])
+    x = emb[1].copy()
+    p = np.zeros(H, np.uint16); hout = np.zeros(H, np.uint16); out = np.zeros(H, np.uint16)
+    ids = np.zeros(4, np.uint32); wts = np.zeros(4, np.uint16)
+    def token():
+        nonlocal x
+        for l in range(n_layers):
+            a = hl[l % len(hl)]
+            Lb.of_gemv_q4(*(P(t) for t in a["proj"]), H, H, P(x), P(p))
+            Lb.of_moe_decode_layer(P(x), P(p), P(a["norm_w"]), P(a["router"]),
+                                   *(P(t) for t in a["gate"]), *(P(t) for t in a["up"]),
+                                   *(P(t) for t in a["down"]), E, H, I, C.c_float(1e-5),
+                                   P(hout), P(ids), P(wts), P(out))
+            x = out.copy()
+        tok = Lb.of_head_q6_argmax(P(hh[0]), P(hh[1]), P(hh[2]), VOCAB, H, P(x))
+        x = emb[tok % VOCAB].copy()
+    token()
+    t0 = time.perf_counter()
+    n = 0
+    while n == 0 or time.perf_counter() - t0 < seconds:
+        token()
+        n += 1
+    dt = time.perf_counter() - t0
+    return {"value": round(n / dt, 3), "unit": "tokens/s", "cores": nthreads, "kind": "port",
+            "sample": f"{n} tokens of the {n_layers}-layer stack at batch 1 ({dt:.1f} s), "
+                      "oracle/mc_oracle_fast.c -O3 OpenMP (two layers' weights reused)"}
+
+
+def bench_cfg4(args, torch, ws, rank, local):
+    """cfg4: L x (Q4 2048x2048 projection + cfg1 MoE layer) + Q6 head argmax +
+    token tail with the embedding gather, one decode step captured in a CUDA
+    graph and replayed; tokens fed back on the device."""
+    from molten_b200 import lfm, synth
+    from molten_b200.stack import DecodeStack
+    ctx = lfm.Context(local)
+    B, L = args.batch, args.layers
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(args.seed * 1000 + 4 + rank)
+    layers = []
+    for _ in range(L):
+        d = synth.moe_layer_torch(gen, "cuda")
+        d["proj"] = synth.quant_weights_torch(gen, H, H, 4)
+        layers.append(d)
+    # the head's 6-bit codes centred on zero (bias = -31.5 scale): with BASELINE's
+    # bias = -8 scale every head row has a large positive mean, the argmax then
+    # hardly depends on the hidden state and all sequences of a batch collapse
+    # onto one token (one routing for the whole batch)
+    head = synth.quant_weights_torch(gen, VOCAB, H, 6, centre=31.5)
+    embed = torch.randn((VOCAB, H), generator=gen, device="cuda").to(torch.bfloat16)
+    st = DecodeStack(ctx, layers, head, embed, B)
+    st.start((torch.arange(B, device="cuda", dtype=torch.int32) * 7919 + 11) % VOCAB)
+    K = min(args.steps, 512)
+    W = max(min(args.warmup, 8), 3)
+    for _ in range(W):
+        st.step()
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    cs = torch.cuda.Stream()
+    cs.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(cs):
+        with torch.cuda.graph(g, stream=cs):
+            st.step()
+    torch.cuda.current_stream().wait_stream(cs)
+    g.replay()
+    torch.cuda.synchronize()
+    barrier(ws)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        a.record()
+        for _ in range(K):
+            g.replay()
+        b.record()
+        torch.cuda.synchronize()
+    ms_ = max_over_ranks(ws, a.elapsed_time(b))
+    step_ms = ms_ / K
+    # bytes of the step: measured distinct experts per layer (last step's routing)
+    U = [int(torch.unique(st.ids[l]).numel()) for l in range(L)]
+    step_bytes = (L * (GEMV_BYTES + ROUTER_BYTES + B * 12 * 1024) + sum(U) * EXPERT_BYTES
+                  + HEAD_BYTES + B * H * 2)
+    value = ws * B * K / (ms_ * 1e-3)
+    gbs = step_bytes / (step_ms * 1e-3) / 1e9
+    hbm, _, src = peaks()
+    # e2e: the public step call eagerly, the first tokens from pinned host memory
+    # and every step's tokens read back to the host
+    htok = torch.empty(B, dtype=torch.int32).pin_memory()
+    hstart = ((torch.arange(B, dtype=torch.int32) * 7919 + 11) % VOCAB).pin_memory()
+    dstart = torch.empty(B, dtype=torch.int32, device="cuda")
+    n_e2e = min(K, 32)
+    torch.cuda.synchronize()
+    barrier(ws)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    dstart.copy_(hstart, non_blocking=True)
+    st.start(dstart)
+    for _ in range(n_e2e):
+        st.step()
+        htok.copy_(st.tokens, non_blocking=True)
+    e1.record()
+    torch.cuda.synchronize()
+    e2e_ms = max_over_ranks(ws, e0.elapsed_time(e1))
+    res = {
+        "metric": f"stacked decode tokens/s (cfg4: {L} x (Q4 proj + MoE layer) + Q6 head, "
+                  f"batch {B})",
+        "value": round(value, 1), "unit": "tokens/s", "n_gpus": ws, "steps": K, "warmup": W,
+        "ms_per_step": round(step_ms, 4), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "q4/q6 codes, bf16 activations, fp32 accumulate",
+        "data": "synthetic (seeded, BASELINE cfg4 shapes; random-init weights per layer; head "
+                "codes centred: bias = -31.5 scale)",
+        "config": {"workload": f"cfg4: {L} layers x (Q4 2048x2048 + E=64 top-4 SwiGLU 2048->1536"
+                               f"->2048) + Q6 65536x2048 head + bf16 embedding gather, batch {B}, "
+                               "one step per CUDA-graph replay",
+                   "batch": B, "gbs": round(gbs, 1), "bytes_per_step": step_bytes,
+                   "distinct_experts_per_layer_mean": round(sum(U) / L, 2),
+                   "l2": f"inputs > L2: {L} layers of weights ({L * 0.342:.1f} GB) streamed per step",
+                   "parallelism": f"replicas x{ws}" if ws > 1 else "single GPU"},
+        "e2e": {"value": round(ws * B * n_e2e / (e2e_ms * 1e-3), 1), "unit": "tokens/s",
+                "h2d_bytes_per_step": B * 4, "d2h_bytes_per_step": B * 4,
+                "note": "eager step calls through molten_b200.stack (no graph), first tokens "
+                        "from pinned host memory, every step's tokens read back"},
+        "roofline": {"bound": "hbm", "kernel": "whole decode step (all layers + head)",
+                     "achieved": round(gbs, 1), "peak": hbm, "unit": "GB/s",
+                     "frac": round(gbs / hbm, 4), "peak_source": f"{src} hbm_gbs",
+                     "traffic": None},
+        "gpu_launches": st.launches_per_step() * K,
+        "clocks": clk.summary(),
+    }
+    if rank == 0 and ws == 1 and not args.no_cpu_baseline and B == 1:
+        res["cpu_baseline"] = cpu_baseline_cfg4(torch, layers, head, embed, L, args.cpu_seconds)
+    return res
+
+
 # ------------------------------------------------------------------ reference arm
 
 def bench_reference(args, ws, rank):
@@ -813,6 +971,8 @@ def main():
             res = bench_cfg1(args, torch, ws, rank, local)
         elif args.workload == "cfg3":
             res = bench_cfg3(args, torch, ws, rank, local)
+        elif args.workload == "cfg4":
+            res = bench_cfg4(args, torch, ws, rank, local)
         else:
             res = bench_gemv(args, torch, ws, rank, local, head=args.workload == "cfg2")
         if rank == 0:

@@ -1,0 +1,82 @@
+"""The stacked decode loop of BASELINE cfg4 on the decode kernels.
+
+One decode step for a batch of B tokens (rows x [B, 2048], each the
+embedding row of the token being decoded):
+
+    for each of the L layers:
+        p   = proj_l(x)                             Q4 2048x2048 GEMV (gemv_quant)
+        out = MoE_l(h = x, b = p)                   add + RMSNorm + router + top-4 +
+                                                    SwiGLU experts + weighted combine
+        x   = out
+    key   = argmax over the Q6 LM head of x         gemv_head_argmax
+    token = key's index; x = embed[token]           token_tail (reads and clears key)
+
+The MoE layer normalises its input (RMSNorm of h + b) before the router and
+the experts, so activations stay bounded over the stack without a separate
+residual stream. B = 1 uses the one-launch fused layer (moe_decode_layer);
+B > 1 the three batched kernels (router_addnorm_route, gemv_gather_act,
+gemv_gather_down_combine4). The token feeds back on the device, so a step
+can be captured once in a CUDA graph and replayed.
+"""
+from __future__ import annotations
+
+import torch
+
+from molten_b200 import lfm
+
+
+class DecodeStack:
+    def __init__(self, ctx: lfm.Context, layers: list[dict], head, embed: torch.Tensor,
+                 batch: int, n_experts: int = 64):
+        self.ctx, self.layers, self.head, self.embed = ctx, layers, head, embed
+        self.B, self.E = batch, n_experts
+        H = embed.shape[1]
+        I = layers[0]["gate"].out_features // n_experts
+        dev = embed.device
+        bf = lambda *s: torch.empty(s, dtype=torch.bfloat16, device=dev)
+        i32 = lambda *s: torch.zeros(s, dtype=torch.int32, device=dev)
+        self.x = bf(batch, H)                    # step input: embedding rows
+        self.p, self.hout, self.normed = bf(batch, H), bf(batch, H), bf(batch, H)
+        self.outs = (bf(batch, H), bf(batch, H))
+        self.logits = torch.empty((batch, n_experts), dtype=torch.float32, device=dev)
+        self.ids = [i32(batch, 4) for _ in layers]
+        self.wts = [bf(batch, 4) for _ in layers]
+        self.counter = i32(batch)
+        self.act = bf(batch, 4, I)
+        self.keys = torch.zeros(batch, dtype=torch.int64, device=dev)
+        self.tokens = i32(batch)
+        self.tail_norm_w = torch.ones(H, dtype=torch.bfloat16, device=dev)
+        self.tail_normed = bf(batch, H)
+        self.ws = None
+        if batch == 1:
+            self.ws = torch.zeros(lfm.moe_decode_workspace_words(I), dtype=torch.int32, device=dev)
+
+    def start(self, tokens: torch.Tensor) -> None:
+        """Loads the embedding rows of the first tokens (int32 [B])."""
+        self.x.copy_(self.embed[tokens.long()])
+
+    def step(self) -> None:
+        ctx, cur = self.ctx, self.x
+        for l, L in enumerate(self.layers):
+            lfm.gemv_quant(ctx, L["proj"], cur, self.p)
+            nxt = self.outs[l % 2]
+            if self.B == 1:
+                lfm.moe_decode_layer(ctx, cur, self.p, L["norm_w"], self.hout, self.normed,
+                                     L["router"], self.logits, None, self.ids[l], self.wts[l],
+                                     L["gate"], L["up"], L["down"], nxt, self.ws,
+                                     n_experts=self.E)
+            else:
+                lfm.router_addnorm_route(ctx, cur, self.p, L["norm_w"], self.hout, self.normed,
+                                         L["router"], self.logits, None, self.ids[l],
+                                         self.wts[l], self.counter)
+                lfm.gemv_gather_act(ctx, L["gate"], L["up"], self.normed, self.ids[l], self.act,
+                                    n_experts=self.E)
+                lfm.gemv_gather_down_combine4(ctx, L["down"], self.act, self.ids[l], self.wts[l],
+                                              nxt, n_experts=self.E)
+            cur = nxt
+        lfm.gemv_head_argmax(ctx, self.head, cur, self.keys)
+        lfm.token_tail(ctx, self.keys, self.tokens,
+                       (self.embed, self.tail_norm_w, self.x, self.tail_normed))
+
+    def launches_per_step(self) -> int:
+        return len(self.layers) * (2 if self.B == 1 else 4) + 2

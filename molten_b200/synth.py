@@ -103,14 +103,16 @@ def zipf_logits_np(g: np.random.Generator, m: int, e: int = N_EXPERTS, s: float 
 # ----------------------------------------------------------- device-side gen
 
 def quant_weights_torch(gen: torch.Generator, out: int, inp: int, bits: int = 4,
-                        device="cuda") -> QuantWeights:
-    """Same distributions as quant_weights_np, generated on the device."""
+                        device="cuda", centre: float = 8.0) -> QuantWeights:
+    """Same distributions as quant_weights_np, generated on the device. `centre`
+    sets bias = -centre * scale + N(0, 1e-3): 8 as BASELINE states for every
+    config; 31.5 centres 6-bit codes (0..63) on zero."""
     words = inp * bits // 32
     codes = torch.randint(-2**31, 2**31 - 1, (out, words), generator=gen, device=device,
                           dtype=torch.int64).to(torch.int32)
     s = torch.empty((out, inp // 64), device=device).uniform_(0.002, 0.02, generator=gen)
     s = s.to(torch.bfloat16)
-    b = (-8.0 * s.float() + torch.randn(s.shape, generator=gen, device=device) * 1e-3)
+    b = (-centre * s.float() + torch.randn(s.shape, generator=gen, device=device) * 1e-3)
     return QuantWeights(codes, s, b.to(torch.bfloat16), 64, bits)
 
 

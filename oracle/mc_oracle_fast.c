@@ -234,3 +234,45 @@ void of_moe_prefill(const uint16_t* x, const float* logits, int m, int E, int H,
   free(ids); free(w); free(counts); free(offsets); free(sorted); free(slot); free(gx);
   free(g); free(u); free(ed); free(pos);
 }
+
+/* Q6 LM head GEMV + argmax over bf16-rounded logits, lowest index on ties
+ * (lfm.metal:1200-1282): the CPU baseline's head for BASELINE cfg4. Codes are
+ * 4 per 3 bytes, little-endian, K*6/8 bytes per row. */
+uint32_t of_head_q6_argmax(const uint8_t* codes, const uint16_t* s, const uint16_t* b, int N, int K,
+                           const uint16_t* xb) {
+  float* x = (float*)malloc(sizeof(float) * K);
+  float* xg = (float*)malloc(sizeof(float) * (K / 64));
+  prep_x(xb, K, x, xg);
+  const int G = K / 64, rb = K * 6 / 8;
+  float best_v = -INFINITY;
+  int best_i = 0;
+#pragma omp parallel
+  {
+    float bv = -INFINITY;
+    int bi = 0;
+#pragma omp for schedule(static)
+    for (int n = 0; n < N; ++n) {
+      const uint8_t* r = codes + (size_t)n * rb;
+      float acc = 0.0f;
+      for (int g = 0; g < G; ++g) {
+        const uint8_t* p = r + 48 * g;
+        const float* xx = x + 64 * g;
+        float qx = 0.0f;
+        for (int t = 0; t < 16; ++t) {
+          const uint32_t b0 = p[3 * t], b1 = p[3 * t + 1], b2 = p[3 * t + 2];
+          qx += (float)(b0 & 63u) * xx[4 * t] + (float)((b0 >> 6) | ((b1 & 15u) << 2)) * xx[4 * t + 1] +
+                (float)((b1 >> 4) | ((b2 & 3u) << 4)) * xx[4 * t + 2] + (float)(b2 >> 2) * xx[4 * t + 3];
+        }
+        acc += bf(s[(size_t)n * G + g]) * qx + bf(b[(size_t)n * G + g]) * xg[g];
+      }
+      const float v = rbf(acc);
+      if (v > bv || (v == bv && n < bi)) { bv = v; bi = n; }
+    }
+#pragma omp critical
+    {
+      if (bv > best_v || (bv == best_v && bi < best_i)) { best_v = bv; best_i = bi; }
+    }
+  }
+  free(x); free(xg);
+  return (uint32_t)best_i;
+}

@@ -1,0 +1,75 @@
+"""BASELINE cfg4's stacked decode loop (molten_b200.stack) on a small stack:
+every step's argmax tokens equal the CPU oracle's bit for bit, eagerly and
+when one step is captured in a CUDA graph and replayed (token fed back on the
+device)."""
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from molten_b200 import synth
+from molten_b200.stack import DecodeStack
+from tests.gpu_util import dev_bf16, dev_qw
+
+pytestmark = pytest.mark.gpu
+
+H = 2048
+
+
+def make_stack(seed, L, E, I, V):
+    g = synth.rng(seed)
+    layers = []
+    for _ in range(L):
+        layers.append(dict(proj=synth.quant_weights_np(g, H, H), norm_w=synth.norm_weight_np(g),
+                           router=synth.router_np(g, E), gate=synth.quant_weights_np(g, E * I, H),
+                           up=synth.quant_weights_np(g, E * I, H),
+                           down=synth.quant_weights_np(g, E * H, I)))
+    head = synth.quant_weights_np(g, V, H, 6)
+    embed = synth.activations_np(g, V, H)
+    return layers, head, embed
+
+
+def oracle_tokens(layers, head, embed, toks, steps, E):
+    out = []
+    for _ in range(steps):
+        x = embed[toks]
+        for L in layers:
+            p = oracle.gemv_quant(*L["proj"], 4, x)
+            _, normed, _, ids, wts = oracle.router_addnorm_route(x, p, L["norm_w"], L["router"], 0,
+                                                                 None, 0)
+            act = oracle.gemv_gather_act(L["gate"], L["up"], normed, ids, n_experts=E)
+            x = oracle.gemv_gather_down_combine4(L["down"], act, ids, wts, n_experts=E)
+        _, toks = oracle.head_argmax(*head, 6, x)
+        out.append(toks.copy())
+    return out
+
+
+@pytest.mark.parametrize("batch", [1, 3])
+def test_stacked_decode_matches_oracle(cuda_ctx, batch):
+    L, E, I, V, steps = 3, 8, 512, 4096, 3
+    layers, head, embed = make_stack(80 + batch, L, E, I, V)
+    start = np.arange(7, 7 + batch, dtype=np.uint32) * 37 % V
+    want = oracle_tokens(layers, head, embed, start, 2 * steps, E)
+    dl = [dict(proj=dev_qw(*l["proj"]), norm_w=dev_bf16(l["norm_w"]), router=dev_bf16(l["router"]),
+               gate=dev_qw(*l["gate"]), up=dev_qw(*l["up"]), down=dev_qw(*l["down"])) for l in layers]
+    st = DecodeStack(cuda_ctx, dl, dev_qw(*head, bits=6), dev_bf16(embed), batch, n_experts=E)
+    st.start(torch.from_numpy(start.view(np.int32)).cuda())
+    for s in range(steps):  # eager
+        st.step()
+        torch.cuda.synchronize()
+        got = st.tokens.cpu().numpy().view(np.uint32)
+        assert np.array_equal(got, want[s]), f"step {s}: {got} != {want[s]}"
+    assert int(st.keys.abs().sum().cpu()) == 0, "token tail leaves the keys cleared"
+    g = torch.cuda.CUDAGraph()
+    stream = torch.cuda.Stream()
+    stream.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(stream):
+        with torch.cuda.graph(g, stream=stream):
+            st.step()
+    torch.cuda.current_stream().wait_stream(stream)
+    # capture records the step without running it; replays continue the sequence
+    for s in range(steps, 2 * steps):
+        g.replay()
+        torch.cuda.synchronize()
+        got = st.tokens.cpu().numpy().view(np.uint32)
+        assert np.array_equal(got, want[s]), f"graph step {s}: {got} != {want[s]}"
