@@ -831,14 +831,15 @@ def bench_cfg4(args, torch, ws, rank, local):
     gen = torch.Generator(device="cuda")
     gen.manual_seed(args.seed * 1000 + 4 + rank)
     layers = []
+    # Weights centred on zero (bias = -7.5 scale for 4-bit codes, -31.5 for the
+    # 6-bit head). With BASELINE's bias = -8 scale every weight has a nonzero
+    # mean; through 40 layers without a residual stream that common mode grows
+    # until every sequence of a batch routes to the same experts and decodes the
+    # same token, which would make a batch as cheap as one sequence.
     for _ in range(L):
-        d = synth.moe_layer_torch(gen, "cuda")
-        d["proj"] = synth.quant_weights_torch(gen, H, H, 4)
+        d = synth.moe_layer_torch(gen, "cuda", centre=7.5)
+        d["proj"] = synth.quant_weights_torch(gen, H, H, 4, centre=7.5)
         layers.append(d)
-    # the head's 6-bit codes centred on zero (bias = -31.5 scale): with BASELINE's
-    # bias = -8 scale every head row has a large positive mean, the argmax then
-    # hardly depends on the hidden state and all sequences of a batch collapse
-    # onto one token (one routing for the whole batch)
     head = synth.quant_weights_torch(gen, VOCAB, H, 6, centre=31.5)
     embed = torch.randn((VOCAB, H), generator=gen, device="cuda").to(torch.bfloat16)
     st = DecodeStack(ctx, layers, head, embed, B)
@@ -898,8 +899,8 @@ def bench_cfg4(args, torch, ws, rank, local):
         "value": round(value, 1), "unit": "tokens/s", "n_gpus": ws, "steps": K, "warmup": W,
         "ms_per_step": round(step_ms, 4), "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "q4/q6 codes, bf16 activations, fp32 accumulate",
-        "data": "synthetic (seeded, BASELINE cfg4 shapes; random-init weights per layer; head "
-                "codes centred: bias = -31.5 scale)",
+        "data": "synthetic (seeded, BASELINE cfg4 shapes; random-init weights per layer, codes "
+                "centred on zero: bias = -7.5 scale (Q4), -31.5 scale (Q6))",
         "config": {"workload": f"cfg4: {L} layers x (Q4 2048x2048 + E=64 top-4 SwiGLU 2048->1536"
                                f"->2048) + Q6 65536x2048 head + bf16 embedding gather, batch {B}, "
                                "one step per CUDA-graph replay",

@@ -117,12 +117,13 @@ def quant_weights_torch(gen: torch.Generator, out: int, inp: int, bits: int = 4,
 
 
 def moe_layer_torch(gen: torch.Generator, device="cuda", e: int = N_EXPERTS, h: int = HIDDEN,
-                    i: int = MOE_INTER) -> dict:
-    """One cfg1 MoE layer: norm gain, bf16 router, stacked gate/up/down."""
+                    i: int = MOE_INTER, centre: float = 8.0) -> dict:
+    """One cfg1 MoE layer: norm gain, bf16 router, stacked gate/up/down
+    (`centre` as in quant_weights_torch)."""
     return {
         "norm_w": (1.0 + 0.02 * torch.randn(h, generator=gen, device=device)).to(torch.bfloat16),
         "router": (0.02 * torch.randn((e, h), generator=gen, device=device)).to(torch.bfloat16),
-        "gate": quant_weights_torch(gen, e * i, h, 4, device),
-        "up": quant_weights_torch(gen, e * i, h, 4, device),
-        "down": quant_weights_torch(gen, e * h, i, 4, device),
+        "gate": quant_weights_torch(gen, e * i, h, 4, device, centre),
+        "up": quant_weights_torch(gen, e * i, h, 4, device, centre),
+        "down": quant_weights_torch(gen, e * h, i, 4, device, centre),
     }
