@@ -159,9 +159,9 @@ int mc_gemv_gather_down_combine4(mc_ctx* ctx, const mc_qweights* down, const uin
  * of calls (it keeps an epoch and tagged intermediate values between calls;
  * workspace[2] != 0 after a call reports a bounded wait that gave up (1) or
  * an expert id out of range (2); the act rows are the bf16 values
- * ((uint16_t*)(workspace + 132))[r*I + i]). All row buffers, the weights'
+ * ((uint16_t*)(workspace + 136))[r*I + i]). All row buffers, the weights'
  * scales/biases and the workspace 16-byte aligned; the expert width I is a
- * multiple of 512 and at most 2048 (each row's scales are one bulk copy). */
+ * multiple of 64 and at most 2048. */
 size_t mc_moe_decode_workspace_words(int moe_inter);
 int mc_moe_decode_layer(mc_ctx* ctx, const uint16_t* h, const uint16_t* b,
                         const uint16_t* norm_w, uint16_t* h_out, uint16_t* normed,
@@ -172,7 +172,7 @@ int mc_moe_decode_layer(mc_ctx* ctx, const uint16_t* h, const uint16_t* b,
                         uint32_t* workspace, size_t ws_words, float eps, float route_eps);
 
 /* mc_moe_decode_layer with no workspace argument and no allocation: the
- * scratch is a fixed 33,296-byte array inside this library (one per device),
+ * scratch is a fixed 33,312-byte array inside this library (one per device),
  * for callers that cannot lend device memory (an engine whose allocator is
  * frozen after start-up, a plugin barred from allocating on the serving
  * path). It has no counterpart in the reference, whose Metal kernels take

@@ -136,6 +136,13 @@ __device__ __forceinline__ unsigned long long mc_ld_poll_u64(const unsigned long
   return v;
 }
 
+// Two 64-bit words in one 16-byte load; each word is read whole (a tagged
+// value published by one 64-bit store is never torn).
+__device__ __forceinline__ void mc_ld_poll_v2u64(const unsigned long long* p,
+                                                 unsigned long long& a, unsigned long long& b) {
+  asm volatile("ld.volatile.global.v2.u64 {%0,%1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
+}
+
 __device__ __forceinline__ uint4 mc_ld_poll_v4(const uint32_t* p) {
   uint4 v;
   asm volatile("ld.volatile.global.v4.u32 {%0,%1,%2,%3}, [%4];"

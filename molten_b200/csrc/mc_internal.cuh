@@ -37,11 +37,16 @@ int mc_fail(int code, const char* fmt, ...);
     if (!(cond)) return mc_fail(MC_EINVAL, __VA_ARGS__);       \
   } while (0)
 
+// A failed runtime call is reported once: the per-thread "last error" it set
+// is cleared (a refused launch is not sticky), so a later launch check does
+// not report it again.
 #define MC_CUDA(call)                                                            \
   do {                                                                           \
     cudaError_t _e = (call);                                                     \
-    if (_e != cudaSuccess)                                                       \
+    if (_e != cudaSuccess) {                                                     \
+      (void)cudaGetLastError();                                                  \
       return mc_fail(MC_ECUDA, "%s failed: %s", #call, cudaGetErrorString(_e));  \
+    }                                                                            \
   } while (0)
 
 // check_quant for the GEMV kernels (mc_api.cu).

@@ -1,37 +1,40 @@
-// One whole MoE decode layer for one token in a single persistent launch:
-// residual add + RMSNorm + router + top-4 (router_addnorm_route), the four
-// experts' gate/up + SwiGLU (gemv_gather_act) and down + weighted combine
-// (gemv_gather_down_combine4) -- moe_decode in lfm.rs:967-1011 after the
-// fused router of lfm.rs:1154-1169.
+// moe_decode (lfm.rs:967-1011) behind the fused router (lfm.rs:1154-1169) as
+// ONE persistent cooperative launch for one token (batch 1): add + RMSNorm +
+// router + top-4 (router_addnorm_route), the four experts' gate/up GEMVs with
+// SwiGLU (gemv_gather_act) and their down GEMVs with the weighted combine
+// (gemv_gather_down_combine4), bit-identical to those three kernels.
 //
-// B200 design. One CTA per SM (cooperative launch: all CTAs co-resident).
-//  * Every CTA computes the RMSNorm itself; CTAs 0..3 also compute 16 router
-//    logits each and publish them.
-//  * As soon as a CTA has the 64 logits it runs the (identical) top-4 and all
-//    512 threads issue its whole share of the expert weights as 16-byte
-//    cp.async copies into shared memory: gate/up row pairs [p0, p1) of the
-//    4*I pairs and the four experts' down rows for output rows [i0, i1),
-//    ~145 KB per SM, so the layer's 21 MB are in flight at once. Gate/up rows
-//    are consumed chunk by chunk as their mbarriers complete.
-//  * The down rows are resident by the time a warp has its expert's act
-//    vector, which every CTA reads from the other CTAs' published values.
+// One CTA per SM, 16 warps. Timeline of a launch:
+//  * every CTA adds h + b and normalises the row (each needs the normed row);
+//    warp 0 of CTAs 0..E-1 has prefetched one router row and publishes that
+//    expert's logit, epoch-tagged, to the workspace;
+//  * warp 0 of every CTA polls the E tagged logits and picks the same top-4;
+//  * every thread issues L2 prefetches for its CTA's slice of the 4 experts'
+//    down rows, then each warp streams its gate/up row pairs straight from
+//    HBM (16-byte non-allocating loads, the next pair's loads issued before
+//    the current pair is reduced) and publishes bf16 act values;
+//  * after a release/acquire count of the CTAs that published, each CTA loads
+//    the act rows and computes its down rows from L2 (4 rows per warp in
+//    flight) and the weighted combine.
+// No bulk copies and no shared staging of weights: the weight stream is the
+// plain load pattern that reaches HBM speed on this part.
 //
-// No grid barrier and no fence: published values are self-validating words
-// carrying the launch's epoch tag (logits: tag32 << 32 | f32 bits; act:
-// tag16 << 16 | bf16 bits), so a consumer polls exactly the words it needs
-// until their tags match. The caller's workspace (u32 words, zeroed once,
-// then owned by one chain of calls) holds:
+// Published values are self-validating words carrying the launch's epoch tag
+// (logits: tag32 << 32 | f32 bits). The caller's workspace (u32 words, zeroed
+// once, then owned by one chain of calls) holds:
 //   ws[0]            epoch (advanced by the last CTA to finish)
 //   ws[1]            CTAs finished (reset by the last one)
 //   ws[2]            sticky error status bits: 1 logits wait gave up,
-//                    2 expert id out of range, 4 gate/up copies wait,
-//                    8 act wait, 16 down copies wait
+//                    2 expert id out of range, 8 act wait
 //   ws[3]            CTAs that published their act rows (reset by the last
 //                    CTA to finish)
-//   ws[4..132)       64 tagged logits (u64)
-//   ws[132..)        act rows as bf16, [slot][row] (2 per word)
-// Every wait is bounded by a %globaltimer deadline; on timeout the CTA
-// records the status and leaves only after its own copies have landed.
+//   ws[4]            router warps that published their logit (reset likewise)
+//   ws[5..8)         reserved
+//   ws[8..136)       64 tagged logits (u64)
+//   ws[136..)        act rows as bf16, [slot][row] (2 per word)
+// Every wait is bounded by a %globaltimer deadline; waiting lanes back off
+// between polls (a few thousand lanes spinning on the same lines slow the
+// writers down).
 //
 // Arithmetic per output is the canonical order of the separate kernels, so
 // results are bit-identical to router_addnorm_route + gemv_gather_act +
@@ -43,45 +46,16 @@
 
 namespace {
 
-constexpr int kThreads = 512;
+constexpr int kThreads = 384;  // 12 warps, 3 per scheduler: up to 168 registers per thread
+                               // (the register file is split per scheduler), room for
+                               // kPairs row pairs in flight per warp
 constexpr int kWarps = kThreads / 32;
+constexpr int kPairs = 4;      // gate/up row pairs each warp has in flight
+constexpr int kDnRows = 5;     // down rows per warp (12 warps, 3 per expert)
 constexpr int H = 2048;
-constexpr int kChunk = 16;                              // gate/up row pairs per mbarrier
 constexpr unsigned long long kTimeoutNs = 200000000ull;  // 200 ms per wait
-
-constexpr int GU_CODE = H / 2;       // 1024 B of codes per gate/up row
-constexpr int GU_SB = (H / 64) * 2;  // 64 B of scales (or biases) per row
-constexpr int GU_PIECES = (2 * GU_CODE + 4 * GU_SB) / 16;  // 16-byte copies per row pair
-constexpr int kActWord = 132;  // first act word in the workspace
-
-struct Layout {
-  int pmax, rmax, nchunk;
-  int off_gc, off_uc, off_gs, off_gb, off_us, off_ub;  // gate/up staging
-  int off_dc, off_ds, off_db;                          // down staging
-  int off_bar, total;
-};
-
-__host__ __device__ inline Layout make_layout(int pmax, int rmax, int I) {
-  Layout L;
-  L.pmax = pmax;
-  L.rmax = rmax;
-  L.nchunk = (pmax + kChunk - 1) / kChunk;
-  const int dn_code = I / 2, dn_sb = (I / 64) * 2;
-  int o = 0;
-  L.off_gc = o; o += pmax * GU_CODE;
-  L.off_uc = o; o += pmax * GU_CODE;
-  L.off_gs = o; o += pmax * GU_SB;
-  L.off_gb = o; o += pmax * GU_SB;
-  L.off_us = o; o += pmax * GU_SB;
-  L.off_ub = o; o += pmax * GU_SB;
-  L.off_dc = o; o += 4 * rmax * dn_code;
-  L.off_ds = o; o += 4 * rmax * dn_sb;
-  L.off_db = o; o += 4 * rmax * dn_sb;
-  o = (o + 15) & ~15;
-  L.off_bar = o; o += (L.nchunk + 5) * 8;  // code chunks, scales/biases, 4 down slots
-  L.total = o;
-  return L;
-}
+constexpr int kLogitWord = 8;  // first tagged-logit word in the workspace
+constexpr int kActWord = 136;  // first act word in the workspace
 
 struct Params {
   const uint16_t* h;
@@ -98,7 +72,7 @@ struct Params {
   uint16_t* out;
   uint32_t* sync;
   float eps, route_eps;
-  int mode, E, I, n_router_ctas;
+  int mode, E, I;
   unsigned long long* trace;
 };
 
@@ -109,15 +83,27 @@ __device__ __forceinline__ void record_error(uint32_t* sync, uint32_t bit) {
   atomicOr(sync + 2, bit);
 }
 
-__device__ __forceinline__ bool mbar_wait_deadline(uint64_t* bar, unsigned long long deadline) {
-  while (!mc_mbar_test_sleep(bar, 0, 20000u))
-    if (mc_globaltimer() > deadline) return false;
-  return true;
+__device__ __forceinline__ void prefetch_l2(const void* p) {
+  asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
 }
 
+// One gate/up row pair of the stacked experts: codes (group `lane`) and the
+// raw bf16 scale/bias words, loaded ahead of use.
+struct PairLoad {
+  QGroup<4> g, u;
+  uint16_t gs, gb, us, ub;
+  __device__ __forceinline__ void load(const Params& P, size_t row, int lane) {
+    g.load(reinterpret_cast<const uint8_t*>(P.gate.codes) + row * (H / 2), lane);
+    u.load(reinterpret_cast<const uint8_t*>(P.up.codes) + row * (H / 2), lane);
+    gs = __ldg(P.gate.scales + row * (H / 64) + lane);
+    gb = __ldg(P.gate.biases + row * (H / 64) + lane);
+    us = __ldg(P.up.scales + row * (H / 64) + lane);
+    ub = __ldg(P.up.biases + row * (H / 64) + lane);
+  }
+};
+
 template <int DT>
-__global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(const Params P, Layout L) {
-  extern __shared__ __align__(128) uint8_t smem[];
+__global__ void __maxnreg__(168) moe_decode_fused_kernel(const Params P) {
   __shared__ __align__(16) float nrow[H];
   __shared__ __align__(16) uint16_t nbf[H];
   __shared__ float red[8];
@@ -135,27 +121,19 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(const Par
   const int p0 = (int)(((long)cta * npairs) / G), p1 = (int)(((long)(cta + 1) * npairs) / G);
   const int i0 = (int)(((long)cta * H) / G), i1 = (int)(((long)(cta + 1) * H) / G);
   const int np = p1 - p0, nr = i1 - i0;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L.off_bar);
   uint32_t* sync = P.sync;
-  unsigned long long* logits64 = reinterpret_cast<unsigned long long*>(sync + 4);
+  unsigned long long* logits64 = reinterpret_cast<unsigned long long*>(sync + kLogitWord);
   uint16_t* act = reinterpret_cast<uint16_t*>(sync + kActWord);
   const uint32_t epoch = *reinterpret_cast<volatile uint32_t*>(sync);
   const uint32_t tag32 = epoch == 0xffffffffu ? 1u : epoch + 1u;
-  const uint32_t tag16 = (tag32 % 65535u) + 1u;
   bool ok = true;
   TRACE(0);
+  if (t == 0) flag_s = 0;
 
-  if (t == 0) {
-    for (int c = 0; c < L.nchunk + 5; ++c) mc_mbar_init(bars + c, 1);
-    mc_fence_barrier_init();
-    flag_s = 0;
-  }
-
-  // ---- router row prefetch (router CTAs), then add + RMSNorm (all CTAs)
-  const int e_mine = cta * kWarps + warp;
-  const bool router_cta = cta < P.n_router_ctas;
+  // ---- router row prefetch (warp 0 of CTA e < E), then add + RMSNorm (all CTAs)
+  const bool router_warp = warp == 0 && cta < P.E;
   RouterRow<DT> rr;
-  if (router_cta && e_mine < P.E) rr.load(P.router_w, e_mine, lane);
+  if (router_warp) rr.load(P.router_w, cta, lane);
   float hp[8];
   if (t < 256) {
     float acc = 0.0f;
@@ -200,31 +178,53 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(const Par
   __syncthreads();
   TRACE(1);
 
-  // ---- router logits: CTA c < n_router_ctas publishes experts 16c .. 16c+15
-  if (router_cta && e_mine < P.E) {
+  // ---- router logit of expert `cta` (warp 0), published epoch-tagged
+  if (router_warp) {
     const float z = rr.dot(nrow, lane);
     if (lane == 0) {
-      P.logits[e_mine] = z;
-      mc_st_publish_u64(logits64 + e_mine,
+      P.logits[cta] = z;
+      mc_st_publish_u64(logits64 + cta,
                         ((unsigned long long)tag32 << 32) | (unsigned long long)__float_as_uint(z));
+      __threadfence();
+      mc_red_release_add(sync + 4, 1u);
     }
   }
   TRACE(2);
 
-  // ---- warp 0 of every CTA: gather the 64 tagged logits, identical top-4
+  // ---- gate/up activations prescaled once (all warps), meanwhile warp 0
+  // gathers the tagged logits
+  float2 xs[32];
+  const float xg = load_group_x<4, 2>(nbf, lane, xs);
   if (warp == 0) {
+    // lane 0 waits (backing off) until all E router warps have published;
+    // then lane l reads logits 2l, 2l+1 in one 16-byte load (tags checked)
     const unsigned long long deadline = mc_globaltimer() + kTimeoutNs;
     bool got = true;
-    for (int i = lane; i < P.E; i += 32) {
-      unsigned long long v;
-      while (((v = mc_ld_poll_u64(logits64 + i)) >> 32) != tag32) {
+    if (lane == 0) {
+      while (mc_ld_acquire(sync + 4) < (uint32_t)P.E) {
         if (mc_globaltimer() > deadline) {
           got = false;
           break;
         }
-        __nanosleep(128);
+        __nanosleep(64);
       }
-      zs[i] = __uint_as_float((uint32_t)v);
+    }
+    got = __shfl_sync(0xffffffffu, got ? 1 : 0, 0) != 0;
+    if (got && 2 * lane < P.E) {
+      const int i = 2 * lane;
+      unsigned long long v0, v1;
+      for (;;) {
+        mc_ld_poll_v2u64(logits64 + i, v0, v1);
+        const bool ready0 = (v0 >> 32) == tag32, ready1 = i + 1 >= P.E || (v1 >> 32) == tag32;
+        if (ready0 && ready1) break;
+        if (mc_globaltimer() > deadline) {
+          got = false;
+          break;
+        }
+        __nanosleep(32);
+      }
+      zs[i] = __uint_as_float((uint32_t)v0);
+      if (i + 1 < P.E) zs[i + 1] = __uint_as_float((uint32_t)v1);
     }
     got = __all_sync(0xffffffffu, got);
     if (!got) {
@@ -256,113 +256,56 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(const Par
   TRACE(3);
   if (flag_s) ok = false;
 
-  // ---- one thread issues this CTA's expert rows as a few bulk (TMA) copies:
-  // the small scale/bias arrays first, then the codes chunk by chunk, then
-  // the down rows; the other warps start on chunks as they land.
-  const int dn_code = I / 2, dn_sb = (I / 64) * 2;
-  uint64_t* bar_sb = bars + L.nchunk;
-  uint64_t* bar_dn = bars + L.nchunk + 1;
-  // at most two expert segments: local pairs [0, qs) and [qs, np)
-  const int slot0 = p0 / I;
-  const int qs = min(np, (slot0 + 1) * I - p0);
-  bool issued = false;  // thread 0 only
-  if (ok && t == 0) {
-    issued = true;
-    const uint64_t pol = mc_policy_evict_normal();
-    for (int c = 0; c < L.nchunk; ++c) {
-      if (c == 1) {
-        // scales/biases right after the first code chunk
-        mc_mbar_expect_tx(bar_sb, (uint32_t)np * (4 * GU_SB));
-        for (int sgi = 0; sgi < 2; ++sgi) {
-          const int qa = sgi == 0 ? 0 : qs, qb = sgi == 0 ? qs : np;
-          if (qa >= qb) continue;
-          const int slot = (p0 + qa) / I;
-          const size_t row = (size_t)ids_s[slot] * I + (p0 + qa - slot * I);
-          const uint32_t n = (uint32_t)(qb - qa) * GU_SB;
-          mc_bulk_g2s(smem + L.off_gs + qa * GU_SB, P.gate.scales + row * (GU_SB / 2), n, bar_sb, pol);
-          mc_bulk_g2s(smem + L.off_gb + qa * GU_SB, P.gate.biases + row * (GU_SB / 2), n, bar_sb, pol);
-          mc_bulk_g2s(smem + L.off_us + qa * GU_SB, P.up.scales + row * (GU_SB / 2), n, bar_sb, pol);
-          mc_bulk_g2s(smem + L.off_ub + qa * GU_SB, P.up.biases + row * (GU_SB / 2), n, bar_sb, pol);
+  const int dn_code = I / 2, Gd = I / 64;
+  if (ok) {
+    // ---- L2 prefetch of this CTA's down rows (codes, scales, biases) of the
+    // 4 experts: contiguous row ranges, one 128-byte line per thread
+    const int code_lines = (nr * dn_code + 127) / 128, sb_lines = (nr * Gd * 2 + 127) / 128;
+    const int per_e = code_lines + 2 * sb_lines;
+    for (int l = t; l < 4 * per_e; l += kThreads) {
+      const int r = l / per_e, k = l % per_e;
+      const size_t row = (size_t)ids_s[r] * H + i0;
+      if (k < code_lines) {
+        prefetch_l2(reinterpret_cast<const uint8_t*>(P.down.codes) + row * dn_code + 128 * k);
+      } else {
+        const int kk = k - code_lines;
+        const uint16_t* base = kk < sb_lines ? P.down.scales : P.down.biases;
+        prefetch_l2(reinterpret_cast<const uint8_t*>(base + row * Gd) + 128 * (kk % sb_lines));
+      }
+    }
+
+    // ---- gate/up + SwiGLU: warp w takes pairs w, w+12, w+24, w+36 of this CTA
+    // (kPairs at a time), every load issued before the first reduction
+    auto pair_row = [&](int q) -> size_t {
+      const int slot = (p0 + q) / I;
+      return (size_t)ids_s[slot] * I + (p0 + q - slot * I);
+    };
+    for (int base = 0; base < np; base += kWarps * kPairs) {
+      PairLoad pl[kPairs];
+#pragma unroll
+      for (int k = 0; k < kPairs; ++k) {
+        const int q = base + warp + kWarps * k;
+        if (q < np) pl[k].load(P, pair_row(q), lane);
+      }
+#pragma unroll
+      for (int k = 0; k < kPairs; ++k) {
+        const int q = base + warp + kWarps * k;
+        if (q >= np) break;
+        float acc_g = 0.0f, acc_u = 0.0f;
+        acc_g = __fadd_rn(acc_g, __fmaf_rn(mc_bf16_to_f32(pl[k].gs), pl[k].g.qx(xs),
+                                           __fmul_rn(mc_bf16_to_f32(pl[k].gb), xg)));
+        acc_u = __fadd_rn(acc_u, __fmaf_rn(mc_bf16_to_f32(pl[k].us), pl[k].u.qx(xs),
+                                           __fmul_rn(mc_bf16_to_f32(pl[k].ub), xg)));
+        const float gsum = mc_warp_butterfly(acc_g);
+        const float usum = mc_warp_butterfly(acc_u);
+        if (lane == 0) {
+          const float g = mc_round_bf16(gsum);
+          const float u = mc_round_bf16(usum);
+          const float sl = mc_round_bf16(mc_silu(g));
+          act[p0 + q] = mc_f32_to_bf16(__fmul_rn(sl, u));
         }
       }
-      const int q0 = c * kChunk, q1 = min(np, q0 + kChunk);
-      if (q0 >= q1) {
-        mc_mbar_arrive(bars + c);
-        continue;
-      }
-      mc_mbar_expect_tx(bars + c, (uint32_t)(q1 - q0) * (2 * GU_CODE));
-      for (int sgi = 0; sgi < 2; ++sgi) {
-        const int qa = max(q0, sgi == 0 ? 0 : qs), qb = min(q1, sgi == 0 ? qs : np);
-        if (qa >= qb) continue;
-        const int slot = (p0 + qa) / I;
-        const size_t row = (size_t)ids_s[slot] * I + (p0 + qa - slot * I);
-        const uint32_t n = (uint32_t)(qb - qa) * GU_CODE;
-        mc_bulk_g2s(smem + L.off_gc + qa * GU_CODE,
-                    reinterpret_cast<const uint8_t*>(P.gate.codes) + row * GU_CODE, n, bars + c, pol);
-        mc_bulk_g2s(smem + L.off_uc + qa * GU_CODE,
-                    reinterpret_cast<const uint8_t*>(P.up.codes) + row * GU_CODE, n, bars + c, pol);
-      }
     }
-    if (L.nchunk < 2) {
-      mc_mbar_expect_tx(bar_sb, (uint32_t)np * (4 * GU_SB));
-      for (int sgi = 0; sgi < 2; ++sgi) {
-        const int qa = sgi == 0 ? 0 : qs, qb = sgi == 0 ? qs : np;
-        if (qa >= qb) continue;
-        const int slot = (p0 + qa) / I;
-        const size_t row = (size_t)ids_s[slot] * I + (p0 + qa - slot * I);
-        const uint32_t n = (uint32_t)(qb - qa) * GU_SB;
-        mc_bulk_g2s(smem + L.off_gs + qa * GU_SB, P.gate.scales + row * (GU_SB / 2), n, bar_sb, pol);
-        mc_bulk_g2s(smem + L.off_gb + qa * GU_SB, P.gate.biases + row * (GU_SB / 2), n, bar_sb, pol);
-        mc_bulk_g2s(smem + L.off_us + qa * GU_SB, P.up.scales + row * (GU_SB / 2), n, bar_sb, pol);
-        mc_bulk_g2s(smem + L.off_ub + qa * GU_SB, P.up.biases + row * (GU_SB / 2), n, bar_sb, pol);
-      }
-    }
-    for (int r = 0; r < 4; ++r) {
-      if (nr == 0) {
-        mc_mbar_arrive(bar_dn + r);
-        continue;
-      }
-      mc_mbar_expect_tx(bar_dn + r, (uint32_t)nr * (dn_code + 2 * dn_sb));
-      const size_t row = (size_t)ids_s[r] * H + i0;
-      mc_bulk_g2s(smem + L.off_dc + r * L.rmax * dn_code,
-                  reinterpret_cast<const uint8_t*>(P.down.codes) + row * dn_code, nr * dn_code,
-                  bar_dn + r, pol);
-      mc_bulk_g2s(smem + L.off_ds + r * L.rmax * dn_sb, P.down.scales + row * (dn_sb / 2),
-                  nr * dn_sb, bar_dn + r, pol);
-      mc_bulk_g2s(smem + L.off_db + r * L.rmax * dn_sb, P.down.biases + row * (dn_sb / 2),
-                  nr * dn_sb, bar_dn + r, pol);
-    }
-  }
-
-  TRACE(13);
-  // ---- gate/up + SwiGLU on the staged rows; act published to the workspace
-  if (ok) {
-    float2 xs[32];
-    const float xg = load_group_x<4, 2>(nbf, lane, xs);
-    const unsigned long long deadline = mc_globaltimer() + kTimeoutNs;
-    bool ready = np == 0 || mbar_wait_deadline(bar_sb, deadline);
-    for (int q = warp; q < np && ready; q += kWarps) {
-      if (!mbar_wait_deadline(bars + q / kChunk, deadline)) {
-        ready = false;
-        break;
-      }
-      if (q == 0) TRACE(8);
-      if (q + kWarps >= np) TRACE(9);
-      const uint8_t* rows[2] = {smem + L.off_gc + q * GU_CODE, smem + L.off_uc + q * GU_CODE};
-      const uint16_t* sc[2] = {reinterpret_cast<const uint16_t*>(smem + L.off_gs + q * GU_SB),
-                               reinterpret_cast<const uint16_t*>(smem + L.off_us + q * GU_SB)};
-      const uint16_t* bi[2] = {reinterpret_cast<const uint16_t*>(smem + L.off_gb + q * GU_SB),
-                               reinterpret_cast<const uint16_t*>(smem + L.off_ub + q * GU_SB)};
-      float sum[2];
-      smem_rows_dot_q4<2>(rows, sc, bi, 32, lane, xs, xg, sum);
-      if (lane == 0) {
-        const float g = mc_round_bf16(sum[0]);
-        const float u = mc_round_bf16(sum[1]);
-        const float sl = mc_round_bf16(mc_silu(g));
-        act[p0 + q] = mc_f32_to_bf16(__fmul_rn(sl, u));
-      }
-    }
-    if (!ready && lane == 0) record_error(sync, 4u);
   }
   __syncthreads();
   TRACE(4);
@@ -378,6 +321,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(const Par
         flag_s = 1;
         break;
       }
+      __nanosleep(32);
     }
   }
   __syncthreads();
@@ -395,13 +339,13 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(const Par
     }
   }
   __syncthreads();
+  TRACE(10);
 
-  // ---- down rows + weighted combine
-  if (ok) {
+  // ---- down rows (from L2, 4 rows per warp in flight) + weighted combine
+  if (ok && warp < 12) {
     const int r = warp & 3;
-    const int Gd = I / 64;
-    float2 xs[32];
-    float xg = 0.0f;
+    float2 dxs[1][32];
+    float dxg[1] = {0.0f};
     if (lane < Gd) {
       const int g = r * Gd + lane;
       const uint4* src = reinterpret_cast<const uint4*>(act_s) + (g << 3);
@@ -416,37 +360,27 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(const Par
           xv[8 * c + 2 * h + 1] = __uint_as_float(wds[h] & 0xffff0000u);
         }
       }
-      xg = prescale_group_x<4>(xv, xs);
+      dxg[0] = prescale_group_x<4>(xv, dxs[0]);
     }
-    __syncwarp();
-    asm volatile("" ::: "memory");
-    TRACE(10);
-    const unsigned long long deadline = mc_globaltimer() + kTimeoutNs;
-    const bool dn_ok = mbar_wait_deadline(bar_dn + r, deadline);
-    TRACE(11);
-    if (!dn_ok) {
-      if (lane == 0) record_error(sync, 16u);
-    } else {
-      const int j0 = warp >> 2;
-      const uint8_t* rows[4];
-      const uint16_t* sc[4];
-      const uint16_t* bi[4];
+    const int j0 = warp >> 2;  // 0..2: rows j0, j0+3, ... of expert slot r
+    const uint8_t* rows[kDnRows];
+    const uint16_t* sc[kDnRows];
+    const uint16_t* bi[kDnRows];
 #pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        const int j = min(j0 + 4 * k, nr - 1);
-        rows[k] = smem + L.off_dc + (r * L.rmax + j) * dn_code;
-        sc[k] = reinterpret_cast<const uint16_t*>(smem + L.off_ds + (r * L.rmax + j) * dn_sb);
-        bi[k] = reinterpret_cast<const uint16_t*>(smem + L.off_db + (r * L.rmax + j) * dn_sb);
-      }
-      float sum[4];
-      smem_rows_dot_q4<4>(rows, sc, bi, Gd, lane, xs, xg, sum);
-      __syncwarp();
-      asm volatile("" ::"f"(sum[0]), "f"(sum[1]), "f"(sum[2]), "f"(sum[3]) : "memory");
-      TRACE(12);
+    for (int k = 0; k < kDnRows; ++k) {
+      const int j = min(j0 + 3 * k, nr - 1);
+      const size_t row = (size_t)ids_s[r] * H + i0 + j;
+      rows[k] = reinterpret_cast<const uint8_t*>(P.down.codes) + row * dn_code;
+      sc[k] = P.down.scales + row * Gd;
+      bi[k] = P.down.biases + row * Gd;
+    }
+    if (nr > 0) {
+      float sum[kDnRows];
+      rows_dot<4, 1, kDnRows>(rows, sc, bi, Gd, lane, dxs, dxg, sum);
       if (lane == 0) {
 #pragma unroll
-        for (int k = 0; k < 4; ++k)
-          if (j0 + 4 * k < nr) p_s[r][j0 + 4 * k] = mc_round_bf16(sum[k]);
+        for (int k = 0; k < kDnRows; ++k)
+          if (j0 + 3 * k < nr) p_s[r][j0 + 3 * k] = mc_round_bf16(sum[k]);
       }
     }
   }
@@ -460,19 +394,14 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(const Par
     P.out[i0 + t] = mc_f32_to_bf16(tot);
   }
 
-  // ---- leave only after this CTA's bulk copies landed (immediate on the
-  // normal path); the last CTA resets the counters and advances the epoch
-  if (issued) {
-    const unsigned long long deadline = mc_globaltimer() + kTimeoutNs;
-    for (int c = 0; c < L.nchunk + 5; ++c)
-      if (!mbar_wait_deadline(bars + c, deadline)) record_error(sync, 16u);
-  }
+  // ---- the last CTA to finish resets the counters and advances the epoch
   TRACE(7);
   if (t == 0) {
     const uint32_t done = atomicAdd(sync + 1, 1u);
     if (done == (uint32_t)G - 1) {
       sync[1] = 0u;
       sync[3] = 0u;
+      sync[4] = 0u;
       __threadfence();
       *reinterpret_cast<volatile uint32_t*>(sync) = tag32;
     }
@@ -509,8 +438,6 @@ extern "C" int mc_moe_decode_layer(mc_ctx* ctx, const uint16_t* h, const uint16_
   MC_REQUIRE(I % 64 == 0 && I <= 2048 && 4 * I <= 4 * 2048 && down->in_features == I &&
                  down->out_features == n_experts * H,
              "moe_decode_layer: expert shapes (I=%d)", I);
-  // a down row's scales (I/64 bf16) are one bulk copy: 16-byte size and start
-  MC_REQUIRE(I % 512 == 0, "moe_decode_layer: expert width %d must be a multiple of 512", I);
   MC_REQUIRE(ws_words >= mc_moe_decode_workspace_words(I),
              "moe_decode_layer: workspace of %zu words < %zu", ws_words,
              mc_moe_decode_workspace_words(I));
@@ -530,30 +457,29 @@ extern "C" int mc_moe_decode_layer(mc_ctx* ctx, const uint16_t* h, const uint16_
                  (const void*)normed != (const void*)h && (const void*)normed != (const void*)b,
              "moe_decode_layer: h_out/normed must not alias h or b");
   const int G = ctx->num_sms;
-  const int pmax = (4 * I + G - 1) / G + 1, rmax = (H + G - 1) / G + 1;
-  MC_REQUIRE(rmax <= 32 && G >= (n_experts + kWarps - 1) / kWarps,
+  // each CTA: <= 15 down rows (3 warps x kDnRows per expert), <= 12 x kPairs
+  // gate/up pairs per pass, one router warp per expert among the CTAs
+  MC_REQUIRE((H + G - 1) / G <= 3 * kDnRows && G >= n_experts,
              "moe_decode_layer: too few SMs (%d)", G);
-  const Layout L = make_layout(pmax, rmax, I);
-  MC_REQUIRE(L.total + 16 * 1024 <= ctx->max_smem_optin,
-             "moe_decode_layer: %d B of staging exceeds shared memory", L.total);
   Params P{h, b, norm_w, h_out, normed, router_w, expert_bias, logits, ids, weights, *gate, *up,
            *down, out, sync, eps, route_eps, route_mode, n_experts, I,
-           (n_experts + kWarps - 1) / kWarps,
            ctx->trace && ctx->trace_len >= 16 * G ? ctx->trace : nullptr};
   void* fn = router_dtype == MC_DTYPE_BF16 ? (void*)moe_decode_fused_kernel<MC_DTYPE_BF16>
                                            : (void*)moe_decode_fused_kernel<MC_DTYPE_F32>;
-  MC_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, L.total));
+  int per_sm = 0;  // every CTA must be resident at once (cross-CTA waits)
+  MC_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, kThreads, 0));
+  MC_REQUIRE(per_sm >= 1, "moe_decode_layer: kernel does not fit one CTA per SM");
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(G);
   cfg.blockDim = dim3(kThreads);
-  cfg.dynamicSmemBytes = L.total;
+  cfg.dynamicSmemBytes = 0;
   cfg.stream = ctx->stream;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeCooperative;
   attr[0].val.cooperative = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  void* args[] = {(void*)&P, (void*)&L};
+  void* args[] = {(void*)&P};
   MC_CUDA(cudaLaunchKernelExC(&cfg, fn, args));
   return mc_after_launch("moe_decode_fused_kernel");
 }

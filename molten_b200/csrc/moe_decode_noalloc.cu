@@ -10,7 +10,8 @@
 // The scratch is the same layout mc_moe_decode_layer documents for its
 // caller-owned workspace: word 0 epoch, word 1 exit counter, word 2 status
 // (cleared before each launch here, copied to the caller's `status` after
-// it), word 3 act counter, words 4..131 tagged router logits, then the
+// it), word 3 act counter, word 4 router counter, words 8..135 tagged router
+// logits, then the
 // bf16 act rows. It serves expert widths up to kNoallocMaxInter; wider layers
 // are rejected with MC_EINVAL before anything is launched.
 //
@@ -34,8 +35,8 @@
 namespace {
 
 constexpr int kNoallocMaxInter = 2048;            // widest expert row served
-constexpr int kNoallocCtlWords = 132;             // control + tagged logits
-constexpr size_t kNoallocWords = kNoallocCtlWords + 4 * (size_t)kNoallocMaxInter;  // 33,296 B
+constexpr int kNoallocCtlWords = 136;             // control + tagged logits
+constexpr size_t kNoallocWords = kNoallocCtlWords + 4 * (size_t)kNoallocMaxInter;  // 33,312 B
 constexpr int kMaxDevices = 64;
 
 static __device__ __align__(256) uint32_t g_decode_scratch[kNoallocWords];

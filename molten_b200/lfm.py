@@ -278,7 +278,7 @@ def moe_decode_layer_noalloc(ctx: Context, h, b, nw, hout, normed, router, logit
 
 def decode_workspace_act(workspace: torch.Tensor, moe_inter: int = FIXED_MOE_INTER):
     """The act rows (bf16 [4, I]) held in a moe_decode_layer workspace."""
-    w = workspace[132:132 + 2 * moe_inter].contiguous()
+    w = workspace[136:136 + 2 * moe_inter].contiguous()
     return w.view(torch.bfloat16).reshape(4, moe_inter)
 
 
