@@ -2,10 +2,14 @@
 // and the canonical per-group dot product.
 //
 // Canonical row order (mirrored by oracle/mc_oracle.c row_dot):
-//   lane l of a warp owns the 64-code groups g = l, l+32, ...; per group two
-//   chains each acc = fma(q*2^e, x*2^-e, acc) in increasing k -- for Q4 the
-//   codes of even words (bit 3 of k clear) and of odd words; for Q6 even and
-//   odd k -- ; qx = chain0 + chain1; term = fma(s, qx, b * xg) with xg the
+//   lane l of a warp owns the 64-code groups g = l, l+32, ...; a group is
+//   four quarters of 16 codes and each quarter p has two chains
+//   c = fma(q*2^e, x*2^-e, c) in increasing k, both starting at +0 -- for
+//   Q4 the codes of the quarter's even word (bit 3 of k clear) and of its
+//   odd word; for Q6 even and odd k --; per parity the quarter chains are
+//   combined (c0 + c1) + (c2 + c3), and qx = even + odd (four independent
+//   chains of 8 instead of one of 32: the group dot is latency bound);
+//   term = fma(s, qx, b * xg) with xg the
 //   left-to-right sum of the group's 64 activations; the lane's terms are
 //   added in increasing g starting from +0; the row sum is the 32-lane xor
 //   butterfly. (Reference arithmetic: dot_word_q4 / GEMV_Q4_BODY,
@@ -27,37 +31,60 @@ __device__ __forceinline__ float2 mc_u64_as_float2(uint64_t v) {
 
 // 16 codes of two adjacent Q4 words (wa = word 2m, wb = word 2m+1 of a group)
 // against 8 activation pairs xs[j] = (x[16m+j], x[16m+8+j]) pre-scaled by E4.
-// The two words sit in an aligned register pair (they come from one 16-byte
-// load), so each 64-bit mask-and-OR yields a float2 of codes directly; chain
-// .x takes word 2m's codes, chain .y word 2m+1's, each in increasing k.
+// Per code pair: two lop3 (mask the code at its bit position, OR the 2^23
+// exponent), one f32x2 add (-2^23) and one f32x2 fma into acc (.x takes word
+// 2m's codes, .y word 2m+1's, each in increasing k). Codes 5..7 (bits 20..31)
+// would reach the exponent, so they are taken from w >> 12. Written as PTX:
+// the compiler's own version of the same operations issued ~1.4x slower
+// (lop3, f32x2 add and fma each issue at half rate, so the instruction
+// count per code is what bounds the decode GEMVs).
 __device__ __forceinline__ void q4_wordpair_fma(uint32_t wa, uint32_t wb, const float2* xs,
                                                 float2& acc) {
-  const float2 neg = make_float2(-MC_MAGIC_F, -MC_MAGIC_F);
-  const uint64_t MAG = 0x4B0000004B000000ull;
-  const uint64_t W = ((uint64_t)wb << 32) | wa;
-  // codes 5..7 (bits 20..31) would reach the exponent: take them from w >> 12
-  const uint64_t S = ((uint64_t)(wb >> 12) << 32) | (wa >> 12);
-  float2 q[8];
-  q[0] = mc_u64_as_float2((W & 0x0000000F0000000Full) | MAG);
-  q[1] = mc_u64_as_float2((W & 0x000000F0000000F0ull) | MAG);
-  q[2] = mc_u64_as_float2((W & 0x00000F0000000F00ull) | MAG);
-  q[3] = mc_u64_as_float2((W & 0x0000F0000000F000ull) | MAG);
-  q[4] = mc_u64_as_float2((W & 0x000F0000000F0000ull) | MAG);
-  q[5] = mc_u64_as_float2((S & 0x00000F0000000F00ull) | MAG);
-  q[6] = mc_u64_as_float2((S & 0x0000F0000000F000ull) | MAG);
-  q[7] = mc_u64_as_float2((S & 0x000F0000000F0000ull) | MAG);
-#pragma unroll
-  for (int j = 0; j < 8; ++j) acc = __ffma2_rn(__fadd2_rn(q[j], neg), xs[j], acc);
+  const unsigned long long NEG = 0xCB000000CB000000ull;  // (-2^23, -2^23)
+  const uint32_t MAG = MC_MAGIC;
+  const uint32_t sa = wa >> 12, sb = wb >> 12;
+  unsigned long long a = *reinterpret_cast<const unsigned long long*>(&acc);
+#define MC_Q4_STEP(J, A, B, M)                                                             \
+  {                                                                                        \
+    uint32_t lo, hi;                                                                       \
+    unsigned long long q;                                                                  \
+    asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(lo) : "r"(A), "n"(M), "r"(MAG));           \
+    asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(hi) : "r"(B), "n"(M), "r"(MAG));           \
+    asm("mov.b64 %0, {%1, %2};" : "=l"(q) : "r"(lo), "r"(hi));                            \
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(q) : "l"(q), "l"(NEG));                          \
+    asm("fma.rn.f32x2 %0, %1, %2, %0;"                                                     \
+        : "+l"(a)                                                                          \
+        : "l"(q), "l"(*reinterpret_cast<const unsigned long long*>(xs + (J))));            \
+  }
+  MC_Q4_STEP(0, wa, wb, 0xF)
+  MC_Q4_STEP(1, wa, wb, 0xF0)
+  MC_Q4_STEP(2, wa, wb, 0xF00)
+  MC_Q4_STEP(3, wa, wb, 0xF000)
+  MC_Q4_STEP(4, wa, wb, 0xF0000)
+  MC_Q4_STEP(5, sa, sb, 0xF00)
+  MC_Q4_STEP(6, sa, sb, 0xF000)
+  MC_Q4_STEP(7, sa, sb, 0xF0000)
+#undef MC_Q4_STEP
+  acc = *reinterpret_cast<const float2*>(&a);
 }
 
-// One Q4 group: 8 words (two uint4) against 32 pre-scaled activation pairs.
+// (c0 + c1) + (c2 + c3) per parity, then even + odd.
+__device__ __forceinline__ float quarters_qx(const float2* c) {
+  const float2 s = __fadd2_rn(__fadd2_rn(c[0], c[1]), __fadd2_rn(c[2], c[3]));
+  return __fadd_rn(s.x, s.y);
+}
+
+// One Q4 group: 8 words (two uint4) against 32 pre-scaled activation pairs;
+// word pair p is quarter p.
 __device__ __forceinline__ float q4_group_qx(uint4 a, uint4 b, const float2* xs) {
-  float2 acc = make_float2(0.0f, 0.0f);
-  q4_wordpair_fma(a.x, a.y, xs + 0, acc);
-  q4_wordpair_fma(a.z, a.w, xs + 8, acc);
-  q4_wordpair_fma(b.x, b.y, xs + 16, acc);
-  q4_wordpair_fma(b.z, b.w, xs + 24, acc);
-  return __fadd_rn(acc.x, acc.y);
+  float2 c[4];
+#pragma unroll
+  for (int p = 0; p < 4; ++p) c[p] = make_float2(0.0f, 0.0f);
+  q4_wordpair_fma(a.x, a.y, xs + 0, c[0]);
+  q4_wordpair_fma(a.z, a.w, xs + 8, c[1]);
+  q4_wordpair_fma(b.x, b.y, xs + 16, c[2]);
+  q4_wordpair_fma(b.z, b.w, xs + 24, c[3]);
+  return quarters_qx(c);
 }
 
 // One 4-code Q6 packet starting at byte `off` (0..3) of (lo, hi).
@@ -82,12 +109,15 @@ __device__ __forceinline__ void q6_packet_fma(uint32_t lo, uint32_t hi, float2 x
 // One Q6 group: 48 bytes (three uint4) against 32 pre-scaled activation pairs.
 __device__ __forceinline__ float q6_group_qx(uint4 a, uint4 b, uint4 c, const float2* xs) {
   const uint32_t W[12] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w, c.x, c.y, c.z, c.w};
-  float2 acc = make_float2(0.0f, 0.0f);
+  float2 q[4];  // packets 4p..4p+3 (codes 16p..16p+15) are quarter p
+#pragma unroll
+  for (int p = 0; p < 4; ++p) q[p] = make_float2(0.0f, 0.0f);
 #pragma unroll
   for (int m = 0; m < 16; ++m) {
     const int base = 3 * m;
     const int wi = base >> 2;
     const int wj = wi + 1 < 12 ? wi + 1 : 11;
+    float2& acc = q[m >> 2];
     switch (base & 3) {
       case 0: q6_packet_fma<0>(W[wi], W[wj], xs[2 * m], xs[2 * m + 1], acc); break;
       case 1: q6_packet_fma<1>(W[wi], W[wj], xs[2 * m], xs[2 * m + 1], acc); break;
@@ -95,7 +125,7 @@ __device__ __forceinline__ float q6_group_qx(uint4 a, uint4 b, uint4 c, const fl
       default: q6_packet_fma<3>(W[wi], W[wj], xs[2 * m], xs[2 * m + 1], acc); break;
     }
   }
-  return __fadd_rn(acc.x, acc.y);
+  return quarters_qx(q);
 }
 
 // Scale exponent of code k for the given bit width (matches MC_E4_* / MC_E6_*).

@@ -5,19 +5,21 @@
 // (gemv_gather_down_combine4), bit-identical to those three kernels.
 //
 // One CTA per SM, 16 warps. Timeline of a launch:
-//  * every CTA adds h + b and normalises the row (each needs the normed row);
-//    warp 0 of CTAs 0..E-1 has prefetched one router row and publishes that
-//    expert's logit, epoch-tagged, to the workspace;
-//  * warp 0 of every CTA polls the E tagged logits and picks the same top-4;
-//  * every thread issues L2 prefetches for its CTA's slice of the 4 experts'
-//    down rows, then each warp streams its gate/up row pairs straight from
-//    HBM (16-byte non-allocating loads, the next pair's loads issued before
-//    the current pair is reduced) and publishes bf16 act values;
-//  * after a release/acquire count of the CTAs that published, each CTA loads
-//    the act rows and computes its down rows from L2 (4 rows per warp in
-//    flight) and the weighted combine.
-// No bulk copies and no shared staging of weights: the weight stream is the
-// plain load pattern that reaches HBM speed on this part.
+//  * thread 0 of CTAs 0..E-1 starts a bulk (TMA) copy of one router row into
+//    shared memory; every CTA adds h + b and normalises the row (each needs
+//    the normed row); the router warps then publish their expert's logit,
+//    epoch-tagged, to the workspace;
+//  * warp 0 of every CTA waits for the E logits and picks the same top-4;
+//  * warp 0 issues this CTA's slice of the 4 experts' gate/up rows (codes,
+//    scales, biases; a few contiguous row ranges) and down codes as 1-D bulk
+//    copies into shared memory: the scales and biases first, then the codes
+//    in chunks of 16 row pairs with one mbarrier each, then the down codes,
+//    so the whole slice (~160 KB at I = 1536) is in flight at once --
+//    per-thread loads reach far less of HBM's rate for a burst of this size;
+//  * the warps compute the row pairs of each chunk as it lands, then publish
+//    the bf16 act values as tagged words; each CTA polls and stages all act
+//    rows and computes its down rows from shared memory and the weighted
+//    combine.
 //
 // Published values are self-validating words carrying the launch's epoch tag
 // (logits: tag32 << 32 | f32 bits). The caller's workspace (u32 words, zeroed
@@ -25,20 +27,22 @@
 //   ws[0]            epoch (advanced by the last CTA to finish)
 //   ws[1]            CTAs finished (reset by the last one)
 //   ws[2]            sticky error status bits: 1 logits wait gave up,
-//                    2 expert id out of range, 8 act wait
-//   ws[3]            CTAs that published their act rows (reset by the last
-//                    CTA to finish)
-//   ws[4]            router warps that published their logit (reset likewise)
-//   ws[5..8)         reserved
-//   ws[8..136)       64 tagged logits (u64)
-//   ws[136..)        act rows as bf16, [slot][row] (2 per word)
-// Every wait is bounded by a %globaltimer deadline; waiting lanes back off
-// between polls (a few thousand lanes spinning on the same lines slow the
-// writers down).
+//                    2 expert id out of range, 8 act wait, 16 a copy wait
+//   ws[3]            reserved (zero)
+//   ws[4]            router warps that published their logit (reset by the
+//                    last CTA to finish)
+//   ws[5..8)         reserved (zero)
+//   ws[8..136)       64 tagged logits (u64: tag32 << 32 | f32 bits)
+//   ws[136..)        act values [slot][row], one tagged word each
+//                    (tag16 << 16 | bf16 bits, tag16 = tag32 % 65535 + 1)
+// Every wait is bounded by a %globaltimer deadline; a CTA whose copies did
+// not all land waits for them (bounded again) before it exits.
 //
 // Arithmetic per output is the canonical order of the separate kernels, so
 // results are bit-identical to router_addnorm_route + gemv_gather_act +
 // gemv_gather_down_combine4 and to the CPU oracle.
+#include <atomic>
+
 #include "gemv_common.cuh"
 #include "mc_async.cuh"
 #include "route_common.cuh"
@@ -46,16 +50,45 @@
 
 namespace {
 
-constexpr int kThreads = 384;  // 12 warps, 3 per scheduler: up to 168 registers per thread
-                               // (the register file is split per scheduler), room for
-                               // kPairs row pairs in flight per warp
+constexpr int kThreads = 512;  // 16 warps, 4 per scheduler (<= 128 registers a thread)
 constexpr int kWarps = kThreads / 32;
-constexpr int kPairs = 4;      // gate/up row pairs each warp has in flight
-constexpr int kDnRows = 5;     // down rows per warp (12 warps, 3 per expert)
+constexpr int kMaxChunks = 8;   // gate/up chunks: 16 row pairs, then 32 each (up to 240)
+constexpr int kDnRows = 4;      // down rows per warp (16 warps, 4 per expert)
 constexpr int H = 2048;
 constexpr unsigned long long kTimeoutNs = 200000000ull;  // 200 ms per wait
-constexpr int kLogitWord = 8;  // first tagged-logit word in the workspace
-constexpr int kActWord = 136;  // first act word in the workspace
+constexpr int kLogitWord = 8;   // first tagged-logit word in the workspace
+constexpr int kActWord = 136;   // first act word in the workspace
+constexpr uint32_t kPrologueBytes = 8192 + 4096 + 8192;         // f32 row, bf16 row, router row
+
+// Byte offsets in dynamic shared memory (identical on host and device).
+// Gate/up chunk c (one mbarrier each) holds local row pairs
+// [chunk_begin(c), chunk_begin(c + 1)): 16 first (one per warp, so compute
+// starts early), then 32 (two per warp, two independent pairs in flight).
+__host__ __device__ inline int chunk_begin(int c) {
+  return c == 0 ? 0 : kWarps + 2 * kWarps * (c - 1);
+}
+__host__ __device__ inline int chunk_count(int np) {
+  return np <= kWarps ? 1 : 1 + (np - kWarps + 2 * kWarps - 1) / (2 * kWarps);
+}
+
+struct Layout {
+  int np_max, nr_max, nchunk_max;
+  uint32_t uc, sb, dn, pro, total;
+};
+
+__host__ __device__ inline Layout make_layout(int I, int G) {
+  Layout L;
+  L.np_max = (4 * I + G - 1) / G;
+  L.nr_max = (H + G - 1) / G;
+  L.nchunk_max = chunk_count(L.np_max);
+  L.uc = (uint32_t)L.np_max * (H / 2);      // gate codes at 0, up codes here
+  L.sb = 2 * L.uc;                          // gate scales, gate biases, up scales, up biases
+  L.dn = L.sb + 4u * (uint32_t)L.np_max * 64u;
+  L.pro = L.dn + 4u * (uint32_t)L.nr_max * (uint32_t)(I / 2);
+  const uint32_t act_bytes = 8u * (uint32_t)I;  // 4 x I bf16, reuses the prologue area
+  L.total = L.pro + (act_bytes > kPrologueBytes ? act_bytes : kPrologueBytes);
+  return L;
+}
 
 struct Params {
   const uint16_t* h;
@@ -76,43 +109,68 @@ struct Params {
   unsigned long long* trace;
 };
 
+constexpr int kTraceSlots = 32;  // per-CTA phase timestamps (mc_set_trace)
 #define TRACE(k) \
-  do { if (P.trace && t == 0) P.trace[16 * blockIdx.x + (k)] = mc_globaltimer(); } while (0)
+  do { if (P.trace && t == 0) P.trace[kTraceSlots * blockIdx.x + (k)] = mc_globaltimer(); } while (0)
 
 __device__ __forceinline__ void record_error(uint32_t* sync, uint32_t bit) {
   atomicOr(sync + 2, bit);
 }
 
-__device__ __forceinline__ void prefetch_l2(const void* p) {
-  asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
+// Waits for phase 0 of `bar` until `deadline`; the waiting warp sleeps
+// between polls.
+__device__ __forceinline__ bool wait_copies(uint64_t* bar, unsigned long long deadline) {
+  while (!mc_mbar_test_sleep(bar, 0, 20000u))
+    if (mc_globaltimer() > deadline) return false;
+  return true;
 }
 
-// One gate/up row pair of the stacked experts: codes (group `lane`) and the
-// raw bf16 scale/bias words, loaded ahead of use.
-struct PairLoad {
-  QGroup<4> g, u;
-  uint16_t gs, gb, us, ub;
-  __device__ __forceinline__ void load(const Params& P, size_t row, int lane) {
-    g.load(reinterpret_cast<const uint8_t*>(P.gate.codes) + row * (H / 2), lane);
-    u.load(reinterpret_cast<const uint8_t*>(P.up.codes) + row * (H / 2), lane);
-    gs = __ldg(P.gate.scales + row * (H / 64) + lane);
-    gb = __ldg(P.gate.biases + row * (H / 64) + lane);
-    us = __ldg(P.up.scales + row * (H / 64) + lane);
-    ub = __ldg(P.up.biases + row * (H / 64) + lane);
+// Router logit of one row in shared memory against the normed f32 row, in
+// the canonical order of RouterRow::dot (lane owns elements 256j + 8*lane +
+// 0..7, j = 0..7, one fma chain, then the warp butterfly).
+template <int DT>
+__device__ __forceinline__ float router_dot_smem(const uint8_t* row, const float* n, int lane) {
+  float acc = 0.0f;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const float4 n0 = *reinterpret_cast<const float4*>(n + 256 * j + 8 * lane);
+    const float4 n1 = *reinterpret_cast<const float4*>(n + 256 * j + 8 * lane + 4);
+    const float nv[8] = {n0.x, n0.y, n0.z, n0.w, n1.x, n1.y, n1.z, n1.w};
+    if (DT == MC_DTYPE_BF16) {
+      const uint4 w = *reinterpret_cast<const uint4*>(row + 2 * (256 * j + 8 * lane));
+      const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        acc = __fmaf_rn(mc_bf16_to_f32((uint16_t)(ww[i >> 1] >> (16 * (i & 1)))), nv[i], acc);
+    } else {
+      const float4 a = *reinterpret_cast<const float4*>(row + 4 * (256 * j + 8 * lane));
+      const float4 b = *reinterpret_cast<const float4*>(row + 4 * (256 * j + 8 * lane + 4));
+      const float wv[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+#pragma unroll
+      for (int i = 0; i < 8; ++i) acc = __fmaf_rn(wv[i], nv[i], acc);
+    }
   }
-};
+  return mc_warp_butterfly(acc);
+}
+
+// One Q4 group (32 code bytes) of a row in shared memory.
+__device__ __forceinline__ float smem_group_qx(const uint8_t* p, const float2* xs) {
+  const uint4* q = reinterpret_cast<const uint4*>(p);
+  return q4_group_qx(q[0], q[1], xs);
+}
 
 template <int DT>
-__global__ void __maxnreg__(168) moe_decode_fused_kernel(const Params P) {
-  __shared__ __align__(16) float nrow[H];
-  __shared__ __align__(16) uint16_t nbf[H];
+__global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(const Params P,
+                                                                      const Layout L) {
+  extern __shared__ __align__(128) uint8_t sm[];
   __shared__ float red[8];
   __shared__ float zs[64];
   __shared__ uint32_t ids_s[4];
   __shared__ uint16_t wts_s[4];
   __shared__ float p_s[4][32];
-  __shared__ __align__(16) uint16_t act_s[4 * 2048];  // 16-byte chunks XOR-swizzled per group
+  __shared__ float gu_s[2][256];  // bf16-rounded gate and up sums per local pair
   __shared__ uint32_t flag_s;
+  __shared__ __align__(8) uint64_t bar_pro, bar_sb, bar_dn, bar_gu[kMaxChunks];
 
   const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
   const int G = gridDim.x, cta = blockIdx.x;
@@ -121,25 +179,49 @@ __global__ void __maxnreg__(168) moe_decode_fused_kernel(const Params P) {
   const int p0 = (int)(((long)cta * npairs) / G), p1 = (int)(((long)(cta + 1) * npairs) / G);
   const int i0 = (int)(((long)cta * H) / G), i1 = (int)(((long)(cta + 1) * H) / G);
   const int np = p1 - p0, nr = i1 - i0;
+  const int nchunk = chunk_count(np);
+  const int dn_code = I / 2, Gd = I / 64;
   uint32_t* sync = P.sync;
   unsigned long long* logits64 = reinterpret_cast<unsigned long long*>(sync + kLogitWord);
-  uint16_t* act = reinterpret_cast<uint16_t*>(sync + kActWord);
+  uint32_t* actw = sync + kActWord;
+  float* nrow = reinterpret_cast<float*>(sm + L.pro);
+  uint16_t* nbf = reinterpret_cast<uint16_t*>(sm + L.pro + 8192);
+  uint8_t* rrow = sm + L.pro + 12288;
+  uint16_t* act_s = reinterpret_cast<uint16_t*>(sm + L.pro);  // after the prologue
   const uint32_t epoch = *reinterpret_cast<volatile uint32_t*>(sync);
   const uint32_t tag32 = epoch == 0xffffffffu ? 1u : epoch + 1u;
+  const uint32_t tag16 = tag32 % 65535u + 1u;  // never 0, differs from the last launch's
+  const bool router_cta = cta < P.E;
+  const unsigned long long t_start = mc_globaltimer();
   bool ok = true;
   TRACE(0);
-  if (t == 0) flag_s = 0;
 
-  // ---- router row prefetch (warp 0 of CTA e < E), then add + RMSNorm (all CTAs)
-  const bool router_warp = warp == 0 && cta < P.E;
-  RouterRow<DT> rr;
-  if (router_warp) rr.load(P.router_w, cta, lane);
+  // ---- barriers, the router row copy, and this thread's h / b / norm_w words
+  if (t == 0) {
+    flag_s = 0;
+    mc_mbar_init(&bar_pro, 1);
+    mc_mbar_init(&bar_sb, 1);
+    mc_mbar_init(&bar_dn, 1);
+    for (int c = 0; c < kMaxChunks; ++c) mc_mbar_init(bar_gu + c, 1);
+    mc_fence_barrier_init();
+    if (router_cta) {
+      const uint32_t rb = DT == MC_DTYPE_BF16 ? 2 * H : 4 * H;
+      mc_mbar_expect_tx(&bar_pro, rb);
+      mc_bulk_g2s(rrow, reinterpret_cast<const uint8_t*>(P.router_w) + (size_t)cta * rb, rb,
+                  &bar_pro, mc_policy_evict_first());
+    }
+  }
+  uint4 hv = make_uint4(0, 0, 0, 0), bv = make_uint4(0, 0, 0, 0), wv = make_uint4(0, 0, 0, 0);
+  if (t < 256) {
+    hv = mc_ldg_stream(reinterpret_cast<const uint4*>(P.h) + t);
+    if (P.badd) bv = mc_ldg_stream(reinterpret_cast<const uint4*>(P.badd) + t);
+    wv = mc_ldg_stream(reinterpret_cast<const uint4*>(P.norm_w) + t);
+  }
+
+  // ---- add + RMSNorm (canonical order of addnorm_row_2048)
   float hp[8];
   if (t < 256) {
     float acc = 0.0f;
-    const uint4 hv = __ldg(reinterpret_cast<const uint4*>(P.h) + t);
-    uint4 bv = make_uint4(0, 0, 0, 0);
-    if (P.badd) bv = __ldg(reinterpret_cast<const uint4*>(P.badd) + t);
     const uint32_t hw[4] = {hv.x, hv.y, hv.z, hv.w}, bw[4] = {bv.x, bv.y, bv.z, bv.w};
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
@@ -159,15 +241,15 @@ __global__ void __maxnreg__(168) moe_decode_fused_kernel(const Params P) {
     for (int j = 1; j < 8; ++j) total = __fadd_rn(total, red[j]);
     const float inv =
         __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fmul_rn(total, 1.0f / 2048.0f), P.eps)));
-    const uint4 wv = __ldg(reinterpret_cast<const uint4*>(P.norm_w) + t);
     const uint32_t ww[4] = {wv.x, wv.y, wv.z, wv.w};
     float n[8];
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
       const float wf = mc_bf16_to_f32((uint16_t)(ww[i >> 1] >> (16 * (i & 1))));
       n[i] = mc_round_bf16(__fmul_rn(__fmul_rn(hp[i], inv), wf));
-      nrow[8 * t + i] = n[i];
     }
+    reinterpret_cast<float4*>(nrow)[2 * t] = make_float4(n[0], n[1], n[2], n[3]);
+    reinterpret_cast<float4*>(nrow)[2 * t + 1] = make_float4(n[4], n[5], n[6], n[7]);
     const uint4 nb = pack8_bf16(n);
     reinterpret_cast<uint4*>(nbf)[t] = nb;
     if (cta == 0) {
@@ -178,14 +260,18 @@ __global__ void __maxnreg__(168) moe_decode_fused_kernel(const Params P) {
   __syncthreads();
   TRACE(1);
 
-  // ---- router logit of expert `cta` (warp 0), published epoch-tagged
-  if (router_warp) {
-    const float z = rr.dot(nrow, lane);
+  // ---- router logit of expert `cta` (warp 0), published epoch-tagged; the
+  // release add (which orders the store before it) counts the published
+  // logits, so readers poll one word instead of all E
+  if (router_cta && warp == 0) {
+    const bool got = wait_copies(&bar_pro, t_start + kTimeoutNs);
+    const float z = got ? router_dot_smem<DT>(rrow, nrow, lane) : 0.0f;
+    TRACE(13);
     if (lane == 0) {
+      if (!got) record_error(sync, 16u);
       P.logits[cta] = z;
       mc_st_publish_u64(logits64 + cta,
                         ((unsigned long long)tag32 << 32) | (unsigned long long)__float_as_uint(z));
-      __threadfence();
       mc_red_release_add(sync + 4, 1u);
     }
   }
@@ -206,9 +292,10 @@ __global__ void __maxnreg__(168) moe_decode_fused_kernel(const Params P) {
           got = false;
           break;
         }
-        __nanosleep(64);
+        __nanosleep(32);
       }
     }
+    TRACE(14);
     got = __shfl_sync(0xffffffffu, got ? 1 : 0, 0) != 0;
     if (got && 2 * lane < P.E) {
       const int i = 2 * lane;
@@ -221,12 +308,13 @@ __global__ void __maxnreg__(168) moe_decode_fused_kernel(const Params P) {
           got = false;
           break;
         }
-        __nanosleep(32);
+        __nanosleep(64);
       }
       zs[i] = __uint_as_float((uint32_t)v0);
       if (i + 1 < P.E) zs[i + 1] = __uint_as_float((uint32_t)v1);
     }
     got = __all_sync(0xffffffffu, got);
+    TRACE(15);
     if (!got) {
       if (lane == 0) {
         record_error(sync, 1u);
@@ -250,104 +338,204 @@ __global__ void __maxnreg__(168) moe_decode_fused_kernel(const Params P) {
         }
         if (flag_s == 2) record_error(sync, 2u);
       }
+      TRACE(12);
     }
   }
   __syncthreads();
   TRACE(3);
   if (flag_s) ok = false;
 
-  const int dn_code = I / 2, Gd = I / 64;
-  if (ok) {
-    // ---- L2 prefetch of this CTA's down rows (codes, scales, biases) of the
-    // 4 experts: contiguous row ranges, one 128-byte line per thread
-    const int code_lines = (nr * dn_code + 127) / 128, sb_lines = (nr * Gd * 2 + 127) / 128;
-    const int per_e = code_lines + 2 * sb_lines;
-    for (int l = t; l < 4 * per_e; l += kThreads) {
-      const int r = l / per_e, k = l % per_e;
-      const size_t row = (size_t)ids_s[r] * H + i0;
-      if (k < code_lines) {
-        prefetch_l2(reinterpret_cast<const uint8_t*>(P.down.codes) + row * dn_code + 128 * k);
-      } else {
-        const int kk = k - code_lines;
-        const uint16_t* base = kk < sb_lines ? P.down.scales : P.down.biases;
-        prefetch_l2(reinterpret_cast<const uint8_t*>(base + row * Gd) + 128 * (kk % sb_lines));
+  // ---- warp 0 issues this CTA's expert rows as bulk copies: the gate/up
+  // scales and biases, the gate/up codes chunk by chunk, then the down codes;
+  // lane 0 posts every byte count first, then the 32 lanes issue the copies
+  // round robin
+  const bool issued = ok;
+  if (ok && warp == 0) {
+    if (lane == 0) {
+      mc_mbar_expect_tx(&bar_sb, (uint32_t)np * 256u);
+      for (int c = 0; c < nchunk; ++c) {
+        const int q0 = chunk_begin(c), q1 = min(np, chunk_begin(c + 1));
+        mc_mbar_expect_tx(bar_gu + c, (uint32_t)(q1 - q0) * (uint32_t)H);
+      }
+      mc_mbar_expect_tx(&bar_dn, 4u * (uint32_t)nr * (uint32_t)dn_code);
+    }
+    __syncwarp();
+    const uint64_t pol = mc_policy_evict_first();
+    int k = 0;
+    auto emit = [&](uint32_t dst, const void* src, uint32_t n, uint64_t* bar) {
+      if ((k++ & 31) == lane) mc_bulk_g2s(sm + dst, src, n, bar, pol);
+    };
+    // local pairs [0, qs) and [qs, np) each lie in one expert slot
+    const int qs = min(np, (p0 / I + 1) * I - p0);
+    const uint32_t sbs = (uint32_t)L.np_max * 64u;
+#pragma unroll
+    for (int sg = 0; sg < 2; ++sg) {
+      const int qa = sg == 0 ? 0 : qs, qb = sg == 0 ? qs : np;
+      if (qa >= qb) continue;
+      const int slot = (p0 + qa) / I;
+      const size_t row = (size_t)ids_s[slot] * I + (p0 + qa - slot * I);
+      const uint32_t n = (uint32_t)(qb - qa) * 64u, d = L.sb + (uint32_t)qa * 64u;
+      emit(d, P.gate.scales + row * 32, n, &bar_sb);
+      emit(d + sbs, P.gate.biases + row * 32, n, &bar_sb);
+      emit(d + 2 * sbs, P.up.scales + row * 32, n, &bar_sb);
+      emit(d + 3 * sbs, P.up.biases + row * 32, n, &bar_sb);
+    }
+    for (int c = 0; c < nchunk; ++c) {
+      const int q0 = chunk_begin(c), q1 = min(np, chunk_begin(c + 1));
+#pragma unroll
+      for (int sg = 0; sg < 2; ++sg) {
+        const int qa = max(q0, sg == 0 ? 0 : qs), qb = min(q1, sg == 0 ? qs : np);
+        if (qa >= qb) continue;
+        const int slot = (p0 + qa) / I;
+        const size_t row = (size_t)ids_s[slot] * I + (p0 + qa - slot * I);
+        const uint32_t n = (uint32_t)(qb - qa);
+        emit((uint32_t)qa * (H / 2), reinterpret_cast<const uint8_t*>(P.gate.codes) + row * (H / 2),
+             n * (H / 2), bar_gu + c);
+        emit(L.uc + (uint32_t)qa * (H / 2),
+             reinterpret_cast<const uint8_t*>(P.up.codes) + row * (H / 2), n * (H / 2), bar_gu + c);
       }
     }
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      const size_t row = (size_t)ids_s[r] * H + i0;
+      emit(L.dn + (uint32_t)(r * L.nr_max) * (uint32_t)dn_code,
+           reinterpret_cast<const uint8_t*>(P.down.codes) + row * dn_code,
+           (uint32_t)(nr * dn_code), &bar_dn);
+    }
+  }
+  TRACE(11);
 
-    // ---- gate/up + SwiGLU: warp w takes pairs w, w+12, w+24, w+36 of this CTA
-    // (kPairs at a time), every load issued before the first reduction
-    auto pair_row = [&](int q) -> size_t {
-      const int slot = (p0 + q) / I;
-      return (size_t)ids_s[slot] * I + (p0 + q - slot * I);
+  // ---- gate/up from shared memory as the chunks land: warp w takes pair w
+  // of chunk 0 and pairs w, w + 16 of every later chunk; lane 0 keeps the
+  // bf16-rounded sums, SwiGLU runs once all pairs are done
+  bool copies_ok = true;
+  if (ok) {
+    const unsigned long long deadline = mc_globaltimer() + kTimeoutNs;
+    const uint32_t sbs = (uint32_t)L.np_max * 64u;
+    const uint16_t* sb16 = reinterpret_cast<const uint16_t*>(sm + L.sb);
+    // gate and up sums of pair q (all lanes get the butterflied values)
+    auto pair_terms = [&](int q, float& ag, float& au) {
+      const float gs = mc_bf16_to_f32(sb16[(q * 64u) / 2 + lane]);
+      const float gb = mc_bf16_to_f32(sb16[(sbs + q * 64u) / 2 + lane]);
+      const float us = mc_bf16_to_f32(sb16[(2 * sbs + q * 64u) / 2 + lane]);
+      const float ub = mc_bf16_to_f32(sb16[(3 * sbs + q * 64u) / 2 + lane]);
+      ag = __fadd_rn(0.0f, __fmaf_rn(gs, smem_group_qx(sm + q * (H / 2) + 32 * lane, xs),
+                                     __fmul_rn(gb, xg)));
+      au = __fadd_rn(0.0f, __fmaf_rn(us, smem_group_qx(sm + L.uc + q * (H / 2) + 32 * lane, xs),
+                                     __fmul_rn(ub, xg)));
     };
-    for (int base = 0; base < np; base += kWarps * kPairs) {
-      PairLoad pl[kPairs];
-#pragma unroll
-      for (int k = 0; k < kPairs; ++k) {
-        const int q = base + warp + kWarps * k;
-        if (q < np) pl[k].load(P, pair_row(q), lane);
+    if (warp < np && !wait_copies(&bar_sb, deadline)) copies_ok = false;
+    for (int c = 0; copies_ok && c < nchunk; ++c) {
+      const int qb = chunk_begin(c), qe = min(np, chunk_begin(c + 1));
+      const int q = qb + warp;
+      if (q >= qe) break;
+      if (!wait_copies(bar_gu + c, deadline)) {
+        copies_ok = false;
+        break;
       }
-#pragma unroll
-      for (int k = 0; k < kPairs; ++k) {
-        const int q = base + warp + kWarps * k;
-        if (q >= np) break;
-        float acc_g = 0.0f, acc_u = 0.0f;
-        acc_g = __fadd_rn(acc_g, __fmaf_rn(mc_bf16_to_f32(pl[k].gs), pl[k].g.qx(xs),
-                                           __fmul_rn(mc_bf16_to_f32(pl[k].gb), xg)));
-        acc_u = __fadd_rn(acc_u, __fmaf_rn(mc_bf16_to_f32(pl[k].us), pl[k].u.qx(xs),
-                                           __fmul_rn(mc_bf16_to_f32(pl[k].ub), xg)));
-        const float gsum = mc_warp_butterfly(acc_g);
-        const float usum = mc_warp_butterfly(acc_u);
+      if (c < 8) TRACE(16 + c);
+      if (c == 0) {
+        float ag, au;
+        pair_terms(q, ag, au);
+        ag = mc_warp_butterfly(ag);
+        au = mc_warp_butterfly(au);
         if (lane == 0) {
-          const float g = mc_round_bf16(gsum);
-          const float u = mc_round_bf16(usum);
-          const float sl = mc_round_bf16(mc_silu(g));
-          act[p0 + q] = mc_f32_to_bf16(__fmul_rn(sl, u));
+          gu_s[0][q] = mc_round_bf16(ag);
+          gu_s[1][q] = mc_round_bf16(au);
+        }
+      } else {
+        const int q2 = q + kWarps, q2c = min(q2, qe - 1);  // a repeat of q when absent
+        float ag, au, ag2, au2;
+        pair_terms(q, ag, au);
+        pair_terms(q2c, ag2, au2);
+        ag = mc_warp_butterfly(ag);
+        au = mc_warp_butterfly(au);
+        ag2 = mc_warp_butterfly(ag2);
+        au2 = mc_warp_butterfly(au2);
+        if (lane == 0) {
+          gu_s[0][q] = mc_round_bf16(ag);
+          gu_s[1][q] = mc_round_bf16(au);
+          if (q2 < qe) {
+            gu_s[0][q2] = mc_round_bf16(ag2);
+            gu_s[1][q2] = mc_round_bf16(au2);
+          }
         }
       }
+      if (c < 8) TRACE(24 + c);
+    }
+    if (!copies_ok && lane == 0) {
+      record_error(sync, 16u);
+      flag_s = 1;
     }
   }
   __syncthreads();
   TRACE(4);
+  // SwiGLU per pair, one thread each: act = bf16(bf16(silu(g)) * u),
+  // published as a tagged word (tag16 << 16 | bf16 bits)
+  if (ok && t < np) {
+    const float sl = mc_round_bf16(mc_silu(gu_s[0][t]));
+    const uint32_t a = mc_f32_to_bf16(__fmul_rn(sl, gu_s[1][t]));
+    mc_st_publish_u32(actw + p0 + t, (tag16 << 16) | a);
+  }
 
-  // ---- act published by every CTA (release/acquire counter, one poller)
-  if (t == 0) {
-    __threadfence();
-    mc_red_release_add(sync + 3, 1u);
-    const unsigned long long deadline = mc_globaltimer() + kTimeoutNs;
-    while (mc_ld_acquire(sync + 3) < (uint32_t)G) {
-      if (mc_globaltimer() > deadline) {
-        record_error(sync, 8u);
-        flag_s = 1;
-        break;
-      }
-      __nanosleep(32);
+  // ---- down scales and biases of this warp's rows (their rows are not
+  // 16-byte multiples for every I), loaded while the act rows are exchanged
+  const int dr = warp & 3, j0 = warp >> 2;  // slot, first row (rows j0, j0+4, ...)
+  uint16_t dsc[kDnRows] = {}, dbi[kDnRows] = {};
+  if (ok && lane < Gd) {
+#pragma unroll
+    for (int k = 0; k < kDnRows; ++k) {
+      const int j = min(j0 + 4 * k, nr - 1);
+      const size_t row = (size_t)ids_s[dr] * H + i0 + j;
+      dsc[k] = __ldg(P.down.scales + row * Gd + lane);
+      dbi[k] = __ldg(P.down.biases + row * Gd + lane);
     }
   }
-  __syncthreads();
-  TRACE(5);
-  if (flag_s) ok = false;
 
-  // ---- stage the act rows once per CTA (L2 -> shared, swizzled so the
-  // per-lane group reads below are bank-conflict free)
+  // ---- stage the act rows once per CTA: poll the tagged words (8 per
+  // 32 bytes) until every tag is this launch's, then store the bf16 values
+  // to shared memory, 16-byte chunks swizzled so the per-lane group reads
+  // below are bank-conflict free
   if (ok) {
-    const int nchunk16 = (4 * I) / 8;  // 16-byte chunks of bf16 act
-    for (int c = t; c < nchunk16; c += kThreads) {
-      const uint4 v = __ldcg(reinterpret_cast<const uint4*>(act) + c);
-      const int g = c >> 3;            // 64-value group (across slots)
+    const unsigned long long deadline = mc_globaltimer() + kTimeoutNs;
+    const int nchunk16 = (4 * I) / 8;  // chunks of 8 act values
+    bool got = true;
+    for (int c = t; got && c < nchunk16; c += kThreads) {
+      uint4 a, b;
+      for (;;) {
+        a = mc_ld_poll_v4(actw + 8 * c);
+        b = mc_ld_poll_v4(actw + 8 * c + 4);
+        const uint32_t hi = (a.x >> 16) & (a.y >> 16) & (a.z >> 16) & (a.w >> 16) &
+                            (b.x >> 16) & (b.y >> 16) & (b.z >> 16) & (b.w >> 16);
+        const uint32_t lo = (a.x >> 16) | (a.y >> 16) | (a.z >> 16) | (a.w >> 16) |
+                            (b.x >> 16) | (b.y >> 16) | (b.z >> 16) | (b.w >> 16);
+        if (hi == tag16 && lo == tag16) break;  // all eight tags equal tag16
+        if (mc_globaltimer() > deadline) {
+          got = false;
+          break;
+        }
+        __nanosleep(64);
+      }
+      const uint4 v = make_uint4(__byte_perm(a.x, a.y, 0x5410), __byte_perm(a.z, a.w, 0x5410),
+                                 __byte_perm(b.x, b.y, 0x5410), __byte_perm(b.z, b.w, 0x5410));
+      const int g = c >> 3;  // 64-value group (across slots)
       reinterpret_cast<uint4*>(act_s)[(g << 3) | ((c & 7) ^ (g & 7))] = v;
+    }
+    if (!got) {
+      record_error(sync, 8u);
+      flag_s = 1;
     }
   }
   __syncthreads();
   TRACE(10);
+  if (flag_s) ok = false;
 
-  // ---- down rows (from L2, 4 rows per warp in flight) + weighted combine
-  if (ok && warp < 12) {
-    const int r = warp & 3;
-    float2 dxs[1][32];
-    float dxg[1] = {0.0f};
+  // ---- down rows from shared memory + weighted combine
+  if (ok) {
+    float2 dxs[32];
+    float dxg = 0.0f;
     if (lane < Gd) {
-      const int g = r * Gd + lane;
+      const int g = dr * Gd + lane;
       const uint4* src = reinterpret_cast<const uint4*>(act_s) + (g << 3);
       float xv[64];
 #pragma unroll
@@ -360,27 +548,28 @@ __global__ void __maxnreg__(168) moe_decode_fused_kernel(const Params P) {
           xv[8 * c + 2 * h + 1] = __uint_as_float(wds[h] & 0xffff0000u);
         }
       }
-      dxg[0] = prescale_group_x<4>(xv, dxs[0]);
+      dxg = prescale_group_x<4>(xv, dxs);
     }
-    const int j0 = warp >> 2;  // 0..2: rows j0, j0+3, ... of expert slot r
-    const uint8_t* rows[kDnRows];
-    const uint16_t* sc[kDnRows];
-    const uint16_t* bi[kDnRows];
+    const bool landed = wait_copies(&bar_dn, mc_globaltimer() + kTimeoutNs);
+    if (!landed && lane == 0) record_error(sync, 16u);
+    TRACE(9);
+    if (landed && nr > 0) {
+      float acc[kDnRows] = {};
+      if (lane < Gd) {  // one branch around all rows so their chains interleave
 #pragma unroll
-    for (int k = 0; k < kDnRows; ++k) {
-      const int j = min(j0 + 3 * k, nr - 1);
-      const size_t row = (size_t)ids_s[r] * H + i0 + j;
-      rows[k] = reinterpret_cast<const uint8_t*>(P.down.codes) + row * dn_code;
-      sc[k] = P.down.scales + row * Gd;
-      bi[k] = P.down.biases + row * Gd;
-    }
-    if (nr > 0) {
-      float sum[kDnRows];
-      rows_dot<4, 1, kDnRows>(rows, sc, bi, Gd, lane, dxs, dxg, sum);
-      if (lane == 0) {
+        for (int k = 0; k < kDnRows; ++k) {
+          const int j = min(j0 + 4 * k, nr - 1);
+          const uint8_t* rowp = sm + L.dn + (uint32_t)(dr * L.nr_max + j) * (uint32_t)dn_code;
+          const float s = mc_bf16_to_f32(dsc[k]);
+          const float b = mc_bf16_to_f32(dbi[k]);
+          acc[k] = __fadd_rn(0.0f, __fmaf_rn(s, smem_group_qx(rowp + 32 * lane, dxs),
+                                             __fmul_rn(b, dxg)));
+        }
+      }
 #pragma unroll
-        for (int k = 0; k < kDnRows; ++k)
-          if (j0 + 3 * k < nr) p_s[r][j0 + 3 * k] = mc_round_bf16(sum[k]);
+      for (int k = 0; k < kDnRows; ++k) {
+        const float sum = mc_warp_butterfly(acc[k]);
+        if (lane == 0 && j0 + 4 * k < nr) p_s[dr][j0 + 4 * k] = mc_round_bf16(sum);
       }
     }
   }
@@ -394,13 +583,22 @@ __global__ void __maxnreg__(168) moe_decode_fused_kernel(const Params P) {
     P.out[i0 + t] = mc_f32_to_bf16(tot);
   }
 
+  // ---- every issued copy has landed before the CTA exits (immediate unless
+  // a wait above gave up)
+  if (t == 0 && (issued || router_cta)) {
+    const unsigned long long deadline = mc_globaltimer() + kTimeoutNs;
+    bool all = !router_cta || wait_copies(&bar_pro, deadline);
+    if (issued) all = wait_copies(&bar_sb, deadline) && wait_copies(&bar_dn, deadline) && all;
+    for (int c = 0; issued && c < nchunk; ++c) all = wait_copies(bar_gu + c, deadline) && all;
+    if (!all) record_error(sync, 16u);
+  }
+
   // ---- the last CTA to finish resets the counters and advances the epoch
   TRACE(7);
   if (t == 0) {
     const uint32_t done = atomicAdd(sync + 1, 1u);
     if (done == (uint32_t)G - 1) {
       sync[1] = 0u;
-      sync[3] = 0u;
       sync[4] = 0u;
       __threadfence();
       *reinterpret_cast<volatile uint32_t*>(sync) = tag32;
@@ -447,9 +645,9 @@ extern "C" int mc_moe_decode_layer(mc_ctx* ctx, const uint16_t* h, const uint16_
              "moe_decode_layer: router dtype %d", router_dtype);
   MC_REQUIRE(route_mode == MC_ROUTE_SOFTMAX_RENORM || route_mode == MC_ROUTE_SIGMOID_BIAS,
              "moe_decode_layer: route mode %d", route_mode);
-  const void* a16[] = {h,            norm_w,       h_out,      normed,     router_w,
-                       gate->scales, gate->biases, up->scales, up->biases, down->scales,
-                       down->biases, sync};
+  const void* a16[] = {h,           norm_w,       h_out,        normed,     router_w,
+                       gate->codes, gate->scales, gate->biases, up->codes,  up->scales,
+                       up->biases,  down->codes,  down->scales, down->biases, sync};
   for (const void* p : a16)
     MC_REQUIRE(mc_aligned(p, 16), "moe_decode_layer: buffers must be 16-byte aligned");
   MC_REQUIRE(!b || mc_aligned(b, 16), "moe_decode_layer: b must be 16-byte aligned");
@@ -457,29 +655,42 @@ extern "C" int mc_moe_decode_layer(mc_ctx* ctx, const uint16_t* h, const uint16_
                  (const void*)normed != (const void*)h && (const void*)normed != (const void*)b,
              "moe_decode_layer: h_out/normed must not alias h or b");
   const int G = ctx->num_sms;
-  // each CTA: <= 15 down rows (3 warps x kDnRows per expert), <= 12 x kPairs
-  // gate/up pairs per pass, one router warp per expert among the CTAs
-  MC_REQUIRE((H + G - 1) / G <= 3 * kDnRows && G >= n_experts,
+  // each CTA: <= 16 down rows (4 warps x kDnRows per expert), <= kMaxChunks
+  // chunks of gate/up pairs, one router row per expert among the CTAs, and
+  // its whole slice of expert rows in shared memory
+  const Layout L = make_layout(I, G);
+  MC_REQUIRE(L.nr_max <= 4 * kDnRows && L.nchunk_max <= kMaxChunks && G >= n_experts,
              "moe_decode_layer: too few SMs (%d)", G);
+  MC_REQUIRE((int)L.total + 4096 <= ctx->max_smem_optin,
+             "moe_decode_layer: %u B of shared memory per CTA exceeds the device's %d", L.total,
+             ctx->max_smem_optin);
   Params P{h, b, norm_w, h_out, normed, router_w, expert_bias, logits, ids, weights, *gate, *up,
            *down, out, sync, eps, route_eps, route_mode, n_experts, I,
-           ctx->trace && ctx->trace_len >= 16 * G ? ctx->trace : nullptr};
+           ctx->trace && ctx->trace_len >= kTraceSlots * G ? ctx->trace : nullptr};
   void* fn = router_dtype == MC_DTYPE_BF16 ? (void*)moe_decode_fused_kernel<MC_DTYPE_BF16>
                                            : (void*)moe_decode_fused_kernel<MC_DTYPE_F32>;
+  // the dynamic shared memory limit is raised once per device and kernel
+  static std::atomic<int> smem_set[2][64];
+  std::atomic<int>& cur = smem_set[router_dtype == MC_DTYPE_BF16 ? 0 : 1][ctx->device & 63];
+  if (cur.load() < (int)L.total) {
+    MC_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 ctx->max_smem_optin - 4096));
+    cur.store(ctx->max_smem_optin - 4096);
+  }
   int per_sm = 0;  // every CTA must be resident at once (cross-CTA waits)
-  MC_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, kThreads, 0));
+  MC_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, kThreads, L.total));
   MC_REQUIRE(per_sm >= 1, "moe_decode_layer: kernel does not fit one CTA per SM");
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(G);
   cfg.blockDim = dim3(kThreads);
-  cfg.dynamicSmemBytes = 0;
+  cfg.dynamicSmemBytes = L.total;
   cfg.stream = ctx->stream;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeCooperative;
   attr[0].val.cooperative = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  void* args[] = {(void*)&P};
+  void* args[] = {(void*)&P, (void*)&L};
   MC_CUDA(cudaLaunchKernelExC(&cfg, fn, args));
   return mc_after_launch("moe_decode_fused_kernel");
 }

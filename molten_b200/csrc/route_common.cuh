@@ -66,54 +66,56 @@ struct RouterRow<MC_DTYPE_F32> {
   }
 };
 
+// Orderable 32-bit key of a candidate: a larger value has a larger key, +0
+// and -0 share one key (they compare equal), a NaN gets 0 like a used or
+// absent entry (never better than a number; -inf maps to 0x007fffff).
+__device__ __forceinline__ uint32_t top4_key(float v) {
+  if (v != v) return 0u;
+  const uint32_t b = __float_as_uint(v == 0.0f ? 0.0f : v);
+  return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+}
+
 // Warp top-4 over E <= 64 logits (lane owns experts lane and lane+32), the
-// selection and weight rules of oracle or_route_topk. Results valid in lane 0.
+// selection and weight rules of oracle or_route_topk: each round takes the
+// largest value, the lowest index among equal values, and index 0 when no
+// candidate is left. A round is two warp reductions (max of the keys, then
+// min of the indices holding it). Results valid in lane 0.
 __device__ __forceinline__ void warp_top4(const float* z, int E, int mode, const float* bias,
                                           float route_eps, uint32_t* ids_out,
                                           uint16_t* w_out) {
   const int lane = threadIdx.x & 31;
   float s0 = -INFINITY, s1 = -INFINITY, v0 = -INFINITY, v1 = -INFINITY;
-  bool u0 = lane >= E, u1 = lane + 32 >= E;
-  if (!u0) {
+  const bool has0 = lane < E, has1 = lane + 32 < E;
+  if (has0) {
     const float zz = z[lane];
     s0 = mode == MC_ROUTE_SOFTMAX_RENORM ? zz : mc_sigmoid(zz);
     v0 = mode == MC_ROUTE_SOFTMAX_RENORM ? zz : __fadd_rn(s0, bias ? bias[lane] : 0.0f);
   }
-  if (!u1) {
+  if (has1) {
     const float zz = z[lane + 32];
     s1 = mode == MC_ROUTE_SOFTMAX_RENORM ? zz : mc_sigmoid(zz);
     v1 = mode == MC_ROUTE_SOFTMAX_RENORM ? zz : __fadd_rn(s1, bias ? bias[lane + 32] : 0.0f);
   }
+  uint32_t k0 = has0 ? top4_key(v0) : 0u, k1 = has1 ? top4_key(v1) : 0u;
   uint32_t ch[4];
+#pragma unroll
+  for (int r = 0; r < 4; ++r) {
+    const uint32_t m = __reduce_max_sync(0xffffffffu, k0 > k1 ? k0 : k1);
+    uint32_t pick = 0u;
+    if (m != 0u) {
+      const uint32_t cand = k0 == m ? (uint32_t)lane : (k1 == m ? (uint32_t)lane + 32u : 64u);
+      pick = __reduce_min_sync(0xffffffffu, cand);
+    }
+    if (pick == (uint32_t)lane) k0 = 0u;
+    if (pick == (uint32_t)lane + 32u) k1 = 0u;
+    ch[r] = pick;
+  }
   float raw[4];
 #pragma unroll
   for (int r = 0; r < 4; ++r) {
-    float bv = -INFINITY;
-    uint32_t bi = 0xffffffffu;
-    if (!u0 && mc_better(v0, (uint32_t)lane, bv, bi)) {
-      bv = v0;
-      bi = (uint32_t)lane;
-    }
-    if (!u1 && mc_better(v1, (uint32_t)(lane + 32), bv, bi)) {
-      bv = v1;
-      bi = (uint32_t)(lane + 32);
-    }
-#pragma unroll
-    for (int m = 16; m >= 1; m >>= 1) {
-      const float ov = __shfl_xor_sync(0xffffffffu, bv, m);
-      const uint32_t oi = __shfl_xor_sync(0xffffffffu, bi, m);
-      if (mc_better(ov, oi, bv, bi)) {
-        bv = ov;
-        bi = oi;
-      }
-    }
-    uint32_t pick = bi == 0xffffffffu ? 0u : bi;
-    if ((uint32_t)lane == pick) u0 = true;
-    if ((uint32_t)lane + 32 == pick) u1 = true;
-    const float ps0 = __shfl_sync(0xffffffffu, s0, pick & 31);
-    const float ps1 = __shfl_sync(0xffffffffu, s1, pick & 31);
-    ch[r] = pick;
-    raw[r] = pick < 32 ? ps0 : ps1;
+    const float a = __shfl_sync(0xffffffffu, s0, ch[r] & 31);
+    const float b = __shfl_sync(0xffffffffu, s1, ch[r] & 31);
+    raw[r] = ch[r] < 32 ? a : b;
   }
   if (lane == 0) {
     if (mode == MC_ROUTE_SOFTMAX_RENORM) {

@@ -277,8 +277,10 @@ def moe_decode_layer_noalloc(ctx: Context, h, b, nw, hout, normed, router, logit
 
 
 def decode_workspace_act(workspace: torch.Tensor, moe_inter: int = FIXED_MOE_INTER):
-    """The act rows (bf16 [4, I]) held in a moe_decode_layer workspace."""
-    w = workspace[136:136 + 2 * moe_inter].contiguous()
+    """The act rows (bf16 [4, I]) held in a moe_decode_layer workspace: one
+    tagged word per value (tag << 16 | bf16 bits), little-endian, so the low
+    16-bit halves are the values."""
+    w = workspace[136:136 + 4 * moe_inter].contiguous().view(torch.int16)[0::2].contiguous()
     return w.view(torch.bfloat16).reshape(4, moe_inter)
 
 

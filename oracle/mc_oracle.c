@@ -113,12 +113,14 @@ static float butterfly32(float* v) {
  * Canonical order (this project's; Apple's simd_sum order is unspecified):
  *   - lane l (0..31) owns groups g = l, l+32, ... and keeps acc_l, starting
  *     at +0.0f;
- *   - per group (64 codes): two chains cE and cO -- Q4: codes of even and
- *     odd 32-bit words (bit 3 of k), Q6: even and odd k -- each
- *     cX = fmaf(q_k * 2^e_k, x_k * 2^-e_k, cX) in increasing k, where e_k is
- *     the bit position the GPU leaves code k at (E4 / E6 below; the product
- *     is exact, the power-of-two pre-scaling of x is what the GPU reads);
- *     qx = cE + cO;
+ *   - per group (64 codes): four quarters p of 16 codes (i = 16p..16p+15
+ *     within the group), each with two chains cE[p] and cO[p] -- Q4: codes
+ *     of the even and odd 32-bit word (bit 3 of k), Q6: even and odd k --
+ *     each starting at +0 and cX[p] = fmaf(q_k * 2^e_k, x_k * 2^-e_k, cX[p])
+ *     in increasing k, where e_k is the bit position the GPU leaves code k
+ *     at (E4 / E6 below; the product is exact, the power-of-two pre-scaling
+ *     of x is what the GPU reads);
+ *     cX = (cX[0] + cX[1]) + (cX[2] + cX[3]); qx = cE + cO;
  *   - xg_g = x_{64g} + x_{64g+1} + ... (left to right) -- shared by all rows;
  *   - term = fmaf(s_g, qx, b_g * xg_g); acc_l = acc_l + term;
  *   - row sum = 32-lane xor butterfly of acc_l.
@@ -160,7 +162,7 @@ static float row_dot(const uint8_t* row, const uint16_t* s, const uint16_t* b,
   for (int l = 0; l < 32; ++l) acc[l] = 0.0f;
   const int G = K / 64;
   for (int g = 0; g < G; ++g) {
-    float cE = 0.0f, cO = 0.0f;
+    float cE[4] = {0.0f, 0.0f, 0.0f, 0.0f}, cO[4] = {0.0f, 0.0f, 0.0f, 0.0f};
     for (int i = 0; i < 64; ++i) {
       int k = 64 * g + i;
       uint32_t q = code_at(row, bits, k);
@@ -168,10 +170,13 @@ static float row_dot(const uint8_t* row, const uint16_t* s, const uint16_t* b,
       float qf = (float)(q << e);
       /* Q4: chain by word parity (bit 3 of k); Q6: by code parity */
       int odd = bits == 4 ? (k >> 3) & 1 : k & 1;
-      if (odd) cO = fmaf(qf, xs[k], cO);
-      else cE = fmaf(qf, xs[k], cE);
+      int p = i >> 4;
+      if (odd) cO[p] = fmaf(qf, xs[k], cO[p]);
+      else cE[p] = fmaf(qf, xs[k], cE[p]);
     }
-    float qx = cE + cO;
+    float sE = (cE[0] + cE[1]) + (cE[2] + cE[3]);
+    float sO = (cO[0] + cO[1]) + (cO[2] + cO[3]);
+    float qx = sE + sO;
     float term = fmaf(bf(s[g]), qx, bf(b[g]) * xg[g]);
     acc[g & 31] = acc[g & 31] + term;
   }
