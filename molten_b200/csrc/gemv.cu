@@ -27,6 +27,8 @@ __global__ void __launch_bounds__(kWarps * 32)
 gemv_kernel(const uint32_t* __restrict__ codes, const uint16_t* __restrict__ scales,
             const uint16_t* __restrict__ biases, const uint16_t* __restrict__ x,
             uint16_t* __restrict__ y, unsigned long long* __restrict__ keys, int N, int K) {
+  mc_pdl_launch_dependents();
+  mc_pdl_wait();
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
   const int b = blockIdx.y;
@@ -113,6 +115,8 @@ token_tail_kernel(unsigned long long* __restrict__ keys, uint32_t* __restrict__ 
                   const uint16_t* __restrict__ embed, int vocab,
                   const uint16_t* __restrict__ norm_w, uint16_t* __restrict__ x_next,
                   uint16_t* __restrict__ normed_next, float eps) {
+  mc_pdl_launch_dependents();
+  mc_pdl_wait();
   __shared__ uint32_t tok_s;
   __shared__ float red[8];
   const int b = blockIdx.x;
@@ -204,8 +208,9 @@ int launch_gemv(mc_ctx* ctx, const mc_qweights* w, const uint16_t* x, uint16_t* 
   int grid = (N + rows_per_cta - 1) / rows_per_cta;
   const int cap = ctx->num_sms * 8;
   if (grid > cap) grid = cap;
-  gemv_kernel<BITS, GPL, R, MODE><<<dim3(grid, batch), kWarps * 32, 0, ctx->stream>>>(
-      w->codes, w->scales, w->biases, x, y, keys, N, K);
+  MC_CUDA(mc_launch_pdl(gemv_kernel<BITS, GPL, R, MODE>, dim3(grid, batch), dim3(kWarps * 32), 0,
+                        ctx->stream,
+      w->codes, w->scales, w->biases, x, y, keys, N, K));
   return mc_after_launch("gemv_kernel");
 }
 
@@ -261,8 +266,8 @@ extern "C" int mc_token_tail(mc_ctx* ctx, unsigned long long* keys, uint32_t* ou
                    mc_aligned(normed_next, 16),
                "token_tail: row buffers must be 16-byte aligned");
   }
-  token_tail_kernel<<<batch, 256, 0, ctx->stream>>>(keys, out_tok, embed, vocab, norm_w, x_next,
-                                                    normed_next, eps);
+  MC_CUDA(mc_launch_pdl(token_tail_kernel, dim3(batch), dim3(256), 0, ctx->stream, keys, out_tok, embed, vocab, norm_w, x_next,
+                                                    normed_next, eps));
   return mc_after_launch("token_tail_kernel");
 }
 

@@ -77,5 +77,33 @@ __device__ __forceinline__ float mc_warp_butterfly(float v) {
 // 2^-e as a float constant (e in 0..23).
 __device__ __forceinline__ float mc_pow2_neg(int e) { return __uint_as_float((uint32_t)(127 - e) << 23); }
 
+// Programmatic dependent launch. The decode-chain kernels are launched with
+// cudaLaunchAttributeProgrammaticStreamSerialization (mc_launch_pdl), so the
+// next kernel of the stream is launched while this one still runs. Each of
+// them calls mc_pdl_launch_dependents() at its start and mc_pdl_wait() before
+// it reads anything an earlier kernel wrote or writes anything an earlier
+// kernel may still read; the wait returns once the predecessors have
+// completed and their memory is visible (at once when there is none).
+__device__ __forceinline__ void mc_pdl_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void mc_pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+template <typename... KArgs, typename... Args>
+cudaError_t mc_launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                          cudaStream_t stream, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
+
 #define MC_MAGIC 0x4B000000u
 #define MC_MAGIC_F 8388608.0f

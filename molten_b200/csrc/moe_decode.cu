@@ -20,6 +20,8 @@ gather_act_kernel(const uint32_t* __restrict__ gc, const uint16_t* __restrict__ 
                   const uint16_t* __restrict__ us, const uint16_t* __restrict__ ub,
                   const uint16_t* __restrict__ x, const uint32_t* __restrict__ ids,
                   uint16_t* __restrict__ act, int I, int E) {
+  mc_pdl_launch_dependents();
+  mc_pdl_wait();
   constexpr int K = 2048, G = 32, R = 2;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int b = blockIdx.y;
@@ -69,6 +71,8 @@ down_combine_kernel(const uint32_t* __restrict__ dc, const uint16_t* __restrict_
                     const uint16_t* __restrict__ db, const uint16_t* __restrict__ act,
                     const uint32_t* __restrict__ ids, const uint16_t* __restrict__ wts,
                     uint16_t* __restrict__ out, int H, int I, int E) {
+  mc_pdl_launch_dependents();
+  mc_pdl_wait();
   constexpr int R = 4;
   __shared__ float p[4][8];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -135,9 +139,9 @@ extern "C" int mc_gemv_gather_act(mc_ctx* ctx, const mc_qweights* gate, const mc
   MC_REQUIRE(x && ids && act && mc_aligned(x, 16), "gemv_gather_act: bad x/ids/act");
   MC_REQUIRE(batch >= 1 && batch <= 65535, "gemv_gather_act: batch %d", batch);
   const dim3 grid(4 * (I / 16), batch);
-  gather_act_kernel<<<grid, kWarps * 32, 0, ctx->stream>>>(gate->codes, gate->scales, gate->biases,
+  MC_CUDA(mc_launch_pdl(gather_act_kernel, grid, dim3(kWarps * 32), 0, ctx->stream, gate->codes, gate->scales, gate->biases,
                                                            up->codes, up->scales, up->biases, x,
-                                                           ids, act, I, n_experts);
+                                                           ids, act, I, n_experts));
   return mc_after_launch("gather_act_kernel");
 }
 
@@ -160,7 +164,7 @@ extern "C" int mc_gemv_gather_down_combine4(mc_ctx* ctx, const mc_qweights* down
              "gemv_gather_down_combine4: bad act/ids/weights/out");
   MC_REQUIRE(batch >= 1 && batch <= 65535, "gemv_gather_down_combine4: batch %d", batch);
   const dim3 grid(H / 8, batch);
-  down_combine_kernel<<<grid, kWarps * 32, 0, ctx->stream>>>(
-      down->codes, down->scales, down->biases, act, ids, weights, out, H, I, n_experts);
+  MC_CUDA(mc_launch_pdl(down_combine_kernel, grid, dim3(kWarps * 32), 0, ctx->stream,
+      down->codes, down->scales, down->biases, act, ids, weights, out, H, I, n_experts));
   return mc_after_launch("down_combine_kernel");
 }

@@ -1,5 +1,5 @@
 // moe_decode (lfm.rs:967-1011) behind the fused router (lfm.rs:1154-1169) as
-// ONE persistent cooperative launch for one token (batch 1): add + RMSNorm +
+// ONE persistent launch (one CTA per SM) for one token (batch 1): add + RMSNorm +
 // router + top-4 (router_addnorm_route), the four experts' gate/up GEMVs with
 // SwiGLU (gemv_gather_act) and their down GEMVs with the weighted combine
 // (gemv_gather_down_combine4), bit-identical to those three kernels.
@@ -188,9 +188,6 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(const Par
   uint16_t* nbf = reinterpret_cast<uint16_t*>(sm + L.pro + 8192);
   uint8_t* rrow = sm + L.pro + 12288;
   uint16_t* act_s = reinterpret_cast<uint16_t*>(sm + L.pro);  // after the prologue
-  const uint32_t epoch = *reinterpret_cast<volatile uint32_t*>(sync);
-  const uint32_t tag32 = epoch == 0xffffffffu ? 1u : epoch + 1u;
-  const uint32_t tag16 = tag32 % 65535u + 1u;  // never 0, differs from the last launch's
   const bool router_cta = cta < P.E;
   const unsigned long long t_start = mc_globaltimer();
   bool ok = true;
@@ -212,10 +209,17 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(const Par
     }
   }
   uint4 hv = make_uint4(0, 0, 0, 0), bv = make_uint4(0, 0, 0, 0), wv = make_uint4(0, 0, 0, 0);
+  if (t < 256) wv = mc_ldg_stream(reinterpret_cast<const uint4*>(P.norm_w) + t);
+  // weights above may be read before the previous kernel of the stream has
+  // finished; its outputs (h, b, the workspace) only after this wait
+  mc_pdl_launch_dependents();
+  mc_pdl_wait();
+  const uint32_t epoch = *reinterpret_cast<volatile uint32_t*>(sync);
+  const uint32_t tag32 = epoch == 0xffffffffu ? 1u : epoch + 1u;
+  const uint32_t tag16 = tag32 % 65535u + 1u;  // never 0, differs from the last launch's
   if (t < 256) {
     hv = mc_ldg_stream(reinterpret_cast<const uint4*>(P.h) + t);
     if (P.badd) bv = mc_ldg_stream(reinterpret_cast<const uint4*>(P.badd) + t);
-    wv = mc_ldg_stream(reinterpret_cast<const uint4*>(P.norm_w) + t);
   }
 
   // ---- add + RMSNorm (canonical order of addnorm_row_2048)
@@ -677,7 +681,12 @@ extern "C" int mc_moe_decode_layer(mc_ctx* ctx, const uint16_t* h, const uint16_
                                  ctx->max_smem_optin - 4096));
     cur.store(ctx->max_smem_optin - 4096);
   }
-  int per_sm = 0;  // every CTA must be resident at once (cross-CTA waits)
+  // The CTAs wait on one another, so all of them must be resident at once:
+  // one CTA per SM, grid = SM count. The launch is not cooperative so that it
+  // can be a programmatic dependent launch (the next kernel's CTAs start as
+  // this one's retire); if another kernel held SMs, the bounded waits would
+  // end with an error status instead of a hang.
+  int per_sm = 0;
   MC_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, kThreads, L.total));
   MC_REQUIRE(per_sm >= 1, "moe_decode_layer: kernel does not fit one CTA per SM");
   cudaLaunchConfig_t cfg = {};
@@ -686,8 +695,8 @@ extern "C" int mc_moe_decode_layer(mc_ctx* ctx, const uint16_t* h, const uint16_
   cfg.dynamicSmemBytes = L.total;
   cfg.stream = ctx->stream;
   cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeCooperative;
-  attr[0].val.cooperative = 1;
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   void* args[] = {(void*)&P, (void*)&L};

@@ -23,6 +23,8 @@ router_addnorm_route_kernel(const uint16_t* __restrict__ h, const uint16_t* __re
                             const float* __restrict__ ebias, int mode, float* logits,
                             uint32_t* __restrict__ ids, uint16_t* __restrict__ wts,
                             uint32_t* counter, int E, float eps, float route_eps) {
+  mc_pdl_launch_dependents();
+  mc_pdl_wait();
   __shared__ __align__(16) float nrow[2048];
   __shared__ float red[8];
   __shared__ uint32_t last_s;
@@ -133,13 +135,13 @@ extern "C" int mc_router_addnorm_route(mc_ctx* ctx, const uint16_t* h, const uin
              "router_addnorm_route: h_out/normed must not alias h or b");
   const dim3 grid((n_experts + 7) / 8, batch);
   if (router_dtype == MC_DTYPE_BF16)
-    router_addnorm_route_kernel<MC_DTYPE_BF16><<<grid, 256, 0, ctx->stream>>>(
+    MC_CUDA(mc_launch_pdl(router_addnorm_route_kernel<MC_DTYPE_BF16>, grid, dim3(256), 0, ctx->stream,
         h, b, norm_w, h_out, normed, router_w, expert_bias, route_mode, logits, ids, weights,
-        counter, n_experts, eps, route_eps);
+        counter, n_experts, eps, route_eps));
   else
-    router_addnorm_route_kernel<MC_DTYPE_F32><<<grid, 256, 0, ctx->stream>>>(
+    MC_CUDA(mc_launch_pdl(router_addnorm_route_kernel<MC_DTYPE_F32>, grid, dim3(256), 0, ctx->stream,
         h, b, norm_w, h_out, normed, router_w, expert_bias, route_mode, logits, ids, weights,
-        counter, n_experts, eps, route_eps);
+        counter, n_experts, eps, route_eps));
   return mc_after_launch("router_addnorm_route_kernel");
 }
 
