@@ -236,6 +236,8 @@ extern "C" int mc_gemv_quant(mc_ctx* ctx, const mc_qweights* w, const uint16_t* 
   MC_REQUIRE(x && y, "gemv_quant: null x or y");
   MC_REQUIRE(batch >= 1 && batch <= 65535, "gemv_quant: batch %d out of range", batch);
   MC_REQUIRE(mc_aligned(x, 16), "gemv_quant: x must be 16-byte aligned");
+  rc = mc_gemv_ring(ctx, w, x, y, nullptr, batch, 0);
+  if (rc != 1) return rc;
   return dispatch_gemv<0>(ctx, w, x, y, nullptr, batch);
 }
 
@@ -248,6 +250,8 @@ extern "C" int mc_gemv_head_argmax(mc_ctx* ctx, const mc_qweights* w, const uint
   MC_REQUIRE(mc_aligned(keys, 8), "gemv_head_argmax: keys must be 8-byte aligned");
   MC_REQUIRE(mc_aligned(x, 16), "gemv_head_argmax: x must be 16-byte aligned");
   MC_REQUIRE(batch >= 1 && batch <= 65535, "gemv_head_argmax: batch %d out of range", batch);
+  rc = mc_gemv_ring(ctx, w, x, nullptr, keys, batch, 1);
+  if (rc != 1) return rc;
   return dispatch_gemv<1>(ctx, w, x, nullptr, keys, batch);
 }
 

@@ -1,0 +1,207 @@
+// Streaming decode GEMV for large row counts (the Q6 LM head + argmax, tall
+// Q4 projections): gemv_quant / gemv_head_argmax (kernels/lfm.rs:112-149,
+// 826-848) at batch 1 and K = 2048.
+//
+// One persistent CTA per SM owns a contiguous range of rows. A producer warp
+// streams them through a ring of shared-memory stages with 1-D bulk (TMA)
+// copies -- per stage 16 rows of codes, their scales and their biases, three
+// contiguous copies -- so several stages (~100 KB) are always in flight and
+// the weight stream never waits on the dequant arithmetic; 16 compute warps
+// take one row each per stage. Per-row arithmetic is the canonical order of
+// gemv_kernel (lane l owns group l, term = fma(s, qx, b * xg), 32-lane
+// butterfly), so outputs are bit-identical to it and to the oracle.
+//
+// The producer starts streaming before the programmatic-dependent-launch
+// wait (weights are never written by earlier kernels); the compute warps wait
+// before they read x. Every mbarrier wait is bounded; a CTA whose copies did
+// not all land waits for them (bounded again) before it exits.
+#include <atomic>
+
+#include "gemv_common.cuh"
+#include "mc_async.cuh"
+
+namespace {
+
+constexpr int kK = 2048;
+constexpr int kRows = 16;                  // rows per stage, one per compute warp
+constexpr int kComputeWarps = kRows;
+constexpr int kThreads = (kComputeWarps + 1) * 32;  // + the producer warp
+constexpr int kMaxStages = 8;
+constexpr unsigned long long kTimeoutNs = 200000000ull;
+
+template <int BITS>
+struct RingShape {
+  static constexpr uint32_t kCode = kK * BITS / 8;               // code bytes per row
+  static constexpr uint32_t kStage = kRows * (kCode + 2 * 64);   // codes + scales + biases
+  static constexpr int kStages = BITS == 6 ? 6 : 8;              // ~160 / ~150 KB
+  static constexpr uint32_t kSmem = kStages * kStage;
+};
+
+__device__ __forceinline__ bool ring_wait(uint64_t* bar, uint32_t parity,
+                                          unsigned long long deadline) {
+  while (!mc_mbar_test_sleep(bar, parity, 20000u))
+    if (mc_globaltimer() > deadline) return false;
+  return true;
+}
+
+// MODE 0: y[n] = bf16(row n . x). MODE 1: keys[0] = max over rows of the
+// argmax key of the bf16-rounded row values (the key must be zero on entry).
+template <int BITS, int MODE>
+__global__ void __launch_bounds__(kThreads, 1)
+gemv_ring_kernel(const uint8_t* __restrict__ codes, const uint16_t* __restrict__ scales,
+                 const uint16_t* __restrict__ biases, const uint16_t* __restrict__ x,
+                 uint16_t* __restrict__ y, unsigned long long* __restrict__ keys, int N,
+                 unsigned int* __restrict__ status) {
+  using S = RingShape<BITS>;
+  extern __shared__ __align__(128) uint8_t sm[];
+  __shared__ __align__(8) uint64_t full[kMaxStages], empty[kMaxStages];
+  __shared__ float bv_s[kComputeWarps];
+  __shared__ uint32_t bi_s[kComputeWarps];
+  const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
+  const int G = gridDim.x, cta = blockIdx.x;
+  const int r0 = (int)(((long)cta * N) / G), r1 = (int)(((long)(cta + 1) * N) / G);
+  const int nst = (r1 - r0 + kRows - 1) / kRows;
+  if (t == 0) {
+    for (int s = 0; s < S::kStages; ++s) {
+      mc_mbar_init(full + s, 1);
+      mc_mbar_init(empty + s, kComputeWarps);
+    }
+    mc_fence_barrier_init();
+  }
+  __syncthreads();
+  mc_pdl_launch_dependents();
+  const unsigned long long deadline = mc_globaltimer() + kTimeoutNs;
+
+  if (warp == kComputeWarps) {
+    // ---- producer: stage s goes to slot s % kStages once the compute warps
+    // have released the slot's previous use
+    bool ok = true;
+    if (lane == 0) {
+      const uint64_t pol = mc_policy_evict_first();
+      for (int s = 0; s < nst; ++s) {
+        const int slot = s % S::kStages;
+        if (s >= S::kStages && !ring_wait(empty + slot, ((s / S::kStages) - 1) & 1, deadline)) {
+          ok = false;
+          break;
+        }
+        const int n0 = r0 + s * kRows, nr = min(kRows, r1 - n0);
+        uint8_t* st = sm + (uint32_t)slot * S::kStage;
+        mc_mbar_expect_tx(full + slot, (uint32_t)nr * (S::kCode + 128u));
+        mc_bulk_g2s(st, codes + (size_t)n0 * S::kCode, (uint32_t)nr * S::kCode, full + slot, pol);
+        mc_bulk_g2s(st + kRows * S::kCode, scales + (size_t)n0 * 32, (uint32_t)nr * 64u,
+                    full + slot, pol);
+        mc_bulk_g2s(st + kRows * (S::kCode + 64u), biases + (size_t)n0 * 32, (uint32_t)nr * 64u,
+                    full + slot, pol);
+      }
+      // every issued copy lands before the CTA exits (immediate unless a
+      // compute warp gave up)
+      const int first = nst > S::kStages ? nst - S::kStages : 0;
+      for (int s = first; s < nst; ++s)
+        ok = ring_wait(full + s % S::kStages, (s / S::kStages) & 1, deadline + kTimeoutNs) && ok;
+      if (!ok) atomicOr(status, 1u);
+    }
+    return;
+  }
+
+  // ---- compute warps: x of group `lane`, pre-scaled, once the previous
+  // kernel's output is visible
+  mc_pdl_wait();
+  float2 xs[32];
+  const float xg = load_group_x<BITS>(x, lane, xs);
+  float best_v = -INFINITY;
+  uint32_t best_i = 0;
+  for (int s = 0; s < nst; ++s) {
+    const int slot = s % S::kStages;
+    if (!ring_wait(full + slot, (s / S::kStages) & 1, deadline)) {
+      if (lane == 0) atomicOr(status, 2u);
+      break;
+    }
+    const int n0 = r0 + s * kRows, nr = min(kRows, r1 - n0);
+    const uint8_t* st = sm + (uint32_t)slot * S::kStage;
+    float sum = 0.0f;
+    if (warp < nr) {
+      const uint16_t* sc = reinterpret_cast<const uint16_t*>(st + kRows * S::kCode);
+      const uint16_t* bi = reinterpret_cast<const uint16_t*>(st + kRows * (S::kCode + 64u));
+      const float sv = mc_bf16_to_f32(sc[warp * 32 + lane]);
+      const float bv = mc_bf16_to_f32(bi[warp * 32 + lane]);
+      QGroup<BITS> q;
+      const uint4* p = reinterpret_cast<const uint4*>(st + warp * S::kCode + lane * (BITS * 8));
+#pragma unroll
+      for (int c = 0; c < BITS / 2; ++c) q.v[c] = p[c];
+      const float acc = __fadd_rn(0.0f, __fmaf_rn(sv, q.qx(xs), __fmul_rn(bv, xg)));
+      sum = mc_warp_butterfly(acc);
+    }
+    __syncwarp();
+    if (lane == 0) mc_mbar_arrive(empty + slot);
+    if (warp < nr) {
+      const int n = n0 + warp;
+      if (MODE == 0) {
+        if (lane == 0) y[n] = mc_f32_to_bf16(sum);
+      } else {
+        const float v = mc_round_bf16(sum);
+        if (mc_better(v, (uint32_t)n, best_v, best_i)) {
+          best_v = v;
+          best_i = (uint32_t)n;
+        }
+      }
+    }
+  }
+  if (MODE == 1) {
+    if (lane == 0) {
+      bv_s[warp] = best_v;
+      bi_s[warp] = best_i;
+    }
+    asm volatile("bar.sync 1, %0;" ::"n"(kComputeWarps * 32));
+    if (t == 0) {
+      float v = bv_s[0];
+      uint32_t i = bi_s[0];
+      for (int w = 1; w < kComputeWarps; ++w)
+        if (mc_better(bv_s[w], bi_s[w], v, i)) {
+          v = bv_s[w];
+          i = bi_s[w];
+        }
+      atomicMax(keys, mc_argmax_key(v, i));
+    }
+  }
+}
+
+__device__ unsigned int g_ring_status;
+
+template <int BITS, int MODE>
+int launch_ring(mc_ctx* ctx, const mc_qweights* w, const uint16_t* x, uint16_t* y,
+                unsigned long long* keys) {
+  using S = RingShape<BITS>;
+  auto fn = gemv_ring_kernel<BITS, MODE>;
+  // per device: the shared-memory limit raised once, the status word's address
+  static std::atomic<bool> ready[64];
+  static unsigned int* status_of[64];
+  const int dev = ctx->device & 63;
+  if (!ready[dev].load()) {
+    MC_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kSmem));
+    MC_CUDA(cudaGetSymbolAddress((void**)&status_of[dev], g_ring_status));
+    ready[dev].store(true);
+  }
+  unsigned int* status = status_of[dev];
+  MC_CUDA(mc_launch_pdl(fn, dim3(ctx->num_sms), dim3(kThreads), S::kSmem, ctx->stream,
+                        reinterpret_cast<const uint8_t*>(w->codes), w->scales, w->biases, x, y,
+                        keys, w->out_features, status));
+  return mc_after_launch("gemv_ring_kernel");
+}
+
+}  // namespace
+
+// Used by mc_gemv_quant / mc_gemv_head_argmax (gemv.cu) for batch 1, K = 2048
+// and at least two stages of rows per SM. Returns 1 when the shape does not
+// qualify (the caller then uses gemv_kernel), else MC_OK or an error code.
+int mc_gemv_ring(mc_ctx* ctx, const mc_qweights* w, const uint16_t* x, uint16_t* y,
+                 unsigned long long* keys, int batch, int mode) {
+  if (batch != 1 || w->in_features != kK || w->group_size != 64) return 1;
+  if (w->out_features < ctx->num_sms * 2 * kRows) return 1;
+  const uint32_t smem = w->bits == 6 ? RingShape<6>::kSmem : RingShape<4>::kSmem;
+  if ((int)smem + 4096 > ctx->max_smem_optin) return 1;
+  if (!mc_aligned(w->codes, 16) || !mc_aligned(w->scales, 16) || !mc_aligned(w->biases, 16))
+    return 1;
+  if (w->bits == 6)
+    return mode ? launch_ring<6, 1>(ctx, w, x, y, keys) : launch_ring<6, 0>(ctx, w, x, y, keys);
+  return mode ? launch_ring<4, 1>(ctx, w, x, y, keys) : launch_ring<4, 0>(ctx, w, x, y, keys);
+}

@@ -54,6 +54,10 @@ int mc_check_gemv_weights(const mc_qweights* w, const char* what);
 
 // Checks the launch that was just issued.
 int mc_after_launch(const char* what);
+// Ring-streamed GEMV (gemv_ring.cu) for batch 1, K = 2048, tall matrices;
+// returns 1 when the shape does not qualify. mode 0: y, mode 1: argmax keys.
+int mc_gemv_ring(mc_ctx* ctx, const mc_qweights* w, const uint16_t* x, uint16_t* y,
+                 unsigned long long* keys, int batch, int mode);
 
 static inline bool mc_aligned(const void* p, size_t a) { return ((uintptr_t)p % a) == 0; }
 

@@ -5,10 +5,9 @@
 // (gemv_gather_down_combine4), bit-identical to those three kernels.
 //
 // One CTA per SM, 16 warps. Timeline of a launch:
-//  * thread 0 of CTAs 0..E-1 starts a bulk (TMA) copy of one router row into
-//    shared memory; every CTA adds h + b and normalises the row (each needs
-//    the normed row); the router warps then publish their expert's logit,
-//    epoch-tagged, to the workspace;
+//  * warp 0 of CTAs 0..E-1 loads one router row; every CTA adds h + b and
+//    normalises the row (each needs the normed row); the router warps then
+//    publish their expert's logit, epoch-tagged, to the workspace;
 //  * warp 0 of every CTA waits for the E logits and picks the same top-4;
 //  * warp 0 issues this CTA's slice of the 4 experts' gate/up rows (codes,
 //    scales, biases; a few contiguous row ranges) and down codes as 1-D bulk
@@ -58,7 +57,7 @@ constexpr int H = 2048;
 constexpr unsigned long long kTimeoutNs = 200000000ull;  // 200 ms per wait
 constexpr int kLogitWord = 8;   // first tagged-logit word in the workspace
 constexpr int kActWord = 136;   // first act word in the workspace
-constexpr uint32_t kPrologueBytes = 8192 + 4096 + 8192;         // f32 row, bf16 row, router row
+constexpr uint32_t kPrologueBytes = 8192 + 4096;  // normed row as f32 and as bf16
 
 // Byte offsets in dynamic shared memory (identical on host and device).
 // Gate/up chunk c (one mbarrier each) holds local row pairs
@@ -125,34 +124,6 @@ __device__ __forceinline__ bool wait_copies(uint64_t* bar, unsigned long long de
   return true;
 }
 
-// Router logit of one row in shared memory against the normed f32 row, in
-// the canonical order of RouterRow::dot (lane owns elements 256j + 8*lane +
-// 0..7, j = 0..7, one fma chain, then the warp butterfly).
-template <int DT>
-__device__ __forceinline__ float router_dot_smem(const uint8_t* row, const float* n, int lane) {
-  float acc = 0.0f;
-#pragma unroll
-  for (int j = 0; j < 8; ++j) {
-    const float4 n0 = *reinterpret_cast<const float4*>(n + 256 * j + 8 * lane);
-    const float4 n1 = *reinterpret_cast<const float4*>(n + 256 * j + 8 * lane + 4);
-    const float nv[8] = {n0.x, n0.y, n0.z, n0.w, n1.x, n1.y, n1.z, n1.w};
-    if (DT == MC_DTYPE_BF16) {
-      const uint4 w = *reinterpret_cast<const uint4*>(row + 2 * (256 * j + 8 * lane));
-      const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
-#pragma unroll
-      for (int i = 0; i < 8; ++i)
-        acc = __fmaf_rn(mc_bf16_to_f32((uint16_t)(ww[i >> 1] >> (16 * (i & 1)))), nv[i], acc);
-    } else {
-      const float4 a = *reinterpret_cast<const float4*>(row + 4 * (256 * j + 8 * lane));
-      const float4 b = *reinterpret_cast<const float4*>(row + 4 * (256 * j + 8 * lane + 4));
-      const float wv[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
-#pragma unroll
-      for (int i = 0; i < 8; ++i) acc = __fmaf_rn(wv[i], nv[i], acc);
-    }
-  }
-  return mc_warp_butterfly(acc);
-}
-
 // One Q4 group (32 code bytes) of a row in shared memory.
 __device__ __forceinline__ float smem_group_qx(const uint8_t* p, const float2* xs) {
   const uint4* q = reinterpret_cast<const uint4*>(p);
@@ -170,7 +141,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(const Par
   __shared__ float p_s[4][32];
   __shared__ float gu_s[2][256];  // bf16-rounded gate and up sums per local pair
   __shared__ uint32_t flag_s;
-  __shared__ __align__(8) uint64_t bar_pro, bar_sb, bar_dn, bar_gu[kMaxChunks];
+  __shared__ __align__(8) uint64_t bar_sb, bar_dn, bar_gu[kMaxChunks];
 
   const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
   const int G = gridDim.x, cta = blockIdx.x;
@@ -186,26 +157,36 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(const Par
   uint32_t* actw = sync + kActWord;
   float* nrow = reinterpret_cast<float*>(sm + L.pro);
   uint16_t* nbf = reinterpret_cast<uint16_t*>(sm + L.pro + 8192);
-  uint8_t* rrow = sm + L.pro + 12288;
   uint16_t* act_s = reinterpret_cast<uint16_t*>(sm + L.pro);  // after the prologue
   const bool router_cta = cta < P.E;
   const unsigned long long t_start = mc_globaltimer();
   bool ok = true;
   TRACE(0);
 
-  // ---- barriers, the router row copy, and this thread's h / b / norm_w words
+  // ---- barriers, the router row (warp 0 of a router CTA, into registers),
+  // and this thread's h / b / norm_w words
   if (t == 0) {
     flag_s = 0;
-    mc_mbar_init(&bar_pro, 1);
     mc_mbar_init(&bar_sb, 1);
     mc_mbar_init(&bar_dn, 1);
     for (int c = 0; c < kMaxChunks; ++c) mc_mbar_init(bar_gu + c, 1);
     mc_fence_barrier_init();
-    if (router_cta) {
-      const uint32_t rb = DT == MC_DTYPE_BF16 ? 2 * H : 4 * H;
-      mc_mbar_expect_tx(&bar_pro, rb);
-      mc_bulk_g2s(rrow, reinterpret_cast<const uint8_t*>(P.router_w) + (size_t)cta * rb, rb,
-                  &bar_pro, mc_policy_evict_first());
+  }
+  RouterRow<DT> rr;
+  if (router_cta && warp == 0) {
+    // the element assignment of RouterRow::load, as streaming loads issued now
+    const uint4* row = reinterpret_cast<const uint4*>(
+        reinterpret_cast<const uint8_t*>(P.router_w) + (size_t)cta * (DT == MC_DTYPE_BF16 ? 2 * H : 4 * H));
+    uint4* w = reinterpret_cast<uint4*>(rr.w);
+    if (DT == MC_DTYPE_BF16) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) w[j] = mc_ldg_stream(row + 32 * j + lane);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        w[2 * j] = mc_ldg_stream(row + 64 * j + 2 * lane);
+        w[2 * j + 1] = mc_ldg_stream(row + 64 * j + 2 * lane + 1);
+      }
     }
   }
   uint4 hv = make_uint4(0, 0, 0, 0), bv = make_uint4(0, 0, 0, 0), wv = make_uint4(0, 0, 0, 0);
@@ -214,13 +195,13 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(const Par
   // finished; its outputs (h, b, the workspace) only after this wait
   mc_pdl_launch_dependents();
   mc_pdl_wait();
-  const uint32_t epoch = *reinterpret_cast<volatile uint32_t*>(sync);
-  const uint32_t tag32 = epoch == 0xffffffffu ? 1u : epoch + 1u;
-  const uint32_t tag16 = tag32 % 65535u + 1u;  // never 0, differs from the last launch's
   if (t < 256) {
     hv = mc_ldg_stream(reinterpret_cast<const uint4*>(P.h) + t);
     if (P.badd) bv = mc_ldg_stream(reinterpret_cast<const uint4*>(P.badd) + t);
   }
+  const uint32_t epoch = *reinterpret_cast<volatile uint32_t*>(sync);
+  const uint32_t tag32 = epoch == 0xffffffffu ? 1u : epoch + 1u;
+  const uint32_t tag16 = tag32 % 65535u + 1u;  // never 0, differs from the last launch's
 
   // ---- add + RMSNorm (canonical order of addnorm_row_2048)
   float hp[8];
@@ -268,11 +249,9 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(const Par
   // release add (which orders the store before it) counts the published
   // logits, so readers poll one word instead of all E
   if (router_cta && warp == 0) {
-    const bool got = wait_copies(&bar_pro, t_start + kTimeoutNs);
-    const float z = got ? router_dot_smem<DT>(rrow, nrow, lane) : 0.0f;
+    const float z = rr.dot(nrow, lane);
     TRACE(13);
     if (lane == 0) {
-      if (!got) record_error(sync, 16u);
       P.logits[cta] = z;
       mc_st_publish_u64(logits64 + cta,
                         ((unsigned long long)tag32 << 32) | (unsigned long long)__float_as_uint(z));
@@ -589,10 +568,9 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(const Par
 
   // ---- every issued copy has landed before the CTA exits (immediate unless
   // a wait above gave up)
-  if (t == 0 && (issued || router_cta)) {
+  if (t == 0 && issued) {
     const unsigned long long deadline = mc_globaltimer() + kTimeoutNs;
-    bool all = !router_cta || wait_copies(&bar_pro, deadline);
-    if (issued) all = wait_copies(&bar_sb, deadline) && wait_copies(&bar_dn, deadline) && all;
+    bool all = wait_copies(&bar_sb, deadline) && wait_copies(&bar_dn, deadline);
     for (int c = 0; issued && c < nchunk; ++c) all = wait_copies(bar_gu + c, deadline) && all;
     if (!all) record_error(sync, 16u);
   }

@@ -117,28 +117,32 @@ __device__ __forceinline__ void warp_top4(const float* z, int E, int mode, const
     const float b = __shfl_sync(0xffffffffu, s1, ch[r] & 31);
     raw[r] = ch[r] < 32 ? a : b;
   }
-  if (lane == 0) {
-    if (mode == MC_ROUTE_SOFTMAX_RENORM) {
-      float ex[4], den = 0.0f;
+  // weights: every lane forms the same numerators and denominator (in rank
+  // order), lane r < 4 divides for rank r, lane 0 collects
+  float num[4], den;
+  if (mode == MC_ROUTE_SOFTMAX_RENORM) {
+    den = 0.0f;
 #pragma unroll
-      for (int r = 0; r < 4; ++r) {
-        ex[r] = mc_exp(__fadd_rn(raw[r], -raw[0]));
-        den = __fadd_rn(den, ex[r]);
-      }
+    for (int r = 0; r < 4; ++r) {
+      num[r] = mc_exp(__fadd_rn(raw[r], -raw[0]));
+      den = __fadd_rn(den, num[r]);
+    }
+  } else {
+    den = route_eps;
 #pragma unroll
-      for (int r = 0; r < 4; ++r) {
-        ids_out[r] = ch[r];
-        w_out[r] = mc_f32_to_bf16(__fdiv_rn(ex[r], den));
-      }
-    } else {
-      float den = route_eps;
+    for (int r = 0; r < 4; ++r) {
+      num[r] = raw[r];
+      den = __fadd_rn(den, raw[r]);
+    }
+  }
+  const float mine = lane == 0 ? num[0] : lane == 1 ? num[1] : lane == 2 ? num[2] : num[3];
+  const uint32_t wb = mc_f32_to_bf16(__fdiv_rn(mine, den));
 #pragma unroll
-      for (int r = 0; r < 4; ++r) den = __fadd_rn(den, raw[r]);
-#pragma unroll
-      for (int r = 0; r < 4; ++r) {
-        ids_out[r] = ch[r];
-        w_out[r] = mc_f32_to_bf16(__fdiv_rn(raw[r], den));
-      }
+  for (int r = 0; r < 4; ++r) {
+    const uint32_t w = __shfl_sync(0xffffffffu, wb, r);
+    if (lane == 0) {
+      ids_out[r] = ch[r];
+      w_out[r] = (uint16_t)w;
     }
   }
 }

@@ -29,9 +29,12 @@ def test_device_math_bit_exact(cuda_ctx):
         assert np.array_equal(got[::17].view(np.uint32), want.view(np.uint32)), op
 
 
+# (4, 8192, ...) and (6, 9999, ...) take the ring-streamed kernel (batch 1,
+# K = 2048, at least 32 rows per SM; 9999 leaves partial stages)
 @pytest.mark.parametrize("bits,n,k,batch", [(4, 2048, 2048, 1), (4, 2048, 1536, 1),
                                             (4, 1000, 2048, 3), (4, 512, 4096, 2),
-                                            (6, 4096, 2048, 1), (6, 96, 2048, 2)])
+                                            (6, 4096, 2048, 1), (6, 96, 2048, 2),
+                                            (4, 8192, 2048, 1), (6, 9999, 2048, 1)])
 def test_gemv_quant_bit_exact(cuda_ctx, bits, n, k, batch):
     g = synth.rng(20 + bits + n + k + batch)
     codes, s, b = synth.quant_weights_np(g, n, k, bits)
@@ -73,6 +76,10 @@ def test_head_argmax_cfg2_and_tail(cuda_ctx):
     key = torch.zeros(2, dtype=torch.int64, device="cuda")
     lfm.gemv_head_argmax(cuda_ctx, w, dev_bf16(x), key)
     assert np.array_equal(key.cpu().numpy().view(np.uint64), keys_o)
+    # batch 1 takes the ring-streamed kernel: same key, tie included
+    key1 = torch.zeros(1, dtype=torch.int64, device="cuda")
+    lfm.gemv_head_argmax(cuda_ctx, w, dev_bf16(x[:1]), key1)
+    assert int(key1.cpu().numpy().view(np.uint64)[0]) == int(keys_o[0])
     emb = synth.activations_np(g, 1024, 2048)
     nw = synth.norm_weight_np(g)
     tok = zeros_u32(2)
