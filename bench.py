@@ -219,6 +219,8 @@ class DecodeChain:
         lf = self.lfm
         h_in, h_out = self.h[self.parity], self.h[1 - self.parity]
         if self.fused:
+            nxt = self.layers[(self.step_i + 1) % len(self.layers)]
+            self.ctx.prefetch_next(nxt["router"], nxt["norm_w"])
             lf.moe_decode_layer(self.ctx, h_in, self.out, L["norm_w"], h_out, self.normed,
                                 L["router"], self.logits, None, self.ids, self.wts, L["gate"],
                                 L["up"], L["down"], self.out, self.sync)

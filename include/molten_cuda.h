@@ -301,6 +301,14 @@ int mc_ep_return(mc_ctx* ctx, const uint16_t* ed, size_t ed_rows, int hidden,
                  const uint32_t* counts_all, int rank, int world, int n_experts,
                  void* const* home_bufs, size_t home_cap_rows, uint32_t* status);
 
+/* Cross-layer prefetch hint (no reference counterpart): the next
+ * mc_moe_decode_layer (or _noalloc) launched on ctx prefetches the byte
+ * ranges [p0, p0 + n0) and [p1, p1 + n1) into L2 once its own expert rows are
+ * streaming, and clears the setting. A decode loop passes the next layer's
+ * router weights and RMSNorm weight, which every CTA of that layer waits for
+ * first. NULL or 0 leaves a range out. */
+int mc_set_l2_prefetch(mc_ctx* ctx, const void* p0, size_t n0, const void* p1, size_t n1);
+
 /* -------------------------------------------------------------- test aid */
 
 /* Profiling aid: when buf (device, n u64 words) is set, the persistent

@@ -93,6 +93,7 @@ SIGNATURES: dict[str, tuple] = {
     "mc_moe_combine_rows": (I, [P, P, P, P, P, I, I, I]),
     "mc_eval_math": (I, [P, I, P, P, I]),
     "mc_set_trace": (I, [P, P, I]),
+    "mc_set_l2_prefetch": (I, [P, P, C.c_size_t, P, C.c_size_t]),
 }
 
 _lib: C.CDLL | None = None

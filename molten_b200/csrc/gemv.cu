@@ -27,13 +27,34 @@ __global__ void __launch_bounds__(kWarps * 32)
 gemv_kernel(const uint32_t* __restrict__ codes, const uint16_t* __restrict__ scales,
             const uint16_t* __restrict__ biases, const uint16_t* __restrict__ x,
             uint16_t* __restrict__ y, unsigned long long* __restrict__ keys, int N, int K) {
-  mc_pdl_launch_dependents();
-  mc_pdl_wait();
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
   const int b = blockIdx.y;
   const int G = K / 64;
   const uint16_t* xb = x + (size_t)b * K;
+  // the first rows' codes, scales and biases into L2 while the previous
+  // kernel may still run (weights are never written by it), then the wait
+  // before x is read
+  {
+    const int row0 = (blockIdx.x * kWarps + warp) * R;
+    const size_t rb = row_bytes<BITS>(K);
+    const int lines = (int)(rb / 128);
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      const int n = row0 + r;
+      if (n < N) {
+        const uint8_t* row = reinterpret_cast<const uint8_t*>(codes) + (size_t)n * rb;
+        for (int l = lane; l < lines; l += 32)
+          asm volatile("prefetch.global.L2 [%0];" ::"l"(row + 128 * l));
+        if (lane == 0) {
+          asm volatile("prefetch.global.L2 [%0];" ::"l"(scales + (size_t)n * G));
+          asm volatile("prefetch.global.L2 [%0];" ::"l"(biases + (size_t)n * G));
+        }
+      }
+    }
+  }
+  mc_pdl_launch_dependents();
+  mc_pdl_wait();
 
   float2 xs[GPL][32];
   float xg[GPL];
@@ -218,11 +239,20 @@ template <int MODE>
 int dispatch_gemv(mc_ctx* ctx, const mc_qweights* w, const uint16_t* x, uint16_t* y,
                   unsigned long long* keys, int batch) {
   const int G = w->in_features / 64;
+  // few rows: one row per warp, so every SM gets work (2048 rows at R = 4
+  // would fill 64 CTAs)
+  const bool few = (long)w->out_features * batch < (long)ctx->num_sms * kWarps * 4;
   if (w->bits == 4) {
-    if (G <= 32) return launch_gemv<4, 1, 4, MODE>(ctx, w, x, y, keys, batch);
+    if (G <= 32) {
+      if (few) return launch_gemv<4, 1, 1, MODE>(ctx, w, x, y, keys, batch);
+      return launch_gemv<4, 1, 4, MODE>(ctx, w, x, y, keys, batch);
+    }
     return launch_gemv<4, 2, 2, MODE>(ctx, w, x, y, keys, batch);
   }
-  if (G <= 32) return launch_gemv<6, 1, 2, MODE>(ctx, w, x, y, keys, batch);
+  if (G <= 32) {
+    if (few) return launch_gemv<6, 1, 1, MODE>(ctx, w, x, y, keys, batch);
+    return launch_gemv<6, 1, 2, MODE>(ctx, w, x, y, keys, batch);
+  }
   return launch_gemv<6, 2, 1, MODE>(ctx, w, x, y, keys, batch);
 }
 

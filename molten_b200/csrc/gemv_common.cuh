@@ -87,23 +87,42 @@ __device__ __forceinline__ float q4_group_qx(uint4 a, uint4 b, const float2* xs)
   return quarters_qx(c);
 }
 
-// One 4-code Q6 packet starting at byte `off` (0..3) of (lo, hi).
+// One 4-code Q6 packet starting at byte OFF (0..3) of (lo, hi): P holds the
+// packet's bytes OFF..OFF+3 (codes at bits 0, 6, 12, 18), Q bytes OFF+1..
+// (code 3 at bits 10..15, below the exponent); per code one lop3 (mask, OR
+// 2^23), per code pair one f32x2 add (-2^23) and one f32x2 fma into acc
+// (.x even codes, .y odd codes). Written as PTX for the same reason as
+// q4_wordpair_fma.
 template <int OFF>
 __device__ __forceinline__ void q6_packet_fma(uint32_t lo, uint32_t hi, float2 x01, float2 x23,
                                               float2& acc) {
-  const float2 neg = make_float2(-MC_MAGIC_F, -MC_MAGIC_F);
+  const unsigned long long NEG = 0xCB000000CB000000ull;
+  const uint32_t MAG = MC_MAGIC;
   constexpr uint32_t selP = (OFF) | ((OFF + 1) << 4) | ((OFF + 2) << 8) | ((OFF + 3) << 12);
   constexpr uint32_t selQ = (OFF + 1) | ((OFF + 2) << 4) | ((OFF + 3) << 8) | ((OFF + 3) << 12);
-  const uint32_t P = __byte_perm(lo, hi, selP);
-  const uint32_t Q = __byte_perm(lo, hi, selQ);
-  float2 c01 = make_float2(__uint_as_float((P & 0x0000003Fu) | MC_MAGIC),
-                           __uint_as_float((P & 0x00000FC0u) | MC_MAGIC));
-  float2 c23 = make_float2(__uint_as_float((P & 0x0003F000u) | MC_MAGIC),
-                           __uint_as_float((Q & 0x0000FC00u) | MC_MAGIC));
-  c01 = __fadd2_rn(c01, neg);
-  c23 = __fadd2_rn(c23, neg);
-  acc = __ffma2_rn(c01, x01, acc);
-  acc = __ffma2_rn(c23, x23, acc);
+  uint32_t P, Q, c0, c1, c2, c3;
+  if (OFF == 0) {
+    P = lo;
+  } else {
+    asm("prmt.b32 %0, %1, %2, %3;" : "=r"(P) : "r"(lo), "r"(hi), "n"(selP));
+  }
+  asm("prmt.b32 %0, %1, %2, %3;" : "=r"(Q) : "r"(lo), "r"(hi), "n"(selQ));
+  asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(c0) : "r"(P), "n"(0x3F), "r"(MAG));
+  asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(c1) : "r"(P), "n"(0xFC0), "r"(MAG));
+  asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(c2) : "r"(P), "n"(0x3F000), "r"(MAG));
+  asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(c3) : "r"(Q), "n"(0xFC00), "r"(MAG));
+  unsigned long long a = *reinterpret_cast<const unsigned long long*>(&acc), q01, q23;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(q01) : "r"(c0), "r"(c1));
+  asm("mov.b64 %0, {%1, %2};" : "=l"(q23) : "r"(c2), "r"(c3));
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(q01) : "l"(q01), "l"(NEG));
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(q23) : "l"(q23), "l"(NEG));
+  asm("fma.rn.f32x2 %0, %1, %2, %0;"
+      : "+l"(a)
+      : "l"(q01), "l"(*reinterpret_cast<const unsigned long long*>(&x01)));
+  asm("fma.rn.f32x2 %0, %1, %2, %0;"
+      : "+l"(a)
+      : "l"(q23), "l"(*reinterpret_cast<const unsigned long long*>(&x23)));
+  acc = *reinterpret_cast<const float2*>(&a);
 }
 
 // One Q6 group: 48 bytes (three uint4) against 32 pre-scaled activation pairs.

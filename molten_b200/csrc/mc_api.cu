@@ -106,6 +106,16 @@ extern "C" int mc_set_trace(mc_ctx* ctx, unsigned long long* buf, int n) {
   return MC_OK;
 }
 
+extern "C" int mc_set_l2_prefetch(mc_ctx* ctx, const void* p0, size_t n0, const void* p1,
+                                  size_t n1) {
+  if (!ctx) return mc_fail(MC_EINVAL, "mc_set_l2_prefetch: null context");
+  ctx->pf_ptr[0] = n0 ? p0 : nullptr;
+  ctx->pf_bytes[0] = p0 ? n0 : 0;
+  ctx->pf_ptr[1] = n1 ? p1 : nullptr;
+  ctx->pf_bytes[1] = p1 ? n1 : 0;
+  return MC_OK;
+}
+
 extern "C" int mc_sync(mc_ctx* ctx) {
   if (!ctx) return mc_fail(MC_EINVAL, "mc_sync: null context");
   MC_CUDA(cudaStreamSynchronize(ctx->stream));

@@ -21,6 +21,8 @@ struct mc_ctx {
   int ep_timeout_ms;
   unsigned long long* trace;  // optional per-CTA phase timestamps (mc_set_trace)
   int trace_len;
+  const void* pf_ptr[2];      // L2 prefetch for the next decode-layer launch
+  size_t pf_bytes[2];         // (mc_set_l2_prefetch; cleared by that launch)
 };
 
 __device__ __forceinline__ unsigned long long mc_globaltimer() {

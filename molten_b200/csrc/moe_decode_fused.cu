@@ -106,6 +106,8 @@ struct Params {
   float eps, route_eps;
   int mode, E, I;
   unsigned long long* trace;
+  const uint8_t* pf[2];  // L2 prefetch ranges for the next layer (128-byte lines)
+  uint32_t pf_lines[2];
 };
 
 constexpr int kTraceSlots = 32;  // per-CTA phase timestamps (mc_set_trace)
@@ -453,6 +455,14 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(const Par
   }
   __syncthreads();
   TRACE(4);
+  // the next layer's router and norm weights into L2 (mc_set_l2_prefetch):
+  // this CTA's share of the lines, while the act rows are exchanged
+#pragma unroll
+  for (int r = 0; r < 2; ++r) {
+    const uint32_t n = P.pf_lines[r];
+    for (uint32_t l = (uint32_t)cta * kThreads + t; l < n; l += (uint32_t)G * kThreads)
+      asm volatile("prefetch.global.L2::evict_last [%0];" ::"l"(P.pf[r] + 128ull * l));
+  }
   // SwiGLU per pair, one thread each: act = bf16(bf16(silu(g)) * u),
   // published as a tagged word (tag16 << 16 | bf16 bits)
   if (ok && t < np) {
@@ -648,7 +658,19 @@ extern "C" int mc_moe_decode_layer(mc_ctx* ctx, const uint16_t* h, const uint16_
              ctx->max_smem_optin);
   Params P{h, b, norm_w, h_out, normed, router_w, expert_bias, logits, ids, weights, *gate, *up,
            *down, out, sync, eps, route_eps, route_mode, n_experts, I,
-           ctx->trace && ctx->trace_len >= kTraceSlots * G ? ctx->trace : nullptr};
+           ctx->trace && ctx->trace_len >= kTraceSlots * G ? ctx->trace : nullptr,
+           {nullptr, nullptr},
+           {0u, 0u}};
+  for (int r = 0; r < 2; ++r) {
+    if (!ctx->pf_ptr[r]) continue;
+    // whole 128-byte lines covering the range
+    const uintptr_t a = (uintptr_t)ctx->pf_ptr[r] & ~(uintptr_t)127;
+    const uintptr_t e = (uintptr_t)ctx->pf_ptr[r] + ctx->pf_bytes[r];
+    P.pf[r] = reinterpret_cast<const uint8_t*>(a);
+    P.pf_lines[r] = (uint32_t)((e - a + 127) / 128);
+    ctx->pf_ptr[r] = nullptr;
+    ctx->pf_bytes[r] = 0;
+  }
   void* fn = router_dtype == MC_DTYPE_BF16 ? (void*)moe_decode_fused_kernel<MC_DTYPE_BF16>
                                            : (void*)moe_decode_fused_kernel<MC_DTYPE_F32>;
   // the dynamic shared memory limit is raised once per device and kernel

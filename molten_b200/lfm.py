@@ -61,6 +61,16 @@ class Context:
     def commit_wait(self) -> None:
         _lib.check(_lib.lib().mc_sync(self.h))
 
+    def prefetch_next(self, *tensors) -> None:
+        """Cross-layer prefetch hint (mc_set_l2_prefetch, no reference
+        counterpart): the next moe_decode_layer on this context pulls up to two
+        tensors (the next layer's router and RMSNorm weights) into L2."""
+        ts = [t for t in tensors if t is not None][:2] + [None, None]
+        args = []
+        for t in ts[:2]:
+            args += [t.data_ptr(), t.numel() * t.element_size()] if t is not None else [None, 0]
+        _lib.check(_lib.lib().mc_set_l2_prefetch(self.h, *args))
+
     def close(self) -> None:
         if self.h:
             _lib.lib().mc_destroy(self.h)

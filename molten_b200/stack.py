@@ -61,6 +61,8 @@ class DecodeStack:
             lfm.gemv_quant(ctx, L["proj"], cur, self.p)
             nxt = self.outs[l % 2]
             if self.B == 1:
+                following = self.layers[(l + 1) % len(self.layers)]
+                ctx.prefetch_next(following["router"], following["norm_w"])
                 lfm.moe_decode_layer(ctx, cur, self.p, L["norm_w"], self.hout, self.normed,
                                      L["router"], self.logits, None, self.ids[l], self.wts[l],
                                      L["gate"], L["up"], L["down"], nxt, self.ws,
