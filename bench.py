@@ -511,7 +511,8 @@ def bench_gemv(args, torch, ws, rank, local, head: bool):
                    "cfg0: Q4 GEMV 2048x2048", "bytes_per_step": nbytes,
                    "l2": f"{n_copies} rotated weight copies ({n_copies * nbytes / 1e6:.0f} MB)"},
         "roofline": {"bound": "hbm", "achieved": round(value / ws, 1), "peak": hbm,
-                     "unit": "GB/s", "frac": round(value / ws / hbm, 4), "peak_source": src},
+                     "unit": "GB/s", "frac": round(value / ws / hbm, 4), "peak_source": src,
+                     "traffic": ncu_traffic("gemv_ring_kernel", "cfg2") if head else None},
         "gpu_launches": (2 if head else 1) * K, "clocks": clk.summary(),
     }
 
