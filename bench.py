@@ -57,6 +57,8 @@ def parse():
     p.add_argument("--workload", choices=["cfg0", "cfg1", "cfg2", "cfg3", "cfg4"], default="cfg1")
     p.add_argument("--batch", type=int, default=1, help="cfg4 decode batch (1, 8, 32)")
     p.add_argument("--layers", type=int, default=40, help="cfg4 stacked layers")
+    p.add_argument("--moe-path", choices=["auto", "fused", "grouped", "gemv"], default="auto",
+                   help="cfg4 expert path (auto: fused at batch 1, gemv below 16, grouped from 16)")
     p.add_argument("--tokens", type=int, default=4096, help="cfg3 prefill chunk")
     p.add_argument("--ep-placement", choices=["balanced", "contiguous"], default="balanced",
                    help="cfg3 on N>1 GPUs: expert-to-GPU placement")
@@ -762,7 +764,7 @@ def bench_cfg3(args, torch, ws, rank, local):
                      "per_kernel_us": {"gemm_gate_up": round(gu_ms * 1e3, 1),
                                        "gemm_down": round(dn_ms * 1e3, 1)},
                      "down_tflops": round(2.0 * S * H * I / (dn_ms * 1e-3) / 1e12, 1)},
-        "gpu_launches": 7 * K,
+        "gpu_launches": lfm.MOE_PREFILL_LAUNCHES * K,
         "clocks": clk.summary(),
     }
     if rank == 0 and ws == 1 and not args.no_cpu_baseline:
@@ -845,7 +847,8 @@ def bench_cfg4(args, torch, ws, rank, local):
         layers.append(d)
     head = synth.quant_weights_torch(gen, VOCAB, H, 6, centre=31.5)
     embed = torch.randn((VOCAB, H), generator=gen, device="cuda").to(torch.bfloat16)
-    st = DecodeStack(ctx, layers, head, embed, B)
+    st = DecodeStack(ctx, layers, head, embed, B,
+                     moe_path=None if args.moe_path == "auto" else args.moe_path)
     st.start((torch.arange(B, device="cuda", dtype=torch.int32) * 7919 + 11) % VOCAB)
     K = min(args.steps, 512)
     W = max(min(args.warmup, 8), 3)
@@ -907,7 +910,8 @@ def bench_cfg4(args, torch, ws, rank, local):
         "config": {"workload": f"cfg4: {L} layers x (Q4 2048x2048 + E=64 top-4 SwiGLU 2048->1536"
                                f"->2048) + Q6 65536x2048 head + bf16 embedding gather, batch {B}, "
                                "one step per CUDA-graph replay",
-                   "batch": B, "gbs": round(gbs, 1), "bytes_per_step": step_bytes,
+                   "batch": B, "moe_path": st.path, "gbs": round(gbs, 1),
+                   "bytes_per_step": step_bytes,
                    "distinct_experts_per_layer_mean": round(sum(U) / L, 2),
                    "l2": f"inputs > L2: {L} layers of weights ({L * 0.342:.1f} GB) streamed per step",
                    "parallelism": f"replicas x{ws}" if ws > 1 else "single GPU"},

@@ -187,14 +187,17 @@ __device__ __forceinline__ float prescale_group_x(const float* xv, float2* xs) {
 // Loads one group's 64 bf16 activations (128 bytes at x + 64*g), writes the
 // pre-scaled pairs and returns the group's left-to-right activation sum.
 // SRC 0: read-only global (__ldg); 1: global written earlier in the same
-// kernel by other CTAs (__ldcg, L2); 2: generic pointer (shared memory).
+// kernel by other CTAs (__ldcg, L2); 2: shared memory holding the row with
+// the 16-byte chunks of group g at g*8 + (c ^ (g & 7)) (XOR swizzle: lanes
+// reading the same chunk of consecutive groups hit different banks; the
+// plain layout is an 8-way conflict that stalls the whole shared-memory pipe).
 template <int BITS, int SRC = 0>
 __device__ __forceinline__ float load_group_x(const uint16_t* __restrict__ x, int g, float2* xs) {
   const uint4* src = reinterpret_cast<const uint4*>(x + 64 * g);
   float xv[64];
 #pragma unroll
   for (int c = 0; c < 8; ++c) {
-    const uint4 v = SRC == 0 ? __ldg(src + c) : (SRC == 1 ? __ldcg(src + c) : src[c]);
+    const uint4 v = SRC == 0 ? __ldg(src + c) : (SRC == 1 ? __ldcg(src + c) : src[c ^ (g & 7)]);
     const uint32_t wds[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
     for (int h = 0; h < 4; ++h) {

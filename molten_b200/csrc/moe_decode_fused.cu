@@ -197,9 +197,16 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(const Par
   // finished; its outputs (h, b, the workspace) only after this wait
   mc_pdl_launch_dependents();
   mc_pdl_wait();
+  TRACE(22);
   if (t < 256) {
     hv = mc_ldg_stream(reinterpret_cast<const uint4*>(P.h) + t);
     if (P.badd) bv = mc_ldg_stream(reinterpret_cast<const uint4*>(P.badd) + t);
+  }
+  if (P.trace && t == 0) {  // profiling aid: when the h / b and norm words arrive
+    asm volatile("" ::"r"(hv.x), "r"(bv.w));
+    TRACE(23);
+    asm volatile("" ::"r"(wv.x), "r"(wv.w));
+    TRACE(29);
   }
   const uint32_t epoch = *reinterpret_cast<volatile uint32_t*>(sync);
   const uint32_t tag32 = epoch == 0xffffffffu ? 1u : epoch + 1u;
@@ -238,7 +245,9 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(const Par
     reinterpret_cast<float4*>(nrow)[2 * t] = make_float4(n[0], n[1], n[2], n[3]);
     reinterpret_cast<float4*>(nrow)[2 * t + 1] = make_float4(n[4], n[5], n[6], n[7]);
     const uint4 nb = pack8_bf16(n);
-    reinterpret_cast<uint4*>(nbf)[t] = nb;
+    // chunk t of the row = chunk t & 7 of group t >> 3, stored swizzled for
+    // load_group_x<., 2>
+    reinterpret_cast<uint4*>(nbf)[(t & ~7) | ((t & 7) ^ ((t >> 3) & 7))] = nb;
     if (cta == 0) {
       reinterpret_cast<uint4*>(P.h_out)[t] = pack8_bf16(hp);
       reinterpret_cast<uint4*>(P.normed)[t] = nb;
@@ -251,6 +260,15 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(const Par
   // release add (which orders the store before it) counts the published
   // logits, so readers poll one word instead of all E
   if (router_cta && warp == 0) {
+    if (P.trace && t == 0) {  // profiling aid: when the router row arrives
+      const uint4* w = reinterpret_cast<const uint4*>(rr.w);
+      uint32_t all = 0;
+#pragma unroll
+      for (int j = 0; j < (DT == MC_DTYPE_BF16 ? 8 : 16); ++j) all ^= w[j].x ^ w[j].w;
+      asm volatile("" ::"r"(all));
+      TRACE(20);
+      TRACE(21);
+    }
     const float z = rr.dot(nrow, lane);
     TRACE(13);
     if (lane == 0) {
@@ -543,6 +561,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(const Par
       }
       dxg = prescale_group_x<4>(xv, dxs);
     }
+    TRACE(28);
     const bool landed = wait_copies(&bar_dn, mc_globaltimer() + kTimeoutNs);
     if (!landed && lane == 0) record_error(sync, 16u);
     TRACE(9);

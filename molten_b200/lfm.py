@@ -21,6 +21,7 @@ FIXED_MOE_INTER = 1536
 ROUTE_SOFTMAX_RENORM = _lib.ROUTE_SOFTMAX_RENORM
 ROUTE_SIGMOID_BIAS = _lib.ROUTE_SIGMOID_BIAS
 PREFILL_CHUNK = 256  # token rows per grouped-GEMM chunk (mc_moe_prefill's sort_map bm)
+MOE_PREFILL_LAUNCHES = 7  # kernels one mc_moe_prefill call launches
 
 
 def ensure(cond: bool, msg: str) -> None:

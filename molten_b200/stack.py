@@ -13,10 +13,22 @@ embedding row of the token being decoded):
 
 The MoE layer normalises its input (RMSNorm of h + b) before the router and
 the experts, so activations stay bounded over the stack without a separate
-residual stream. B = 1 uses the one-launch fused layer (moe_decode_layer);
-B > 1 the three batched kernels (router_addnorm_route, gemv_gather_act,
-gemv_gather_down_combine4). The token feeds back on the device, so a step
-can be captured once in a CUDA graph and replayed.
+residual stream. The expert part runs one of three ways (``moe_path``):
+
+  "fused"    B = 1: the one-launch fused layer (moe_decode_layer), the
+             default at batch 1;
+  "grouped"  B > 1: router_addnorm_route for the B rows, then the prefill
+             MoE FFN (moe_prefill: route, sort, gather, tensor-core grouped
+             GEMMs, combine), so each routed expert's rows are read and
+             dequantised once per step for all of its tokens -- the default
+             from B = 16; activations match the oracle within the prefill
+             tolerance, the ids given the same logits bit for bit;
+  "gemv"     any B: router_addnorm_route, gemv_gather_act and
+             gemv_gather_down_combine4, per-token GEMVs bit-identical to the
+             oracle -- the default for 1 < B < 16.
+
+The token feeds back on the device, so a step can be captured once in a CUDA
+graph and replayed.
 """
 from __future__ import annotations
 
@@ -27,9 +39,14 @@ from molten_b200 import lfm
 
 class DecodeStack:
     def __init__(self, ctx: lfm.Context, layers: list[dict], head, embed: torch.Tensor,
-                 batch: int, n_experts: int = 64):
+                 batch: int, n_experts: int = 64, moe_path: str | None = None):
         self.ctx, self.layers, self.head, self.embed = ctx, layers, head, embed
         self.B, self.E = batch, n_experts
+        # measured on B200 (40 layers): batch 8 runs faster on the per-token
+        # GEMVs, batch 32 on the grouped expert GEMMs
+        self.path = moe_path or ("fused" if batch == 1 else "gemv" if batch < 16 else "grouped")
+        lfm.ensure(self.path in ("fused", "grouped", "gemv"), f"moe_path {self.path!r}")
+        lfm.ensure(self.path != "fused" or batch == 1, "the fused layer is batch 1")
         H = embed.shape[1]
         I = layers[0]["gate"].out_features // n_experts
         dev = embed.device
@@ -48,8 +65,12 @@ class DecodeStack:
         self.tail_norm_w = torch.ones(H, dtype=torch.bfloat16, device=dev)
         self.tail_normed = bf(batch, H)
         self.ws = None
-        if batch == 1:
+        if self.path == "fused":
             self.ws = torch.zeros(lfm.moe_decode_workspace_words(I), dtype=torch.int32, device=dev)
+        self.pws = None
+        if self.path == "grouped":
+            nb = lfm.moe_prefill_workspace_size(batch, n_experts, H, I)
+            self.pws = torch.zeros(nb, dtype=torch.uint8, device=dev)
 
     def start(self, tokens: torch.Tensor) -> None:
         """Loads the embedding rows of the first tokens (int32 [B])."""
@@ -60,7 +81,7 @@ class DecodeStack:
         for l, L in enumerate(self.layers):
             lfm.gemv_quant(ctx, L["proj"], cur, self.p)
             nxt = self.outs[l % 2]
-            if self.B == 1:
+            if self.path == "fused":
                 following = self.layers[(l + 1) % len(self.layers)]
                 ctx.prefetch_next(following["router"], following["norm_w"])
                 lfm.moe_decode_layer(ctx, cur, self.p, L["norm_w"], self.hout, self.normed,
@@ -71,14 +92,19 @@ class DecodeStack:
                 lfm.router_addnorm_route(ctx, cur, self.p, L["norm_w"], self.hout, self.normed,
                                          L["router"], self.logits, None, self.ids[l],
                                          self.wts[l], self.counter)
-                lfm.gemv_gather_act(ctx, L["gate"], L["up"], self.normed, self.ids[l], self.act,
-                                    n_experts=self.E)
-                lfm.gemv_gather_down_combine4(ctx, L["down"], self.act, self.ids[l], self.wts[l],
-                                              nxt, n_experts=self.E)
+                if self.path == "grouped":
+                    lfm.moe_prefill(ctx, self.normed, self.logits, L["gate"], L["up"], L["down"],
+                                    self.pws, nxt, n_experts=self.E)
+                else:
+                    lfm.gemv_gather_act(ctx, L["gate"], L["up"], self.normed, self.ids[l],
+                                        self.act, n_experts=self.E)
+                    lfm.gemv_gather_down_combine4(ctx, L["down"], self.act, self.ids[l],
+                                                  self.wts[l], nxt, n_experts=self.E)
             cur = nxt
         lfm.gemv_head_argmax(ctx, self.head, cur, self.keys)
         lfm.token_tail(ctx, self.keys, self.tokens,
                        (self.embed, self.tail_norm_w, self.x, self.tail_normed))
 
     def launches_per_step(self) -> int:
-        return len(self.layers) * (2 if self.B == 1 else 4) + 2
+        per_layer = {"fused": 2, "gemv": 4, "grouped": 2 + lfm.MOE_PREFILL_LAUNCHES}[self.path]
+        return len(self.layers) * per_layer + 2

@@ -52,7 +52,9 @@ def test_stacked_decode_matches_oracle(cuda_ctx, batch):
     want = oracle_tokens(layers, head, embed, start, 2 * steps, E)
     dl = [dict(proj=dev_qw(*l["proj"]), norm_w=dev_bf16(l["norm_w"]), router=dev_bf16(l["router"]),
                gate=dev_qw(*l["gate"]), up=dev_qw(*l["up"]), down=dev_qw(*l["down"])) for l in layers]
-    st = DecodeStack(cuda_ctx, dl, dev_qw(*head, bits=6), dev_bf16(embed), batch, n_experts=E)
+    # batch 1: the fused layer; batch 3: the per-token GEMV path (both bit-exact)
+    st = DecodeStack(cuda_ctx, dl, dev_qw(*head, bits=6), dev_bf16(embed), batch, n_experts=E,
+                     moe_path="fused" if batch == 1 else "gemv")
     st.start(torch.from_numpy(start.view(np.int32)).cuda())
     for s in range(steps):  # eager
         st.step()
@@ -73,3 +75,37 @@ def test_stacked_decode_matches_oracle(cuda_ctx, batch):
         torch.cuda.synchronize()
         got = st.tokens.cpu().numpy().view(np.uint32)
         assert np.array_equal(got, want[s]), f"graph step {s}: {got} != {want[s]}"
+
+
+def test_stacked_decode_grouped_path(cuda_ctx):
+    """The batched decode's tensor-core expert path (moe_prefill per layer),
+    teacher-forced from the bit-exact GEMV path's tokens every step: the
+    hidden rows after the last layer agree within the prefill tolerance, and
+    the greedy tokens agree except on near-ties of the head (checked on the
+    oracle's head values of the GEMV path's rows)."""
+    L, E, I, V, steps, batch = 3, 8, 512, 4096, 3, 5
+    layers, head, embed = make_stack(91, L, E, I, V)
+    dl = [dict(proj=dev_qw(*l["proj"]), norm_w=dev_bf16(l["norm_w"]), router=dev_bf16(l["router"]),
+               gate=dev_qw(*l["gate"]), up=dev_qw(*l["up"]), down=dev_qw(*l["down"])) for l in layers]
+    stacks = {p: DecodeStack(cuda_ctx, dl, dev_qw(*head, bits=6), dev_bf16(embed), batch,
+                             n_experts=E, moe_path=p) for p in ("gemv", "grouped")}
+    toks = torch.from_numpy((np.arange(batch, dtype=np.uint32) * 53 % V).view(np.int32)).cuda()
+    for s in range(steps):
+        for st in stacks.values():
+            st.start(toks)
+            st.step()
+        torch.cuda.synchronize()
+        a = stacks["gemv"].outs[(L - 1) % 2].float()
+        b = stacks["grouped"].outs[(L - 1) % 2].float()
+        rms = float(a.pow(2).mean().sqrt())
+        err = float((a - b).abs().max())
+        assert err <= 2e-2 * rms + 2e-2 * float(a.abs().max()), f"step {s}: max err {err}, rms {rms}"
+        ta = stacks["gemv"].tokens.cpu().numpy().view(np.uint32)
+        tb = stacks["grouped"].tokens.cpu().numpy().view(np.uint32)
+        for r in np.nonzero(ta != tb)[0]:
+            x = stacks["gemv"].outs[(L - 1) % 2][r:r + 1].contiguous().view(torch.int16).cpu().numpy()
+            v = synth.bf16_bits_to_f32(oracle.gemv_quant(*head, 6, x.view(np.uint16))[0])
+            gap = float(v[ta[r]] - v[tb[r]])
+            assert 0.0 <= gap <= 2e-2 * float(np.abs(v).max()), f"step {s} row {r}: gap {gap}"
+        toks = stacks["gemv"].tokens.clone()
+    assert stacks["grouped"].launches_per_step() == L * 9 + 2
