@@ -35,7 +35,9 @@
 //               tile; down: warps 2-5 the first 32 K of every row, 6-9 the
 //               second. Then the epilogue from TMEM, half the columns each.
 // Two rings: token rows (bfull: TMA tx, bempty: tcgen05.commit) and weight
-// tiles (afull: dequant arrivals, aempty: tcgen05.commit).
+// tiles (afull: one arrival per dequant warp, aempty: tcgen05.commit). The
+// TMA and MMA roles run on whole warps with one elected lane issuing, and
+// every wait a warp takes gives all its lanes one answer.
 // Every wait is bounded by a %globaltimer deadline; on timeout the kernel
 // records status bit 1, stops issuing and still drains what it issued before
 // freeing TMEM.
@@ -189,6 +191,20 @@ __device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t parity, volatil
   return true;
 }
 
+// The same wait for a whole warp, with one answer for all lanes.
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volatile uint32_t* abort_f) {
+  return __all_sync(0xffffffffu, wait_bar(bar, parity, abort_f));
+}
+
+// One lane of a converged warp (the lowest), chosen with elect.sync.
+__device__ __forceinline__ bool elect_one() {
+  uint32_t e;
+  asm volatile(
+      "{\n .reg .pred p;\n elect.sync _|p, 0xffffffff;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(e));
+  return e != 0;
+}
+
 // ---- epilogue arithmetic ------------------------------------------------------
 // Single-value float->bf16 conversions and MUFU exp/rcp each issue at about
 // 16 per clock per SM, so the epilogue rounds with integer ops (round to
@@ -281,12 +297,12 @@ grouped_gemm_kernel(const __grid_constant__ TokenMaps tm, const GemmParams P) {
       mc_mbar_init(&bempty[s], 1);
     }
     for (int s = 0; s < C::ASTAGES; ++s) {
-      mc_mbar_init(&afull[s], kDeqThreads);
+      mc_mbar_init(&afull[s], kDeqThreads / 32);
       mc_mbar_init(&aempty[s], 1);
     }
     for (int b = 0; b < 2; ++b) {
       mc_mbar_init(&acc_full[b], 1);
-      mc_mbar_init(&acc_empty[b], kDeqThreads);
+      mc_mbar_init(&acc_empty[b], kDeqThreads / 32);
     }
     mc_mbar_init(&drain_bar, 1);
     mc_fence_barrier_init();
@@ -312,56 +328,70 @@ grouped_gemm_kernel(const __grid_constant__ TokenMaps tm, const GemmParams P) {
 
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer
-    if (lane == 0) {
-      uint32_t it = 0;
-      for (int i = 0, item = cta_item(0); item < total && !abort_s; item = cta_item(++i)) {
-        const Item w = item_info(P, item, nblk);
-        const CUtensorMap* map = w.n <= 64 ? &tm.m64 : (w.n <= 128 ? &tm.m128 : &tm.m256);
-        const uint32_t bytes = (uint32_t)(w.n <= 64 ? 64 : (w.n <= 128 ? 128 : 256)) * BK * 2;
-        for (int kk = 0; kk < ksteps; ++kk, ++it) {
-          const int s = it % C::BSTAGES;
-          const uint32_t ph = (it / C::BSTAGES) & 1;
-          if (!wait_bar(&bempty[s], ph ^ 1, &abort_s)) {
-            abort_s = 1;
-            break;
-          }
+    // The issuing roles run their loops on the whole warp (stage indices and
+    // descriptors are warp-uniform) and one elected lane issues: a lone lane
+    // in a divergent branch issued tcgen05.mma at about half the rate the
+    // tensor pipe takes them while the dequant warps kept its sub-partition busy.
+    uint32_t it = 0;
+    for (int i = 0, item = cta_item(0); item < total; item = cta_item(++i)) {
+      if (__any_sync(0xffffffffu, abort_s != 0)) break;
+      const Item w = item_info(P, item, nblk);
+      const CUtensorMap* map = w.n <= 64 ? &tm.m64 : (w.n <= 128 ? &tm.m128 : &tm.m256);
+      const uint32_t bytes = (uint32_t)(w.n <= 64 ? 64 : (w.n <= 128 ? 128 : 256)) * BK * 2;
+      bool ok = true;
+      for (int kk = 0; kk < ksteps; ++kk, ++it) {
+        const int s = it % C::BSTAGES;
+        const uint32_t ph = (it / C::BSTAGES) & 1;
+        if (!warp_wait(&bempty[s], ph ^ 1, &abort_s)) {
+          ok = false;
+          break;
+        }
+        if (elect_one()) {
           mc_mbar_expect_tx(&bfull[s], bytes);
           tma_load_2d(smem + s * C::B_BYTES, map, kk * BK, (int)w.m0, &bfull[s]);
         }
+        __syncwarp();
       }
-      if (abort_s) {
-        // loads already issued finish within microseconds; give them a bounded
-        // time to land before the CTA may leave
-        for (int k = 0; k < 200; ++k) __nanosleep(1000);
+      if (!ok) {
+        if (lane == 0) abort_s = 1;
+        break;
       }
+    }
+    __syncwarp();
+    if (abort_s) {
+      // loads already issued finish within microseconds; give them a bounded
+      // time to land before the CTA may leave
+      for (int k = 0; k < 200; ++k) __nanosleep(1000);
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
-      uint32_t it = 0, j = 0;
-      for (int i = 0, item = cta_item(0); item < total && !abort_s; item = cta_item(++i), ++j) {
-        const Item w = item_info(P, item, nblk);
-        const uint32_t idesc = idesc_for(w.n);
-        const int buf = (int)(j % C::NBUF);
-        const uint32_t use = j / C::NBUF;
-        if (!wait_bar(&acc_empty[buf], (use & 1) ^ 1, &abort_s)) {
-          abort_s = 1;
+    // (lane 0 is the elected lane: the commits track its MMAs, and the
+    // shutdown drain below commits from lane 0 too)
+    uint32_t it = 0, j = 0;
+    for (int i = 0, item = cta_item(0); item < total; item = cta_item(++i), ++j) {
+      if (__any_sync(0xffffffffu, abort_s != 0)) break;
+      const Item w = item_info(P, item, nblk);
+      const uint32_t idesc = idesc_for(w.n);
+      const int buf = (int)(j % C::NBUF);
+      const uint32_t use = j / C::NBUF;
+      if (!warp_wait(&acc_empty[buf], (use & 1) ^ 1, &abort_s)) {
+        if (lane == 0) abort_s = 1;
+        break;
+      }
+      tc_fence_after();
+      const uint32_t d0 = tmem + (uint32_t)(buf * C::ACC_COLS);
+      bool ok = true;
+      for (int kk = 0; kk < ksteps; ++kk, ++it) {
+        const int sb = it % C::BSTAGES, sa = it % C::ASTAGES;
+        if (!warp_wait(&bfull[sb], (it / C::BSTAGES) & 1, &abort_s) ||
+            !warp_wait(&afull[sa], (it / C::ASTAGES) & 1, &abort_s)) {
+          ok = false;
           break;
         }
         tc_fence_after();
-        const uint32_t d0 = tmem + (uint32_t)(buf * C::ACC_COLS);
-        bool ok = true;
-        for (int kk = 0; kk < ksteps; ++kk, ++it) {
-          const int sb = it % C::BSTAGES, sa = it % C::ASTAGES;
-          if (!wait_bar(&bfull[sb], (it / C::BSTAGES) & 1, &abort_s) ||
-              !wait_bar(&afull[sa], (it / C::ASTAGES) & 1, &abort_s)) {
-            abort_s = 1;
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          const uint64_t bdesc = sw128_desc(mc_smem_u32(smem + sb * C::B_BYTES));
-          const uint32_t abase = mc_smem_u32(a_ring + sa * C::A_STAGE);
+        const uint64_t bdesc = sw128_desc(mc_smem_u32(smem + sb * C::B_BYTES));
+        const uint32_t abase = mc_smem_u32(a_ring + sa * C::A_STAGE);
+        if (elect_one()) {
 #pragma unroll
           for (int ti = 0; ti < C::NMAT; ++ti) {
             const uint64_t adesc = sw128_desc(abase + ti * C::A_BYTES);
@@ -373,9 +403,14 @@ grouped_gemm_kernel(const __grid_constant__ TokenMaps tm, const GemmParams P) {
           umma_commit(&bempty[sb]);  // both stages free once these MMAs have read them
           umma_commit(&aempty[sa]);
         }
-        if (!ok) break;
-        umma_commit(&acc_full[buf]);
+        __syncwarp();
       }
+      if (!ok) {
+        if (lane == 0) abort_s = 1;
+        break;
+      }
+      if (elect_one()) umma_commit(&acc_full[buf]);
+      __syncwarp();
     }
     __syncwarp();
   } else {
@@ -428,7 +463,7 @@ grouped_gemm_kernel(const __grid_constant__ TokenMaps tm, const GemmParams P) {
     auto do_slice = [&](const uint4* c, uint32_t itk, float sc, float bi) -> bool {
       const int s = itk % C::ASTAGES;
       const uint32_t ph = (itk / C::ASTAGES) & 1;
-      if (!wait_bar(&aempty[s], ph ^ 1, &abort_s)) return false;
+      if (!warp_wait(&aempty[s], ph ^ 1, &abort_s)) return false;
       uint8_t* row = a_ring + s * C::A_STAGE + (GU ? grp * C::A_BYTES : 0) + d * 128;
       uint32_t W[4 * NU];
 #pragma unroll
@@ -440,12 +475,14 @@ grouped_gemm_kernel(const __grid_constant__ TokenMaps tm, const GemmParams P) {
       }
       dequant_words<2 * NU>(W, sc, bi, row, d & 7, GU ? 0 : 4 * grp);
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-      mc_mbar_arrive(&afull[s]);
+      __syncwarp();
+      if (lane == 0) mc_mbar_arrive(&afull[s]);
       return true;
     };
     uint32_t it = 0, j = 0;
     Item w = start_item(cta_item(0) < total ? cta_item(0) : 0);
-    for (int i = 0, item = cta_item(0); item < total && !abort_s; item = cta_item(++i), ++j) {
+    for (int i = 0, item = cta_item(0); item < total; item = cta_item(++i), ++j) {
+      if (__any_sync(0xffffffffu, abort_s != 0)) break;
       if (!w.ok && dt == 0 && P.status) atomicOr(P.status, 2u);
       bool ok = true;
       for (int kk = 0; kk < ksteps; kk += 2) {
@@ -478,7 +515,7 @@ grouped_gemm_kernel(const __grid_constant__ TokenMaps tm, const GemmParams P) {
       // ---- epilogue: TMEM [feature][token] -> bf16 out[token][feature]
       const int buf = (int)(j % C::NBUF);
       const uint32_t use = j / C::NBUF;
-      if (!wait_bar(&acc_full[buf], use & 1, &abort_s)) {
+      if (!warp_wait(&acc_full[buf], use & 1, &abort_s)) {
         abort_s = 1;
         break;
       }
@@ -516,7 +553,8 @@ grouped_gemm_kernel(const __grid_constant__ TokenMaps tm, const GemmParams P) {
         }
       }
       tc_fence_before();
-      mc_mbar_arrive(&acc_empty[buf]);
+      __syncwarp();
+      if (lane == 0) mc_mbar_arrive(&acc_empty[buf]);
     }
   }
 
