@@ -268,6 +268,8 @@ extern "C" int mc_gemv_quant(mc_ctx* ctx, const mc_qweights* w, const uint16_t* 
   MC_REQUIRE(mc_aligned(x, 16), "gemv_quant: x must be 16-byte aligned");
   rc = mc_gemv_ring(ctx, w, x, y, nullptr, batch, 0);
   if (rc != 1) return rc;
+  rc = mc_gemv_batched(ctx, w, x, y, nullptr, batch, 0);
+  if (rc != 1) return rc;
   return dispatch_gemv<0>(ctx, w, x, y, nullptr, batch);
 }
 
@@ -281,6 +283,8 @@ extern "C" int mc_gemv_head_argmax(mc_ctx* ctx, const mc_qweights* w, const uint
   MC_REQUIRE(mc_aligned(x, 16), "gemv_head_argmax: x must be 16-byte aligned");
   MC_REQUIRE(batch >= 1 && batch <= 65535, "gemv_head_argmax: batch %d out of range", batch);
   rc = mc_gemv_ring(ctx, w, x, nullptr, keys, batch, 1);
+  if (rc != 1) return rc;
+  rc = mc_gemv_batched(ctx, w, x, nullptr, keys, batch, 1);
   if (rc != 1) return rc;
   return dispatch_gemv<1>(ctx, w, x, nullptr, keys, batch);
 }

@@ -46,6 +46,41 @@ def test_gemv_quant_bit_exact(cuda_ctx, bits, n, k, batch):
     assert_bits_equal(host_bits(y), want, f"gemv q{bits} {n}x{k} b{batch}")
 
 
+# batch >= 2 on matrices of at least 256 rows per SM takes the batched kernel
+# (each code decoded once for up to 8 tokens, the butterfly replayed in-lane):
+# a partial token group (5, 9), K < 2048 (groups 16..31 / 24..31 idle)
+@pytest.mark.parametrize("bits,n,k,batch", [(6, 40000, 2048, 2), (4, 38000, 1536, 5),
+                                            (6, 65536, 2048, 9), (4, 40000, 1024, 3)])
+def test_gemv_batched_bit_exact(cuda_ctx, bits, n, k, batch):
+    g = synth.rng(60 + bits + k + batch)
+    codes, s, b = synth.quant_weights_np(g, n, k, bits)
+    x = synth.activations_np(g, batch, k)
+    w = dev_qw(codes, s, b, bits)
+    y = empty_bf16(batch, n)
+    lfm.gemv_quant(cuda_ctx, w, dev_bf16(x), y)
+    want = oracle.gemv_quant(codes, s, b, bits, x)
+    assert_bits_equal(host_bits(y), want, f"batched gemv q{bits} {n}x{k} b{batch}")
+
+
+def test_head_argmax_batched(cuda_ctx):
+    """Q6 65536 x 2048 head at batch 11 (two token groups, the second partial):
+    keys bit-exact, including a forced tie resolved to the lower row."""
+    g = synth.rng(43)
+    n, k = 65536, 2048
+    codes, s, b = synth.quant_weights_np(g, n, k, 6)
+    x = synth.activations_np(g, 11, k)
+    y = oracle.gemv_quant(codes, s, b, 6, x[9:10])[0]
+    win = int(np.argmax(synth.bf16_bits_to_f32(y)))
+    lo = win // 3
+    codes[lo], s[lo], b[lo] = codes[win], s[win], b[win]
+    keys_o, toks_o = oracle.head_argmax(codes, s, b, 6, x)
+    assert toks_o[9] == lo
+    w = dev_qw(codes, s, b, 6)
+    key = torch.zeros(11, dtype=torch.int64, device="cuda")
+    lfm.gemv_head_argmax(cuda_ctx, w, dev_bf16(x), key)
+    assert np.array_equal(key.cpu().numpy().view(np.uint64), keys_o)
+
+
 def test_golden_gemv_and_head(cuda_ctx):
     for name, bits in (("q4_gemv", 4), ("q6_head", 6)):
         d = np.load(make_golden.path(name))
