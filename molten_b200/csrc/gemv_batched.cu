@@ -20,8 +20,10 @@
 // the two is "own" does not matter). Groups at or past K/64 contribute +0,
 // as the idle lanes of the butterfly do.
 //
-// K <= 2048 (one group per lane in the canonical order); larger K and
-// unaligned operands stay on gemv_kernel.
+// Short matrices split K over up to 8 warps per row block (each one subtree
+// of the butterfly, the subtrees then added in its order) so that a 2048-row
+// projection still fills the SMs. K <= 2048 (one group per lane in the
+// canonical order); larger K and unaligned operands stay on gemv_kernel.
 #include <atomic>
 
 #include "gemv_common.cuh"
@@ -165,7 +167,7 @@ __global__ void __launch_bounds__(kThreadsB, 1)
 gemv_batched_kernel(const uint8_t* __restrict__ codes, const uint16_t* __restrict__ scales,
                     const uint16_t* __restrict__ biases, const uint16_t* __restrict__ x,
                     uint16_t* __restrict__ y, unsigned long long* __restrict__ keys, int N, int K,
-                    int batch) {
+                    int batch, int ks_log2) {
   extern __shared__ __align__(16) uint8_t smb[];
   float2* xs_s = reinterpret_cast<float2*>(smb);
   float* xg_s = reinterpret_cast<float*>(smb + T * BatchedShape<T>::kPairs);
@@ -214,8 +216,29 @@ gemv_batched_kernel(const uint8_t* __restrict__ codes, const uint16_t* __restric
     best_i[t] = 0;
   }
 
+  // K split: KS = 2^ks_log2 warps share a row block, part p taking the
+  // groups whose visit index s has s >> (5 - ks_log2) == p -- one subtree of
+  // the butterfly -- and the parts are then added in the butterfly's order
+  // (balanced tree over p). A CTA covers kWarpsB / KS row blocks per pass;
+  // every warp of the CTA runs the same number of passes.
+  const int KS = 1 << ks_log2;
+  const int part = warp & (KS - 1);
+  const int rbl = warp >> ks_log2;
+  const int rb_per_cta = kWarpsB >> ks_log2;
+  const int s_lo = part << (5 - ks_log2), s_hi = (part + 1) << (5 - ks_log2);
+  // loop bounds of the visit digits i1..i4 (i0 always runs 0..1)
+  int lo[5], hi[5];
+#pragma unroll
+  for (int d = 1; d < 5; ++d) {
+    const bool fixed = d >= 5 - ks_log2;
+    lo[d] = fixed ? (s_lo >> d) & 1 : 0;
+    hi[d] = fixed ? lo[d] + 1 : 2;
+  }
+  __shared__ float part_s[kWarpsB][T][32];
+
   const int nrb = (N + 31) / 32;
-  for (int rb = blockIdx.x * kWarpsB + warp; rb < nrb; rb += gridDim.x * kWarpsB) {
+  for (int base = blockIdx.x * rb_per_cta; base < nrb; base += gridDim.x * rb_per_cta) {
+    const int rb = base + rbl;
     const int row = rb * 32 + lane;
     const bool on = row < N;
     const int rr = on ? row : N - 1;
@@ -227,26 +250,29 @@ gemv_batched_kernel(const uint8_t* __restrict__ codes, const uint16_t* __restric
     // the next group's codes and scale / bias load while this one computes
     RawGroup<BITS> cur, nxt;
     uint16_t s_cur = 0, b_cur = 0, s_nxt = 0, b_nxt = 0;
-    if (0 < G) {
-      cur.load(crow, 0);
-      s_cur = __ldg(srow);
-      b_cur = __ldg(brow);
+    {
+      const int g0 = (int)(__brev((unsigned)s_lo) >> 27);
+      if (g0 < G) {
+        cur.load(crow, g0);
+        s_cur = __ldg(srow + g0);
+        b_cur = __ldg(brow + g0);
+      }
     }
     float l1[T], l2[T], l3[T], l4[T], l5[T];
 #pragma unroll 1
-    for (int i4 = 0; i4 < 2; ++i4) {
+    for (int i4 = lo[4]; i4 < hi[4]; ++i4) {
 #pragma unroll 1
-      for (int i3 = 0; i3 < 2; ++i3) {
+      for (int i3 = lo[3]; i3 < hi[3]; ++i3) {
 #pragma unroll 1
-        for (int i2 = 0; i2 < 2; ++i2) {
+        for (int i2 = lo[2]; i2 < hi[2]; ++i2) {
 #pragma unroll 1
-          for (int i1 = 0; i1 < 2; ++i1) {
+          for (int i1 = lo[1]; i1 < hi[1]; ++i1) {
 #pragma unroll
             for (int i0 = 0; i0 < 2; ++i0) {
               const int s = i0 + 2 * i1 + 4 * i2 + 8 * i3 + 16 * i4;
               const int g = 16 * i0 + 8 * i1 + 4 * i2 + 2 * i3 + i4;
               const int gn = (int)(__brev((unsigned)(s + 1)) >> 27);
-              if (s + 1 < 32 && gn < G) {
+              if (s + 1 < s_hi && gn < G) {
                 nxt.load(crow, gn);
                 s_nxt = __ldg(srow + gn);
                 b_nxt = __ldg(brow + gn);
@@ -276,29 +302,53 @@ gemv_batched_kernel(const uint8_t* __restrict__ codes, const uint16_t* __restric
               b_cur = b_nxt;
             }
 #pragma unroll
-            for (int t = 0; t < T; ++t) l2[t] = i1 ? __fadd_rn(l2[t], l1[t]) : l1[t];
+            for (int t = 0; t < T; ++t) l2[t] = i1 != lo[1] ? __fadd_rn(l2[t], l1[t]) : l1[t];
           }
 #pragma unroll
-          for (int t = 0; t < T; ++t) l3[t] = i2 ? __fadd_rn(l3[t], l2[t]) : l2[t];
+          for (int t = 0; t < T; ++t) l3[t] = i2 != lo[2] ? __fadd_rn(l3[t], l2[t]) : l2[t];
         }
 #pragma unroll
-        for (int t = 0; t < T; ++t) l4[t] = i3 ? __fadd_rn(l4[t], l3[t]) : l3[t];
+        for (int t = 0; t < T; ++t) l4[t] = i3 != lo[3] ? __fadd_rn(l4[t], l3[t]) : l3[t];
       }
 #pragma unroll
-      for (int t = 0; t < T; ++t) l5[t] = i4 ? __fadd_rn(l5[t], l4[t]) : l4[t];
+      for (int t = 0; t < T; ++t) l5[t] = i4 != lo[4] ? __fadd_rn(l5[t], l4[t]) : l4[t];
     }
 
-    if (MODE == 0) {
+    if (KS > 1) {
+      // the parts' subtree sums, added level by level (p, p ^ 1), (.., .. ^ 2), ..
 #pragma unroll
-      for (int t = 0; t < T; ++t)
-        if (on && t < nt) y[(size_t)(t0 + t) * N + row] = mc_f32_to_bf16(l5[t]);
-    } else {
+      for (int t = 0; t < T; ++t) part_s[warp][t][lane] = l5[t];
+      __syncthreads();
+      if (part == 0) {
 #pragma unroll
-      for (int t = 0; t < T; ++t) {
-        const float v = mc_round_bf16(l5[t]);
-        if (on && mc_better(v, (uint32_t)row, best_v[t], best_i[t])) {
-          best_v[t] = v;
-          best_i[t] = (uint32_t)row;
+        for (int t = 0; t < T; ++t) {
+          float v[8];
+#pragma unroll
+          for (int q = 0; q < 8; ++q) v[q] = q < KS ? part_s[warp + q][t][lane] : 0.0f;
+#pragma unroll
+          for (int w = 8; w > 1; w >>= 1)
+            if (w <= KS) {
+#pragma unroll
+              for (int q = 0; q < w / 2; ++q) v[q] = __fadd_rn(v[2 * q], v[2 * q + 1]);
+            }
+          l5[t] = v[0];
+        }
+      }
+      __syncthreads();
+    }
+    if (part == 0) {
+      if (MODE == 0) {
+#pragma unroll
+        for (int t = 0; t < T; ++t)
+          if (on && t < nt) y[(size_t)(t0 + t) * N + row] = mc_f32_to_bf16(l5[t]);
+      } else {
+#pragma unroll
+        for (int t = 0; t < T; ++t) {
+          const float v = mc_round_bf16(l5[t]);
+          if (on && mc_better(v, (uint32_t)row, best_v[t], best_i[t])) {
+            best_v[t] = v;
+            best_i[t] = (uint32_t)row;
+          }
         }
       }
     }
@@ -353,14 +403,18 @@ int launch_batched(mc_ctx* ctx, const mc_qweights* w, const uint16_t* x, uint16_
   }
   const int groups = (batch + T - 1) / T;
   const int nrb = (w->out_features + 31) / 32;
-  const int need = (nrb + kWarpsB - 1) / kWarpsB;
+  // split K over up to 8 warps per row block until the warps fill one CTA per SM
+  int ks_log2 = 0;
+  while (ks_log2 < 3 && ((long)nrb * groups << ks_log2) < (long)ctx->num_sms * kWarpsB) ++ks_log2;
+  const int rb_per_cta = kWarpsB >> ks_log2;
+  const int need = (nrb + rb_per_cta - 1) / rb_per_cta;
   // one CTA per SM in all: the token groups share the SMs
   int gx = (ctx->num_sms + groups - 1) / groups;
   if (gx > need) gx = need;
   if (gx < 1) gx = 1;
   MC_CUDA(mc_launch_pdl(fn, dim3(gx, groups), dim3(kThreadsB), smem, ctx->stream,
                         reinterpret_cast<const uint8_t*>(w->codes), w->scales, w->biases, x, y,
-                        keys, w->out_features, w->in_features, batch));
+                        keys, w->out_features, w->in_features, batch, ks_log2));
   return mc_after_launch("gemv_batched_kernel");
 }
 
@@ -374,14 +428,16 @@ int dispatch_batched(mc_ctx* ctx, const mc_qweights* w, const uint16_t* x, uint1
 
 }  // namespace
 
-// Used by mc_gemv_quant / mc_gemv_head_argmax (gemv.cu) for batch >= 2,
-// K <= 2048 and tall matrices (at least 32 rows per warp slot of one CTA per
-// SM). Returns 1 when the call does not qualify (the caller then uses
-// gemv_kernel), else MC_OK or an error code.
+// Used by mc_gemv_quant / mc_gemv_head_argmax (gemv.cu) for K <= 2048 and
+// batch >= 2 on tall matrices (at least 32 rows per warp slot of one CTA per
+// SM), batch >= 8 on any. Returns 1 when the call does not qualify (the
+// caller then uses gemv_kernel), else MC_OK or an error code.
 int mc_gemv_batched(mc_ctx* ctx, const mc_qweights* w, const uint16_t* x, uint16_t* y,
                     unsigned long long* keys, int batch, int mode) {
   if (batch < 2 || w->group_size != 64 || w->in_features > 64 * kMaxG) return 1;
-  if ((long)w->out_features < (long)ctx->num_sms * kWarpsB * 32) return 1;
+  // short matrices (the 2048-row projection) from batch 8: measured on B200 at
+  // batch 8 / 32, 12.0 / 39.9 us per-token vs 10.5 / 17.9 us here (K split 8)
+  if ((long)w->out_features < (long)ctx->num_sms * kWarpsB * 32 && batch < 8) return 1;
   if ((int)BatchedShape<8>::kSmem + 4096 > ctx->max_smem_optin) return 1;
   if (!mc_aligned(w->codes, 16) || !mc_aligned(x, 16)) return 1;
   if (w->bits == 6)

@@ -60,8 +60,9 @@ int mc_after_launch(const char* what);
 // returns 1 when the shape does not qualify. mode 0: y, mode 1: argmax keys.
 int mc_gemv_ring(mc_ctx* ctx, const mc_qweights* w, const uint16_t* x, uint16_t* y,
                  unsigned long long* keys, int batch, int mode);
-// Batched GEMV (gemv_batched.cu) for batch >= 2, K <= 2048, tall matrices:
-// each code decoded once for up to 8 tokens; same return convention.
+// Batched GEMV (gemv_batched.cu) for K <= 2048 at batch >= 2 on tall
+// matrices, batch >= 8 on any: each code decoded once for up to 8 tokens;
+// same return convention.
 int mc_gemv_batched(mc_ctx* ctx, const mc_qweights* w, const uint16_t* x, uint16_t* y,
                     unsigned long long* keys, int batch, int mode);
 

@@ -46,11 +46,15 @@ def test_gemv_quant_bit_exact(cuda_ctx, bits, n, k, batch):
     assert_bits_equal(host_bits(y), want, f"gemv q{bits} {n}x{k} b{batch}")
 
 
-# batch >= 2 on matrices of at least 256 rows per SM takes the batched kernel
-# (each code decoded once for up to 8 tokens, the butterfly replayed in-lane):
-# a partial token group (5, 9), K < 2048 (groups 16..31 / 24..31 idle)
+# batch >= 2 on matrices of at least 256 rows per SM, and batch >= 8 on any,
+# take the batched kernel (each code decoded once for up to 8 tokens, the
+# butterfly replayed in-lane; short matrices split K over 2-8 warps): partial
+# token groups (5, 9, 12), K < 2048 (groups 16..31 / 24..31 idle), a partial
+# row block (1000 rows)
 @pytest.mark.parametrize("bits,n,k,batch", [(6, 40000, 2048, 2), (4, 38000, 1536, 5),
-                                            (6, 65536, 2048, 9), (4, 40000, 1024, 3)])
+                                            (6, 65536, 2048, 9), (4, 40000, 1024, 3),
+                                            (4, 2048, 2048, 8), (4, 2048, 2048, 32),
+                                            (6, 1000, 2048, 9), (4, 2048, 1536, 12)])
 def test_gemv_batched_bit_exact(cuda_ctx, bits, n, k, batch):
     g = synth.rng(60 + bits + k + batch)
     codes, s, b = synth.quant_weights_np(g, n, k, bits)
