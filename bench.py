@@ -58,7 +58,7 @@ def parse():
     p.add_argument("--batch", type=int, default=1, help="cfg4 decode batch (1, 8, 32)")
     p.add_argument("--layers", type=int, default=40, help="cfg4 stacked layers")
     p.add_argument("--moe-path", choices=["auto", "fused", "grouped", "gemv"], default="auto",
-                   help="cfg4 expert path (auto: fused at batch 1, gemv below 16, grouped from 16)")
+                   help="cfg4 expert path (auto: fused at batch 1, gemv up to 16, grouped above)")
     p.add_argument("--tokens", type=int, default=4096, help="cfg3 prefill chunk")
     p.add_argument("--ep-placement", choices=["balanced", "contiguous"], default="balanced",
                    help="cfg3 on N>1 GPUs: expert-to-GPU placement")

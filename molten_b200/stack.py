@@ -21,11 +21,12 @@ residual stream. The expert part runs one of three ways (``moe_path``):
              MoE FFN (moe_prefill: route, sort, gather, tensor-core grouped
              GEMMs, combine), so each routed expert's rows are read and
              dequantised once per step for all of its tokens -- the default
-             from B = 16; activations match the oracle within the prefill
+             above B = 16 (measured on B200: 2276 vs 1987 tokens/s for "gemv"
+             vs "grouped" at B = 16, 2473 vs 3123 at B = 32); activations match the oracle within the prefill
              tolerance, the ids given the same logits bit for bit;
   "gemv"     any B: router_addnorm_route, gemv_gather_act and
              gemv_gather_down_combine4, per-token GEMVs bit-identical to the
-             oracle -- the default for 1 < B < 16.
+             oracle -- the default for 1 < B <= 16.
 
 The token feeds back on the device, so a step can be captured once in a CUDA
 graph and replayed.
@@ -44,7 +45,7 @@ class DecodeStack:
         self.B, self.E = batch, n_experts
         # measured on B200 (40 layers): batch 8 runs faster on the per-token
         # GEMVs, batch 32 on the grouped expert GEMMs
-        self.path = moe_path or ("fused" if batch == 1 else "gemv" if batch < 16 else "grouped")
+        self.path = moe_path or ("fused" if batch == 1 else "gemv" if batch <= 16 else "grouped")
         lfm.ensure(self.path in ("fused", "grouped", "gemv"), f"moe_path {self.path!r}")
         lfm.ensure(self.path != "fused" or batch == 1, "the fused layer is batch 1")
         H = embed.shape[1]
