@@ -202,8 +202,11 @@ class DecodeChain:
         g = torch.Generator(device=dev)
         g.manual_seed(seed + 12345)
         bf = torch.bfloat16
-        self.h = [torch.randn(1, H, generator=g, device=dev).to(bf) for _ in range(2)]
-        self.out = torch.randn(1, H, generator=g, device=dev).to(bf)
+        # rows: h[0], out (the layer's b input and its output), h[1] -- so the
+        # step's two input rows are adjacent whichever h is current
+        self.io = torch.randn(3, H, generator=g, device=dev).to(bf)
+        self.h = [self.io[0:1], self.io[2:3]]
+        self.out = self.io[1:2]
         self.normed = torch.empty(1, H, device=dev, dtype=bf)
         self.logits = torch.empty(1, E, device=dev, dtype=torch.float32)
         self.ids = torch.zeros(1, 4, device=dev, dtype=torch.int32)
@@ -401,31 +404,44 @@ def bench_cfg1(args, torch, ws, rank, local):
     hbm, _, src = peaks()
     achieved = kbytes[dom] / (per[dom] * 1e-3) / 1e9
 
-    # end to end through the public API with host buffers
-    n_e2e = min(K, 2000)
-    pin_in = torch.empty((2, H), dtype=torch.bfloat16).pin_memory()
-    pin_in.copy_(torch.randn(2, H).to(torch.bfloat16))
+    # end to end through the public API with host buffers: every step copies
+    # its two input rows (h, b) from pinned host memory in one 8 KB copy and
+    # reads its output row back; 2 x sets steps (both h parities, every weight
+    # set) are captured once through molten_b200.lfm and replayed, so the
+    # host's per-call overhead does not stand in for the step
+    n_cap = 2 * len(layers)
+    reps = max(1, min(K, 2000) // n_cap)
+    n_e2e = reps * n_cap
+    pin_in = torch.empty((2, 2, H), dtype=torch.bfloat16).pin_memory()
+    rows = torch.randn(2, H).to(torch.bfloat16)
+    pin_in[0].copy_(rows)          # parity 0: io[0:2] = (h, b)
+    pin_in[1].copy_(rows.flip(0))  # parity 1: io[1:3] = (b, h)
     pin_out = torch.empty((1, H), dtype=torch.bfloat16).pin_memory()
-    for _ in range(3):
-        chain.h[chain.parity].copy_(pin_in[0:1], non_blocking=True)
-        chain.out.copy_(pin_in[1:2], non_blocking=True)
+
+    def e2e_step():
+        dst = chain.io[0:2] if chain.parity == 0 else chain.io[1:3]
+        chain.lfm.copy_async(chain.ctx, dst, pin_in[chain.parity])
         chain.step()
-        pin_out.copy_(chain.out, non_blocking=True)
+        chain.lfm.copy_async(chain.ctx, pin_out, chain.out)
+
+    for _ in range(n_cap):
+        e2e_step()
+    torch.cuda.synchronize()
+    g_e2e = capture(torch, e2e_step, n_cap)
+    g_e2e.replay()
     torch.cuda.synchronize()
     barrier(ws)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     t0 = time.perf_counter()
     e0.record()
-    for _ in range(n_e2e):
-        chain.h[chain.parity].copy_(pin_in[0:1], non_blocking=True)
-        chain.out.copy_(pin_in[1:2], non_blocking=True)
-        chain.step()
-        pin_out.copy_(chain.out, non_blocking=True)
+    for _ in range(reps):
+        g_e2e.replay()
     e1.record()
     torch.cuda.synchronize()
     wall = time.perf_counter() - t0
     e2e_ms = max(e0.elapsed_time(e1), wall * 1e3)
     e2e_ms = max_over_ranks(ws, e2e_ms)
+    del g_e2e
     e2e = ws * LAYER_BYTES * n_e2e / (e2e_ms * 1e-3) / 1e9
 
     cpu = None
@@ -446,8 +462,10 @@ def bench_cfg1(args, torch, ws, rank, local):
                    "parallelism": f"replicas x{ws}" if ws > 1 else "single GPU"},
         "e2e": {"value": round(e2e, 2), "unit": "GB/s", "h2d_bytes_per_step": 2 * H * 2,
                 "d2h_bytes_per_step": H * 2,
-                "note": f"{n_e2e} steps through molten_b200.lfm (ctypes -> C ABI) with "
-                        "pinned host input/output rows"},
+                "note": f"{n_e2e} steps through molten_b200.lfm (ctypes -> C ABI), each "
+                        "staging its h and b rows in from pinned host memory and its output "
+                        "row out with mc_copy_async (one 8 KB and one 4 KB copy); "
+                        f"{n_cap} steps per CUDA-graph replay"},
         "roofline": {"bound": "hbm", "kernel": names[dom], "achieved": round(achieved, 1),
                      "peak": hbm, "unit": "GB/s", "frac": round(achieved / hbm, 4),
                      "peak_source": f"{src} (MEASURED_PEAKS.json hbm_gbs)" if src == "measured"

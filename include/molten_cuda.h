@@ -309,6 +309,19 @@ int mc_ep_return(mc_ctx* ctx, const uint16_t* ed, size_t ed_rows, int hidden,
  * first. NULL or 0 leaves a range out. */
 int mc_set_l2_prefetch(mc_ctx* ctx, const void* p0, size_t n0, const void* p1, size_t n1);
 
+/* Host <-> device staging (replaces Tensor::write_bytes, tensor.rs:127-146,
+ * and the host reads of Tensor::contents / to_f32 / to_u32, tensor.rs:165-200,
+ * which on the reference's unified memory touch the shared buffer directly).
+ * Copies bytes from src to dst in ctx's stream order. When both are
+ * addressable by the context's device -- its own memory, or page-locked host
+ * memory mapped into the device address space -- and 16-byte aligned with a
+ * size that is a multiple of 16, one small copy kernel does it (chained to
+ * the kernels around it like the decode kernels, far shorter than a DMA copy
+ * for the few-KB rows of a decode step); otherwise cudaMemcpyAsync. The
+ * ranges must not overlap. Asynchronous: host memory read or written here
+ * must stay untouched until the stream reaches the copy. */
+int mc_copy_async(mc_ctx* ctx, void* dst, const void* src, size_t bytes);
+
 /* -------------------------------------------------------------- test aid */
 
 /* Profiling aid: when buf (device, n u64 words) is set, the persistent

@@ -94,6 +94,7 @@ SIGNATURES: dict[str, tuple] = {
     "mc_eval_math": (I, [P, I, P, P, I]),
     "mc_set_trace": (I, [P, P, I]),
     "mc_set_l2_prefetch": (I, [P, P, C.c_size_t, P, C.c_size_t]),
+    "mc_copy_async": (I, [P, P, P, C.c_size_t]),
 }
 
 _lib: C.CDLL | None = None

@@ -116,6 +116,56 @@ extern "C" int mc_set_l2_prefetch(mc_ctx* ctx, const void* p0, size_t n0, const 
   return MC_OK;
 }
 
+namespace {
+
+// dst[i] = src[i] for n 16-byte words; either side may be pinned host memory
+// mapped into the device's address space. Chained with programmatic
+// dependent launch like the decode kernels: the copy waits for the kernel
+// before it, and the next kernel's pre-wait part overlaps it. Loads are
+// cache-volatile, so host writes made between graph replays are seen.
+__global__ void __launch_bounds__(256) copy16_kernel(uint4* __restrict__ dst,
+                                                     const uint4* __restrict__ src, size_t n) {
+  mc_pdl_launch_dependents();
+  mc_pdl_wait();
+  for (size_t i = (size_t)blockIdx.x * 256 + threadIdx.x; i < n; i += (size_t)gridDim.x * 256)
+    dst[i] = __ldcv(src + i);
+}
+
+// Memory this context's device can read and write at p: its own device
+// memory, or page-locked host memory mapped at the same address (UVA).
+bool device_addressable(const mc_ctx* ctx, const void* p) {
+  cudaPointerAttributes a;
+  if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+    (void)cudaGetLastError();
+    return false;
+  }
+  if (a.type == cudaMemoryTypeDevice) return a.device == ctx->device;
+  if (a.type == cudaMemoryTypeHost) return a.devicePointer == p;
+  return false;
+}
+
+}  // namespace
+
+extern "C" int mc_copy_async(mc_ctx* ctx, void* dst, const void* src, size_t bytes) {
+  MC_REQUIRE(ctx, "copy_async: null context");
+  if (bytes == 0) return MC_OK;
+  MC_REQUIRE(dst && src, "copy_async: null pointer");
+  const char* d = static_cast<const char*>(dst);
+  const char* s = static_cast<const char*>(src);
+  MC_REQUIRE(d + bytes <= s || s + bytes <= d, "copy_async: overlapping ranges");
+  if (bytes % 16 == 0 && mc_aligned(dst, 16) && mc_aligned(src, 16) &&
+      device_addressable(ctx, dst) && device_addressable(ctx, src)) {
+    const size_t n = bytes / 16;
+    size_t blocks = (n + 255) / 256;
+    if (blocks > (size_t)ctx->num_sms * 4) blocks = (size_t)ctx->num_sms * 4;
+    MC_CUDA(mc_launch_pdl(copy16_kernel, dim3((unsigned)blocks), dim3(256), 0, ctx->stream,
+                          static_cast<uint4*>(dst), static_cast<const uint4*>(src), n));
+    return mc_after_launch("copy16_kernel");
+  }
+  MC_CUDA(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDefault, ctx->stream));
+  return MC_OK;
+}
+
 extern "C" int mc_sync(mc_ctx* ctx) {
   if (!ctx) return mc_fail(MC_EINVAL, "mc_sync: null context");
   MC_CUDA(cudaStreamSynchronize(ctx->stream));

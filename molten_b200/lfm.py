@@ -96,6 +96,19 @@ def _u32(*ts):
             ensure(t.dtype == torch.int32, "expects U32 (int32 storage)")
 
 
+def copy_async(ctx: Context, dst: torch.Tensor, src: torch.Tensor) -> None:
+    """Stream-ordered copy between device tensors and page-locked host tensors
+    (Tensor::write_bytes / contents, tensor.rs:127-146, 165-200; on the GPU's
+    own memory model the host rows are staged by the device). Same byte
+    count, both contiguous; host tensors must be pinned."""
+    for t in (dst, src):
+        ensure(t.is_contiguous(), "copy_async: tensors must be contiguous")
+        ensure(t.is_cuda or t.is_pinned(), "copy_async: host tensors must be pinned")
+    nbytes = dst.numel() * dst.element_size()
+    ensure(nbytes == src.numel() * src.element_size(), "copy_async: byte counts differ")
+    _lib.call("mc_copy_async", ctx.handle, dst.data_ptr(), src.data_ptr(), nbytes)
+
+
 # ----------------------------------------------------------------- decode ops
 
 def gemv_quant(ctx: Context, w: QuantWeights, x: torch.Tensor, y: torch.Tensor) -> None:

@@ -312,3 +312,24 @@ def test_fused_moe_decode_layer(cuda_ctx, moe_layer, mode, seed):
         assert_bits_equal(host_bits(lfm.decode_workspace_act(ws)), act_o.reshape(4, 1536), "act")
         out_o = oracle.gemv_gather_down_combine4(moe_layer["down"], act_o, io, wo)
         assert_bits_equal(host_bits(out), out_o, "out")
+
+
+def test_copy_async_host_device(cuda_ctx):
+    """mc_copy_async: pinned host -> device and back through the copy kernel
+    (16-byte multiples), an odd byte count through the cudaMemcpyAsync path,
+    and unpinned host memory refused by the wrapper."""
+    src = torch.randn(3, 2048).to(torch.bfloat16).pin_memory()
+    dev = torch.empty((3, 2048), dtype=torch.bfloat16, device="cuda")
+    back = torch.empty((3, 2048), dtype=torch.bfloat16, pin_memory=True)
+    lfm.copy_async(cuda_ctx, dev, src)
+    lfm.copy_async(cuda_ctx, back, dev)
+    cuda_ctx.commit_wait()
+    assert torch.equal(back.view(torch.int16), src.view(torch.int16))
+    assert torch.equal(dev.cpu().view(torch.int16), src.view(torch.int16))
+    odd = torch.arange(7, dtype=torch.int16).pin_memory()
+    d7 = torch.zeros(7, dtype=torch.int16, device="cuda")
+    lfm.copy_async(cuda_ctx, d7, odd)
+    cuda_ctx.commit_wait()
+    assert torch.equal(d7.cpu(), odd)
+    with pytest.raises(ValueError):
+        lfm.copy_async(cuda_ctx, d7, torch.zeros(7, dtype=torch.int16))
