@@ -188,9 +188,11 @@ extern "C" int mc_gemv_gather_down_combine4(mc_ctx* ctx, const mc_qweights* down
   MC_REQUIRE(act && ids && weights && out && mc_aligned(act, 16),
              "gemv_gather_down_combine4: bad act/ids/weights/out");
   MC_REQUIRE(batch >= 1 && batch <= 65535, "gemv_gather_down_combine4: batch %d", batch);
-  if (batch >= 4 && H % 32 == 0) {
-    const dim3 grid(H / 32, batch);
-    MC_CUDA(mc_launch_pdl(down_combine_kernel<4>, grid, dim3(kWarps * 32), 0, ctx->stream,
+  // two tiles per warp from batch 4 (four: 166 registers, one CTA fewer per
+  // SM, measured slower)
+  if (batch >= 4 && H % 16 == 0) {
+    const dim3 grid(H / 16, batch);
+    MC_CUDA(mc_launch_pdl(down_combine_kernel<2>, grid, dim3(kWarps * 32), 0, ctx->stream,
                           down->codes, down->scales, down->biases, act, ids, weights, out, H, I,
                           n_experts));
   } else {

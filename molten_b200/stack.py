@@ -21,7 +21,7 @@ residual stream. The expert part runs one of three ways (``moe_path``):
              MoE FFN (moe_prefill: route, sort, gather, tensor-core grouped
              GEMMs, combine), so each routed expert's rows are read and
              dequantised once per step for all of its tokens -- the default
-             above B = 16 (measured on B200: 2276 vs 1987 tokens/s for "gemv"
+             above B = 16 (measured on B200: 2439 vs 1987 tokens/s for "gemv"
              vs "grouped" at B = 16, 2473 vs 3123 at B = 32); activations match the oracle within the prefill
              tolerance, the ids given the same logits bit for bit;
   "gemv"     any B: router_addnorm_route, gemv_gather_act and
