@@ -226,9 +226,10 @@ def moe_layer():
     return L
 
 
-@pytest.mark.parametrize("batch,seed", [(1, 0), (1, 1), (1, 2), (1, 3), (4, 7)])
+@pytest.mark.parametrize("batch,seed", [(1, 0), (1, 1), (1, 2), (1, 3), (4, 7), (8, 9)])
 def test_moe_decode_layer_cfg1(cuda_ctx, moe_layer, batch, seed):
-    """BASELINE cfg1: fused add+norm+router+top-4, gate/up/SiLU, down+combine."""
+    """BASELINE cfg1: fused add+norm+router+top-4, gate/up/SiLU, down+combine
+    (batch 4 and 8 take the two- and four-tile expert GEMV variants)."""
     g = synth.rng(1000 + seed)
     h = synth.activations_np(g, batch, 2048)
     badd = synth.activations_np(g, batch, 2048)
