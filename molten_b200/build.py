@@ -8,6 +8,7 @@ contract (bit-identical ids and tokens).
 """
 from __future__ import annotations
 
+import fcntl
 import os
 import subprocess
 import sys
@@ -39,17 +40,24 @@ def needs_build() -> bool:
 
 
 def build(force: bool = False, verbose: bool = False) -> Path:
+    """Compiles the library if a source is newer. Concurrent callers (the
+    spawned ranks of multi-process tests) are serialised by an exclusive lock
+    next to the library; each re-checks staleness under it."""
     if not force and not needs_build():
         return LIB
-    tmp = LIB.with_suffix(".so.tmp")
-    cmd = [NVCC, *NVCC_FLAGS, "-shared", "-o", str(tmp), *map(str, sources()),
-           "-ldl"]
-    if verbose:
-        print(" ".join(cmd), file=sys.stderr)
-    r = subprocess.run(cmd, capture_output=True, text=True)
-    if r.returncode != 0:
-        raise RuntimeError(f"nvcc failed ({r.returncode}):\n{r.stdout}\n{r.stderr}")
-    os.replace(tmp, LIB)
+    with open(HERE / ".build.lock", "w") as lock:
+        fcntl.flock(lock, fcntl.LOCK_EX)
+        if not force and not needs_build():
+            return LIB
+        tmp = LIB.with_suffix(f".so.{os.getpid()}.tmp")
+        cmd = [NVCC, *NVCC_FLAGS, "-shared", "-o", str(tmp), *map(str, sources()),
+               "-ldl"]
+        if verbose:
+            print(" ".join(cmd), file=sys.stderr)
+        r = subprocess.run(cmd, capture_output=True, text=True)
+        if r.returncode != 0:
+            raise RuntimeError(f"nvcc failed ({r.returncode}):\n{r.stdout}\n{r.stderr}")
+        os.replace(tmp, LIB)
     return LIB
 
 

@@ -10,6 +10,7 @@ here also runs on the GPU box's host CPU.
 """
 from __future__ import annotations
 
+import fcntl
 import os
 import subprocess
 import sys
@@ -28,20 +29,26 @@ def _stale(lib: Path, src: Path) -> bool:
                                                           Path(__file__).stat().st_mtime)
 
 
+def _compile(cmd_head: list[str], lib: Path, src: Path, tail: list[str]) -> None:
+    tmp = f"{lib}.{os.getpid()}.tmp"
+    subprocess.run([*cmd_head, "-o", tmp, str(src), *tail], check=True)
+    os.replace(tmp, lib)
+
+
 def build(force: bool = False) -> tuple[Path, Path | None]:
+    """Compiles what is stale. Several processes (the spawned ranks of the
+    multi-process tests) may call this at once: an exclusive lock on
+    _build/.lock serialises them, and each re-checks staleness under it."""
     OUT.mkdir(exist_ok=True)
-    src = HERE / "mc_oracle.c"
-    if force or _stale(EXACT, src):
-        cmd = ["gcc", "-O2", "-ffp-contract=off", "-fno-fast-math", *COMMON, "-o",
-               str(EXACT) + ".tmp", str(src), "-lm"]
-        subprocess.run(cmd, check=True)
-        os.replace(str(EXACT) + ".tmp", EXACT)
-    fast_src = HERE / "mc_oracle_fast.c"
-    if fast_src.exists() and (force or _stale(FAST, fast_src)):
-        cmd = ["gcc", "-O3", "-fopenmp", "-ffast-math", *COMMON, "-o", str(FAST) + ".tmp",
-               str(fast_src), "-lm"]
-        subprocess.run(cmd, check=True)
-        os.replace(str(FAST) + ".tmp", FAST)
+    with open(OUT / ".lock", "w") as lock:
+        fcntl.flock(lock, fcntl.LOCK_EX)
+        src = HERE / "mc_oracle.c"
+        if force or _stale(EXACT, src):
+            _compile(["gcc", "-O2", "-ffp-contract=off", "-fno-fast-math", *COMMON], EXACT, src,
+                     ["-lm"])
+        fast_src = HERE / "mc_oracle_fast.c"
+        if fast_src.exists() and (force or _stale(FAST, fast_src)):
+            _compile(["gcc", "-O3", "-fopenmp", "-ffast-math", *COMMON], FAST, fast_src, ["-lm"])
     return EXACT, FAST if FAST.exists() else None
 
 

@@ -12,8 +12,8 @@
  * reference project) and fixes every fp32 reduction order so that the CUDA
  * kernels can be checked bit for bit. Where the reference's order is that of
  * Apple's simd_sum (unspecified), the canonical order below is this
- * project's choice, shared with the CUDA kernels and documented in
- * DESIGN.md. It is pinned by hand-computable known answers in
+ * project's choice, shared with the CUDA kernels and stated at the top of
+ * molten_b200/csrc/gemv_common.cuh. It is pinned by hand-computable known answers in
  * tests/test_oracle.py and by the committed fixtures in tests/golden/.
  *
  * Build: oracle/build.py (gcc -O2 -ffp-contract=off; fmaf only where named).
