@@ -5,12 +5,15 @@
  * src/kernels/{lfm,quant,elementwise}.rs expose to src/lfm.rs. Every entry
  * point below names the reference function it replaces (paths inside the
  * reference project). A Rust `src/cuda.rs` binds these with `extern "C"`
- * (see INTEGRATION.md); tests and bench.py bind them with ctypes.
+ * declarations mirroring the prototypes below; tests and bench.py bind them
+ * with ctypes.
  *
  * Conventions
- *  - All pointers are DEVICE pointers owned by the caller; no entry point
+ *  - All pointers are DEVICE pointers owned by the caller (mc_copy_async
+ *    also takes page-locked host pointers); no compute entry point
  *    allocates device memory (scratch is passed in, as the reference's
- *    `Scratch` is preallocated by the caller, lfm.rs:557-626).
+ *    `Scratch` is preallocated by the caller, lfm.rs:557-626) -- only
+ *    mc_ep_alloc, the expert-parallel exchange-buffer allocator, does.
  *  - bf16 values travel as uint16_t bit patterns.
  *  - Work is enqueued on the context's stream and is asynchronous, like
  *    `ComputePass::dispatch_at` (metal.rs:326-355); mc_sync is `commit_wait`.
