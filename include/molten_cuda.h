@@ -13,8 +13,8 @@
  *    also takes page-locked host pointers); no compute entry point
  *    allocates device memory (scratch is passed in, as the reference's
  *    `Scratch` is preallocated by the caller, lfm.rs:557-626) -- except
- *    mc_ep_alloc (expert-parallel exchange buffers) and the first call of
- *    mc_moe_decode_layer_noalloc on a device (its own workspace).
+ *    mc_ep_alloc (expert-parallel exchange buffers); the scratch of
+ *    mc_moe_decode_layer_noalloc is a static device array of the library.
  *  - bf16 values travel as uint16_t bit patterns.
  *  - Work is enqueued on the context's stream and is asynchronous, like
  *    `ComputePass::dispatch_at` (metal.rs:326-355); mc_sync is `commit_wait`.
