@@ -223,6 +223,17 @@ int mc_moe_sort_map(mc_ctx* ctx, const uint32_t* ids, int m, int n_experts, int 
 int mc_gather_rows_bf16(mc_ctx* ctx, const uint16_t* table, const uint32_t* ids, int rows,
                         int hidden, uint16_t* out);
 
+/* Dense Q4 GEMM for the prefill's non-expert projections (replaces
+ * dequant_q4_bf16_bulk + gemm_bf16_nt, quant.metal:69-114, gemm.rs:33-60, as
+ * lfm.rs:661-671 calls them): c[m][N] = a[m][K] . bf16(s*q + b)[N][K]^T, the
+ * weights dequantised on the fly into the tensor-core tiles (never written
+ * out). Runs the grouped GEMM with one expert over 256-row chunks; the chunk
+ * list goes to `workspace` (device, mc_gemm_q4_workspace_words(m) u32,
+ * 16-byte aligned). N and K multiples of 128; status as for the grouped GEMM. */
+size_t mc_gemm_q4_workspace_words(int m);
+int mc_gemm_q4(mc_ctx* ctx, const uint16_t* a, int m, const mc_qweights* w, uint16_t* c,
+               uint32_t* workspace, size_t ws_words, uint32_t* status);
+
 /* gemm_q4_grouped_mlx (quant.rs:228-266 -> lfm_qmm_t_body
  * quant_nax.metal:4091-4234): C[i][n] = sum_k A[i][k] * bf16(s*q+b)[e*N+n][k]
  * for the rows i of each tile's expert e; A bf16 [rows][K] (expert-sorted),

@@ -95,6 +95,8 @@ SIGNATURES: dict[str, tuple] = {
     "mc_set_trace": (I, [P, P, I]),
     "mc_set_l2_prefetch": (I, [P, P, C.c_size_t, P, C.c_size_t]),
     "mc_copy_async": (I, [P, P, P, C.c_size_t]),
+    "mc_gemm_q4_workspace_words": (C.c_size_t, [I]),
+    "mc_gemm_q4": (I, [P, P, I, QP, P, P, C.c_size_t, P]),
 }
 
 _lib: C.CDLL | None = None

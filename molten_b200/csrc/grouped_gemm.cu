@@ -626,6 +626,16 @@ int launch(mc_ctx* ctx, const uint16_t* a, int rows, const mc_qweights* w0, cons
   return mc_after_launch("grouped_gemm_kernel");
 }
 
+// Row chunks of a dense GEMM (one expert): tiles[i] = {256 i, min(256 i + 256,
+// m), 0, 0}, *n_tiles = their count.
+__global__ void dense_tiles_kernel(uint4* __restrict__ tiles, uint32_t* __restrict__ n_tiles,
+                                   int m) {
+  const int T = (m + MAXN - 1) / MAXN;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < T; i += gridDim.x * blockDim.x)
+    tiles[i] = make_uint4((uint32_t)(i * MAXN), (uint32_t)min((i + 1) * MAXN, m), 0u, 0u);
+  if (blockIdx.x == 0 && threadIdx.x == 0) *n_tiles = (uint32_t)T;
+}
+
 int check_grouped(const uint16_t* a, int rows, const mc_qweights* w, int n_experts,
                   const uint16_t* out, const uint32_t* tiles, const uint32_t* n_tiles,
                   int max_tiles, const char* what) {
@@ -658,6 +668,27 @@ extern "C" int mc_gemm_q4_grouped(mc_ctx* ctx, const uint16_t* a, int rows, cons
   int rc = check_grouped(a, rows, w, n_experts, c, tiles, n_tiles, max_tiles, "gemm_q4_grouped");
   if (rc) return rc;
   return launch<false>(ctx, a, rows, w, nullptr, n_experts, c, tiles, n_tiles, max_tiles, status);
+}
+
+extern "C" size_t mc_gemm_q4_workspace_words(int m) {
+  return m < 1 ? 0 : (size_t)4 * ((m + MAXN - 1) / MAXN) + 4;
+}
+
+extern "C" int mc_gemm_q4(mc_ctx* ctx, const uint16_t* a, int m, const mc_qweights* w,
+                          uint16_t* c, uint32_t* workspace, size_t ws_words, uint32_t* status) {
+  MC_REQUIRE(ctx, "gemm_q4: null context");
+  MC_REQUIRE(m >= 1, "gemm_q4: m %d", m);
+  MC_REQUIRE(workspace && ws_words >= mc_gemm_q4_workspace_words(m),
+             "gemm_q4: workspace of %zu words, %zu needed", ws_words, mc_gemm_q4_workspace_words(m));
+  const int T = (m + MAXN - 1) / MAXN;
+  uint32_t* tiles = workspace;
+  uint32_t* n_tiles = workspace + 4 * (size_t)T;
+  int rc = check_grouped(a, m, w, 1, c, tiles, n_tiles, T, "gemm_q4");
+  if (rc) return rc;
+  dense_tiles_kernel<<<(T + 255) / 256, 256, 0, ctx->stream>>>(reinterpret_cast<uint4*>(tiles),
+                                                              n_tiles, m);
+  if ((rc = mc_after_launch("dense_tiles_kernel"))) return rc;
+  return launch<false>(ctx, a, m, w, nullptr, 1, c, tiles, n_tiles, T, status);
 }
 
 extern "C" int mc_gemm_q4_grouped_gu(mc_ctx* ctx, const uint16_t* a, int rows,

@@ -355,6 +355,25 @@ def gemm_q4_grouped(ctx: Context, a: torch.Tensor, w: QuantWeights, c: torch.Ten
               _p(c), _p(tiles), _p(n_tiles), tiles.numel() // 4, _p(status))
 
 
+def gemm_q4_workspace_words(m: int) -> int:
+    return int(_lib.lib().mc_gemm_q4_workspace_words(m))
+
+
+def gemm_q4(ctx: Context, a: torch.Tensor, w: QuantWeights, c: torch.Tensor,
+            workspace: torch.Tensor, status: torch.Tensor | None = None) -> None:
+    """dequant_q4_bf16_bulk + gemm_bf16_nt (quant.metal:69-114, gemm.rs:33-60;
+    the prefill projections of lfm.rs:661-671): c = a . bf16(W)^T on the
+    tensor cores, W dequantised on the fly. workspace: int32
+    [gemm_q4_workspace_words(m)]."""
+    check_quant(w)
+    m, k = a.shape
+    ensure(k == w.in_features and tuple(c.shape) == (m, w.out_features), "gemm_q4 shapes")
+    _bf16(a, c)
+    _u32(workspace, status)
+    _lib.call("mc_gemm_q4", ctx.handle, _p(a), m, _lib.C.byref(w.qw()), _p(c), _p(workspace),
+              workspace.numel(), _p(status))
+
+
 def gemm_q4_grouped_gu(ctx: Context, a: torch.Tensor, gate: QuantWeights, up: QuantWeights,
                        act: torch.Tensor, tiles: torch.Tensor, n_tiles: torch.Tensor,
                        n_experts: int = 64, status: torch.Tensor | None = None) -> None:

@@ -193,3 +193,22 @@ def test_grouped_gemm_flags_malformed_tile(cuda_ctx):
     want = oracle.gemm_q4_grouped(a, w, np.array([0, rows], np.uint32),
                                   np.array([0, 0], np.uint32), E)
     assert_close_bf16(host_bits(c), want, "good tile beside a malformed one", min_equal=0.8)
+
+
+@pytest.mark.parametrize("m,n,k", [(700, 256, 2048), (256, 384, 1536), (40, 128, 256)])
+def test_dense_gemm_q4_matches_oracle(cuda_ctx, m, n, k):
+    """mc_gemm_q4 (prefill projections, dequant_q4_bf16_bulk + gemm_bf16_nt):
+    the grouped kernel with one expert over 256-row chunks, the last one partial
+    (700, 40 rows), against the oracle's one-expert grouped GEMM."""
+    g = synth.rng(90 + m)
+    a = synth.activations_np(g, m, k)
+    codes, s, b = synth.quant_weights_np(g, n, k, 4)
+    ws = torch.zeros(lfm.gemm_q4_workspace_words(m), dtype=torch.int32, device="cuda")
+    c = empty_bf16(m, n)
+    st = zeros_u32(1)
+    lfm.gemm_q4(cuda_ctx, dev_bf16(a), dev_qw(codes, s, b), c, ws, st)
+    torch.cuda.synchronize()
+    assert int(host_u32(st)[0]) == 0
+    want = oracle.gemm_q4_grouped(a, (codes, s, b), np.array([m], np.uint32),
+                                  np.array([0], np.uint32), 1)
+    assert_close_bf16(host_bits(c), want, f"dense {m}x{n}x{k}", min_equal=0.8)
