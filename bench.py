@@ -11,7 +11,13 @@ weights stream from HBM. value = algorithmic bytes (the four selected experts'
 Q4 codes + scales/biases, the router, the activation rows) / device time.
 
 Other workloads (--workload): cfg0 (Q4 GEMV 2048x2048), cfg2 (Q6 head +
-argmax 65536x2048).
+argmax 65536x2048), cfg3 (the 4096-token prefill MoE FFN with Zipf routing;
+expert-parallel under torchrun) and cfg4 (the 40-layer stacked decode loop at
+--batch 1/8/32).
+
+e2e: the same work through the public API with the step's inputs copied in
+from pinned host memory and its result read back inside the timed region
+(cfg1 stages its rows with mc_copy_async, 32 steps per CUDA-graph replay).
 
 Multi-GPU: the decode path does not shard (one token's layer is a dependent
 chain), so N GPUs run N independent replicas ("replicas only"); value is the
