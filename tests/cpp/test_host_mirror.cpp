@@ -83,6 +83,72 @@ int main() {
   expect_error("copy reaches the ABI", MC_EINVAL, "null context",
                [&] { molten::kernels::copy_async(ctx, p, p, 16); });
 
+  // the rest of the op surface: one failing check each
+  namespace K = molten::kernels;
+  QuantWeights gate = w, up = w;  // [64 * 32][2048]: expert width 32
+  gate.codes.shape = {2048, 256};
+  expect_error("token tail", MC_EINVAL, "token tail shapes", [&] {
+    K::token_tail(ctx, Tensor(p, {2}, DType::U64), Tensor(p, {3}, DType::U32), nullptr, nullptr,
+                  nullptr, nullptr);
+  });
+  expect_error("token tail embed", MC_EINVAL, "needs norm_w", [&] {
+    const Tensor emb(p, {100, 2048}, DType::BF16);
+    K::token_tail(ctx, Tensor(p, {2}, DType::U64), Tensor(p, {2}, DType::U32), &emb, nullptr,
+                  nullptr, nullptr);
+  });
+  expect_error("argmax out", MC_EINVAL, "argmax out shape", [&] {
+    K::argmax_bf16(ctx, Tensor(p, {3, 65536}, DType::BF16), Tensor(p, {2}, DType::U32));
+  });
+  expect_error("gather act ids", MC_EINVAL, "gather act ids shape", [&] {
+    K::gemv_gather_act(ctx, gate, up, x, Tensor(p, {2, 3}, DType::U32),
+                       Tensor(p, {2, 4, 32}, DType::BF16));
+  });
+  expect_error("gather act out", MC_EINVAL, "gather act output shape", [&] {
+    K::gemv_gather_act(ctx, gate, up, x, ids, Tensor(p, {2, 4, 31}, DType::BF16));
+  });
+  expect_error("down out", MC_EINVAL, "down output shape", [&] {
+    QuantWeights d{Tensor(p, {64 * 2048, 16}, DType::U32), Tensor(p, {64 * 2048, 2}, DType::BF16),
+                   Tensor(p, {64 * 2048, 2}, DType::BF16), 64, 4};
+    K::gemv_gather_down_combine4(ctx, d, Tensor(p, {2, 4, 128}, DType::BF16), ids, wts,
+                                 Tensor(p, {2, 2047}, DType::BF16));
+  });
+  expect_error("decode workspace", MC_EINVAL, "decode workspace too small", [&] {
+    const Tensor nw(p, {2048}, DType::BF16);
+    K::moe_decode_layer(ctx, Tensor(p, {1, 2048}, DType::BF16), nullptr, nw,
+                        Tensor(p, {1, 2048}, DType::BF16), Tensor(p, {1, 2048}, DType::BF16),
+                        router, Tensor(p, {1, 64}, DType::F32), nullptr,
+                        Tensor(p, {1, 4}, DType::U32), Tensor(p, {1, 4}, DType::BF16), gate, up, w,
+                        Tensor(p, {1, 2048}, DType::BF16), Tensor(p, {4}, DType::U32), 64);
+  });
+  expect_error("grouped out", MC_EINVAL, "grouped GEMM output shape", [&] {
+    K::gemm_q4_grouped_mlx(ctx, a, w, Tensor(p, {300, 31}, DType::BF16),
+                           Tensor(p, {16, 4}, DType::U32), Tensor(p, {1}, DType::U32), 64);
+  });
+  expect_error("grouped gu out", MC_EINVAL, "grouped gate/up output shape", [&] {
+    K::gemm_q4_grouped_mlx_gu(ctx, a, gate, up, Tensor(p, {300, 33}, DType::BF16),
+                              Tensor(p, {16, 4}, DType::U32), Tensor(p, {1}, DType::U32), 64);
+  });
+  expect_error("gather rows", MC_EINVAL, "gather shapes", [&] {
+    K::gather_rows_bf16(ctx, Tensor(p, {100, 2048}, DType::BF16), Tensor(p, {5}, DType::U32),
+                        Tensor(p, {5, 2047}, DType::BF16));
+  });
+  expect_error("silu_mul dtype", MC_EINVAL, "silu_mul BF16 only", [&] {
+    K::silu_mul_bf16(ctx, Tensor(p, {8}, DType::F32), Tensor(p, {8}, DType::BF16),
+                     Tensor(p, {8}, DType::BF16));
+  });
+  expect_error("combine slots", MC_EINVAL, "combine slot shapes", [&] {
+    K::moe_combine_rows(ctx, Tensor(p, {16, 2048}, DType::BF16), Tensor(p, {3, 4}, DType::U32),
+                        Tensor(p, {4, 4}, DType::BF16), Tensor(p, {4, 2048}, DType::BF16));
+  });
+  expect_error("prefill logits", MC_EINVAL, "prefill logits shape", [&] {
+    K::moe_prefill(ctx, Tensor(p, {16, 2048}, DType::BF16), Tensor(p, {16, 63}, DType::F32), gate,
+                   up, w, Tensor(p, {1024}, DType::U32), Tensor(p, {16, 2048}, DType::BF16), 64);
+  });
+  expect_error("prefill reaches the ABI", MC_EINVAL, "null context", [&] {
+    K::moe_prefill(ctx, Tensor(p, {16, 2048}, DType::BF16), Tensor(p, {16, 64}, DType::F32), gate,
+                   up, w, Tensor(p, {1024}, DType::U32), Tensor(p, {16, 2048}, DType::BF16), 64);
+  });
+
   // a real context: an error without a GPU, a working handle with one
   try {
     molten::Context real(0);
