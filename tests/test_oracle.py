@@ -253,3 +253,20 @@ def test_golden_fixtures_reproduce():
         got = case(inputs_only=False, data=data)
         for key, val in got.items():
             assert np.array_equal(val, data[key]), (name, key)
+
+
+def test_dense_gemm_one_expert_matches_float64():
+    """The oracle behind mc_gemm_q4 (dequant_q4_bf16_bulk + gemm_bf16_nt,
+    quant.metal:69-114, gemm.rs:33-60): its one-expert grouped GEMM equals a
+    float64 product of a and the bf16-dequantised weights, the fp32 sums within
+    accumulation rounding and the bf16 outputs their rounding."""
+    g = G(12)
+    m, n, k = 37, 256, 1024
+    a = synth.activations_np(g, m, k)
+    codes, s, b = synth.quant_weights_np(g, n, k, 4)
+    c, acc = oracle.gemm_q4_grouped(a, (codes, s, b), np.array([m], np.uint32),
+                                    np.array([0], np.uint32), 1, with_acc=True)
+    w = f32(oracle.dequant_q4(codes, s, b)).astype(np.float64)
+    ref = f32(a).astype(np.float64) @ w.T
+    np.testing.assert_allclose(acc, ref, rtol=1e-4, atol=1e-3)
+    assert np.array_equal(c, synth.f32_to_bf16_bits(acc))
