@@ -150,8 +150,7 @@ extern "C" int mc_copy_async(mc_ctx* ctx, void* dst, const void* src, size_t byt
   MC_REQUIRE(ctx, "copy_async: null context");
   if (bytes == 0) return MC_OK;
   MC_REQUIRE(dst && src, "copy_async: null pointer");
-  const char* d = static_cast<const char*>(dst);
-  const char* s = static_cast<const char*>(src);
+  const uintptr_t d = reinterpret_cast<uintptr_t>(dst), s = reinterpret_cast<uintptr_t>(src);
   MC_REQUIRE(d + bytes <= s || s + bytes <= d, "copy_async: overlapping ranges");
   if (bytes % 16 == 0 && mc_aligned(dst, 16) && mc_aligned(src, 16) &&
       device_addressable(ctx, dst) && device_addressable(ctx, src)) {
