@@ -87,7 +87,9 @@ int mc_check_quant(const mc_qweights* w);
 
 /* gemv_quant (kernels/lfm.rs:112-149 -> lfm_gemv_q4_bf16_k2048
  * lfm.metal:161-183, lfm_gemv_q6_bf16_x4 :245-297): y[b] = W . x[b] for
- * `batch` independent bf16 rows x[batch][in] -> y[batch][out]. bits 4 or 6. */
+ * `batch` independent bf16 rows x[batch][in] -> y[batch][out]. bits 4 or 6,
+ * in <= 4096; 4-bit rows also up to in = 16384 (lfm_gemv_q4_bf16_k11776,
+ * the dense FFN's down projection). */
 int mc_gemv_quant(mc_ctx* ctx, const mc_qweights* w, const uint16_t* x, uint16_t* y,
                   int batch);
 
@@ -183,13 +185,18 @@ int mc_moe_decode_layer(mc_ctx* ctx, const uint16_t* h, const uint16_t* b,
  * every buffer from the caller. Limits and duties:
  *  - expert width I = gate->out_features / n_experts at most 2048, else
  *    MC_EINVAL before any launch;
- *  - the first call on each device is the set-up: it looks up the array's
- *    address with that device current and zeroes it on ctx's stream, waiting
- *    for that, so it blocks and must come before any stream capture;
+ *  - every argument is checked before anything is enqueued; then the
+ *    array's address is looked up with ctx's device current, and the first
+ *    call on each device also zeroes it on ctx's stream, waiting for that, so
+ *    the first call blocks and must come before any stream capture; each
+ *    call is then one kernel launch;
  *  - the scratch is shared by every context and stream of the process on a
  *    device, so calls whose kernels could overlap race: order them;
  *  - `status` (device u32, may be NULL) receives this call's status word,
- *    the codes mc_moe_decode_layer leaves in workspace[2]. */
+ *    the codes mc_moe_decode_layer leaves in workspace[2]; the kernel clears
+ *    the word in the array, so each call reports its own launch only;
+ *  - a device reset (cudaDeviceReset) reloads the library's device code:
+ *    the array then starts zeroed again, as on first use. */
 int mc_moe_decode_layer_noalloc(mc_ctx* ctx, const uint16_t* h, const uint16_t* b,
                                 const uint16_t* norm_w, uint16_t* h_out, uint16_t* normed,
                                 const void* router_w, int router_dtype,
@@ -197,6 +204,35 @@ int mc_moe_decode_layer_noalloc(mc_ctx* ctx, const uint16_t* h, const uint16_t* 
                                 uint32_t* ids, uint16_t* weights, const mc_qweights* gate,
                                 const mc_qweights* up, const mc_qweights* down, int n_experts,
                                 uint16_t* out, uint32_t* status, float eps, float route_eps);
+
+/* ------------------------------------------------ decode neighbours */
+
+/* proj3_gemv_scatter (kernels/lfm.rs:150-205 -> lfm_proj3_gemv_scatter_bf16
+ * lfm.metal:1020-1068): the Q, K and V Q4 GEMVs of one bf16 row x[2048] in
+ * one launch: q_out[nq], k_out[nk], and V row i stored straight into the KV
+ * cache at position pos: v_cache[((i / 64) * max_seq + pos) * 64 + i % 64]
+ * (v_cache bf16 [nv / 64][max_seq][64]; no other cache entry is written). */
+int mc_proj3_gemv_scatter(mc_ctx* ctx, const mc_qweights* q, const mc_qweights* k,
+                          const mc_qweights* v, const uint16_t* x, uint16_t* q_out,
+                          uint16_t* k_out, uint16_t* v_cache, int max_seq, int pos);
+
+/* conv3_gemv (kernels/lfm.rs:207-246 -> lfm_conv3_gemv_split_bf16
+ * lfm.metal:1070-1110): the short conv's input projection w_proj [3C][2048]
+ * (rows c, C + c, 2C + c are channel c's b, c and x) on one bf16 row x, then
+ * the two-tap conv with taps bf16 [C][3] and state bf16 [2][C]:
+ * v2 = bf16(b * x), z = bf16((t0 * state[0][c] + t1 * state[1][c]) + t2 * v2),
+ * out[c] = bf16(c * z), new_state[0][c] = state[1][c], new_state[1][c] = v2
+ * (new_state must not alias state). */
+int mc_conv3_gemv(mc_ctx* ctx, const mc_qweights* w_proj, const uint16_t* x,
+                  const uint16_t* taps, const uint16_t* state, uint16_t* out,
+                  uint16_t* new_state, int channels);
+
+/* gemv_gu_act (kernels/lfm.rs:462-495 -> lfm_gemv_q4_gu_act_bf16
+ * lfm.metal:1447-1498): the dense FFN front half, act[b][n] =
+ * bf16(bf16(silu(bf16(gate_n . x[b]))) * bf16(up_n . x[b])) for bf16 rows
+ * x[batch][in] (in <= 4096), act[batch][out]. */
+int mc_gemv_gu_act(mc_ctx* ctx, const mc_qweights* gate, const mc_qweights* up,
+                   const uint16_t* x, uint16_t* act, int batch);
 
 /* ----------------------------------------------------------- prefill path */
 
@@ -346,6 +382,22 @@ int mc_copy_async(mc_ctx* ctx, void* dst, const void* src, size_t bytes);
  * 5 act published, 10 act loaded, 11 down rows landed, 12 down computed,
  * 6 combine, 7 exit). NULL switches it off (the default). */
 int mc_set_trace(mc_ctx* ctx, unsigned long long* buf, int n);
+
+/* Limit of every bounded device wait (cross-CTA flags, copy barriers, peer
+ * flags) of the kernels launched on ctx from now on, in nanoseconds; 0
+ * restores each kernel's default (200 ms for the decode kernels, 1 s for the
+ * grouped GEMMs and the expert-parallel barriers). A wait that runs out sets
+ * the kernel's status bit and the kernel returns; nothing hangs. No
+ * reference counterpart (Metal kernels there never wait on one another). */
+int mc_set_wait_limit(mc_ctx* ctx, unsigned long long ns);
+
+/* Test aid: flags that make later launches on ctx skip one step so that a
+ * bounded wait runs out on purpose (the failure-detection tests use it with a
+ * short mc_set_wait_limit). MC_TEST_SKIP_LOGIT_PUBLISH: the router warps of
+ * mc_moe_decode_layer(_noalloc) publish no logits, so every CTA's logit wait
+ * gives up and status bit 1 is set. 0 (the default) for normal work. */
+#define MC_TEST_SKIP_LOGIT_PUBLISH 1
+int mc_set_test_flags(mc_ctx* ctx, int flags);
 
 /* Evaluates the library's device math on x[n] into y[n]: op 0 = mc_exp,
  * 1 = SiLU, 2 = sigmoid, 3 = bf16 rounding. Lets tests check the device

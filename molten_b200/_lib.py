@@ -18,6 +18,8 @@ MC_EUNSUPPORTED = -3
 MC_ENCCL = -4
 MC_ETIMEOUT = -5
 
+TEST_SKIP_LOGIT_PUBLISH = 1
+
 ROUTE_SOFTMAX_RENORM = 0
 ROUTE_SIGMOID_BIAS = 1
 DTYPE_BF16 = 0
@@ -82,6 +84,9 @@ SIGNATURES: dict[str, tuple] = {
     "mc_ep_return": (I, [P, P, C.c_size_t, I, P, I, I, I, P, C.c_size_t, P]),
     "mc_moe_decode_layer_noalloc": (I, [P, P, P, P, P, P, P, I, P, I, P, P, P, QP, QP, QP, I, P,
                                         P, F, F]),
+    "mc_proj3_gemv_scatter": (I, [P, QP, QP, QP, P, P, P, P, I, I]),
+    "mc_conv3_gemv": (I, [P, QP, P, P, P, P, P, I]),
+    "mc_gemv_gu_act": (I, [P, QP, QP, P, P, I]),
     "mc_moe_route_batch": (I, [P, P, I, I, I, P, F, P, P]),
     "mc_moe_sort_map": (I, [P, P, I, I, I, P, P, P, P, P, P, I]),
     "mc_gather_rows_bf16": (I, [P, P, P, I, I, P]),
@@ -94,6 +99,8 @@ SIGNATURES: dict[str, tuple] = {
     "mc_eval_math": (I, [P, I, P, P, I]),
     "mc_set_trace": (I, [P, P, I]),
     "mc_set_l2_prefetch": (I, [P, P, C.c_size_t, P, C.c_size_t]),
+    "mc_set_wait_limit": (I, [P, C.c_ulonglong]),
+    "mc_set_test_flags": (I, [P, I]),
     "mc_copy_async": (I, [P, P, P, C.c_size_t]),
     "mc_gemm_q4_workspace_words": (C.c_size_t, [I]),
     "mc_gemm_q4": (I, [P, P, I, QP, P, P, C.c_size_t, P]),

@@ -184,11 +184,14 @@ def load_quant(ckpt: Checkpoint, base: str, expected_rows: int, expected_k: int,
 
 
 def load_moe_layer(ckpt: Checkpoint, layer: int, n_experts: int = 64, hidden: int = 2048,
-                   inter: int = 1536, device="cuda") -> dict:
+                   inter: int = 1536, device="cuda", allow_missing_bias: bool = False) -> dict:
     """One MoE layer's tensors under the reference's names (lfm.rs:326-366):
     ffn_norm, the router (`feed_forward.gate.weight`, [E][H], F32 or BF16),
-    `expert_bias` when present, and the stacked Q4 experts
-    `feed_forward.switch_mlp.{gate,up,down}_proj`."""
+    `expert_bias` and the stacked Q4 experts
+    `feed_forward.switch_mlp.{gate,up,down}_proj`. The reference requires
+    `expert_bias` (lfm.rs:359; its sigmoid routing selects on it), so a layer
+    without it is an error unless `allow_missing_bias` (then "expert_bias" is
+    None, for the BASELINE softmax routing, which has no bias)."""
     p = f"model.layers.{layer}"
     moe = f"{p}.feed_forward"
     norm = load_tensor(ckpt, f"{p}.ffn_norm.weight", device)
@@ -197,7 +200,11 @@ def load_moe_layer(ckpt: Checkpoint, layer: int, n_experts: int = 64, hidden: in
     _ensure(router.numel() == n_experts * hidden, f"{moe}: router shape")
     bias = None
     if ckpt.meta(f"{moe}.expert_bias") is not None:
-        bias = load_tensor(ckpt, f"{moe}.expert_bias", device).reshape(n_experts)
+        bias = load_tensor(ckpt, f"{moe}.expert_bias", device)
+        _ensure(bias.numel() == n_experts, f"{moe}: expert_bias shape")
+        bias = bias.reshape(n_experts)
+    else:
+        _ensure(allow_missing_bias, f"missing {moe}.expert_bias")
     return {
         "norm_w": norm.reshape(hidden),
         "router": router.reshape(n_experts, hidden),

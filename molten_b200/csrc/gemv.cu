@@ -261,11 +261,15 @@ int dispatch_gemv(mc_ctx* ctx, const mc_qweights* w, const uint16_t* x, uint16_t
 extern "C" int mc_gemv_quant(mc_ctx* ctx, const mc_qweights* w, const uint16_t* x, uint16_t* y,
                              int batch) {
   MC_REQUIRE(ctx, "gemv_quant: null context");
-  int rc = mc_check_gemv_weights(w, "gemv_quant");
+  int rc = mc_check_gemv_weights_k(w, "gemv_quant", 16384);
   if (rc) return rc;
   MC_REQUIRE(x && y, "gemv_quant: null x or y");
   MC_REQUIRE(batch >= 1 && batch <= 65535, "gemv_quant: batch %d out of range", batch);
   MC_REQUIRE(mc_aligned(x, 16), "gemv_quant: x must be 16-byte aligned");
+  if (w->in_features > 4096) {  // the dense FFN's down projection (K = 11776)
+    MC_REQUIRE(w->bits == 4, "gemv_quant: %d-bit rows wider than 4096 are not built", w->bits);
+    return mc_gemv_q4_wide(ctx, w, x, y, batch);
+  }
   rc = mc_gemv_ring(ctx, w, x, y, nullptr, batch, 0);
   if (rc != 1) return rc;
   rc = mc_gemv_batched(ctx, w, x, y, nullptr, batch, 0);

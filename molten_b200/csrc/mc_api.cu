@@ -23,14 +23,18 @@ int mc_after_launch(const char* what) {
 // in_features a multiple of 64, codes 16-byte aligned (rows are read as
 // 16-byte vectors), rows in range.
 int mc_check_gemv_weights(const mc_qweights* w, const char* what) {
+  return mc_check_gemv_weights_k(w, what, 4096);
+}
+
+int mc_check_gemv_weights_k(const mc_qweights* w, const char* what, int max_k) {
   if (!w) return mc_fail(MC_EINVAL, "%s: null weights", what);
   if (w->bits != 4 && w->bits != 6)
     return mc_fail(MC_EUNSUPPORTED, "%s: unsupported bit width %d", what, w->bits);
   if (w->group_size != 64)
     return mc_fail(MC_EUNSUPPORTED, "%s: group size %d (only 64 is built)", what, w->group_size);
-  if (w->in_features <= 0 || w->in_features % 64 != 0 || w->in_features > 4096)
-    return mc_fail(MC_EINVAL, "%s: in_features %d must be a positive multiple of 64 <= 4096",
-                   what, w->in_features);
+  if (w->in_features <= 0 || w->in_features % 64 != 0 || w->in_features > max_k)
+    return mc_fail(MC_EINVAL, "%s: in_features %d must be a positive multiple of 64 <= %d",
+                   what, w->in_features, max_k);
   if (w->out_features <= 0)
     return mc_fail(MC_EINVAL, "%s: out_features %d", what, w->out_features);
   if (!w->codes || !w->scales || !w->biases)
@@ -106,6 +110,20 @@ extern "C" int mc_set_trace(mc_ctx* ctx, unsigned long long* buf, int n) {
   return MC_OK;
 }
 
+extern "C" int mc_set_wait_limit(mc_ctx* ctx, unsigned long long ns) {
+  if (!ctx) return mc_fail(MC_EINVAL, "mc_set_wait_limit: null context");
+  ctx->wait_limit_ns = ns;
+  return MC_OK;
+}
+
+extern "C" int mc_set_test_flags(mc_ctx* ctx, int flags) {
+  if (!ctx) return mc_fail(MC_EINVAL, "mc_set_test_flags: null context");
+  if (flags & ~MC_TEST_SKIP_LOGIT_PUBLISH)
+    return mc_fail(MC_EINVAL, "mc_set_test_flags: unknown flags 0x%x", flags);
+  ctx->test_flags = flags;
+  return MC_OK;
+}
+
 extern "C" int mc_set_l2_prefetch(mc_ctx* ctx, const void* p0, size_t n0, const void* p1,
                                   size_t n1) {
   if (!ctx) return mc_fail(MC_EINVAL, "mc_set_l2_prefetch: null context");
@@ -151,6 +169,7 @@ extern "C" int mc_copy_async(mc_ctx* ctx, void* dst, const void* src, size_t byt
   if (bytes == 0) return MC_OK;
   MC_REQUIRE(dst && src, "copy_async: null pointer");
   const uintptr_t d = reinterpret_cast<uintptr_t>(dst), s = reinterpret_cast<uintptr_t>(src);
+  MC_REQUIRE(bytes <= UINTPTR_MAX - (d > s ? d : s), "copy_async: range wraps the address space");
   MC_REQUIRE(d + bytes <= s || s + bytes <= d, "copy_async: overlapping ranges");
   if (bytes % 16 == 0 && mc_aligned(dst, 16) && mc_aligned(src, 16) &&
       device_addressable(ctx, dst) && device_addressable(ctx, src)) {

@@ -15,15 +15,32 @@ struct mc_ctx {
   int num_sms;
   int max_smem_optin;
   int l2_bytes;
-  void* nccl_comm;   // ncclComm_t when expert parallelism is initialised
-  int ep_rank;
-  int ep_size;
-  int ep_timeout_ms;
   unsigned long long* trace;  // optional per-CTA phase timestamps (mc_set_trace)
   int trace_len;
   const void* pf_ptr[2];      // L2 prefetch for the next decode-layer launch
   size_t pf_bytes[2];         // (mc_set_l2_prefetch; cleared by that launch)
+  unsigned long long wait_limit_ns;  // bounded-wait limit (mc_set_wait_limit; 0 = default)
+  int test_flags;             // MC_TEST_* (mc_set_test_flags; 0 in production)
+  struct mc_ep_state* ep;     // expert-parallel state (mc_ep_init), or NULL
 };
+
+// Wait limit a kernel with default `dflt` uses on this context.
+static inline unsigned long long mc_wait_limit(const mc_ctx* ctx, unsigned long long dflt) {
+  return ctx->wait_limit_ns ? ctx->wait_limit_ns : dflt;
+}
+
+// The fused decode layer behind mc_moe_decode_layer and
+// mc_moe_decode_layer_noalloc (moe_decode_fused.cu).
+int mc_decode_layer_impl(mc_ctx* ctx, const uint16_t* h, const uint16_t* b,
+                         const uint16_t* norm_w, uint16_t* h_out, uint16_t* normed,
+                         const void* router_w, int router_dtype, const float* expert_bias,
+                         int route_mode, float* logits, uint32_t* ids, uint16_t* weights,
+                         const mc_qweights* gate, const mc_qweights* up, const mc_qweights* down,
+                         int n_experts, uint16_t* out, uint32_t* sync, size_t ws_words, float eps,
+                         float route_eps, bool noalloc, uint32_t* status_out);
+// The built-in decode scratch of ctx's device and its size in u32 words; the
+// first call per device zeroes it (moe_decode_noalloc.cu).
+int mc_noalloc_decode_scratch(mc_ctx* ctx, uint32_t** ptr, size_t* words);
 
 __device__ __forceinline__ unsigned long long mc_globaltimer() {
   unsigned long long t;
@@ -51,8 +68,13 @@ int mc_fail(int code, const char* fmt, ...);
     }                                                                            \
   } while (0)
 
-// check_quant for the GEMV kernels (mc_api.cu).
+// check_quant for the GEMV kernels (mc_api.cu): inputs up to 4096, or up to
+// max_k for the kernels that take wider rows.
 int mc_check_gemv_weights(const mc_qweights* w, const char* what);
+int mc_check_gemv_weights_k(const mc_qweights* w, const char* what, int max_k);
+// Q4 GEMV for 4096 < K <= 16384 (gemv_fused.cu).
+int mc_gemv_q4_wide(mc_ctx* ctx, const mc_qweights* w, const uint16_t* x, uint16_t* y,
+                    int batch);
 
 // Checks the launch that was just issued.
 int mc_after_launch(const char* what);

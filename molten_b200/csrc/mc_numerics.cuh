@@ -146,3 +146,115 @@ MC_HD bool mc_better(float v, uint32_t i, float bv, uint32_t bi) {
 #define MC_E6_1 6
 #define MC_E6_2 12
 #define MC_E6_3 10
+
+// ---------------------------------------------------------------- sampling
+// Pieces of the sampled draw (sample.cu), restated in the CPU oracle.
+
+// log(x) for float x > 0.
+// Method: x = 2^e * m with m in [sqrt(1/2), sqrt(2)); log(m) = 2 atanh(s) with
+// s = (m - 1) / (m + 1), |s| <= 0.1716, summed as the odd series
+// 2s (1 + s^2/3 + s^4/5 + ... + s^10/11) (truncation below 2e-11); then
+// e * ln2 added with ln2 split into a high part with trailing zero bits and a
+// low part, as fdlibm's logf splits it (ln2_hi = 0x3f317180, ln2_lo =
+// 0x3717f7d1). Subnormal inputs are scaled by 2^23 first. 0 gives -inf,
+// negative or NaN inputs NaN, +inf itself.
+MC_HD float mc_log(float x) {
+  uint32_t u = mc_f32_bits(x);
+  if (!(x == x) || x < 0.0f) return mc_bits_f32(0x7fc00000u);
+  if (x == 0.0f) return mc_bits_f32(0xff800000u);
+  if (u >= 0x7f800000u) return x;
+  int e = 0;
+  if (u < 0x00800000u) {
+    x = MC_MUL(x, 8388608.0f);  // 2^23, exact
+    u = mc_f32_bits(x);
+    e = -23;
+  }
+  e += (int)(u >> 23) - 127;
+  uint32_t mu = (u & 0x007fffffu) | 0x3f800000u;  // m in [1, 2)
+  if (mu > 0x3fb504f3u) {                           // m > sqrt(2): use m / 2
+    mu -= 0x00800000u;
+    e += 1;
+  }
+  const float m = mc_bits_f32(mu);
+  const float s = MC_DIV(MC_ADD(m, -1.0f), MC_ADD(m, 1.0f));
+  const float z = MC_MUL(s, s);
+  float p = 9.09090936183929443359e-02f;             // 1/11
+  p = MC_FMA(p, z, 1.11111111938953399658e-01f);     // 1/9
+  p = MC_FMA(p, z, 1.42857149243354797363e-01f);     // 1/7
+  p = MC_FMA(p, z, 2.00000002980232238770e-01f);     // 1/5
+  p = MC_FMA(p, z, 3.33333343267440795898e-01f);     // 1/3
+  const float two_s = MC_ADD(s, s);
+  const float lm = MC_FMA(MC_MUL(two_s, z), p, two_s);
+  const float ef = (float)e;
+  const float LN2_HI = 6.9313812256e-01f;  // 0x3f317180
+  const float LN2_LO = 9.0580006145e-06f;  // 0x3717f7d1
+  return MC_FMA(ef, LN2_HI, MC_FMA(ef, LN2_LO, lm));
+}
+
+// Philox4x32-10 (Salmon, Moraes, Dror, Shaw, "Parallel random numbers: as
+// easy as 1, 2, 3", SC 2011): ten rounds of two 32x32->64 multiplies with the
+// round key bumped by the Weyl constants.
+MC_HD void mc_philox4x32_10(uint32_t c[4], uint32_t k0, uint32_t k1) {
+  for (int r = 0; r < 10; ++r) {
+    const unsigned long long p0 = (unsigned long long)0xD2511F53u * c[0];
+    const unsigned long long p1 = (unsigned long long)0xCD9E8D57u * c[2];
+    const uint32_t hi0 = (uint32_t)(p0 >> 32), lo0 = (uint32_t)p0;
+    const uint32_t hi1 = (uint32_t)(p1 >> 32), lo1 = (uint32_t)p1;
+    const uint32_t n0 = hi1 ^ c[1] ^ k0, n2 = hi0 ^ c[3] ^ k1;
+    c[0] = n0;
+    c[1] = lo1;
+    c[2] = n2;
+    c[3] = lo0;
+    k0 += 0x9E3779B9u;
+    k1 += 0xBB67AE85u;
+  }
+}
+
+// Philox counter word 2 of the draw ("SAMP").
+#define MC_SAMPLE_DOMAIN 0x53414D50u
+
+// The 32-bit uniform word of token `id` for the draw at position `pos`:
+// word id % 4 of Philox4x32-10 with counter (id / 4, pos, "SAMP", 0) and key
+// (seed mod 2^32, seed / 2^32).
+MC_HD uint32_t mc_sample_word(uint32_t id, uint32_t pos, uint32_t seed_lo, uint32_t seed_hi) {
+  uint32_t c[4] = {id >> 2, pos, MC_SAMPLE_DOMAIN, 0u};
+  mc_philox4x32_10(c, seed_lo, seed_hi);
+  return c[id & 3u];
+}
+
+// Gumbel(0, 1) from a 32-bit uniform word: V = (x + 0.5) / 2^32, E = -log(1 - V)
+// (an Exp(1) variate; for V < 1/64 from the series V + V^2/2 + V^3/3 + V^4/4,
+// which keeps full relative precision for the small E whose G wins), G = -log(E).
+MC_HD float mc_gumbel(uint32_t x) {
+  const float v = MC_MUL(MC_ADD((float)x, 0.5f), 2.3283064365386963e-10f);
+  float e;
+  if (v < 0.015625f) {
+    e = MC_MUL(v, MC_ADD(1.0f, MC_MUL(v, MC_ADD(0.5f, MC_MUL(v, MC_ADD(0.33333334f,
+                                                                      MC_MUL(v, 0.25f)))))));
+  } else {
+    float t = MC_ADD(1.0f, -v);
+    if (t < 2.9802322387695312e-08f) t = 2.9802322387695312e-08f;  // 2^-25
+    e = -mc_log(t);
+  }
+  return -mc_log(e);
+}
+
+// Orderable 32-bit key of a float (larger key, larger value; -0 folds to +0),
+// the high word of mc_argmax_key, and back.
+MC_HD uint32_t mc_fkey(float v) {
+  uint32_t u = mc_f32_bits(v);
+  if ((u << 1) == 0u) u = 0u;
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+MC_HD float mc_kfloat(uint32_t k) {
+  return mc_bits_f32((k & 0x80000000u) ? (k & 0x7fffffffu) : ~k);
+}
+
+// Processed logit of the draw: w = pen(v) * inv_temp with pen(v) = v *
+// inv_penalty (v > 0) or v * penalty (v <= 0) for seen tokens; -0 folds to +0.
+MC_HD float mc_sample_w(float v, bool seen, float inv_temp, float penalty, float inv_penalty) {
+  if (seen) v = v > 0.0f ? MC_MUL(v, inv_penalty) : MC_MUL(v, penalty);
+  uint32_t u = mc_f32_bits(MC_MUL(v, inv_temp));
+  if ((u << 1) == 0u) u = 0u;
+  return mc_bits_f32(u);
+}

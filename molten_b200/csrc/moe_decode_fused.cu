@@ -54,7 +54,7 @@ constexpr int kWarps = kThreads / 32;
 constexpr int kMaxChunks = 8;   // gate/up chunks: 16 row pairs, then 32 each (up to 240)
 constexpr int kDnRows = 4;      // down rows per warp (16 warps, 4 per expert)
 constexpr int H = 2048;
-constexpr unsigned long long kTimeoutNs = 200000000ull;  // 200 ms per wait
+constexpr unsigned long long kTimeoutNs = 200000000ull;  // default limit per wait: 200 ms
 constexpr int kLogitWord = 8;   // first tagged-logit word in the workspace
 constexpr int kActWord = 136;   // first act word in the workspace
 constexpr uint32_t kPrologueBytes = 8192 + 4096;  // normed row as f32 and as bf16
@@ -108,6 +108,13 @@ struct Params {
   unsigned long long* trace;
   const uint8_t* pf[2];  // L2 prefetch ranges for the next layer (128-byte lines)
   uint32_t pf_lines[2];
+  unsigned long long timeout_ns;  // limit of every bounded wait (mc_set_wait_limit)
+  // report_status: the last CTA moves ws[2] to *status_out (when non-null)
+  // and clears it, so the word reports one launch (the allocation-free entry
+  // point); otherwise ws[2] stays sticky in the caller's workspace
+  uint32_t* status_out;
+  int report_status;
+  int skip_publish;  // test aid (mc_set_test_flags): router warps publish nothing
 };
 
 constexpr int kTraceSlots = 32;  // per-CTA phase timestamps (mc_set_trace)
@@ -271,7 +278,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(const Par
     }
     const float z = rr.dot(nrow, lane);
     TRACE(13);
-    if (lane == 0) {
+    if (lane == 0 && !P.skip_publish) {
       P.logits[cta] = z;
       mc_st_publish_u64(logits64 + cta,
                         ((unsigned long long)tag32 << 32) | (unsigned long long)__float_as_uint(z));
@@ -287,7 +294,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(const Par
   if (warp == 0) {
     // lane 0 waits (backing off) until all E router warps have published;
     // then lane l reads logits 2l, 2l+1 in one 16-byte load (tags checked)
-    const unsigned long long deadline = mc_globaltimer() + kTimeoutNs;
+    const unsigned long long deadline = mc_globaltimer() + P.timeout_ns;
     bool got = true;
     if (lane == 0) {
       while (mc_ld_acquire(sync + 4) < (uint32_t)P.E) {
@@ -413,7 +420,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(const Par
   // bf16-rounded sums, SwiGLU runs once all pairs are done
   bool copies_ok = true;
   if (ok) {
-    const unsigned long long deadline = mc_globaltimer() + kTimeoutNs;
+    const unsigned long long deadline = mc_globaltimer() + P.timeout_ns;
     const uint32_t sbs = (uint32_t)L.np_max * 64u;
     const uint16_t* sb16 = reinterpret_cast<const uint16_t*>(sm + L.sb);
     // gate and up sums of pair q (all lanes get the butterflied values)
@@ -508,7 +515,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(const Par
   // to shared memory, 16-byte chunks swizzled so the per-lane group reads
   // below are bank-conflict free
   if (ok) {
-    const unsigned long long deadline = mc_globaltimer() + kTimeoutNs;
+    const unsigned long long deadline = mc_globaltimer() + P.timeout_ns;
     const int nchunk16 = (4 * I) / 8;  // chunks of 8 act values
     bool got = true;
     for (int c = t; got && c < nchunk16; c += kThreads) {
@@ -562,7 +569,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(const Par
       dxg = prescale_group_x<4>(xv, dxs);
     }
     TRACE(28);
-    const bool landed = wait_copies(&bar_dn, mc_globaltimer() + kTimeoutNs);
+    const bool landed = wait_copies(&bar_dn, mc_globaltimer() + P.timeout_ns);
     if (!landed && lane == 0) record_error(sync, 16u);
     TRACE(9);
     if (landed && nr > 0) {
@@ -598,7 +605,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(const Par
   // ---- every issued copy has landed before the CTA exits (immediate unless
   // a wait above gave up)
   if (t == 0 && issued) {
-    const unsigned long long deadline = mc_globaltimer() + kTimeoutNs;
+    const unsigned long long deadline = mc_globaltimer() + P.timeout_ns;
     bool all = wait_copies(&bar_sb, deadline) && wait_copies(&bar_dn, deadline);
     for (int c = 0; issued && c < nchunk; ++c) all = wait_copies(bar_gu + c, deadline) && all;
     if (!all) record_error(sync, 16u);
@@ -607,8 +614,14 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(const Par
   // ---- the last CTA to finish resets the counters and advances the epoch
   TRACE(7);
   if (t == 0) {
+    if (P.report_status) __threadfence();  // this CTA's status bits before its count
     const uint32_t done = atomicAdd(sync + 1, 1u);
     if (done == (uint32_t)G - 1) {
+      if (P.report_status) {
+        __threadfence();
+        const uint32_t st = atomicExch(sync + 2, 0u);
+        if (P.status_out) *P.status_out = st;
+      }
       sync[1] = 0u;
       sync[4] = 0u;
       __threadfence();
@@ -623,14 +636,17 @@ extern "C" size_t mc_moe_decode_workspace_words(int moe_inter) {
   return (size_t)kActWord + 4 * (size_t)(moe_inter > 0 ? moe_inter : 0);
 }
 
-extern "C" int mc_moe_decode_layer(mc_ctx* ctx, const uint16_t* h, const uint16_t* b,
-                                   const uint16_t* norm_w, uint16_t* h_out, uint16_t* normed,
-                                   const void* router_w, int router_dtype,
-                                   const float* expert_bias, int route_mode, float* logits,
-                                   uint32_t* ids, uint16_t* weights, const mc_qweights* gate,
-                                   const mc_qweights* up, const mc_qweights* down, int n_experts,
-                                   uint16_t* out, uint32_t* sync, size_t ws_words, float eps,
-                                   float route_eps) {
+// The fused decode layer behind both entry points. With `noalloc` the
+// workspace arguments are ignored: every argument is checked first, then the
+// library's built-in scratch is fetched (its first use on a device sets it
+// up), and the launch reports its status word to `status_out` and clears it.
+int mc_decode_layer_impl(mc_ctx* ctx, const uint16_t* h, const uint16_t* b,
+                         const uint16_t* norm_w, uint16_t* h_out, uint16_t* normed,
+                         const void* router_w, int router_dtype, const float* expert_bias,
+                         int route_mode, float* logits, uint32_t* ids, uint16_t* weights,
+                         const mc_qweights* gate, const mc_qweights* up, const mc_qweights* down,
+                         int n_experts, uint16_t* out, uint32_t* sync, size_t ws_words, float eps,
+                         float route_eps, bool noalloc, uint32_t* status_out) {
   MC_REQUIRE(ctx, "moe_decode_layer: null context");
   int rc;
   if ((rc = mc_check_gemv_weights(gate, "moe_decode_layer gate"))) return rc;
@@ -647,18 +663,21 @@ extern "C" int mc_moe_decode_layer(mc_ctx* ctx, const uint16_t* h, const uint16_
   MC_REQUIRE(I % 64 == 0 && I <= 2048 && 4 * I <= 4 * 2048 && down->in_features == I &&
                  down->out_features == n_experts * H,
              "moe_decode_layer: expert shapes (I=%d)", I);
-  MC_REQUIRE(ws_words >= mc_moe_decode_workspace_words(I),
+  MC_REQUIRE(noalloc || ws_words >= mc_moe_decode_workspace_words(I),
              "moe_decode_layer: workspace of %zu words < %zu", ws_words,
              mc_moe_decode_workspace_words(I));
-  MC_REQUIRE(h && norm_w && h_out && normed && router_w && logits && ids && weights && out && sync,
+  MC_REQUIRE(h && norm_w && h_out && normed && router_w && logits && ids && weights && out &&
+                 (noalloc || sync),
              "moe_decode_layer: null pointer");
+  MC_REQUIRE(!status_out || mc_aligned(status_out, 4), "moe_decode_layer: status misaligned");
   MC_REQUIRE(router_dtype == MC_DTYPE_BF16 || router_dtype == MC_DTYPE_F32,
              "moe_decode_layer: router dtype %d", router_dtype);
   MC_REQUIRE(route_mode == MC_ROUTE_SOFTMAX_RENORM || route_mode == MC_ROUTE_SIGMOID_BIAS,
              "moe_decode_layer: route mode %d", route_mode);
   const void* a16[] = {h,           norm_w,       h_out,        normed,     router_w,
                        gate->codes, gate->scales, gate->biases, up->codes,  up->scales,
-                       up->biases,  down->codes,  down->scales, down->biases, sync};
+                       up->biases,  down->codes,  down->scales, down->biases,
+                       noalloc ? (const void*)h : (const void*)sync};
   for (const void* p : a16)
     MC_REQUIRE(mc_aligned(p, 16), "moe_decode_layer: buffers must be 16-byte aligned");
   MC_REQUIRE(!b || mc_aligned(b, 16), "moe_decode_layer: b must be 16-byte aligned");
@@ -675,11 +694,22 @@ extern "C" int mc_moe_decode_layer(mc_ctx* ctx, const uint16_t* h, const uint16_
   MC_REQUIRE((int)L.total + 4096 <= ctx->max_smem_optin,
              "moe_decode_layer: %u B of shared memory per CTA exceeds the device's %d", L.total,
              ctx->max_smem_optin);
+  // every check has passed: only now may the built-in scratch be set up
+  if (noalloc) {
+    size_t words = 0;
+    const int rc2 = mc_noalloc_decode_scratch(ctx, &sync, &words);
+    if (rc2) return rc2;
+    MC_REQUIRE(words >= mc_moe_decode_workspace_words(I), "moe_decode_layer: scratch too small");
+  }
   Params P{h, b, norm_w, h_out, normed, router_w, expert_bias, logits, ids, weights, *gate, *up,
            *down, out, sync, eps, route_eps, route_mode, n_experts, I,
            ctx->trace && ctx->trace_len >= kTraceSlots * G ? ctx->trace : nullptr,
            {nullptr, nullptr},
-           {0u, 0u}};
+           {0u, 0u},
+           ctx->wait_limit_ns ? ctx->wait_limit_ns : kTimeoutNs,
+           status_out,
+           noalloc ? 1 : 0,
+           (ctx->test_flags & MC_TEST_SKIP_LOGIT_PUBLISH) ? 1 : 0};
   for (int r = 0; r < 2; ++r) {
     if (!ctx->pf_ptr[r]) continue;
     // whole 128-byte lines covering the range
@@ -721,4 +751,17 @@ extern "C" int mc_moe_decode_layer(mc_ctx* ctx, const uint16_t* h, const uint16_
   void* args[] = {(void*)&P, (void*)&L};
   MC_CUDA(cudaLaunchKernelExC(&cfg, fn, args));
   return mc_after_launch("moe_decode_fused_kernel");
+}
+
+extern "C" int mc_moe_decode_layer(mc_ctx* ctx, const uint16_t* h, const uint16_t* b,
+                                   const uint16_t* norm_w, uint16_t* h_out, uint16_t* normed,
+                                   const void* router_w, int router_dtype,
+                                   const float* expert_bias, int route_mode, float* logits,
+                                   uint32_t* ids, uint16_t* weights, const mc_qweights* gate,
+                                   const mc_qweights* up, const mc_qweights* down, int n_experts,
+                                   uint16_t* out, uint32_t* sync, size_t ws_words, float eps,
+                                   float route_eps) {
+  return mc_decode_layer_impl(ctx, h, b, norm_w, h_out, normed, router_w, router_dtype,
+                              expert_bias, route_mode, logits, ids, weights, gate, up, down,
+                              n_experts, out, sync, ws_words, eps, route_eps, false, nullptr);
 }

@@ -9,19 +9,24 @@
 //
 // The scratch is the same layout mc_moe_decode_layer documents for its
 // caller-owned workspace: word 0 epoch, word 1 exit counter, word 2 status
-// (cleared before each launch here, copied to the caller's `status` after
-// it), word 3 act counter, word 4 router counter, words 8..135 tagged router
-// logits, then the
-// bf16 act rows. It serves expert widths up to kNoallocMaxInter; wider layers
-// are rejected with MC_EINVAL before anything is launched.
+// (moved to the caller's `status` and cleared by the launch's last CTA, so it
+// reports that call only), word 3 reserved, word 4 router counter, words
+// 8..135 tagged router logits, then the bf16 act rows. It serves expert
+// widths up to kNoallocMaxInter; wider layers are rejected with MC_EINVAL
+// before anything is launched.
 //
-// All of it must be zero before the first launch on a device. The first call
-// on each device does that set-up: it makes the device current, looks up the
-// array's address with cudaGetSymbolAddress, zeroes it on the context's
-// stream and waits for that. So the first call blocks and must come before
-// any stream capture. Afterwards every launch leaves the control words as the
-// next one needs them (the last CTA clears the counters and advances the
-// epoch).
+// Every argument is checked before anything is enqueued. All of the scratch
+// must be zero before the first launch on a device: the first call on each
+// device (after its checks pass) makes the device current, zeroes the array
+// on the context's stream and waits for that. So the first call blocks and
+// must come before any stream capture. Afterwards every launch leaves the
+// control words as the next one needs them (the last CTA clears the counters
+// and the status word and advances the epoch), and each call is one kernel
+// launch, chained to its neighbours like the workspace entry point.
+//
+// The array's device address is looked up with cudaGetSymbolAddress on every
+// call (with the context's device current), never cached: a host-side name of
+// a __device__ array is not a device address.
 //
 // There is ONE scratch per device, shared by every context and stream of the
 // process on that device: two calls whose kernels can overlap on the device
@@ -42,39 +47,50 @@ constexpr int kMaxDevices = 64;
 static __device__ __align__(256) uint32_t g_decode_scratch[kNoallocWords];
 
 std::mutex g_setup_mu;
-uint32_t* g_scratch_ptr[kMaxDevices] = {};
+bool g_zeroed[kMaxDevices] = {};
 
-// Address of this device's scratch; the first call per device zeroes it.
-int scratch_for(mc_ctx* ctx, uint32_t** out) {
-  MC_REQUIRE(ctx->device >= 0 && ctx->device < kMaxDevices,
-             "moe_decode_layer_noalloc: device %d out of range", ctx->device);
-  std::lock_guard<std::mutex> lock(g_setup_mu);
-  if (g_scratch_ptr[ctx->device]) {
-    *out = g_scratch_ptr[ctx->device];
-    return MC_OK;
-  }
+// Runs `fn` with ctx's device current, restoring the caller's device.
+template <typename F>
+cudaError_t on_device(int device, F fn) {
   int prev = -1;
-  MC_CUDA(cudaGetDevice(&prev));
-  if (prev != ctx->device) MC_CUDA(cudaSetDevice(ctx->device));
-  void* p = nullptr;
-  cudaError_t e = cudaGetSymbolAddress(&p, g_decode_scratch);
-  if (e == cudaSuccess) e = cudaMemsetAsync(p, 0, sizeof(uint32_t) * kNoallocWords, ctx->stream);
-  if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
-  if (prev != ctx->device) {
-    cudaError_t e2 = cudaSetDevice(prev);
+  cudaError_t e = cudaGetDevice(&prev);
+  if (e != cudaSuccess) return e;
+  if (prev != device && (e = cudaSetDevice(device)) != cudaSuccess) return e;
+  e = fn();
+  if (prev != device) {
+    const cudaError_t e2 = cudaSetDevice(prev);
     if (e == cudaSuccess) e = e2;
   }
-  if (e != cudaSuccess)
-    return mc_fail(MC_ECUDA,
-                   "moe_decode_layer_noalloc: scratch set-up on device %d failed: %s "
-                   "(the first call on a device must not be inside a stream capture)",
-                   ctx->device, cudaGetErrorString(e));
-  g_scratch_ptr[ctx->device] = static_cast<uint32_t*>(p);
-  *out = g_scratch_ptr[ctx->device];
-  return MC_OK;
+  return e;
 }
 
 }  // namespace
+
+int mc_noalloc_decode_scratch(mc_ctx* ctx, uint32_t** out, size_t* words) {
+  MC_REQUIRE(ctx->device >= 0 && ctx->device < kMaxDevices,
+             "moe_decode_layer_noalloc: device %d out of range", ctx->device);
+  std::lock_guard<std::mutex> lock(g_setup_mu);
+  void* p = nullptr;
+  const bool first = !g_zeroed[ctx->device];
+  cudaError_t e = on_device(ctx->device, [&]() {
+    cudaError_t r = cudaGetSymbolAddress(&p, g_decode_scratch);
+    if (r == cudaSuccess && first)
+      r = cudaMemsetAsync(p, 0, sizeof(uint32_t) * kNoallocWords, ctx->stream);
+    if (r == cudaSuccess && first) r = cudaStreamSynchronize(ctx->stream);
+    return r;
+  });
+  if (e != cudaSuccess) {
+    (void)cudaGetLastError();
+    return mc_fail(MC_ECUDA,
+                   "moe_decode_layer_noalloc: scratch %s on device %d failed: %s "
+                   "(the first call on a device must not be inside a stream capture)",
+                   first ? "set-up" : "lookup", ctx->device, cudaGetErrorString(e));
+  }
+  g_zeroed[ctx->device] = true;
+  *out = static_cast<uint32_t*>(p);
+  *words = kNoallocWords;
+  return MC_OK;
+}
 
 extern "C" int mc_moe_decode_layer_noalloc(
     mc_ctx* ctx, const uint16_t* h, const uint16_t* b, const uint16_t* norm_w, uint16_t* h_out,
@@ -89,17 +105,8 @@ extern "C" int mc_moe_decode_layer_noalloc(
              "moe_decode_layer_noalloc: expert width %ld exceeds the built-in scratch "
              "(max %d; use mc_moe_decode_layer with a workspace)",
              inter, kNoallocMaxInter);
-  uint32_t* scratch = nullptr;
-  int rc = scratch_for(ctx, &scratch);
-  if (rc) return rc;
-  // the status word reports this call only (the workspace variant keeps it sticky)
-  MC_CUDA(cudaMemsetAsync(scratch + 2, 0, sizeof(uint32_t), ctx->stream));
-  rc = mc_moe_decode_layer(ctx, h, b, norm_w, h_out, normed, router_w, router_dtype, expert_bias,
-                           route_mode, logits, ids, weights, gate, up, down, n_experts, out,
-                           scratch, kNoallocWords, eps, route_eps);
-  if (rc) return rc;
-  if (status)
-    MC_CUDA(cudaMemcpyAsync(status, scratch + 2, sizeof(uint32_t), cudaMemcpyDeviceToDevice,
-                            ctx->stream));
-  return MC_OK;
+  // the remaining checks, then the scratch set-up, then the one launch
+  return mc_decode_layer_impl(ctx, h, b, norm_w, h_out, normed, router_w, router_dtype,
+                              expert_bias, route_mode, logits, ids, weights, gate, up, down,
+                              n_experts, out, nullptr, 0, eps, route_eps, true, status);
 }

@@ -381,11 +381,14 @@ def moe_prefill_ep_peer(ops: "CudaOps", px: PeerExchange, x: torch.Tensor,
     return ops.combine(px.home[:4 * m], slotpos, gw, m)
 
 
-def moe_prefill_ep_emulated(ctx, xs, logits, gate, up, down, n_experts: int, placement=None):
+def moe_prefill_ep_emulated(ctx, xs, logits, gate, up, down, n_experts: int, placement=None,
+                            return_state: bool = False):
     """`world = len(xs)` ranks emulated on ONE GPU with the same device code as
     moe_prefill_ep_peer (dispatch, row chunks, grouped GEMMs on each rank's
     expert slice, return, combine), the ranks' kernels run one after another
-    so stream order stands in for the barriers. Returns every rank's output."""
+    so stream order stands in for the barriers. Returns every rank's output
+    and the status word (and, with return_state, each rank's ids, gate
+    weights, sorted order and slot positions)."""
     from molten_b200 import _lib, lfm
     world = len(xs)
     E, per = n_experts, n_experts // world
@@ -410,7 +413,7 @@ def moe_prefill_ep_emulated(ctx, xs, logits, gate, up, down, n_experts: int, pla
     for r in range(world):
         ids, gw = ops[r].route(logits[r])
         counts, slotpos, ids_sorted = ops[r].sort(ids, xs[r].shape[0])
-        st.append((gw, counts, slotpos, ids_sorted))
+        st.append((gw, counts, slotpos, ids_sorted, ids))
     counts_all = torch.stack([s[1] for s in st]).contiguous()
     max_tiles = recv_cap // CHUNK + per + 1
     eds = []
@@ -437,4 +440,7 @@ def moe_prefill_ep_emulated(ctx, xs, logits, gate, up, down, n_experts: int, pla
     torch.cuda.synchronize()
     for o in ops:
         status |= o.status
+    if return_state:
+        inner = [dict(ids=s[4], gw=s[0], ids_sorted=s[3], slotpos=s[2]) for s in st]
+        return outs, int(status.cpu()[0]), inner
     return outs, int(status.cpu()[0])

@@ -37,6 +37,21 @@ def _p(t: torch.Tensor | None) -> int | None:
     return t.data_ptr()
 
 
+STATUS_BITS = {1: "a logits wait gave up", 2: "an expert id out of range",
+               4: "rows beyond a capacity", 8: "an act wait gave up",
+               16: "a copy wait gave up"}
+
+
+def raise_on_status(word: torch.Tensor, what: str) -> None:
+    """Reads a kernel status word (waits for the stream) and raises
+    McError(MC_ETIMEOUT) if any bit is set: a bounded wait that ran out (or a
+    malformed input the kernel skipped) means the outputs are not valid."""
+    v = int(word.reshape(-1)[0].item()) & 0xffffffff
+    if v:
+        why = ", ".join(m for b, m in STATUS_BITS.items() if v & b) or "unknown bits"
+        raise _lib.McError(_lib.MC_ETIMEOUT, f"{what}: status 0x{v:x} ({why})")
+
+
 class Context:
     """MetalContext + ComputePass stand-in: one device and stream (metal.rs:91-400).
 
@@ -71,6 +86,15 @@ class Context:
         for t in ts[:2]:
             args += [t.data_ptr(), t.numel() * t.element_size()] if t is not None else [None, 0]
         _lib.check(_lib.lib().mc_set_l2_prefetch(self.h, *args))
+
+    def set_wait_limit(self, ns: int) -> None:
+        """Limit of every bounded device wait of later launches (0 = each
+        kernel's default); a wait that runs out sets a status bit."""
+        _lib.check(_lib.lib().mc_set_wait_limit(self.h, int(ns)))
+
+    def set_test_flags(self, flags: int) -> None:
+        """Test aid (mc_set_test_flags): 0 for normal work."""
+        _lib.check(_lib.lib().mc_set_test_flags(self.h, int(flags)))
 
     def close(self) -> None:
         if self.h:
@@ -251,6 +275,64 @@ def gemv_gather_down_combine4(ctx: Context, down: QuantWeights, act: torch.Tenso
               _p(ids), _p(weights), _p(out), n_experts, batch)
 
 
+def proj3_gemv_scatter(ctx: Context, q: QuantWeights, k: QuantWeights, v: QuantWeights,
+                       x: torch.Tensor, q_out: torch.Tensor, k_out: torch.Tensor,
+                       v_cache: torch.Tensor, pos: int) -> None:
+    """Decode-only Q, K, V projections in one launch, V written into the KV
+    cache at ``pos`` (kernels/lfm.rs:150-205). v_cache: bf16
+    [nv / 64, max_seq, 64]."""
+    kdim = x.numel()
+    nq, nk, nv = q.out_features, k.out_features, v.out_features
+    ensure(q.in_features == kdim and k.in_features == kdim and v.in_features == kdim,
+           "proj3 input width")
+    ensure(q.bits == 4 and k.bits == 4 and v.bits == 4 and q.group_size == 64
+           and k.group_size == 64 and v.group_size == 64, "proj3 is affine 4-bit/64")
+    ensure(kdim == FIXED_HIDDEN, "proj3 input width is the compile-time hidden size")
+    ensure(q_out.numel() == nq and k_out.numel() == nk and nv % 64 == 0, "proj3 output shape")
+    _bf16(x, q_out, k_out, v_cache)
+    ensure(v_cache.dim() == 3, "proj3 KV cache shape")
+    max_seq = v_cache.shape[1]
+    ensure(v_cache.shape[0] * 64 == nv and v_cache.shape[2] == 64 and 0 <= pos < max_seq,
+           "proj3 KV cache shape")
+    for w in (q, k, v):
+        check_quant(w)
+    _lib.call("mc_proj3_gemv_scatter", ctx.handle, _lib.C.byref(q.qw()), _lib.C.byref(k.qw()),
+              _lib.C.byref(v.qw()), _p(x), _p(q_out), _p(k_out), _p(v_cache), max_seq, pos)
+
+
+def conv3_gemv(ctx: Context, wproj: QuantWeights, x: torch.Tensor, w: torch.Tensor,
+               state: torch.Tensor, out: torch.Tensor, new_state: torch.Tensor) -> None:
+    """Decode-only short-conv B/C/X projection and the conv in one launch
+    (kernels/lfm.rs:207-246). w: taps bf16 [H, 3]; state, new_state bf16 [2, H]."""
+    kdim, h = x.numel(), out.numel()
+    ensure(wproj.out_features == 3 * h and wproj.in_features == kdim, "conv3 projection shape")
+    ensure(wproj.bits == 4 and wproj.group_size == 64, "conv3 projection 4-bit/64")
+    ensure(kdim == FIXED_HIDDEN, "conv3 input width is the compile-time hidden size")
+    ensure(w.numel() == 3 * h, "conv3 tap shape")
+    ensure(tuple(state.shape) == (2, h) and tuple(new_state.shape) == (2, h), "conv3 state shape")
+    _bf16(x, w, state, out, new_state)
+    check_quant(wproj)
+    _lib.call("mc_conv3_gemv", ctx.handle, _lib.C.byref(wproj.qw()), _p(x), _p(w), _p(state),
+              _p(out), _p(new_state), h)
+
+
+def gemv_gu_act(ctx: Context, gate: QuantWeights, up: QuantWeights, x: torch.Tensor,
+                act: torch.Tensor) -> None:
+    """Decode dense FFN front half, act = silu(x gate^T) * (x up^T) with the
+    separate GEMVs' bf16 roundings (kernels/lfm.rs:462-495). x [B, K] (or
+    [K]), act [B, N]."""
+    n, k = gate.out_features, gate.in_features
+    ensure(gate.bits == 4 and up.bits == 4, "dense gate/up must be 4-bit")
+    ensure(up.out_features == n and up.in_features == k and up.group_size == gate.group_size,
+           "dense gate/up shapes")
+    ensure(x.numel() % k == 0 and act.numel() == (x.numel() // k) * n, "dense gate/up rows")
+    _bf16(x, act)
+    for w in (gate, up):
+        check_quant(w)
+    _lib.call("mc_gemv_gu_act", ctx.handle, _lib.C.byref(gate.qw()), _lib.C.byref(up.qw()),
+              _p(x), _p(act), x.numel() // k)
+
+
 def moe_decode_workspace_words(moe_inter: int = FIXED_MOE_INTER) -> int:
     """u32 words of workspace moe_decode_layer needs (zero it once)."""
     return int(_lib.lib().mc_moe_decode_workspace_words(moe_inter))
@@ -259,10 +341,12 @@ def moe_decode_workspace_words(moe_inter: int = FIXED_MOE_INTER) -> int:
 def moe_decode_layer(ctx: Context, h, b, nw, hout, normed, router, logits, bias, ids, weights,
                      gate: QuantWeights, up: QuantWeights, down: QuantWeights, out, workspace,
                      eps: float = 1e-5, route_mode: int = ROUTE_SOFTMAX_RENORM,
-                     route_eps: float = 1e-6, n_experts: int = 64) -> None:
+                     route_eps: float = 1e-6, n_experts: int = 64, check: bool = False) -> None:
     """moe_decode (lfm.rs:967-1011) with the fused router, one persistent launch
     for one token. ``workspace``: int32 [moe_decode_workspace_words(I)], zeroed
-    once, then reused by one chain of calls (it carries an epoch)."""
+    once, then reused by one chain of calls (it carries an epoch; its word 2
+    is the sticky status). ``check``: wait for the launch and raise McError
+    if the status word is nonzero."""
     for w in (gate, up, down):
         check_quant(w)
     e, k = router.shape
@@ -275,17 +359,21 @@ def moe_decode_layer(ctx: Context, h, b, nw, hout, normed, router, logits, bias,
               _p(router), dt, _p(bias), route_mode, _p(logits), _p(ids), _p(weights),
               _lib.C.byref(gate.qw()), _lib.C.byref(up.qw()), _lib.C.byref(down.qw()),
               n_experts, _p(out), _p(workspace), workspace.numel(), eps, route_eps)
+    if check:
+        raise_on_status(workspace[2:3], "moe_decode_layer")
 
 
 def moe_decode_layer_noalloc(ctx: Context, h, b, nw, hout, normed, router, logits, bias, ids,
                              weights, gate: QuantWeights, up: QuantWeights, down: QuantWeights,
                              out, status=None, eps: float = 1e-5,
                              route_mode: int = ROUTE_SOFTMAX_RENORM, route_eps: float = 1e-6,
-                             n_experts: int = 64) -> None:
+                             n_experts: int = 64, check: bool = False) -> None:
     """moe_decode_layer with the library's built-in per-device scratch instead
     of a caller workspace (expert width <= 2048). The first call per device
     sets the scratch up and blocks; calls that could overlap on one device
-    race. ``status``: optional int32 [1] receiving this call's status word."""
+    race. ``status``: optional int32 [1] receiving this call's status word;
+    ``check`` (needs ``status``) waits and raises McError if it is nonzero."""
+    ensure(not check or status is not None, "check needs a status word")
     for w in (gate, up, down):
         check_quant(w)
     e, k = router.shape
@@ -298,6 +386,8 @@ def moe_decode_layer_noalloc(ctx: Context, h, b, nw, hout, normed, router, logit
               _p(normed), _p(router), dt, _p(bias), route_mode, _p(logits), _p(ids), _p(weights),
               _lib.C.byref(gate.qw()), _lib.C.byref(up.qw()), _lib.C.byref(down.qw()),
               n_experts, _p(out), _p(status), eps, route_eps)
+    if check:
+        raise_on_status(status, "moe_decode_layer_noalloc")
 
 
 def decode_workspace_act(workspace: torch.Tensor, moe_inter: int = FIXED_MOE_INTER):
@@ -422,8 +512,10 @@ def moe_prefill_workspace_size(m: int, n_experts: int = 64, hidden: int = FIXED_
 def moe_prefill(ctx: Context, x: torch.Tensor, logits: torch.Tensor, gate: QuantWeights,
                 up: QuantWeights, down: QuantWeights, workspace: torch.Tensor, out: torch.Tensor,
                 n_experts: int = 64, route_mode: int = ROUTE_SOFTMAX_RENORM,
-                bias: torch.Tensor | None = None) -> None:
-    """moe_prefill (lfm.rs:847-965) from the router logits on, all on device."""
+                bias: torch.Tensor | None = None, check: bool = False) -> None:
+    """moe_prefill (lfm.rs:847-965) from the router logits on, all on device.
+    ``check``: wait and raise McError if the grouped GEMMs' status word (in
+    the workspace) is nonzero."""
     for w in (gate, up, down):
         check_quant(w)
     m, h = x.shape
@@ -434,6 +526,10 @@ def moe_prefill(ctx: Context, x: torch.Tensor, logits: torch.Tensor, gate: Quant
     _lib.call("mc_moe_prefill", ctx.handle, _p(x), _p(logits), m, _lib.C.byref(gate.qw()),
               _lib.C.byref(up.qw()), _lib.C.byref(down.qw()), n_experts, route_mode, _p(bias),
               _p(workspace), workspace.numel(), _p(out))
+    if check:
+        I = gate.out_features // n_experts
+        raise_on_status(prefill_workspace_view(workspace, m, n_experts, h, I)["status"],
+                        "moe_prefill")
 
 
 def prefill_workspace_view(workspace: torch.Tensor, m: int, n_experts: int = 64,

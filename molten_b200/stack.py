@@ -106,6 +106,29 @@ class DecodeStack:
         lfm.token_tail(ctx, self.keys, self.tokens,
                        (self.embed, self.tail_norm_w, self.x, self.tail_normed))
 
+    def status_words(self) -> list[torch.Tensor]:
+        """The device status words this stack's kernels report into (the
+        fused layer's sticky workspace word, the grouped GEMMs' word)."""
+        words = []
+        if self.ws is not None:
+            words.append(self.ws[2:3])
+        if self.pws is not None:
+            I = self.layers[0]["gate"].out_features // self.E
+            words.append(lfm.prefill_workspace_view(self.pws, self.B, self.E, self.x.shape[1],
+                                                    I)["status"])
+        return words
+
+    def check(self) -> None:
+        """Waits for the stream and raises McError if any kernel of the steps
+        run so far reported a wait that ran out (the tokens are then invalid)."""
+        for w in self.status_words():
+            lfm.raise_on_status(w, f"decode stack ({self.path})")
+
+    def read_tokens(self) -> torch.Tensor:
+        """The last step's tokens on the host, after check()."""
+        self.check()
+        return self.tokens.cpu()
+
     def launches_per_step(self) -> int:
         per_layer = {"fused": 2, "gemv": 4, "grouped": 2 + lfm.MOE_PREFILL_LAUNCHES}[self.path]
         return len(self.layers) * per_layer + 2

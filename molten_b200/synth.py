@@ -63,13 +63,15 @@ def tensor_u32(t: torch.Tensor) -> np.ndarray:
     return t.detach().cpu().contiguous().numpy().view(np.uint32)
 
 
-def quant_weights_np(g: np.random.Generator, out: int, inp: int, bits: int = 4):
-    """(codes u32 [out, in*bits/32], scales bf16 bits, biases bf16 bits)."""
+def quant_weights_np(g: np.random.Generator, out: int, inp: int, bits: int = 4,
+                     centre: float = 8.0):
+    """(codes u32 [out, in*bits/32], scales bf16 bits, biases bf16 bits);
+    bias = -centre * scale + N(0, 1e-3) (BASELINE: centre 8)."""
     words = inp * bits // 32
     codes = g.integers(0, 2**32, size=(out, words), dtype=np.uint64).astype(np.uint32)
     s = g.uniform(0.002, 0.02, size=(out, inp // 64)).astype(np.float32)
     sb = f32_to_bf16_bits(s)
-    b = -8.0 * bf16_bits_to_f32(sb) + g.normal(0.0, 1e-3, size=s.shape).astype(np.float32)
+    b = -centre * bf16_bits_to_f32(sb) + g.normal(0.0, 1e-3, size=s.shape).astype(np.float32)
     bb = f32_to_bf16_bits(b.astype(np.float32))
     return codes, sb, bb
 

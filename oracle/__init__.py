@@ -262,3 +262,43 @@ def moe_prefill(x, logits, gate, up, down, mode=0, bias=None, n_experts=64):
                          _ptr(r["ids_sorted"]), _ptr(r["slotpos"]), _ptr(r["act"]),
                          _ptr(r["ed"]), _ptr(r["out"]))
     return r
+
+
+def proj3_gemv_scatter(q, k, v, x, v_cache, pos):
+    """(q bf16 [nq], k bf16 [nk], the updated copy of v_cache bf16
+    [nv/64][max_seq][64]) for weights q/k/v = (codes, scales, biases)."""
+    nq, nk, nv = q[0].shape[0], k[0].shape[0], v[0].shape[0]
+    K = q[0].shape[1] * 8
+    x = np.ascontiguousarray(x.reshape(K))
+    qo, ko = np.zeros(nq, np.uint16), np.zeros(nk, np.uint16)
+    vc = np.ascontiguousarray(v_cache).copy()
+    max_seq = vc.shape[1]
+    lib().or_proj3_gemv_scatter(*(_ptr(a) for a in q), *(_ptr(a) for a in k),
+                                *(_ptr(a) for a in v), nq, nk, nv, K, _ptr(x), _ptr(qo),
+                                _ptr(ko), _ptr(vc), max_seq, pos)
+    return qo, ko, vc
+
+
+def conv3_gemv(w_proj, x, taps, state):
+    """(out bf16 [H], new_state bf16 [2][H]) of the short conv for one row."""
+    codes, scales, biases = w_proj
+    H = codes.shape[0] // 3
+    K = codes.shape[1] * 8
+    out = np.zeros(H, np.uint16)
+    ns = np.zeros((2, H), np.uint16)
+    lib().or_conv3_gemv(_ptr(codes), _ptr(scales), _ptr(biases), H, K,
+                        _ptr(np.ascontiguousarray(x.reshape(K))), _ptr(np.ascontiguousarray(taps)),
+                        _ptr(np.ascontiguousarray(state)), _ptr(out), _ptr(ns))
+    return out, ns
+
+
+def gemv_gu_act(gate, up, x):
+    """act bf16 [B][N] of the dense FFN front half."""
+    N = gate[0].shape[0]
+    K = gate[0].shape[1] * 8
+    x = np.ascontiguousarray(x.reshape(-1, K))
+    B = x.shape[0]
+    act = np.zeros((B, N), np.uint16)
+    lib().or_gemv_gu_act(*(_ptr(a) for a in gate), *(_ptr(a) for a in up), N, K, _ptr(x), B,
+                         _ptr(act))
+    return act

@@ -1,7 +1,9 @@
 """Builds the CPU oracle (test infrastructure only).
 
 libmc_oracle.so: the bit-careful restatement (mc_oracle.c), compiled with
--ffp-contract=off so only the fmaf calls it names are fused. Output goes to
+-ffp-contract=off so only the fmaf calls it names are fused (-O3 and OpenMP
+change no result: without -ffast-math nothing is reassociated, and the
+parallel loops split independent outputs). Output goes to
 oracle/_build/ (git-ignored; it travels to the GPU box with the tree, and the
 box rebuilds it if missing -- gcc is in the image).
 
@@ -44,8 +46,8 @@ def build(force: bool = False) -> tuple[Path, Path | None]:
         fcntl.flock(lock, fcntl.LOCK_EX)
         src = HERE / "mc_oracle.c"
         if force or _stale(EXACT, src):
-            _compile(["gcc", "-O2", "-ffp-contract=off", "-fno-fast-math", *COMMON], EXACT, src,
-                     ["-lm"])
+            _compile(["gcc", "-O3", "-fopenmp", "-ffp-contract=off", "-fno-fast-math", *COMMON],
+                     EXACT, src, ["-lm"])
         fast_src = HERE / "mc_oracle_fast.c"
         if fast_src.exists() and (force or _stale(FAST, fast_src)):
             _compile(["gcc", "-O3", "-fopenmp", "-ffast-math", *COMMON], FAST, fast_src, ["-lm"])

@@ -16,7 +16,7 @@
  * molten_b200/csrc/gemv_common.cuh. It is pinned by hand-computable known answers in
  * tests/test_oracle.py and by the committed fixtures in tests/golden/.
  *
- * Build: oracle/build.py (gcc -O2 -ffp-contract=off; fmaf only where named).
+ * Build: oracle/build.py (gcc -O3 -fopenmp -ffp-contract=off; fmaf only where named).
  *
  * Conventions (weights.rs:7-20, quant.rs:1-3, lfm.metal:185-199):
  *   Q4: codes u32[N][K/8], 8 codes per word, low nibble first.
@@ -197,6 +197,7 @@ void or_gemv_quant(const void* codes, const uint16_t* scales, const uint16_t* bi
   for (int bb = 0; bb < B; ++bb) {
     for (int k = 0; k < K; ++k) xf[k] = bf(x[(size_t)bb * K + k]);
     prescale(xf, K, bits, xs, xg);
+#pragma omp parallel for schedule(static)
     for (int n = 0; n < N; ++n) {
       const uint8_t* row = (const uint8_t*)codes + (size_t)n * row_bytes(bits, K);
       float v = row_dot(row, scales + (size_t)n * G, biases + (size_t)n * G, bits, K, xs, xg);
@@ -216,21 +217,24 @@ void or_head_argmax(const void* codes, const uint16_t* scales, const uint16_t* b
   float* xf = (float*)malloc(sizeof(float) * K);
   float* xs = (float*)malloc(sizeof(float) * K);
   float* xg = (float*)malloc(sizeof(float) * (K / 64));
+  float* lg = (float*)malloc(sizeof(float) * N);
   const int G = K / 64;
   for (int bb = 0; bb < B; ++bb) {
     for (int k = 0; k < K; ++k) xf[k] = bf(x[(size_t)bb * K + k]);
     prescale(xf, K, bits, xs, xg);
-    float bv = -INFINITY;
-    uint32_t bi = 0;
+#pragma omp parallel for schedule(static)
     for (int n = 0; n < N; ++n) {
       const uint8_t* row = (const uint8_t*)codes + (size_t)n * row_bytes(bits, K);
-      float v = rb(row_dot(row, scales + (size_t)n * G, biases + (size_t)n * G, bits, K, xs, xg));
-      if (better(v, (uint32_t)n, bv, bi)) { bv = v; bi = (uint32_t)n; }
+      lg[n] = rb(row_dot(row, scales + (size_t)n * G, biases + (size_t)n * G, bits, K, xs, xg));
     }
+    float bv = -INFINITY;
+    uint32_t bi = 0;
+    for (int n = 0; n < N; ++n)
+      if (better(lg[n], (uint32_t)n, bv, bi)) { bv = lg[n]; bi = (uint32_t)n; }
     if (keys) keys[bb] = or_argmax_key(bv, bi);
     if (tokens) tokens[bb] = bi;
   }
-  free(xf); free(xs); free(xg);
+  free(xf); free(xs); free(xg); free(lg);
 }
 
 /* argmax_bf16 (kernels/lfm.rs:794-820; lfm.metal:1126-1192): ties to the
@@ -376,6 +380,7 @@ void or_gemv_gather_act(const void* gc, const uint16_t* gs, const uint16_t* gb,
     prescale(xf, H, 4, xs, xg);
     for (int r = 0; r < 4; ++r) {
       const size_t e = ids[4 * bb + r];
+#pragma omp parallel for schedule(static)
       for (int i = 0; i < I; ++i) {
         const size_t row = e * I + i;
         float g = row_dot((const uint8_t*)gc + row * rb_, gs + row * G, gb + row * G, 4, H, xs, xg);
@@ -404,6 +409,7 @@ void or_gemv_gather_down_combine4(const void* dc, const uint16_t* ds, const uint
       for (int k = 0; k < I; ++k) xf[r * I + k] = bf(act[((size_t)bb * 4 + r) * I + k]);
       prescale(xf + r * I, I, 4, xs + r * I, xg + r * G);
     }
+#pragma omp parallel for schedule(static)
     for (int i = 0; i < H; ++i) {
       float tot = 0.0f;
       for (int r = 0; r < 4; ++r) {
@@ -416,6 +422,67 @@ void or_gemv_gather_down_combine4(const void* dc, const uint16_t* ds, const uint
     }
   }
   free(xf); free(xs); free(xg);
+}
+
+/* --------------------------------------------- decode neighbours */
+
+/* proj3_gemv_scatter (kernels/lfm.rs:150-205 -> lfm_proj3_gemv_scatter_bf16
+ * lfm.metal:1020-1068): the Q, K and V GEMVs of one row x (K = 2048) in the
+ * canonical row order; q[i] = bf16(Q_i . x), k[i] = bf16(K_i . x), and V row
+ * i goes to the cache slot v_cache[((i / 64) * max_seq + pos) * 64 + i % 64]
+ * (v_cache bf16 [nv / 64][max_seq][64]; nothing else of it is written). */
+void or_proj3_gemv_scatter(const void* qc, const uint16_t* qs, const uint16_t* qb,
+                           const void* kc, const uint16_t* ks, const uint16_t* kb,
+                           const void* vc, const uint16_t* vs, const uint16_t* vb,
+                           int nq, int nk, int nv, int K, const uint16_t* x, uint16_t* q,
+                           uint16_t* k, uint16_t* v_cache, int max_seq, int pos) {
+  uint16_t* tmp = (uint16_t*)malloc(sizeof(uint16_t) * (size_t)(nv > 0 ? nv : 1));
+  or_gemv_quant(qc, qs, qb, 4, nq, K, x, 1, q, NULL);
+  or_gemv_quant(kc, ks, kb, 4, nk, K, x, 1, k, NULL);
+  or_gemv_quant(vc, vs, vb, 4, nv, K, x, 1, tmp, NULL);
+  for (int i = 0; i < nv; ++i)
+    v_cache[((size_t)(i / 64) * max_seq + pos) * 64 + i % 64] = tmp[i];
+  free(tmp);
+}
+
+/* conv3_gemv (kernels/lfm.rs:207-246 -> lfm_conv3_gemv_split_bf16
+ * lfm.metal:1070-1110): rows c, H + c, 2H + c of the [3H][K] projection give
+ * b, c, x for channel c (each bf16-rounded); with the two-tap state
+ * (v0 = state[c], v1 = state[H + c]) and taps w[c][0..2]:
+ *   v2 = bf16(b * x); z = bf16((w0 * v0 + w1 * v1) + w2 * v2) (no fused
+ *   multiply-add, left to right: this project's order, the reference's is
+ *   its compiler's); out[c] = bf16(c * z);
+ *   new_state[c] = state[H + c]; new_state[H + c] = v2. */
+void or_conv3_gemv(const void* codes, const uint16_t* scales, const uint16_t* biases, int H,
+                   int K, const uint16_t* x, const uint16_t* w, const uint16_t* state,
+                   uint16_t* out, uint16_t* new_state) {
+  uint16_t* p = (uint16_t*)malloc(sizeof(uint16_t) * 3 * (size_t)H);
+  or_gemv_quant(codes, scales, biases, 4, 3 * H, K, x, 1, p, NULL);
+  for (int ch = 0; ch < H; ++ch) {
+    const float b = bf(p[ch]), c = bf(p[H + ch]), xv = bf(p[2 * H + ch]);
+    const float v0 = bf(state[ch]), v1 = bf(state[H + ch]);
+    const float v2 = rb(b * xv);
+    const float z = (bf(w[3 * ch]) * v0 + bf(w[3 * ch + 1]) * v1) + bf(w[3 * ch + 2]) * v2;
+    out[ch] = or_f32_to_bf16(c * rb(z));
+    new_state[H + ch] = or_f32_to_bf16(v2);
+    new_state[ch] = state[H + ch];
+  }
+  free(p);
+}
+
+/* gemv_gu_act (kernels/lfm.rs:462-495 -> lfm_gemv_q4_gu_act_bf16
+ * lfm.metal:1447-1498): the dense FFN front half, act[b][n] =
+ * bf16(bf16(silu(bf16(gate_n . x))) * bf16(up_n . x)). x bf16 [B][K]. */
+void or_gemv_gu_act(const void* gc, const uint16_t* gs, const uint16_t* gb, const void* uc,
+                    const uint16_t* us, const uint16_t* ub, int N, int K, const uint16_t* x,
+                    int B, uint16_t* act) {
+  uint16_t* g = (uint16_t*)malloc(sizeof(uint16_t) * (size_t)N * B);
+  uint16_t* u = (uint16_t*)malloc(sizeof(uint16_t) * (size_t)N * B);
+  or_gemv_quant(gc, gs, gb, 4, N, K, x, B, g, NULL);
+  or_gemv_quant(uc, us, ub, 4, N, K, x, B, u, NULL);
+  for (size_t i = 0; i < (size_t)N * B; ++i)
+    act[i] = or_f32_to_bf16(rb(or_silu(bf(g[i]))) * bf(u[i]));
+  free(g); free(u);
 }
 
 /* ------------------------------------------------------------- prefill */
@@ -466,33 +533,53 @@ void or_dequant_q4(const uint32_t* codes, const uint16_t* scales, const uint16_t
 /* Grouped Q4 GEMM reference (quant.rs:228-266 -> lfm_qmm_t_body
  * quant_nax.metal:4091-4234): for sorted row i of expert e,
  * C[i][n] = bf16(sum_k A[i][k] * Wdeq[e*N + n][k]) with fp32 accumulation in
- * increasing k (the tensor-op order on the GPU differs, hence a tolerance).
- * A rows are given already in sorted order (gx / act). */
+ * increasing k from 0.0f (the tensor-op order on the GPU differs, hence a
+ * tolerance). A rows are given already in sorted order (gx / act).
+ * Each output keeps that one sequential chain; only the loop nest around it
+ * is arranged for speed (the dequantised expert transposed to [K][N], blocks
+ * of rows sharing each pass over it, row blocks spread over OpenMP threads),
+ * so the result does not depend on the thread count. */
+#define OR_RB 8
 void or_gemm_q4_grouped(const uint16_t* A, int S, int K, const uint32_t* codes,
                         const uint16_t* scales, const uint16_t* biases, int N,
                         const uint32_t* counts, const uint32_t* offsets, int E,
                         uint16_t* C, float* Cacc) {
   uint16_t* wd = (uint16_t*)malloc(sizeof(uint16_t) * (size_t)N * K);
-  float* af = (float*)malloc(sizeof(float) * K);
-  float* wf = (float*)malloc(sizeof(float) * (size_t)N * K);
+  float* wt = (float*)malloc(sizeof(float) * (size_t)N * K);  /* [K][N] */
   for (int e = 0; e < E; ++e) {
     if (counts[e] == 0) continue;
     or_dequant_q4(codes + (size_t)e * N * (K / 8), scales + (size_t)e * N * (K / 64),
                   biases + (size_t)e * N * (K / 64), N, K, wd);
-    for (size_t j = 0; j < (size_t)N * K; ++j) wf[j] = bf(wd[j]);
-    for (uint32_t i = offsets[e]; i < offsets[e] + counts[e]; ++i) {
-      for (int k = 0; k < K; ++k) af[k] = bf(A[(size_t)i * K + k]);
-      for (int n = 0; n < N; ++n) {
-        const float* wr = wf + (size_t)n * K;
-        float a = 0.0f;
-        for (int k = 0; k < K; ++k) a = a + af[k] * wr[k];
-        if (Cacc) Cacc[(size_t)i * N + n] = a;
-        C[(size_t)i * N + n] = or_f32_to_bf16(a);
+    for (int n = 0; n < N; ++n)
+      for (int k = 0; k < K; ++k) wt[(size_t)k * N + n] = bf(wd[(size_t)n * K + k]);
+    const long i0 = offsets[e], rows = counts[e];
+    const long nblk = (rows + OR_RB - 1) / OR_RB;
+#pragma omp parallel for schedule(dynamic, 1)
+    for (long blk = 0; blk < nblk; ++blk) {
+      const long r0 = i0 + blk * OR_RB;
+      const int rb = (int)((rows - blk * OR_RB) < OR_RB ? (rows - blk * OR_RB) : OR_RB);
+      float* acc = (float*)calloc((size_t)OR_RB * N, sizeof(float));
+      float af[OR_RB];
+      for (int k = 0; k < K; ++k) {
+        const float* wrow = wt + (size_t)k * N;
+        for (int r = 0; r < rb; ++r) af[r] = bf(A[(size_t)(r0 + r) * K + k]);
+        for (int r = 0; r < rb; ++r) {
+          float* ar = acc + (size_t)r * N;
+          const float a = af[r];
+          for (int n = 0; n < N; ++n) ar[n] = ar[n] + a * wrow[n];
+        }
       }
+      for (int r = 0; r < rb; ++r)
+        for (int n = 0; n < N; ++n) {
+          const float a = acc[(size_t)r * N + n];
+          if (Cacc) Cacc[(size_t)(r0 + r) * N + n] = a;
+          C[(size_t)(r0 + r) * N + n] = or_f32_to_bf16(a);
+        }
+      free(acc);
     }
   }
   (void)S;
-  free(wd); free(af); free(wf);
+  free(wd); free(wt);
 }
 
 /* silu_mul_bf16 (elementwise.metal:7-15). */

@@ -163,3 +163,17 @@ def test_rejects_malformed_checkpoints(tmp_path):
     assert list(c.names()) == ["x"]
     with pytest.raises(ValueError, match="unsupported dtype F16"):
         c.read("x")
+
+
+def test_missing_expert_bias_is_an_error(tmp_path):
+    """The reference requires feed_forward.expert_bias (lfm.rs:359): a layer
+    without it fails to load unless the caller opts out for bias-free routing."""
+    g = synth.rng(8)
+    t = _moe_tensors(g, 1, 4, 128, 64)
+    del t["model.layers.1.feed_forward.expert_bias"]
+    ck.write_safetensors(tmp_path / ck.SINGLE_NAME, t)
+    c = ck.Checkpoint.open(tmp_path)
+    with pytest.raises(ValueError, match="missing model.layers.1.feed_forward.expert_bias"):
+        ck.load_moe_layer(c, 1, 4, 128, 64, device="cpu")
+    L = ck.load_moe_layer(c, 1, 4, 128, 64, device="cpu", allow_missing_bias=True)
+    assert L["expert_bias"] is None

@@ -59,7 +59,7 @@ def test_stacked_decode_matches_oracle(cuda_ctx, batch):
     for s in range(steps):  # eager
         st.step()
         torch.cuda.synchronize()
-        got = st.tokens.cpu().numpy().view(np.uint32)
+        got = st.read_tokens().numpy().view(np.uint32)
         assert np.array_equal(got, want[s]), f"step {s}: {got} != {want[s]}"
     assert int(st.keys.abs().sum().cpu()) == 0, "token tail leaves the keys cleared"
     g = torch.cuda.CUDAGraph()
@@ -73,7 +73,7 @@ def test_stacked_decode_matches_oracle(cuda_ctx, batch):
     for s in range(steps, 2 * steps):
         g.replay()
         torch.cuda.synchronize()
-        got = st.tokens.cpu().numpy().view(np.uint32)
+        got = st.read_tokens().numpy().view(np.uint32)
         assert np.array_equal(got, want[s]), f"graph step {s}: {got} != {want[s]}"
 
 
@@ -100,8 +100,8 @@ def test_stacked_decode_grouped_path(cuda_ctx):
         rms = float(a.pow(2).mean().sqrt())
         err = float((a - b).abs().max())
         assert err <= 2e-2 * rms + 2e-2 * float(a.abs().max()), f"step {s}: max err {err}, rms {rms}"
-        ta = stacks["gemv"].tokens.cpu().numpy().view(np.uint32)
-        tb = stacks["grouped"].tokens.cpu().numpy().view(np.uint32)
+        ta = stacks["gemv"].read_tokens().numpy().view(np.uint32)
+        tb = stacks["grouped"].read_tokens().numpy().view(np.uint32)
         for r in np.nonzero(ta != tb)[0]:
             x = stacks["gemv"].outs[(L - 1) % 2][r:r + 1].contiguous().view(torch.int16).cpu().numpy()
             v = synth.bf16_bits_to_f32(oracle.gemv_quant(*head, 6, x.view(np.uint16))[0])
