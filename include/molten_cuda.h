@@ -234,6 +234,43 @@ int mc_conv3_gemv(mc_ctx* ctx, const mc_qweights* w_proj, const uint16_t* x,
 int mc_gemv_gu_act(mc_ctx* ctx, const mc_qweights* gate, const mc_qweights* up,
                    const uint16_t* x, uint16_t* act, int batch);
 
+/* ------------------------------------------------- sampling draw */
+
+/* Sampling (lfm/sample.rs:87-213; docs/PROTOCOL.md:48-75): temperature
+ * (>= 1e-6; temperature 0 is the greedy head, not this call), top_k (0 or
+ * >= vocab: off), top_p in (0, 1] (1: off), repetition_penalty in
+ * [1e-6, 1e6] (1: off), 64-bit seed. */
+typedef struct mc_sampling {
+  float temperature;
+  uint32_t top_k;
+  float top_p;
+  float repetition_penalty;
+  uint64_t seed;
+} mc_sampling;
+
+/* SampleScratch::encode_draw (lfm/sample.rs:248-338 -> lfm_sample_gumbel /
+ * _prep / _levels / _gather / _finish, lfm_sample.metal:161-930): draws the
+ * token at absolute position `pos` from the bf16 logits row [vocab] (vocab a
+ * multiple of 4) into *key, the zeroed 64-bit argmax key the greedy head
+ * writes, so mc_token_tail reads and clears it for both paths. w_i =
+ * pen(v_i) / T; kept set {w >= tau} (top-k ties kept, then the smallest
+ * top-p prefix with its boundary tie group); the kept token with the
+ * largest w + Gumbel(Philox4x32-10 word) wins, ties to the lower id. `seen`
+ * (u32 bitmap [vocab / 32], needed only with a penalty) marks the
+ * sequence's tokens. The top-k / top-p threshold is exact: integer counts
+ * and per-token masses rint(exp(w - max w) * 2^40) summed in 64 bits.
+ * workspace: mc_sample_workspace_bytes(vocab) device bytes, 256-byte
+ * aligned, zeroed once before the first call (every call leaves it zero);
+ * unused (may be NULL) when top_k and top_p are both off. */
+size_t mc_sample_workspace_bytes(int vocab);
+int mc_sample_draw(mc_ctx* ctx, const uint16_t* logits, int vocab, const uint32_t* seen,
+                   const mc_sampling* s, uint32_t pos, unsigned long long* key,
+                   void* workspace, size_t ws_bytes);
+/* SampleScratch::encode_mark (lfm/sample.rs:340-353 -> lfm_sample_mark
+ * lfm_sample.metal:922-931): after mc_token_tail wrote *tok, sets its bit in
+ * `seen`. */
+int mc_sample_mark(mc_ctx* ctx, const uint32_t* tok, uint32_t* seen, int vocab);
+
 /* ----------------------------------------------------------- prefill path */
 
 /* moe_route_batch (kernels/lfm.rs:536-555 -> lfm.metal:1558-1602): per-token
