@@ -260,8 +260,9 @@ typedef struct mc_sampling {
  * sequence's tokens. The top-k / top-p threshold is exact: integer counts
  * and per-token masses rint(exp(w - max w) * 2^40) summed in 64 bits.
  * workspace: mc_sample_workspace_bytes(vocab) device bytes, 256-byte
- * aligned, zeroed once before the first call (every call leaves it zero);
- * unused (may be NULL) when top_k and top_p are both off. */
+ * aligned, zeroed once before the first call (every call leaves its control
+ * words zero again; the rest is scratch); unused (may be NULL) when top_k
+ * and top_p are both off. */
 size_t mc_sample_workspace_bytes(int vocab);
 int mc_sample_draw(mc_ctx* ctx, const uint16_t* logits, int vocab, const uint32_t* seen,
                    const mc_sampling* s, uint32_t pos, unsigned long long* key,

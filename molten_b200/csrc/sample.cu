@@ -31,8 +31,9 @@
 // clears the histogram for the next level.
 //
 // Launches: temperature only -> one (draw); top-k or top-p -> prep, three
-// levels, draw; both -> prep, six levels, draw. The workspace is zero before
-// the first call and every call leaves it zero.
+// levels, draw; both -> prep, six levels, draw. The workspace's control part
+// (plan and histogram) is zero before the first call and every call leaves
+// it zero; the processed logits after it are scratch.
 #include "mc_internal.cuh"
 
 namespace {

@@ -302,3 +302,50 @@ def gemv_gu_act(gate, up, x):
     lib().or_gemv_gu_act(*(_ptr(a) for a in gate), *(_ptr(a) for a in up), N, K, _ptr(x), B,
                          _ptr(act))
     return act
+
+
+def sample_draw(logits, seen=None, temperature=1.0, top_k=0, top_p=1.0, penalty=1.0, seed=0,
+                pos=0):
+    """(argmax key u64, threshold key u32) of the sampled draw over bf16
+    logits [V]; seen: u32 bitmap [V/32] or None."""
+    logits = np.ascontiguousarray(logits.reshape(-1))
+    V = logits.shape[0]
+    tau = C.c_uint32(0)
+    L = lib()
+    L.or_sample_draw.restype = C.c_uint64
+    L.or_sample_draw.argtypes = [C.c_void_p, C.c_int, C.c_void_p, C.c_float, C.c_uint32,
+                                 C.c_float, C.c_float, C.c_uint64, C.c_uint32,
+                                 C.POINTER(C.c_uint32)]
+    key = L.or_sample_draw(_ptr(logits), V, _ptr(seen), temperature, top_k, top_p, penalty,
+                           seed, pos, C.byref(tau))
+    return int(key), int(tau.value)
+
+
+def gumbel(x: int) -> float:
+    L = lib()
+    L.or_gumbel.restype = C.c_float
+    L.or_gumbel.argtypes = [C.c_uint32]
+    return L.or_gumbel(x)
+
+
+def log(x: float) -> float:
+    L = lib()
+    L.or_log.restype = C.c_float
+    L.or_log.argtypes = [C.c_float]
+    return L.or_log(x)
+
+
+def sample_word(i: int, pos: int, seed: int) -> int:
+    L = lib()
+    L.or_sample_word.restype = C.c_uint32
+    L.or_sample_word.argtypes = [C.c_uint32] * 4
+    return L.or_sample_word(i, pos, seed & 0xffffffff, seed >> 32)
+
+
+def philox4x32_10(counter, key):
+    """Philox4x32-10 of a 4-word counter and 2-word key -> 4 words."""
+    c = (C.c_uint32 * 4)(*counter)
+    L = lib()
+    L.or_philox4x32_10.argtypes = [C.c_void_p, C.c_uint32, C.c_uint32]
+    L.or_philox4x32_10(C.cast(c, C.c_void_p), key[0], key[1])
+    return [int(v) for v in c]

@@ -485,6 +485,174 @@ void or_gemv_gu_act(const void* gc, const uint16_t* gs, const uint16_t* gb, cons
   free(g); free(u);
 }
 
+/* ------------------------------------------------- sampling
+ * Contract: docs/PROTOCOL.md:48-75 and lfm_sample.metal:1-27 (w = pen(v)/T;
+ * kept set {w >= tau}: top-k ties kept, then the smallest top-p prefix with
+ * its boundary tie group; Gumbel-max draw with Philox4x32-10, counter
+ * (id/4, pos, "SAMP", 0), key (seed lo, seed hi); ties to the lower id).
+ * The threshold follows this project's exact integer definition (the GPU
+ * finds the same one by radix selection): top-k by counts; top-p by
+ * per-token masses m_i = rint(exp(w_i - max w) * 2^40) summed in 64 bits,
+ * target ceil(rint(top_p * 2^32) * Z / 2^32) with Z the mass of the top-k
+ * kept set (or of the whole vocabulary). log, Philox and the Gumbel
+ * transform are written again here with the same steps as the CUDA side
+ * (molten_b200/csrc/mc_numerics.cuh). */
+
+/* log: x = 2^e m, m in [sqrt(1/2), sqrt(2)); 2 atanh((m-1)/(m+1)) by its odd
+ * series to s^11; e ln2 with fdlibm's logf split of ln2. */
+float or_log(float x) {
+  uint32_t u = u_of(x);
+  if (x != x || x < 0.0f) return f_of(0x7fc00000u);
+  if (x == 0.0f) return f_of(0xff800000u);
+  if (u >= 0x7f800000u) return x;
+  int e = 0;
+  if (u < 0x00800000u) { x = x * 8388608.0f; u = u_of(x); e = -23; }
+  e += (int)(u >> 23) - 127;
+  uint32_t mu = (u & 0x007fffffu) | 0x3f800000u;
+  if (mu > 0x3fb504f3u) { mu -= 0x00800000u; e += 1; }
+  const float m = f_of(mu);
+  const float s = (m + -1.0f) / (m + 1.0f);
+  const float z = s * s;
+  float p = 9.09090936183929443359e-02f;
+  p = fmaf(p, z, 1.11111111938953399658e-01f);
+  p = fmaf(p, z, 1.42857149243354797363e-01f);
+  p = fmaf(p, z, 2.00000002980232238770e-01f);
+  p = fmaf(p, z, 3.33333343267440795898e-01f);
+  const float two_s = s + s;
+  const float lm = fmaf(two_s * z, p, two_s);
+  const float ef = (float)e;
+  return fmaf(ef, 6.9313812256e-01f, fmaf(ef, 9.0580006145e-06f, lm));
+}
+
+/* Philox4x32-10 (Salmon et al., SC 2011). */
+static void or_philox(uint32_t c[4], uint32_t k0, uint32_t k1) {
+  for (int r = 0; r < 10; ++r) {
+    const uint64_t p0 = (uint64_t)0xD2511F53u * c[0];
+    const uint64_t p1 = (uint64_t)0xCD9E8D57u * c[2];
+    const uint32_t n0 = (uint32_t)(p1 >> 32) ^ c[1] ^ k0;
+    const uint32_t n2 = (uint32_t)(p0 >> 32) ^ c[3] ^ k1;
+    c[1] = (uint32_t)p1;
+    c[3] = (uint32_t)p0;
+    c[0] = n0;
+    c[2] = n2;
+    k0 += 0x9E3779B9u;
+    k1 += 0xBB67AE85u;
+  }
+}
+
+void or_philox4x32_10(uint32_t* c, uint32_t k0, uint32_t k1) { or_philox(c, k0, k1); }
+
+uint32_t or_sample_word(uint32_t id, uint32_t pos, uint32_t seed_lo, uint32_t seed_hi) {
+  uint32_t c[4] = {id >> 2, pos, 0x53414D50u, 0u};
+  or_philox(c, seed_lo, seed_hi);
+  return c[id & 3u];
+}
+
+/* Gumbel(0, 1) of a uniform word (lfm_sample.metal:129-142 semantics). */
+float or_gumbel(uint32_t x) {
+  const float v = ((float)x + 0.5f) * 2.3283064365386963e-10f;
+  float e;
+  if (v < 0.015625f) {
+    e = v * (1.0f + v * (0.5f + v * (0.33333334f + v * 0.25f)));
+  } else {
+    float t = 1.0f + -v;
+    if (t < 2.9802322387695312e-08f) t = 2.9802322387695312e-08f;
+    e = -or_log(t);
+  }
+  return -or_log(e);
+}
+
+static uint32_t fkey(float v) {
+  uint32_t u = u_of(v);
+  if ((u << 1) == 0u) u = 0u;
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+static float kfloat(uint32_t k) { return f_of((k & 0x80000000u) ? (k & 0x7fffffffu) : ~k); }
+
+/* lfm_sample.metal:96-105. */
+float or_sample_w(float v, int seen, float inv_temp, float penalty, float inv_penalty) {
+  if (seen) v = v > 0.0f ? v * inv_penalty : v * penalty;
+  uint32_t u = u_of(v * inv_temp);
+  if ((u << 1) == 0u) u = 0u;
+  return f_of(u);
+}
+
+static uint64_t token_mass(float w, float M) {
+  const float e = or_exp(w - M);
+  if (e != e) return 0u;
+  return (uint64_t)llrintf(e * 1099511627776.0f);
+}
+
+typedef struct { uint32_t key; uint64_t mass; } or_km;
+
+static int cmp_key_desc(const void* a, const void* b) {
+  const uint32_t x = ((const or_km*)a)->key, y = ((const or_km*)b)->key;
+  return x < y ? 1 : (x > y ? -1 : 0);
+}
+
+/* The draw: returns the argmax key (value w + G desc, id asc) of the kept
+ * tokens and the threshold key in *tau_out (0: every token kept). top_k 0
+ * or >= V is off; top_p >= 1 is off. */
+uint64_t or_sample_draw(const uint16_t* logits, int V, const uint32_t* seen, float temperature,
+                        uint32_t top_k, float top_p, float penalty, uint64_t seed, uint32_t pos,
+                        uint32_t* tau_out) {
+  const float inv_temp = 1.0f / temperature, inv_pen = 1.0f / penalty;
+  const int use_pen = penalty != 1.0f && seen != NULL;
+  if (top_k >= (uint32_t)V) top_k = 0;
+  float* w = (float*)malloc(sizeof(float) * V);
+  uint32_t* keys = (uint32_t*)malloc(sizeof(uint32_t) * V);
+  uint32_t mk = 0;
+  for (int i = 0; i < V; ++i) {
+    const int sn = use_pen && ((seen[i >> 5] >> (i & 31)) & 1u);
+    w[i] = or_sample_w(bf(logits[i]), sn, inv_temp, penalty, inv_pen);
+    keys[i] = fkey(w[i]);
+    if (keys[i] > mk) mk = keys[i];
+  }
+  uint32_t tau = 0;
+  if (top_k != 0 || top_p < 1.0f) {
+    const float M = kfloat(mk);
+    or_km* srt = (or_km*)malloc(sizeof(or_km) * V);
+    for (int i = 0; i < V; ++i) {
+      srt[i].key = keys[i];
+      srt[i].mass = token_mass(w[i], M);
+    }
+    qsort(srt, V, sizeof(or_km), cmp_key_desc);
+    uint32_t tau_k = 0;
+    if (top_k) tau_k = srt[top_k - 1].key;  /* the k-th largest; ties kept */
+    tau = tau_k;
+    if (top_p < 1.0f) {
+      uint64_t Z = 0;
+      for (int i = 0; i < V && srt[i].key >= tau_k; ++i) Z += srt[i].mass;
+      const uint64_t pf = (uint64_t)llrintf(top_p * 4294967296.0f);
+      const unsigned __int128 prod = (unsigned __int128)pf * Z + 0xffffffffu;
+      uint64_t target = (uint64_t)(prod >> 32);
+      if (target == 0) target = 1;
+      /* the largest key whose mass at or above it reaches the target: walk
+       * the distinct keys downwards, each tie group added whole */
+      uint64_t cum = 0;
+      tau = srt[V - 1].key;
+      for (int j = 0; j < V;) {
+        int j2 = j;
+        while (j2 < V && srt[j2].key == srt[j].key) cum += srt[j2++].mass;
+        if (cum >= target) { tau = srt[j].key; break; }
+        j = j2;
+      }
+    }
+    free(srt);
+  }
+  uint64_t best = 0;
+  const uint32_t slo = (uint32_t)seed, shi = (uint32_t)(seed >> 32);
+  for (int i = 0; i < V; ++i) {
+    if (keys[i] < tau) continue;
+    const float g = or_gumbel(or_sample_word((uint32_t)i, pos, slo, shi));
+    const uint64_t k = or_argmax_key(w[i] + g, (uint32_t)i);
+    if (k > best) best = k;
+  }
+  if (tau_out) *tau_out = tau;
+  free(w); free(keys);
+  return best;
+}
+
 /* ------------------------------------------------------------- prefill */
 
 /* moe_route_batch (kernels/lfm.rs:536-555; lfm.metal:1558-1602). */
