@@ -390,6 +390,57 @@ int mc_ep_return(mc_ctx* ctx, const uint16_t* ed, size_t ed_rows, int hidden,
                  const uint32_t* counts_all, int rank, int world, int n_experts,
                  void* const* home_bufs, size_t home_cap_rows, uint32_t* status);
 
+/* ------------------------- expert-parallel prefill through the C ABI alone
+ * One process per GPU. A host with no PyTorch drives the whole step:
+ *   rank 0: mc_ep_unique_id(id) and hands the 128 bytes to the other ranks
+ *           (its own channel);
+ *   every rank: mc_ep_init(ctx, W, rank, id, timeout_ms) -> a non-blocking
+ *           NCCL communicator, every NCCL call watched with
+ *           ncclCommGetAsyncError against the timeout and aborted past it;
+ *           mc_ep_reserve(ctx, m_max, E, slots_per_rank, H, I) (collective:
+ *           allocates the exchange buffers and maps every rank's through CUDA
+ *           IPC);
+ *           mc_ep_place(load, ...) on the same load matrix -> the same slot
+ *           tables everywhere; the rank loads the weights of its slots
+ *           (slot_expert[rank*spr ..]) stacked in slot order;
+ *           mc_ep_moe_prefill(...) per step (collective; no host sync);
+ *           mc_ep_status(ctx, &st) when it wants the step's status bits
+ *           (1 a GEMM wait, 2 a malformed tile or expert id, 4 rows beyond a
+ *           capacity, 8 a cross-rank barrier that gave up); mc_sync waits for
+ *           the stream while watching the communicator;
+ *           mc_ep_finalize(ctx) (collective) at the end.
+ * No counterpart in the reference, whose moe_prefill (lfm.rs:847-965) runs
+ * on one device; the per-step arithmetic is moe_prefill's, so each rank's
+ * output equals it within the grouped GEMMs' tolerance and its ids, sorted
+ * order and slot positions are bit-exact. mc_ep_init and mc_ep_reserve
+ * allocate (cudaMalloc) and synchronise; mc_ep_moe_prefill allocates
+ * nothing. */
+int mc_ep_unique_id(void* out128);
+int mc_ep_init(mc_ctx* ctx, int nranks, int rank, const void* nccl_unique_id, int timeout_ms);
+int mc_ep_reserve(mc_ctx* ctx, int m_max, int n_experts, int slots_per_rank, int hidden,
+                  int moe_inter);
+/* Host-only placement: load[s][e] (pairs of source rank s routed to expert
+ * e, e.g. one routing pass) -> tables[s][e] (the slot source s sends expert
+ * e's rows to) and slot_expert[W * slots_per_rank] (the expert each slot
+ * holds, -1 if none). Spare slots (W * spr > E) replicate the hottest
+ * experts. Deterministic. */
+int mc_ep_place(const unsigned long long* load, int world, int n_experts, int slots_per_rank,
+                uint32_t* tables, int32_t* slot_expert);
+/* One step on this rank's m tokens (m <= m_max): x bf16 [m][H], logits f32
+ * [m][E], the rank's slot weights gate/up [spr*I][H], down [spr*H][I],
+ * slot_table (device u32 [E]: this rank's row of mc_ep_place's tables),
+ * out bf16 [m][H]. */
+int mc_ep_moe_prefill(mc_ctx* ctx, const uint16_t* x, const float* logits, int m,
+                      const mc_qweights* gate, const mc_qweights* up, const mc_qweights* down,
+                      const uint32_t* slot_table, int route_mode, const float* expert_bias,
+                      uint16_t* out);
+/* Waits for the stream; *out = the status bits since the last call (then
+ * cleared). */
+int mc_ep_status(mc_ctx* ctx, uint32_t* out);
+/* The last step's all-gathered pair counts [W][W * spr] (host copy; waits). */
+int mc_ep_counts(mc_ctx* ctx, uint32_t* out, size_t n);
+int mc_ep_finalize(mc_ctx* ctx);
+
 /* Cross-layer prefetch hint (no reference counterpart): the next
  * mc_moe_decode_layer (or _noalloc) launched on ctx prefetches the byte
  * ranges [p0, p0 + n0) and [p1, p1 + n1) into L2 once its own expert rows are
@@ -435,6 +486,9 @@ int mc_set_wait_limit(mc_ctx* ctx, unsigned long long ns);
  * mc_moe_decode_layer(_noalloc) publish no logits, so every CTA's logit wait
  * gives up and status bit 1 is set. 0 (the default) for normal work. */
 #define MC_TEST_SKIP_LOGIT_PUBLISH 1
+/* MC_TEST_SKIP_BARRIER_ARRIVE: the expert-parallel barrier of this rank
+ * waits without arriving, so its wait runs out and sets status bit 8. */
+#define MC_TEST_SKIP_BARRIER_ARRIVE 2
 int mc_set_test_flags(mc_ctx* ctx, int flags);
 
 /* Evaluates the library's device math on x[n] into y[n]: op 0 = mc_exp,

@@ -19,6 +19,7 @@ MC_ENCCL = -4
 MC_ETIMEOUT = -5
 
 TEST_SKIP_LOGIT_PUBLISH = 1
+TEST_SKIP_BARRIER_ARRIVE = 2
 
 ROUTE_SOFTMAX_RENORM = 0
 ROUTE_SIGMOID_BIAS = 1
@@ -93,6 +94,14 @@ SIGNATURES: dict[str, tuple] = {
     "mc_ipc_close": (I, [P, P]),
     "mc_ep_dispatch": (I, [P, P, I, I, P, P, I, I, I, P, C.c_size_t, P]),
     "mc_ep_tiles": (I, [P, P, I, I, I, I, P, P, P, I]),
+    "mc_ep_unique_id": (I, [P]),
+    "mc_ep_init": (I, [P, I, I, P, I]),
+    "mc_ep_reserve": (I, [P, I, I, I, I, I]),
+    "mc_ep_place": (I, [P, I, I, I, P, P]),
+    "mc_ep_moe_prefill": (I, [P, P, P, I, QP, QP, QP, P, I, P, P]),
+    "mc_ep_status": (I, [P, P]),
+    "mc_ep_counts": (I, [P, P, C.c_size_t]),
+    "mc_ep_finalize": (I, [P]),
     "mc_ep_return": (I, [P, P, C.c_size_t, I, P, I, I, I, P, C.c_size_t, P]),
     "mc_moe_decode_layer_noalloc": (I, [P, P, P, P, P, P, P, I, P, I, P, P, P, QP, QP, QP, I, P,
                                         P, F, F]),

@@ -118,7 +118,7 @@ extern "C" int mc_set_wait_limit(mc_ctx* ctx, unsigned long long ns) {
 
 extern "C" int mc_set_test_flags(mc_ctx* ctx, int flags) {
   if (!ctx) return mc_fail(MC_EINVAL, "mc_set_test_flags: null context");
-  if (flags & ~MC_TEST_SKIP_LOGIT_PUBLISH)
+  if (flags & ~(MC_TEST_SKIP_LOGIT_PUBLISH | MC_TEST_SKIP_BARRIER_ARRIVE))
     return mc_fail(MC_EINVAL, "mc_set_test_flags: unknown flags 0x%x", flags);
   ctx->test_flags = flags;
   return MC_OK;
@@ -186,15 +186,15 @@ extern "C" int mc_copy_async(mc_ctx* ctx, void* dst, const void* src, size_t byt
 
 extern "C" int mc_sync(mc_ctx* ctx) {
   if (!ctx) return mc_fail(MC_EINVAL, "mc_sync: null context");
+  if (ctx->ep) return mc_ep_wait(ctx);
   MC_CUDA(cudaStreamSynchronize(ctx->stream));
   MC_CUDA(cudaGetLastError());
   return MC_OK;
 }
 
-int mc_ep_teardown(mc_ctx* ctx);
-
 extern "C" int mc_destroy(mc_ctx* ctx) {
   if (!ctx) return MC_OK;
+  mc_ep_release(ctx);
   if (ctx->owns_stream) cudaStreamDestroy(ctx->stream);
   free(ctx);
   return MC_OK;

@@ -38,6 +38,10 @@ int mc_decode_layer_impl(mc_ctx* ctx, const uint16_t* h, const uint16_t* b,
                          const mc_qweights* gate, const mc_qweights* up, const mc_qweights* down,
                          int n_experts, uint16_t* out, uint32_t* sync, size_t ws_words, float eps,
                          float route_eps, bool noalloc, uint32_t* status_out);
+// Expert-parallel state (ep_prefill.cu): waits for the stream while watching
+// the communicator (mc_sync with a communicator); releases it on mc_destroy.
+int mc_ep_wait(mc_ctx* ctx);
+void mc_ep_release(mc_ctx* ctx);
 // The built-in decode scratch of ctx's device and its size in u32 words; the
 // first call per device zeroes it (moe_decode_noalloc.cu).
 int mc_noalloc_decode_scratch(mc_ctx* ctx, uint32_t** ptr, size_t* words);

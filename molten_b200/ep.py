@@ -444,3 +444,84 @@ def moe_prefill_ep_emulated(ctx, xs, logits, gate, up, down, n_experts: int, pla
         inner = [dict(ids=s[4], gw=s[0], ids_sorted=s[3], slotpos=s[2]) for s in st]
         return outs, int(status.cpu()[0]), inner
     return outs, int(status.cpu()[0])
+
+
+# ------------------------------------------------- the C-ABI expert-parallel step
+# The whole step runs inside the library (mc_ep_moe_prefill): routing, slot
+# relabelling, sort, the NCCL all-gather of the counts, dispatch over NVLink,
+# device-side barriers, the grouped GEMMs, the return and the combine. Python
+# only bootstraps the NCCL unique id and loads each rank's slot weights.
+
+def place_slots(load, world: int, slots_per_rank: int):
+    """Slot placement with hot-expert replication (mc_ep_place): load[s][e]
+    pairs -> (tables u32 [world][E], slot_expert i32 [world * spr])."""
+    import ctypes as C
+    from molten_b200 import _lib
+    load = np.ascontiguousarray(np.asarray(load, dtype=np.uint64))
+    W, E = load.shape
+    tables = np.zeros((W, E), np.uint32)
+    slot_expert = np.zeros(W * slots_per_rank, np.int32)
+    ptr = lambda a: a.ctypes.data_as(C.c_void_p)
+    _lib.call("mc_ep_place", ptr(load), W, E, slots_per_rank, ptr(tables), ptr(slot_expert))
+    return tables, slot_expert
+
+
+def slot_weights(w, slot_expert_of_rank, n_experts: int):
+    """This rank's slot weights: the rows of each slot's expert of a stacked
+    [E*N][K] QuantWeights, in slot order (an empty slot repeats expert 0; no
+    row is ever routed to it)."""
+    return placed_slice(w, [int(e) if e >= 0 else 0 for e in slot_expert_of_rank], n_experts)
+
+
+class EpPrefill:
+    """One rank's expert-parallel prefill through the C ABI."""
+
+    def __init__(self, ctx, rank: int, world: int, timeout_ms: int = 120000, group=None):
+        import ctypes as C
+        from molten_b200 import _lib
+        self.lib, self.ctx, self.rank, self.world = _lib, ctx, rank, world
+        uid = (C.c_char * 128)()
+        if rank == 0:
+            _lib.call("mc_ep_unique_id", uid)
+        if world > 1:
+            obj = [bytes(uid) if rank == 0 else None]
+            dist.broadcast_object_list(obj, src=0, group=group)
+            uid = (C.c_char * 128).from_buffer_copy(obj[0])
+        _lib.call("mc_ep_init", ctx.handle, world, rank, uid, timeout_ms)
+        self.reserved = False
+
+    def reserve(self, m_max: int, n_experts: int, slots_per_rank: int, hidden: int,
+                moe_inter: int) -> None:
+        self.E, self.spr, self.H, self.I = n_experts, slots_per_rank, hidden, moe_inter
+        self.lib.call("mc_ep_reserve", self.ctx.handle, m_max, n_experts, slots_per_rank, hidden,
+                      moe_inter)
+        self.reserved = True
+
+    def step(self, x, logits, gate, up, down, table, out, route_mode: int = 0, bias=None):
+        """x bf16 [m][H], logits f32 [m][E], this rank's slot weights,
+        table: device int32 [E] (this rank's row of the placement), out bf16 [m][H]."""
+        from molten_b200 import lfm
+        m = x.shape[0]
+        lfm.ensure(logits.shape == (m, self.E), "logits shape")
+        self.lib.call("mc_ep_moe_prefill", self.ctx.handle, lfm._p(x), lfm._p(logits), m,
+                      self.lib.C.byref(gate.qw()), self.lib.C.byref(up.qw()),
+                      self.lib.C.byref(down.qw()), lfm._p(table), route_mode, lfm._p(bias),
+                      lfm._p(out))
+
+    def status(self) -> int:
+        import ctypes as C
+        v = C.c_uint32(0)
+        self.lib.call("mc_ep_status", self.ctx.handle, C.byref(v))
+        return int(v.value)
+
+    def counts(self) -> np.ndarray:
+        """The last step's all-gathered pair counts [world][world * spr]."""
+        import ctypes as C
+        n = self.world * self.world * self.spr
+        a = np.zeros(n, np.uint32)
+        self.lib.call("mc_ep_counts", self.ctx.handle, a.ctypes.data_as(C.c_void_p), n)
+        return a.reshape(self.world, self.world * self.spr)
+
+    def finalize(self) -> None:
+        if self.ctx is not None and self.ctx.h:
+            self.lib.call("mc_ep_finalize", self.ctx.handle)

@@ -208,3 +208,23 @@ def test_cfg4_grouped_path_teacher_forced_full_size(cuda_ctx, cfg4):
                      bf16_err_stats(got, out_o))
         assert_rows_close(got, want, np.arange(B), f"layer {l}: out")
         x = out_o
+
+
+def test_cfg3_ep_through_the_c_abi_one_rank_full_size(cfg3):
+    """cfg3 through mc_ep_moe_prefill on a one-rank communicator (the
+    library's whole expert-parallel step: NCCL counts all-gather, dispatch,
+    device barriers, GEMMs, return, combine), with replicated slots."""
+    from tests.test_ep_capi_gpu import _run_rank
+    want = cfg3["want"]
+    load = np.bincount(want["ids"].ravel(), minlength=E)[None, :]
+    ctx = lfm.Context(0)
+    try:
+        outs, status, counts = _run_rank(ctx, 0, 1, cfg3["x"], cfg3["logits"],
+                                         (cfg3["gate"], cfg3["up"], cfg3["down"]), E, I, E + 4,
+                                         load, steps=1)
+    finally:
+        ctx.close()
+    assert status == 0
+    assert counts.sum() == 4 * M
+    record_stats("cfg3 ep (C ABI, one rank) out", bf16_err_stats(outs[0], want["out"]))
+    assert_rows_close(outs[0], want, np.arange(M), "cfg3 ep C ABI out")
