@@ -10,22 +10,33 @@ rotate over 16 independently seeded layer weight sets (5.4 GB, > 40x L2), so
 weights stream from HBM. value = algorithmic bytes (the four selected experts'
 Q4 codes + scales/biases, the router, the activation rows) / device time.
 
+Which workload runs by default (--workload auto) depends on the node: on a
+node with ONE GPU it is cfg1 above; on a node with SEVERAL GPUs it is cfg3,
+the 4096-token prefill MoE FFN with Zipf routing, the one path that shards,
+so `bench.py --gpus N` for N = 1, 2, 4, 8 traces its expert-parallel
+scaling curve with one metric: N = 1 runs the single-GPU prefill
+(mc_moe_prefill), N > 1 (under torchrun) the expert-parallel step through the
+C ABI (mc_ep_moe_prefill: 4096 tokens per GPU, 64/N experts per GPU plus
+--ep-spare replica slots, rows over NVLink, device-side barriers), with the
+busiest rank's rows, the rows it sent and its phase times per rank in
+`config.per_rank`.
+
 Other workloads (--workload): cfg0 (Q4 GEMV 2048x2048), cfg2 (Q6 head +
-argmax 65536x2048), cfg3 (the 4096-token prefill MoE FFN with Zipf routing;
-expert-parallel under torchrun) and cfg4 (the 40-layer stacked decode loop at
+argmax 65536x2048) and cfg4 (the 40-layer stacked decode loop at
 --batch 1/8/32).
 
 e2e: the same work through the public API with the step's inputs copied in
 from pinned host memory and its result read back inside the timed region
 (cfg1 stages its rows with mc_copy_async, 32 steps per CUDA-graph replay).
 
-Multi-GPU: the decode path does not shard (one token's layer is a dependent
-chain), so N GPUs run N independent replicas ("replicas only"); value is the
-sum over ranks of bytes / the max-over-ranks device time.
+Multi-GPU decode (--workload cfg1/cfg0/cfg2/cfg4 with --gpus N): the decode
+path does not shard (one token's layer is a dependent chain), so N GPUs run N
+independent replicas ("replicas only"); value is the sum over ranks of bytes
+/ the max-over-ranks device time.
 
 --impl reference times the CPU port of the same arithmetic (oracle/, the only
 CPU implementation of this path: the reference is Metal-only) on the host's
-cores, rank 0 only.
+cores, rank 0 only, on the workload the molten arm would run.
 """
 from __future__ import annotations
 
@@ -60,7 +71,9 @@ def parse():
     p.add_argument("--steps", type=int, default=20000)
     p.add_argument("--warmup", type=int, default=200)
     p.add_argument("--impl", choices=["molten", "reference"], default="molten")
-    p.add_argument("--workload", choices=["cfg0", "cfg1", "cfg2", "cfg3", "cfg4"], default="cfg1")
+    p.add_argument("--workload", choices=["auto", "cfg0", "cfg1", "cfg2", "cfg3", "cfg4"],
+                   default="auto",
+                   help="auto: cfg1 on a node with one GPU, cfg3 on a node with several")
     p.add_argument("--batch", type=int, default=1, help="cfg4 decode batch (1, 8, 32)")
     p.add_argument("--layers", type=int, default=40, help="cfg4 stacked layers")
     p.add_argument("--moe-path", choices=["auto", "fused", "grouped", "gemv"], default="auto",
@@ -68,8 +81,8 @@ def parse():
     p.add_argument("--tokens", type=int, default=4096, help="cfg3 prefill chunk")
     p.add_argument("--ep-placement", choices=["balanced", "contiguous"], default="balanced",
                    help="cfg3 on N>1 GPUs: expert-to-GPU placement")
-    p.add_argument("--ep-exchange", choices=["peer", "nccl"], default="peer",
-                   help="cfg3 on N>1 GPUs: rows over NVLink peer memory or NCCL point-to-point")
+    p.add_argument("--ep-spare", type=int, default=1,
+                   help="cfg3 on N>1 GPUs: spare expert slots per GPU (hot-expert replicas)")
     p.add_argument("--seed", type=int, default=0)
     p.add_argument("--sets", type=int, default=16, help="rotated weight sets (cfg1)")
     p.add_argument("--decode-path", choices=["fused", "split"], default="fused",
@@ -554,6 +567,14 @@ def zipf_logits_torch(torch, gen, m, e=E, s=1.0, device="cuda", perm_gen=None):
     return (base[None, :] - torch.log(-torch.log(u))).contiguous()
 
 
+CFG3_METRIC = "prefill grouped-GEMM tokens/s (cfg3: 4096-token MoE FFN, Zipf routing)"
+CFG3_WORKLOAD = ("cfg3: 4096 tokens per GPU x 2048, E=64 top-4 Zipf(s=1) routing, "
+                 "SwiGLU 2048->1536->2048 Q4")
+# kernels one mc_ep_moe_prefill launches: route, relabel, sort (2), row chunks,
+# dispatch, barrier, gate/up GEMM, down GEMM, return, barrier, combine
+EP_STEP_LAUNCHES = 12
+
+
 def prefill_flops(S):
     return 2.0 * S * (2 * I * H + H * I)  # gate + up + down, padding excluded
 
@@ -590,9 +611,12 @@ def cpu_baseline_prefill(torch, layer, x, logits, seconds):
 
 
 def bench_cfg3_ep(args, torch, ws, rank, local):
-    """cfg3 expert-parallel over ws GPUs: each rank holds 64/ws experts and its
-    own 4096 tokens (weak scaling); rows cross NVLink by NCCL point-to-point
-    both ways every step (molten_b200.ep)."""
+    """cfg3 expert-parallel over ws GPUs through the C ABI's one-call step
+    (mc_ep_moe_prefill): each rank holds its own 4096 tokens (weak scaling)
+    and the weights of its expert slots -- 64/ws experts plus, by default,
+    one spare slot that replicates a hot expert (placement from one routing
+    pass, mc_ep_place); rows cross NVLink by peer stores both ways, the
+    ranks meet at device-side barriers, counts travel by NCCL."""
     import numpy as np
     import torch.distributed as dist
     from molten_b200 import ep, lfm, synth
@@ -607,55 +631,57 @@ def bench_cfg3_ep(args, torch, ws, rank, local):
     pg.manual_seed(args.seed * 1000 + 7)           # one expert popularity order for all
     x = torch.randn((m, H), generator=tg, device="cuda").to(torch.bfloat16)
     logits = zipf_logits_torch(torch, tg, m, perm_gen=pg)
-    if args.ep_placement == "balanced":
-        # one routing pass measures the expert load; the placement is fixed from then on
-        probe = ep.CudaOps(ctx, None, None, None, E, rank, ws)
-        ids, _ = probe.route(logits)
-        counts, _, _ = probe.sort(ids, m)
-        load = ep.gather_counts(counts, ws).sum(axis=0)
-        table, experts = ep.place_experts(load, ws)
-        sl = {k: ep.placed_slice(layer[k], experts[rank], E) for k in ("gate", "up", "down")}
-        ops = ep.CudaOps(ctx, sl["gate"], sl["up"], sl["down"], E, rank, ws, placement=table)
+    # one routing pass measures the load; the placement is fixed from then on
+    ids = torch.zeros((m, 4), dtype=torch.int32, device="cuda")
+    gw = torch.empty((m, 4), dtype=torch.bfloat16, device="cuda")
+    lfm.moe_route_batch(ctx, logits, None, ids, gw, m)
+    mine = torch.bincount(ids.view(-1).long(), minlength=E).to(torch.int64)
+    loads = [torch.zeros_like(mine) for _ in range(ws)]
+    dist.all_gather(loads, mine)
+    load = torch.stack(loads).cpu().numpy().astype(np.uint64)
+    spr = E // ws + (args.ep_spare if args.ep_placement == "balanced" else 0)
+    if args.ep_placement == "contiguous":
+        tables = np.tile(np.arange(E, dtype=np.uint32), (ws, 1))
+        slot_expert = np.arange(E, dtype=np.int32)
     else:
-        sl = {k: ep.expert_slice(layer[k], rank, ws, E) for k in ("gate", "up", "down")}
-        ops = ep.CudaOps(ctx, sl["gate"], sl["up"], sl["down"], E, rank, ws)
+        tables, slot_expert = ep.place_slots(load, ws, spr)
+    own = slot_expert[rank * spr:(rank + 1) * spr]
+    gate, up, down = (ep.slot_weights(layer[k], own, E) for k in ("gate", "up", "down"))
     del layer
-    px = None
-    if args.ep_exchange == "peer":
-        px = ep.PeerExchange(ctx, rank, ws, m, H, I, E)
-        step = lambda: (ep.moe_prefill_ep_peer(ops, px, x, logits), None)
-    else:
-        step = lambda: ep.moe_prefill_ep(ops, x, logits, rank, ws)
+    table = torch.from_numpy(tables[rank].view(np.int32).copy()).cuda()
+    out = torch.empty((m, H), dtype=torch.bfloat16, device="cuda")
+    epp = ep.EpPrefill(ctx, rank, ws)
+    epp.reserve(m, E, spr, H, I)
+    step = lambda: epp.step(x, logits, gate, up, down, table, out)
     K, W = args.steps, max(args.warmup, 3)
     for _ in range(W):
-        out, plan = step()
-    torch.cuda.synchronize()
-    st = int(ops.status.cpu()[0]) | (int(px.status.cpu()[0]) if px else 0)
+        step()
+    st = epp.status()
     if st:
-        raise RuntimeError(f"exchange / grouped GEMM status {st}")
+        raise RuntimeError(f"expert-parallel step status {st}")
     barrier(ws)
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clk:
         a.record()
         for _ in range(K):
-            out, plan = step()
+            step()
         b.record()
         torch.cuda.synchronize()
     ms_ = max_over_ranks(ws, a.elapsed_time(b))
     value = ws * m * K / (ms_ * 1e-3)
-    # rows this rank computed and rows that crossed NVLink (each way), per step
-    if px is not None:
-        ca = px.counts_all.cpu().numpy().astype(np.int64)
-        per = E // ws
-        recv_rows = int(ca[:, rank * per:(rank + 1) * per].sum())
-        remote = int(ca[rank].sum() - ca[rank, rank * per:(rank + 1) * per].sum())
-    else:
-        recv_rows = plan.recv_rows
-        remote = sum(n for peer, _, n in plan.send if peer != rank)
-    loads = torch.tensor([recv_rows, remote], dtype=torch.float64, device="cuda")
-    lmax, lmin = loads.clone(), loads.clone()
-    dist.all_reduce(lmax, op=dist.ReduceOp.MAX)
-    dist.all_reduce(lmin, op=dist.ReduceOp.MIN)
+    st = epp.status()
+    # per rank: rows its slots computed, rows it sent over NVLink, phase times
+    counts = epp.counts().astype(np.int64)          # [ws][ws * spr]
+    recv_rows = int(counts[:, rank * spr:(rank + 1) * spr].sum())
+    sent_remote = int(counts[rank].sum() - counts[rank, rank * spr:(rank + 1) * spr].sum())
+    epp.set_profile(True)
+    step()
+    phases = epp.phase_ms()
+    epp.set_profile(False)
+    per_rank = [None] * ws
+    dist.all_gather_object(per_rank, {"rank": rank, "rows_computed": recv_rows,
+                                      "rows_sent_remote": sent_remote,
+                                      "phase_ms": {k: round(v, 4) for k, v in phases.items()}})
     # e2e: host rows in, host rows out, through the same call
     hx, hl = x.cpu().pin_memory(), logits.cpu().pin_memory()
     hout = torch.empty((m, H), dtype=torch.bfloat16).pin_memory()
@@ -666,41 +692,43 @@ def bench_cfg3_ep(args, torch, ws, rank, local):
     for _ in range(n_e2e):
         x.copy_(hx, non_blocking=True)
         logits.copy_(hl, non_blocking=True)
-        out, _ = step()
+        step()
         hout.copy_(out, non_blocking=True)
     e1.record()
     torch.cuda.synchronize()
     e2e_ms = max_over_ranks(ws, e0.elapsed_time(e1))
-    if px is not None:
-        px.close()
+    st |= epp.status()
+    epp.finalize()
+    if st:
+        raise RuntimeError(f"expert-parallel step status {st}")
     _, bf16_peak, src = peaks()
-    useful = prefill_flops(4 * m)                   # per rank per step (weak scaling)
+    rows_max = max(r["rows_computed"] for r in per_rank)
+    useful = prefill_flops(rows_max)                # the busiest rank's GEMM work
     achieved = useful / (ms_ / K * 1e-3) / 1e12
     return {
-        "metric": "prefill grouped-GEMM tokens/s (cfg3: 4096-token MoE FFN, Zipf routing)",
+        "metric": CFG3_METRIC,
         "value": round(value, 1), "unit": "tokens/s", "n_gpus": ws, "steps": K, "warmup": W,
         "ms_per_step": round(ms_ / K, 4), "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "q4 weights dequantised to bf16, bf16 x bf16 -> fp32 tcgen05",
         "data": "synthetic (seeded; Zipf(s=1) + Gumbel router logits sharing one expert "
                 "popularity order across ranks, random-init weights)",
-        "config": {"workload": f"cfg3 expert-parallel: {m} tokens per rank x 2048, E=64 top-4 "
-                               f"({E // ws} experts per GPU), SwiGLU 2048->1536->2048 Q4",
-                   "parallelism": f"ep{ws}",
-                   "placement": ("greedy by the expert load of one routing pass"
+        "config": {"workload": CFG3_WORKLOAD, "parallelism": f"ep{ws}",
+                   "slots_per_rank": spr,
+                   "placement": ("greedy by the expert load of one routing pass, hot experts "
+                                 "replicated in the spare slots (mc_ep_place)"
                                  if args.ep_placement == "balanced" else "contiguous ranges"),
-                   "exchange": ("rows copied into the owners' buffers over NVLink peer memory "
-                                "(CUDA IPC), in-stream NCCL barriers, no host sync"
-                                if px is not None else "NCCL point-to-point rows both ways"),
-                   "rows_computed_per_rank_max_min": [int(lmax[0]), int(lmin[0])],
-                   "rows_sent_remote_per_rank_max": int(lmax[1]),
+                   "exchange": "one library call per step (mc_ep_moe_prefill): NCCL counts "
+                               "all-gather, rows stored into the owners' buffers over NVLink "
+                               "(CUDA IPC), device-side bounded barriers, no host sync",
+                   "per_rank": per_rank,
                    "l2": "expert weights > L2, streamed every step"},
         "e2e": {"value": round(ws * m * n_e2e / (e2e_ms * 1e-3), 1), "unit": "tokens/s",
                 "h2d_bytes_per_step": m * H * 2 + m * E * 4, "d2h_bytes_per_step": m * H * 2},
-        "roofline": {"bound": "tensor", "kernel": "whole EP step per GPU (grouped GEMMs + "
-                     "exchange + dispatch)", "achieved": round(achieved, 1), "peak": bf16_peak,
+        "roofline": {"bound": "tensor", "kernel": "whole EP step, busiest rank (grouped GEMMs "
+                     "+ exchange + barriers)", "achieved": round(achieved, 1), "peak": bf16_peak,
                      "unit": "TFLOP/s", "frac": round(achieved / bf16_peak, 4),
                      "peak_source": f"{src} bf16_tflops (burst)", "traffic": None},
-        "gpu_launches": (10 if args.ep_exchange == "peer" else 9) * K,
+        "gpu_launches": EP_STEP_LAUNCHES * K,
         "clocks": clk.summary(),
     }
 
@@ -770,13 +798,13 @@ def bench_cfg3(args, torch, ws, rank, local):
     torch.cuda.synchronize()
     e2e_ms = max_over_ranks(ws, max(e0.elapsed_time(e1), (time.perf_counter() - t0) * 1e3))
     res = {
-        "metric": "prefill grouped-GEMM tokens/s (cfg3: 4096-token MoE FFN, Zipf routing)",
+        "metric": CFG3_METRIC,
         "value": round(value, 1), "unit": "tokens/s", "n_gpus": ws, "steps": K, "warmup": W,
         "ms_per_step": round(ms_ / K, 4), "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "q4 weights dequantised to bf16, bf16 x bf16 -> fp32 tcgen05",
         "data": "synthetic (seeded; Zipf(s=1) + Gumbel router logits, random-init weights)",
-        "config": {"workload": f"cfg3: {m} tokens x 2048, E=64 top-4, SwiGLU 2048->1536->2048 Q4",
-                   "pairs": S, "row_tiles": n_tiles, "useful_gflop_per_step": prefill_flops(S) / 1e9,
+        "config": {"workload": CFG3_WORKLOAD, "parallelism": "single GPU (mc_moe_prefill)",
+                   "tokens": m, "pairs": S, "row_tiles": n_tiles, "useful_gflop_per_step": prefill_flops(S) / 1e9,
                    "l2": "expert weights 340 MB > L2, streamed every step"},
         "e2e": {"value": round(ws * m * n_e2e / (e2e_ms * 1e-3), 1), "unit": "tokens/s",
                 "h2d_bytes_per_step": m * H * 2 + m * E * 4, "d2h_bytes_per_step": m * H * 2},
@@ -958,7 +986,9 @@ def bench_cfg4(args, torch, ws, rank, local):
 # ------------------------------------------------------------------ reference arm
 
 def bench_reference(args, ws, rank):
-    """The CPU port of the path on all host cores, cfg1 metric and config."""
+    """The CPU port of the path on all host cores (the reference itself is
+    Metal-only), on the same workload, metric and unit as the molten arm:
+    cfg1 decode GB/s, or cfg3 prefill tokens/s. Rank 0 only."""
     if rank != 0:
         return None
     import torch
@@ -969,8 +999,23 @@ def bench_reference(args, ws, rank):
     W = max(args.warmup, 1)
     K = args.steps
     secs = min(args.cpu_seconds, 60.0)
-    # bounded sample: each "step" is a fixed-duration slice of layer-tokens
+    # bounded sample: each "step" is a fixed-duration slice of work
     per_step = max(secs / max(K, 1), 0.05)
+    if args.workload == "cfg3":
+        x = torch.randn((256, H), generator=gen).to(torch.bfloat16)
+        logits = zipf_logits_torch(torch, gen, 256, device="cpu")
+        r = cpu_baseline_prefill(torch, layer, x, logits, per_step * min(K, 200))
+        v = r["value"]
+        return {
+            "metric": CFG3_METRIC, "value": v, "unit": "tokens/s", "n_gpus": ws, "steps": K,
+            "warmup": W, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "impl": "reference", "dtype": "q4 weights dequantised to bf16, fp32 accumulate",
+            "data": "synthetic (seeded; Zipf(s=1) + Gumbel router logits)",
+            "config": {"workload": CFG3_WORKLOAD},
+            "cpu_baseline": r,
+            "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0},
+        }
     r = cpu_baseline_cfg1(torch, layer, per_step * min(K, 200))
     v = r["value"]
     return {
@@ -987,8 +1032,18 @@ def bench_reference(args, ws, rank):
     }
 
 
+def node_gpus() -> int:
+    import torch
+    return torch.cuda.device_count() if torch.cuda.is_available() else 0
+
+
 def main():
     args = parse()
+    if args.workload == "auto":
+        # the decode layer on a one-GPU node; on a node with several GPUs the
+        # prefill FFN, the one path that shards, at every --gpus N (N = 1
+        # runs the single-GPU prefill, the base of the scaling curve)
+        args.workload = "cfg3" if node_gpus() > 1 else "cfg1"
     if args.impl == "reference":
         ws = int(os.environ.get("WORLD_SIZE", "1"))
         rank = int(os.environ.get("RANK", "0"))

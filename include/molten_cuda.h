@@ -440,6 +440,12 @@ int mc_ep_status(mc_ctx* ctx, uint32_t* out);
 /* The last step's all-gathered pair counts [W][W * spr] (host copy; waits). */
 int mc_ep_counts(mc_ctx* ctx, uint32_t* out, size_t n);
 int mc_ep_finalize(mc_ctx* ctx);
+/* Profiling aid: with `on`, each step records events at its phase
+ * boundaries; mc_ep_phase_ms waits and writes the last step's six phase
+ * times in ms (route + relabel + sort, counts all-gather, row chunks +
+ * dispatch + barrier, grouped GEMMs, return + barrier, combine). */
+int mc_ep_set_profile(mc_ctx* ctx, int on);
+int mc_ep_phase_ms(mc_ctx* ctx, float* out6);
 
 /* Cross-layer prefetch hint (no reference counterpart): the next
  * mc_moe_decode_layer (or _noalloc) launched on ctx prefetches the byte

@@ -102,6 +102,8 @@ SIGNATURES: dict[str, tuple] = {
     "mc_ep_status": (I, [P, P]),
     "mc_ep_counts": (I, [P, P, C.c_size_t]),
     "mc_ep_finalize": (I, [P]),
+    "mc_ep_set_profile": (I, [P, I]),
+    "mc_ep_phase_ms": (I, [P, P]),
     "mc_ep_return": (I, [P, P, C.c_size_t, I, P, I, I, I, P, C.c_size_t, P]),
     "mc_moe_decode_layer_noalloc": (I, [P, P, P, P, P, P, P, I, P, I, P, P, P, QP, QP, QP, I, P,
                                         P, F, F]),

@@ -45,6 +45,10 @@ namespace {
 constexpr int kMaxRanks = 8;
 constexpr int kChunk = 256;  // token rows per grouped-GEMM chunk
 constexpr unsigned long long kBarrierNs = 1000000000ull;  // default barrier limit: 1 s
+// Phases of a step timed by mc_ep_set_profile: route + relabel + sort, the
+// counts all-gather, row chunks + dispatch + barrier, the two grouped GEMMs,
+// return + barrier, combine.
+constexpr int kPhases = 6;
 
 // ------------------------------------------------------------ NCCL at run time
 struct NcclApi {
@@ -115,6 +119,9 @@ struct mc_ep_state {
   uint32_t *counts_all, *tiles, *n_tiles, *rows, *status, *epoch;
   uint16_t *gw, *act, *ed;
   int sort_max_tiles = 0, max_tiles = 0;
+  // phase timing (mc_ep_set_profile): events at the step's phase boundaries
+  int profile = 0;
+  cudaEvent_t ev[kPhases + 1] = {};
 };
 
 namespace {
@@ -195,6 +202,11 @@ int ep_barrier(mc_ctx* ctx) {
 }
 
 void free_state(mc_ep_state* ep, bool close_peers) {
+  for (int k = 0; k <= kPhases; ++k)
+    if (ep->ev[k]) {
+      cudaEventDestroy(ep->ev[k]);
+      ep->ev[k] = nullptr;
+    }
   if (close_peers)
     for (int r = 0; r < ep->world; ++r)
       if (r != ep->rank && ep->peer_base[r]) cudaIpcCloseMemHandle(ep->peer_base[r]);
@@ -377,6 +389,11 @@ extern "C" int mc_ep_moe_prefill(mc_ctx* ctx, const uint16_t* x, const float* lo
   const NcclApi* api = nccl();
   const int S = 4 * m, W = ep->world;
   int rc;
+  auto mark = [&](int k) -> int {
+    if (ep->profile) MC_CUDA(cudaEventRecord(ep->ev[k], ctx->stream));
+    return MC_OK;
+  };
+  if ((rc = mark(0))) return rc;
   if ((rc = mc_moe_route_batch(ctx, logits, m, ep->E, route_mode, expert_bias, 1e-6f, ep->ids,
                                ep->gw)))
     return rc;
@@ -385,11 +402,13 @@ extern "C" int mc_ep_moe_prefill(mc_ctx* ctx, const uint16_t* x, const float* lo
                             ep->ids_sorted, ep->slotpos, ep->sort_tiles, ep->sort_ntiles,
                             ep->sort_max_tiles)))
     return rc;
+  if ((rc = mark(1))) return rc;
   if ((rc = nccl_settle(ctx,
                         api->all_gather(ep->counts, ep->counts_all, (size_t)ep->E_slots,
                                         ncclUint32, ep->comm, ctx->stream),
                         "ep_moe_prefill counts all-gather")))
     return rc;
+  if ((rc = mark(2))) return rc;
   if ((rc = mc_ep_tiles(ctx, ep->counts_all, ep->rank, W, ep->E_slots, kChunk, ep->tiles,
                         ep->n_tiles, ep->rows, ep->max_tiles)))
     return rc;
@@ -397,6 +416,7 @@ extern "C" int mc_ep_moe_prefill(mc_ctx* ctx, const uint16_t* x, const float* lo
                            ep->E_slots, ep->recv_ptr, ep->recv_cap, ep->status)))
     return rc;
   if ((rc = ep_barrier(ctx))) return rc;
+  if ((rc = mark(3))) return rc;
   uint16_t* recv = static_cast<uint16_t*>(ep->recv_ptr[ep->rank]);
   const int rows = (int)ep->recv_cap;
   if ((rc = mc_gemm_q4_grouped_gu(ctx, recv, rows, gate, up, ep->spr, ep->act, ep->tiles,
@@ -405,12 +425,35 @@ extern "C" int mc_ep_moe_prefill(mc_ctx* ctx, const uint16_t* x, const float* lo
   if ((rc = mc_gemm_q4_grouped(ctx, ep->act, rows, down, ep->spr, ep->ed, ep->tiles, ep->n_tiles,
                                ep->max_tiles, ep->status)))
     return rc;
+  if ((rc = mark(4))) return rc;
   if ((rc = mc_ep_return(ctx, ep->ed, ep->recv_cap, ep->H, ep->counts_all, ep->rank, W,
                          ep->E_slots, ep->home_ptr, ep->home_cap, ep->status)))
     return rc;
   if ((rc = ep_barrier(ctx))) return rc;
-  return mc_moe_combine_rows(ctx, static_cast<uint16_t*>(ep->home_ptr[ep->rank]), ep->slotpos,
-                             ep->gw, out, m, 4, ep->H);
+  if ((rc = mark(5))) return rc;
+  if ((rc = mc_moe_combine_rows(ctx, static_cast<uint16_t*>(ep->home_ptr[ep->rank]), ep->slotpos,
+                                ep->gw, out, m, 4, ep->H)))
+    return rc;
+  return mark(6);
+}
+
+extern "C" int mc_ep_set_profile(mc_ctx* ctx, int on) {
+  MC_REQUIRE(ctx && ctx->ep, "ep_set_profile: call mc_ep_init first");
+  mc_ep_state* ep = ctx->ep;
+  if (on && !ep->ev[0])
+    for (int k = 0; k <= kPhases; ++k) MC_CUDA(cudaEventCreate(&ep->ev[k]));
+  ep->profile = on ? 1 : 0;
+  return MC_OK;
+}
+
+extern "C" int mc_ep_phase_ms(mc_ctx* ctx, float* out) {
+  MC_REQUIRE(ctx && ctx->ep && out, "ep_phase_ms: bad arguments");
+  mc_ep_state* ep = ctx->ep;
+  MC_REQUIRE(ep->ev[0], "ep_phase_ms: profiling was never switched on");
+  int rc = mc_sync(ctx);
+  if (rc) return rc;
+  for (int k = 0; k < kPhases; ++k) MC_CUDA(cudaEventElapsedTime(out + k, ep->ev[k], ep->ev[k + 1]));
+  return MC_OK;
 }
 
 extern "C" int mc_ep_status(mc_ctx* ctx, uint32_t* out) {

@@ -522,6 +522,19 @@ class EpPrefill:
         self.lib.call("mc_ep_counts", self.ctx.handle, a.ctypes.data_as(C.c_void_p), n)
         return a.reshape(self.world, self.world * self.spr)
 
+    def set_profile(self, on: bool) -> None:
+        self.lib.call("mc_ep_set_profile", self.ctx.handle, 1 if on else 0)
+
+    PHASES = ("route_sort", "counts_allgather", "dispatch_barrier", "gemms", "return_barrier",
+              "combine")
+
+    def phase_ms(self) -> dict:
+        """The last profiled step's phase times (ms)."""
+        import ctypes as C
+        a = (C.c_float * 6)()
+        self.lib.call("mc_ep_phase_ms", self.ctx.handle, a)
+        return {k: float(v) for k, v in zip(self.PHASES, a)}
+
     def finalize(self) -> None:
         if self.ctx is not None and self.ctx.h:
             self.lib.call("mc_ep_finalize", self.ctx.handle)
