@@ -81,6 +81,8 @@ def parse():
     p.add_argument("--tokens", type=int, default=4096, help="cfg3 prefill chunk")
     p.add_argument("--ep-placement", choices=["balanced", "contiguous"], default="balanced",
                    help="cfg3 on N>1 GPUs: expert-to-GPU placement")
+    p.add_argument("--ep", action="store_true",
+                   help="cfg3: the expert-parallel step even on one GPU (a one-rank communicator)")
     p.add_argument("--ep-spare", type=int, default=1,
                    help="cfg3 on N>1 GPUs: spare expert slots per GPU (hot-expert replicas)")
     p.add_argument("--seed", type=int, default=0)
@@ -734,7 +736,7 @@ def bench_cfg3_ep(args, torch, ws, rank, local):
 
 
 def bench_cfg3(args, torch, ws, rank, local):
-    if ws > 1:
+    if ws > 1 or args.ep:
         return bench_cfg3_ep(args, torch, ws, rank, local)
     from molten_b200 import lfm, synth
     ctx = lfm.Context(local)

@@ -385,6 +385,88 @@ inline void moe_prefill(Context& ctx, const Tensor& x, const Tensor& logits,
                        workspace.data, workspace.nbytes(), out.as<uint16_t>()));
 }
 
+// proj3_gemv_scatter (kernels/lfm.rs:150-205): Q, K, V projections of one
+// row in one launch, V written into the KV cache [nv/64][max_seq][64] at pos.
+inline void proj3_gemv_scatter(Context& ctx, const QuantWeights& q, const QuantWeights& k,
+                               const QuantWeights& v, const Tensor& x, const Tensor& q_out,
+                               const Tensor& k_out, const Tensor& v_cache, int pos) {
+  const int64_t kdim = x.numel();
+  const int64_t nq = q.out_features(), nk = k.out_features(), nv = v.out_features();
+  ensure(q.in_features() == kdim && k.in_features() == kdim && v.in_features() == kdim,
+         "proj3 input width");
+  ensure(q.bits == 4 && k.bits == 4 && v.bits == 4 && q.group_size == 64 &&
+             k.group_size == 64 && v.group_size == 64,
+         "proj3 is affine 4-bit/64");
+  ensure(kdim == 2048, "proj3 input width is the compile-time hidden size");
+  ensure(q_out.numel() == nq && k_out.numel() == nk && nv % 64 == 0, "proj3 output shape");
+  ensure(x.dtype == DType::BF16 && q_out.dtype == DType::BF16 && k_out.dtype == DType::BF16,
+         "proj3 BF16");
+  ensure(v_cache.shape.size() == 3 && v_cache.dim(0) * 64 == nv && v_cache.dim(2) == 64 &&
+             pos >= 0 && pos < v_cache.dim(1),
+         "proj3 KV cache shape");
+  check_quant(q);
+  check_quant(k);
+  check_quant(v);
+  const mc_qweights a = q.abi(), b = k.abi(), c = v.abi();
+  check(mc_proj3_gemv_scatter(ctx.handle(), &a, &b, &c, x.as<const uint16_t>(),
+                              q_out.as<uint16_t>(), k_out.as<uint16_t>(), v_cache.as<uint16_t>(),
+                              (int)v_cache.dim(1), pos));
+}
+
+// conv3_gemv (kernels/lfm.rs:207-246): short-conv B/C/X projection and the
+// conv; w taps [H][3], state and new_state [2][H].
+inline void conv3_gemv(Context& ctx, const QuantWeights& wproj, const Tensor& x, const Tensor& w,
+                       const Tensor& state, const Tensor& out, const Tensor& new_state) {
+  const int64_t kdim = x.numel(), h = out.numel();
+  ensure(wproj.out_features() == 3 * h && wproj.in_features() == kdim, "conv3 projection shape");
+  ensure(wproj.bits == 4 && wproj.group_size == 64, "conv3 projection 4-bit/64");
+  ensure(kdim == 2048, "conv3 input width is the compile-time hidden size");
+  ensure(w.numel() == 3 * h, "conv3 tap shape");
+  ensure(state.shape == std::vector<int64_t>{2, h} && new_state.shape == std::vector<int64_t>{2, h},
+         "conv3 state shape");
+  check_quant(wproj);
+  const mc_qweights q = wproj.abi();
+  check(mc_conv3_gemv(ctx.handle(), &q, x.as<const uint16_t>(), w.as<const uint16_t>(),
+                      state.as<const uint16_t>(), out.as<uint16_t>(), new_state.as<uint16_t>(),
+                      (int)h));
+}
+
+// gemv_gu_act (kernels/lfm.rs:462-495): dense FFN front half.
+inline void gemv_gu_act(Context& ctx, const QuantWeights& gate, const QuantWeights& up,
+                        const Tensor& x, const Tensor& act) {
+  const int64_t n = gate.out_features(), k = gate.in_features();
+  ensure(gate.bits == 4 && up.bits == 4, "dense gate/up must be 4-bit");
+  ensure(up.out_features() == n && up.in_features() == k && up.group_size == gate.group_size,
+         "dense gate/up shapes");
+  ensure(x.numel() % k == 0 && act.numel() == x.numel() / k * n, "dense gate/up rows");
+  ensure(x.dtype == DType::BF16 && act.dtype == DType::BF16, "dense gate/up BF16");
+  check_quant(gate);
+  check_quant(up);
+  const mc_qweights g = gate.abi(), u = up.abi();
+  check(mc_gemv_gu_act(ctx.handle(), &g, &u, x.as<const uint16_t>(), act.as<uint16_t>(),
+                       (int)(x.numel() / k)));
+}
+
+// SampleScratch::encode_draw / encode_mark (lfm/sample.rs:248-353): the
+// sampled token of position pos into the zeroed argmax key `best`, read and
+// cleared by token_tail; the workspace of mc_sample_workspace_bytes(vocab)
+// bytes is zeroed once by the caller.
+inline void sample_draw(Context& ctx, const Tensor& logits, const Tensor* seen,
+                        const mc_sampling& s, uint32_t pos, const Tensor& best,
+                        const Tensor& workspace) {
+  ensure(logits.dtype == DType::BF16, "sampling logits row");
+  ensure(best.dtype == DType::U64 && best.numel() >= 1, "sampling key");
+  ensure(s.repetition_penalty == 1.0f || seen, "a repetition penalty needs the seen set");
+  check(mc_sample_draw(ctx.handle(), logits.as<const uint16_t>(), (int)logits.numel(),
+                       seen ? seen->as<const uint32_t>() : nullptr, &s, pos,
+                       best.as<unsigned long long>(), workspace.data, workspace.nbytes()));
+}
+
+inline void sample_mark(Context& ctx, const Tensor& tok, const Tensor& seen, int vocab) {
+  ensure(tok.numel() == 1 && tok.dtype == DType::U32, "sampled token slot");
+  check(mc_sample_mark(ctx.handle(), tok.as<const uint32_t>(), seen.as<uint32_t>(), vocab));
+}
+
 // Tensor::write_bytes / contents (tensor.rs:127-146, 165-200): stream-ordered
 // copy between device memory and page-locked host memory.
 inline void copy_async(Context& ctx, void* dst, const void* src, size_t bytes) {

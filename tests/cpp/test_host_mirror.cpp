@@ -161,6 +161,37 @@ int main() {
     }
   }
 
+  // decode neighbours and the sampling draw: each check fires, then the ABI
+  {
+    QuantWeights q{Tensor(p, {2048, 256}, DType::U32), Tensor(p, {2048, 32}, DType::BF16),
+                   Tensor(p, {2048, 32}, DType::BF16), 64, 4};
+    QuantWeights kv{Tensor(p, {512, 256}, DType::U32), Tensor(p, {512, 32}, DType::BF16),
+                    Tensor(p, {512, 32}, DType::BF16), 64, 4};
+    const Tensor x1(p, {2048}, DType::BF16), qo(p, {2048}, DType::BF16), ko(p, {512}, DType::BF16);
+    expect_error("proj3 cache shape", MC_EINVAL, "proj3 KV cache shape", [&] {
+      molten::kernels::proj3_gemv_scatter(ctx, q, kv, kv, x1, qo, ko,
+                                          Tensor(p, {8, 16, 64}, DType::BF16), 16);
+    });
+    expect_error("proj3 reaches the ABI", MC_EINVAL, "null context", [&] {
+      molten::kernels::proj3_gemv_scatter(ctx, q, kv, kv, x1, qo, ko,
+                                          Tensor(p, {8, 16, 64}, DType::BF16), 3);
+    });
+    QuantWeights c3{Tensor(p, {3 * 64, 256}, DType::U32), Tensor(p, {3 * 64, 32}, DType::BF16),
+                    Tensor(p, {3 * 64, 32}, DType::BF16), 64, 4};
+    expect_error("conv3 state shape", MC_EINVAL, "conv3 state shape", [&] {
+      molten::kernels::conv3_gemv(ctx, c3, x1, Tensor(p, {64, 3}, DType::BF16),
+                                  Tensor(p, {3, 64}, DType::BF16), Tensor(p, {64}, DType::BF16),
+                                  Tensor(p, {2, 64}, DType::BF16));
+    });
+    expect_error("gu_act rows", MC_EINVAL, "dense gate/up rows", [&] {
+      molten::kernels::gemv_gu_act(ctx, q, q, x1, Tensor(p, {100}, DType::BF16));
+    });
+    mc_sampling sp{1.0f, 0, 1.0f, 1.5f, 7};
+    expect_error("sampling needs the seen set", MC_EINVAL, "needs the seen set", [&] {
+      molten::kernels::sample_draw(ctx, Tensor(p, {65536}, DType::BF16), nullptr, sp, 0,
+                                   Tensor(p, {1}, DType::U64), Tensor(p, {64}, DType::U32));
+    });
+  }
   std::printf("%s (%d failures)\n", failures ? "FAILED" : "ok", failures);
   return failures ? 1 : 0;
 }
