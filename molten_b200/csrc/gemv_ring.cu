@@ -27,7 +27,7 @@ constexpr int kRows = 16;                  // rows per stage, one per compute wa
 constexpr int kComputeWarps = kRows;
 constexpr int kThreads = (kComputeWarps + 1) * 32;  // + the producer warp
 constexpr int kMaxStages = 8;
-constexpr unsigned long long kTimeoutNs = 200000000ull;
+constexpr unsigned long long kTimeoutNs = 200000000ull;  // default limit per wait: 200 ms
 
 template <int BITS>
 struct RingShape {
@@ -51,7 +51,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 gemv_ring_kernel(const uint8_t* __restrict__ codes, const uint16_t* __restrict__ scales,
                  const uint16_t* __restrict__ biases, const uint16_t* __restrict__ x,
                  uint16_t* __restrict__ y, unsigned long long* __restrict__ keys, int N,
-                 unsigned int* __restrict__ status) {
+                 unsigned int* __restrict__ status, unsigned long long timeout_ns) {
   using S = RingShape<BITS>;
   extern __shared__ __align__(128) uint8_t sm[];
   __shared__ __align__(8) uint64_t full[kMaxStages], empty[kMaxStages];
@@ -70,7 +70,7 @@ gemv_ring_kernel(const uint8_t* __restrict__ codes, const uint16_t* __restrict__
   }
   __syncthreads();
   mc_pdl_launch_dependents();
-  const unsigned long long deadline = mc_globaltimer() + kTimeoutNs;
+  const unsigned long long deadline = mc_globaltimer() + timeout_ns;
 
   if (warp == kComputeWarps) {
     // ---- producer: stage s goes to slot s % kStages once the compute warps
@@ -97,7 +97,7 @@ gemv_ring_kernel(const uint8_t* __restrict__ codes, const uint16_t* __restrict__
       // compute warp gave up)
       const int first = nst > S::kStages ? nst - S::kStages : 0;
       for (int s = first; s < nst; ++s)
-        ok = ring_wait(full + s % S::kStages, (s / S::kStages) & 1, deadline + kTimeoutNs) && ok;
+        ok = ring_wait(full + s % S::kStages, (s / S::kStages) & 1, deadline + timeout_ns) && ok;
       if (!ok) atomicOr(status, 1u);
     }
     return;
@@ -184,7 +184,7 @@ int launch_ring(mc_ctx* ctx, const mc_qweights* w, const uint16_t* x, uint16_t* 
   unsigned int* status = status_of[dev];
   MC_CUDA(mc_launch_pdl(fn, dim3(ctx->num_sms), dim3(kThreads), S::kSmem, ctx->stream,
                         reinterpret_cast<const uint8_t*>(w->codes), w->scales, w->biases, x, y,
-                        keys, w->out_features, status));
+                        keys, w->out_features, status, mc_wait_limit(ctx, kTimeoutNs)));
   return mc_after_launch("gemv_ring_kernel");
 }
 

@@ -54,7 +54,7 @@ constexpr int BK = 64;     // K per stage
 constexpr int MAXN = 256;  // token rows per chunk (the MMA's N, rounded up to 16)
 constexpr int kDeqThreads = 256;
 constexpr int kThreads = 64 + kDeqThreads;
-constexpr unsigned long long kTimeoutNs = 1000000000ull;  // 1 s per wait
+constexpr unsigned long long kTimeoutNs = 1000000000ull;  // default limit per wait: 1 s
 
 template <bool GU>
 struct Cfg {
@@ -81,6 +81,7 @@ struct GemmParams {
   const uint32_t* n_tiles;
   uint32_t* status;
   int N, K, rows, max_tiles, n_experts;
+  unsigned long long timeout_ns;  // limit of every bounded wait (mc_set_wait_limit)
 };
 
 // One work item: token rows [m0, mend) of expert e against feature block nb.
@@ -181,9 +182,10 @@ __device__ __forceinline__ void tmem_wait_ld() {
 
 // Bounded mbarrier wait that also gives up when another role aborted. The
 // clock is read only once the barrier was found incomplete.
-__device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t parity, volatile uint32_t* abort_f) {
+__device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t parity, volatile uint32_t* abort_f,
+                                         unsigned long long timeout_ns) {
   if (mc_mbar_test_sleep(bar, parity, 20000u)) return true;
-  const unsigned long long deadline = mc_globaltimer() + kTimeoutNs;
+  const unsigned long long deadline = mc_globaltimer() + timeout_ns;
   while (!mc_mbar_test_sleep(bar, parity, 20000u)) {
     if (*abort_f) return false;
     if (mc_globaltimer() > deadline) return false;
@@ -192,8 +194,9 @@ __device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t parity, volatil
 }
 
 // The same wait for a whole warp, with one answer for all lanes.
-__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volatile uint32_t* abort_f) {
-  return __all_sync(0xffffffffu, wait_bar(bar, parity, abort_f));
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volatile uint32_t* abort_f,
+                                          unsigned long long timeout_ns) {
+  return __all_sync(0xffffffffu, wait_bar(bar, parity, abort_f, timeout_ns));
 }
 
 // One lane of a converged warp (the lowest), chosen with elect.sync.
@@ -342,7 +345,7 @@ grouped_gemm_kernel(const __grid_constant__ TokenMaps tm, const GemmParams P) {
       for (int kk = 0; kk < ksteps; ++kk, ++it) {
         const int s = it % C::BSTAGES;
         const uint32_t ph = (it / C::BSTAGES) & 1;
-        if (!warp_wait(&bempty[s], ph ^ 1, &abort_s)) {
+        if (!warp_wait(&bempty[s], ph ^ 1, &abort_s, P.timeout_ns)) {
           ok = false;
           break;
         }
@@ -374,7 +377,7 @@ grouped_gemm_kernel(const __grid_constant__ TokenMaps tm, const GemmParams P) {
       const uint32_t idesc = idesc_for(w.n);
       const int buf = (int)(j % C::NBUF);
       const uint32_t use = j / C::NBUF;
-      if (!warp_wait(&acc_empty[buf], (use & 1) ^ 1, &abort_s)) {
+      if (!warp_wait(&acc_empty[buf], (use & 1) ^ 1, &abort_s, P.timeout_ns)) {
         if (lane == 0) abort_s = 1;
         break;
       }
@@ -383,8 +386,8 @@ grouped_gemm_kernel(const __grid_constant__ TokenMaps tm, const GemmParams P) {
       bool ok = true;
       for (int kk = 0; kk < ksteps; ++kk, ++it) {
         const int sb = it % C::BSTAGES, sa = it % C::ASTAGES;
-        if (!warp_wait(&bfull[sb], (it / C::BSTAGES) & 1, &abort_s) ||
-            !warp_wait(&afull[sa], (it / C::ASTAGES) & 1, &abort_s)) {
+        if (!warp_wait(&bfull[sb], (it / C::BSTAGES) & 1, &abort_s, P.timeout_ns) ||
+            !warp_wait(&afull[sa], (it / C::ASTAGES) & 1, &abort_s, P.timeout_ns)) {
           ok = false;
           break;
         }
@@ -463,7 +466,7 @@ grouped_gemm_kernel(const __grid_constant__ TokenMaps tm, const GemmParams P) {
     auto do_slice = [&](const uint4* c, uint32_t itk, float sc, float bi) -> bool {
       const int s = itk % C::ASTAGES;
       const uint32_t ph = (itk / C::ASTAGES) & 1;
-      if (!warp_wait(&aempty[s], ph ^ 1, &abort_s)) return false;
+      if (!warp_wait(&aempty[s], ph ^ 1, &abort_s, P.timeout_ns)) return false;
       uint8_t* row = a_ring + s * C::A_STAGE + (GU ? grp * C::A_BYTES : 0) + d * 128;
       uint32_t W[4 * NU];
 #pragma unroll
@@ -515,7 +518,7 @@ grouped_gemm_kernel(const __grid_constant__ TokenMaps tm, const GemmParams P) {
       // ---- epilogue: TMEM [feature][token] -> bf16 out[token][feature]
       const int buf = (int)(j % C::NBUF);
       const uint32_t use = j / C::NBUF;
-      if (!warp_wait(&acc_full[buf], use & 1, &abort_s)) {
+      if (!warp_wait(&acc_full[buf], use & 1, &abort_s, P.timeout_ns)) {
         abort_s = 1;
         break;
       }
@@ -566,7 +569,7 @@ grouped_gemm_kernel(const __grid_constant__ TokenMaps tm, const GemmParams P) {
       // no MMA may still write TMEM when it is freed: this commit arrives once
       // every MMA issued before it has completed
       umma_commit(&drain_bar);
-      const unsigned long long dl = mc_globaltimer() + kTimeoutNs;
+      const unsigned long long dl = mc_globaltimer() + P.timeout_ns;
       while (!mc_mbar_test_sleep(&drain_bar, 0, 20000u))
         if (mc_globaltimer() > dl) break;
     }
@@ -619,7 +622,7 @@ int launch(mc_ctx* ctx, const uint16_t* a, int rows, const mc_qweights* w0, cons
       (rc = make_a_map(&tm.m256, a, rows, K, 256)))
     return rc;
   GemmParams P{*w0, GU ? *w1 : *w0, out, reinterpret_cast<const uint4*>(tiles), n_tiles, status,
-               N, K, rows, max_tiles, n_experts};
+               N, K, rows, max_tiles, n_experts, mc_wait_limit(ctx, kTimeoutNs)};
   MC_CUDA(cudaFuncSetAttribute(grouped_gemm_kernel<GU>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                C::SMEM));
   grouped_gemm_kernel<GU><<<ctx->num_sms, kThreads, C::SMEM, ctx->stream>>>(tm, P);
