@@ -395,15 +395,18 @@ int mc_ep_return(mc_ctx* ctx, const uint16_t* ed, size_t ed_rows, int hidden,
  *   rank 0: mc_ep_unique_id(id) and hands the 128 bytes to the other ranks
  *           (its own channel);
  *   every rank: mc_ep_init(ctx, W, rank, id, timeout_ms) -> a non-blocking
- *           NCCL communicator, every NCCL call watched with
- *           ncclCommGetAsyncError against the timeout and aborted past it;
+ *           NCCL communicator (set-up and teardown), every NCCL call watched
+ *           with ncclCommGetAsyncError against the timeout and aborted past
+ *           it;
  *           mc_ep_reserve(ctx, m_max, E, slots_per_rank, H, I) (collective:
  *           allocates the exchange buffers and maps every rank's through CUDA
  *           IPC);
  *           mc_ep_place(load, ...) on the same load matrix -> the same slot
  *           tables everywhere; the rank loads the weights of its slots
  *           (slot_expert[rank*spr ..]) stacked in slot order;
- *           mc_ep_moe_prefill(...) per step (collective; no host sync);
+ *           mc_ep_moe_prefill(...) per step (collective; no host sync; the
+ *           counts and rows move by peer stores, the down GEMM's epilogue
+ *           returns each expert row to its source, bounded device barriers);
  *           mc_ep_status(ctx, &st) when it wants the step's status bits
  *           (1 a GEMM wait, 2 a malformed tile or expert id, 4 rows beyond a
  *           capacity, 8 a cross-rank barrier that gave up); mc_sync waits for
@@ -437,13 +440,14 @@ int mc_ep_moe_prefill(mc_ctx* ctx, const uint16_t* x, const float* logits, int m
 /* Waits for the stream; *out = the status bits since the last call (then
  * cleared). */
 int mc_ep_status(mc_ctx* ctx, uint32_t* out);
-/* The last step's all-gathered pair counts [W][W * spr] (host copy; waits). */
+/* The last step's pair counts of every rank [W][W * spr] (host copy; waits). */
 int mc_ep_counts(mc_ctx* ctx, uint32_t* out, size_t n);
 int mc_ep_finalize(mc_ctx* ctx);
 /* Profiling aid: with `on`, each step records events at its phase
  * boundaries; mc_ep_phase_ms waits and writes the last step's six phase
- * times in ms (route + relabel + sort, counts all-gather, row chunks +
- * dispatch + barrier, grouped GEMMs, return + barrier, combine). */
+ * times in ms (route + relabel + sort, counts exchange + barrier, row chunks
+ * + return map + dispatch + barrier, grouped GEMMs with the return, the
+ * barrier after it, combine). */
 int mc_ep_set_profile(mc_ctx* ctx, int on);
 int mc_ep_phase_ms(mc_ctx* ctx, float* out6);
 

@@ -4,12 +4,13 @@
 // W ranks (one process per GPU) and one call runs a whole step:
 //
 //   route (top-4) -> relabel model experts to slots (this rank's table) ->
-//   sort by slot -> all-gather of the per-slot pair counts (NCCL) ->
-//   receive-side row chunks -> dispatch: rows stored straight into the
-//   owners' receive buffers over NVLink (CUDA IPC mappings) -> barrier ->
-//   grouped gate/up (+SwiGLU) and down GEMMs on the received rows ->
-//   return: expert rows stored into the sources' home buffers -> barrier ->
-//   weighted combine at home.
+//   sort by slot -> publish the per-slot pair counts into every rank's
+//   count table (peer stores) + barrier -> receive-side row chunks and the
+//   return map -> dispatch: rows stored straight into the owners' receive
+//   buffers over NVLink (CUDA IPC mappings) -> barrier -> grouped gate/up
+//   (+SwiGLU) GEMM -> down GEMM whose epilogue stores each expert row
+//   straight into its source's home buffer (the return overlaps the GEMM) ->
+//   barrier -> weighted combine at home.
 //
 // Slots. E_slots = W * slots_per_rank; rank r owns slots [r*spr, (r+1)*spr)
 // and holds their weights stacked in slot order. With spr = E / W and an
@@ -23,9 +24,10 @@
 // system fence, so the rows the previous kernels stored are visible first)
 // and polls its own flag words (acquire loads) with a deadline; a wait that
 // runs out sets status bit 8 and the kernel returns. The NCCL communicator
-// is non-blocking: every call on it is followed by polling
+// (non-blocking: every call on it is followed by polling
 // ncclCommGetAsyncError with a host deadline, and mc_sync / mc_ep_finalize
-// abort it (ncclCommAbort) when the deadline passes.
+// abort it, ncclCommAbort, when the deadline passes) sets the ranks up and
+// tears them down; a step itself makes no NCCL call.
 //
 // NCCL is loaded at run time (dlopen of libnccl.so.2, the copy already in the
 // process if there is one), so the library loads and its single-GPU entry
@@ -46,9 +48,11 @@ constexpr int kMaxRanks = 8;
 constexpr int kChunk = 256;  // token rows per grouped-GEMM chunk
 constexpr unsigned long long kBarrierNs = 1000000000ull;  // default barrier limit: 1 s
 // Phases of a step timed by mc_ep_set_profile: route + relabel + sort, the
-// counts all-gather, row chunks + dispatch + barrier, the two grouped GEMMs,
-// return + barrier, combine.
+// counts exchange (peer stores + barrier), row chunks + return map +
+// dispatch + barrier, the two grouped GEMMs (the down GEMM returning its
+// rows), the barrier after the return, combine.
 constexpr int kPhases = 6;
+constexpr size_t kCountsOff = 256;  // count table after the flag words in the control area
 
 // ------------------------------------------------------------ NCCL at run time
 struct NcclApi {
@@ -113,11 +117,13 @@ struct mc_ep_state {
   void* recv_ptr[kMaxRanks] = {};
   void* home_ptr[kMaxRanks] = {};
   uint32_t* flag_ptr[kMaxRanks] = {};
+  uint32_t* counts_ptr[kMaxRanks] = {};  // every rank's count table [W][E_slots]
   // local device scratch
   uint8_t* scratch = nullptr;
   uint32_t *ids, *counts, *offsets, *ids_sorted, *slotpos, *sort_tiles, *sort_ntiles;
   uint32_t *counts_all, *tiles, *n_tiles, *rows, *status, *epoch;
   uint16_t *gw, *act, *ed;
+  uint16_t** row_out;  // return map: recv row -> its row in the source's home buffer
   int sort_max_tiles = 0, max_tiles = 0;
   // phase timing (mc_ep_set_profile): events at the step's phase boundaries
   int profile = 0;
@@ -156,6 +162,9 @@ int nccl_settle(mc_ctx* ctx, ncclResult_t r, const char* what) {
 struct FlagPtrs {
   uint32_t* p[kMaxRanks];
 };
+struct PtrTable {
+  void* p[kMaxRanks];
+};
 
 __device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
   asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
@@ -170,9 +179,9 @@ __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
 // `rank` of every rank's flag words, then waits (bounded) until every slot of
 // its own flag words has reached the epoch. test_skip: this rank does not
 // arrive (a failure-detection test with one rank makes its own wait run out).
-__global__ void ep_barrier_kernel(FlagPtrs flags, uint32_t* epoch_word, int rank, int W,
-                                  unsigned long long timeout_ns, uint32_t* status, int test_skip) {
-  if (threadIdx.x != 0) return;
+__device__ void ep_barrier_thread(const FlagPtrs& flags, uint32_t* epoch_word, int rank, int W,
+                                  unsigned long long timeout_ns, uint32_t* status,
+                                  int test_skip) {
   const uint32_t epoch = *epoch_word + 1u;
   *epoch_word = epoch;
   __threadfence_system();
@@ -188,6 +197,55 @@ __global__ void ep_barrier_kernel(FlagPtrs flags, uint32_t* epoch_word, int rank
       }
       __nanosleep(200);
     }
+  }
+}
+
+__global__ void ep_barrier_kernel(FlagPtrs flags, uint32_t* epoch_word, int rank, int W,
+                                  unsigned long long timeout_ns, uint32_t* status, int test_skip) {
+  if (threadIdx.x == 0) ep_barrier_thread(flags, epoch_word, rank, W, timeout_ns, status, test_skip);
+}
+
+// This rank's pair counts into row `rank` of every rank's count table, then
+// the barrier: afterwards every rank holds all ranks' counts.
+__global__ void __launch_bounds__(256)
+ep_publish_counts_kernel(const uint32_t* __restrict__ counts, FlagPtrs tables, int E_slots,
+                         FlagPtrs flags, uint32_t* epoch_word, int rank, int W,
+                         unsigned long long timeout_ns, uint32_t* status, int test_skip) {
+  for (int e = threadIdx.x; e < E_slots; e += blockDim.x) {
+    const uint32_t v = counts[e];
+    for (int p = 0; p < W; ++p) tables.p[p][(size_t)rank * E_slots + e] = v;
+  }
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x == 0) ep_barrier_thread(flags, epoch_word, rank, W, timeout_ns, status, test_skip);
+}
+
+// The return map: received row i (local slot j, source s, k-th of that
+// segment) -> row off_s[slot] + k of source s's home buffer. grid (W * spr).
+__global__ void __launch_bounds__(256)
+ep_rowmap_kernel(const uint32_t* __restrict__ counts_all, int rank, int W, int E_slots, int H,
+                 PtrTable home, size_t home_cap, uint16_t** __restrict__ row_out,
+                 size_t recv_cap, uint32_t* status) {
+  const int spr = E_slots / W;
+  const int src = blockIdx.x / spr, slot = rank * spr + blockIdx.x % spr;
+  uint32_t row0 = 0, slot0 = 0;
+  for (int j = rank * spr; j < slot; ++j)
+    for (int s = 0; s < W; ++s) row0 += counts_all[s * E_slots + j];
+  for (int s = 0; s < src; ++s) row0 += counts_all[s * E_slots + slot];
+  for (int e = 0; e < slot; ++e) slot0 += counts_all[src * E_slots + e];
+  const uint32_t n = counts_all[src * E_slots + slot];
+  uint16_t* base = static_cast<uint16_t*>(home.p[src]);
+  for (uint32_t k = threadIdx.x; k < n; k += blockDim.x) {
+    if (row0 + k >= recv_cap) {
+      if (status) atomicOr(status, 4u);
+      continue;
+    }
+    if (slot0 + k >= home_cap) {
+      row_out[row0 + k] = nullptr;
+      if (status) atomicOr(status, 4u);
+      continue;
+    }
+    row_out[row0 + k] = base + (size_t)(slot0 + k) * H;
   }
 }
 
@@ -294,12 +352,13 @@ extern "C" int mc_ep_reserve(mc_ctx* ctx, int m_max, int n_experts, int slots_pe
   ep->recv_off = 0;
   ep->home_off = al(ep->recv_cap * hidden * 2);
   ep->flag_off = al(ep->home_off + ep->home_cap * hidden * 2);
-  const size_t own_bytes = ep->flag_off + 256;
+  const size_t ctl_bytes = kCountsOff + (size_t)W * (W * slots_per_rank) * 4;
+  const size_t own_bytes = ep->flag_off + al(ctl_bytes);
   MC_CUDA(cudaSetDevice(ctx->device));
   void* p = nullptr;
   MC_CUDA(cudaMalloc(&p, own_bytes));
   ep->own = static_cast<uint8_t*>(p);
-  MC_CUDA(cudaMemsetAsync(ep->own + ep->flag_off, 0, 256, ctx->stream));
+  MC_CUDA(cudaMemsetAsync(ep->own + ep->flag_off, 0, al(ctl_bytes), ctx->stream));
   // local scratch
   const size_t S = 4 * (size_t)m_max;
   ep->sort_max_tiles = (int)((S + kChunk - 1) / kChunk + ep->E_slots);
@@ -315,7 +374,7 @@ extern "C" int mc_ep_reserve(mc_ctx* ctx, int m_max, int n_experts, int slots_pe
   carve((void**)&ep->slotpos, S * 4);
   carve((void**)&ep->sort_tiles, (size_t)ep->sort_max_tiles * 16);
   carve((void**)&ep->sort_ntiles, 16);
-  carve((void**)&ep->counts_all, (size_t)W * ep->E_slots * 4);
+  carve((void**)&ep->row_out, ep->recv_cap * sizeof(uint16_t*));
   carve((void**)&ep->tiles, (size_t)ep->max_tiles * 16);
   carve((void**)&ep->n_tiles, 16);
   carve((void**)&ep->rows, 16);
@@ -362,7 +421,9 @@ extern "C" int mc_ep_reserve(mc_ctx* ctx, int m_max, int n_experts, int slots_pe
     ep->recv_ptr[r] = b + ep->recv_off;
     ep->home_ptr[r] = b + ep->home_off;
     ep->flag_ptr[r] = reinterpret_cast<uint32_t*>(b + ep->flag_off);
+    ep->counts_ptr[r] = reinterpret_cast<uint32_t*>(b + ep->flag_off + kCountsOff);
   }
+  ep->counts_all = ep->counts_ptr[ep->rank];
   MC_CUDA(cudaMemsetAsync(ep->act, 0, (size_t)W * sizeof(h), ctx->stream));
   ep->reserved = 1;
   // every rank's flags are zero and mapped before the first barrier
@@ -386,7 +447,6 @@ extern "C" int mc_ep_moe_prefill(mc_ctx* ctx, const uint16_t* x, const float* lo
              "ep_moe_prefill: local weights must be this rank's %d slots stacked ([%d][%d], "
              "[%d][%d])",
              ep->spr, ep->spr * ep->I, ep->H, ep->spr * ep->H, ep->I);
-  const NcclApi* api = nccl();
   const int S = 4 * m, W = ep->world;
   int rc;
   auto mark = [&](int k) -> int {
@@ -403,15 +463,31 @@ extern "C" int mc_ep_moe_prefill(mc_ctx* ctx, const uint16_t* x, const float* lo
                             ep->sort_max_tiles)))
     return rc;
   if ((rc = mark(1))) return rc;
-  if ((rc = nccl_settle(ctx,
-                        api->all_gather(ep->counts, ep->counts_all, (size_t)ep->E_slots,
-                                        ncclUint32, ep->comm, ctx->stream),
-                        "ep_moe_prefill counts all-gather")))
-    return rc;
+  {
+    FlagPtrs tables, flags;
+    for (int r = 0; r < kMaxRanks; ++r) {
+      tables.p[r] = r < W ? ep->counts_ptr[r] : nullptr;
+      flags.p[r] = r < W ? ep->flag_ptr[r] : nullptr;
+    }
+    ep_publish_counts_kernel<<<1, 256, 0, ctx->stream>>>(
+        ep->counts, tables, ep->E_slots, flags, ep->epoch, ep->rank, W,
+        mc_wait_limit(ctx, kBarrierNs), ep->status,
+        (ctx->test_flags & MC_TEST_SKIP_BARRIER_ARRIVE) ? 1 : 0);
+    if ((rc = mc_after_launch("ep_publish_counts_kernel"))) return rc;
+  }
   if ((rc = mark(2))) return rc;
   if ((rc = mc_ep_tiles(ctx, ep->counts_all, ep->rank, W, ep->E_slots, kChunk, ep->tiles,
                         ep->n_tiles, ep->rows, ep->max_tiles)))
     return rc;
+  {
+    PtrTable home;
+    for (int r = 0; r < kMaxRanks; ++r) home.p[r] = r < W ? ep->home_ptr[r] : nullptr;
+    ep_rowmap_kernel<<<W * ep->spr, 256, 0, ctx->stream>>>(ep->counts_all, ep->rank, W,
+                                                            ep->E_slots, ep->H, home,
+                                                            ep->home_cap, ep->row_out,
+                                                            ep->recv_cap, ep->status);
+    if ((rc = mc_after_launch("ep_rowmap_kernel"))) return rc;
+  }
   if ((rc = mc_ep_dispatch(ctx, x, m, ep->H, ep->ids_sorted, ep->counts_all, ep->rank, W,
                            ep->E_slots, ep->recv_ptr, ep->recv_cap, ep->status)))
     return rc;
@@ -422,13 +498,11 @@ extern "C" int mc_ep_moe_prefill(mc_ctx* ctx, const uint16_t* x, const float* lo
   if ((rc = mc_gemm_q4_grouped_gu(ctx, recv, rows, gate, up, ep->spr, ep->act, ep->tiles,
                                   ep->n_tiles, ep->max_tiles, ep->status)))
     return rc;
-  if ((rc = mc_gemm_q4_grouped(ctx, ep->act, rows, down, ep->spr, ep->ed, ep->tiles, ep->n_tiles,
-                               ep->max_tiles, ep->status)))
+  // the down GEMM stores each expert row straight into its source's home row
+  if ((rc = mc_gemm_q4_grouped_rows(ctx, ep->act, rows, down, ep->spr, ep->row_out, ep->tiles,
+                                    ep->n_tiles, ep->max_tiles, ep->status)))
     return rc;
   if ((rc = mark(4))) return rc;
-  if ((rc = mc_ep_return(ctx, ep->ed, ep->recv_cap, ep->H, ep->counts_all, ep->rank, W,
-                         ep->E_slots, ep->home_ptr, ep->home_cap, ep->status)))
-    return rc;
   if ((rc = ep_barrier(ctx))) return rc;
   if ((rc = mark(5))) return rc;
   if ((rc = mc_moe_combine_rows(ctx, static_cast<uint16_t*>(ep->home_ptr[ep->rank]), ep->slotpos,

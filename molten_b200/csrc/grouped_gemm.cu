@@ -82,6 +82,11 @@ struct GemmParams {
   uint32_t* status;
   int N, K, rows, max_tiles, n_experts;
   unsigned long long timeout_ns;  // limit of every bounded wait (mc_set_wait_limit)
+  // when set, output row r goes to row_out[r] (a bf16 row of N features,
+  // local or another GPU's, null = dropped) instead of out + r * N: the
+  // expert-parallel step returns expert rows to their source ranks straight
+  // from this epilogue
+  uint16_t* const* row_out;
 };
 
 // One work item: token rows [m0, mend) of expert e against feature block nb.
@@ -527,7 +532,7 @@ grouped_gemm_kernel(const __grid_constant__ TokenMaps tm, const GemmParams P) {
       const int n16 = cur.n >> 4, split = (n16 + 1) >> 1;
       const int c_lo = grp ? split : 0, c_hi = grp ? n16 : split;
       const uint32_t lane_base = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(buf * C::ACC_COLS);
-      uint16_t* ocol = P.out + (size_t)cur.nb * BF + f;
+      uint16_t* ocol = P.row_out ? nullptr : P.out + (size_t)cur.nb * BF + f;
 #pragma unroll 1
       for (int c = c_lo; c < c_hi; ++c) {
         uint32_t g[16], u[16];
@@ -550,6 +555,17 @@ grouped_gemm_kernel(const __grid_constant__ TokenMaps tm, const GemmParams P) {
             o1 = __uint_as_float(g[i2 + 1]);
           }
           const uint32_t pk = pack_bf16x2(o0, o1);
+          if (P.row_out) {
+            if (cur.ok && r0 + i2 < cur.mend) {
+              uint16_t* rp = P.row_out[r0 + i2];
+              if (rp) rp[(size_t)cur.nb * BF + f] = (uint16_t)pk;
+            }
+            if (cur.ok && r0 + i2 + 1 < cur.mend) {
+              uint16_t* rp = P.row_out[r0 + i2 + 1];
+              if (rp) rp[(size_t)cur.nb * BF + f] = (uint16_t)(pk >> 16);
+            }
+            continue;
+          }
           if (cur.ok && r0 + i2 < cur.mend) ocol[(size_t)(r0 + i2) * P.N] = (uint16_t)pk;
           if (cur.ok && r0 + i2 + 1 < cur.mend)
             ocol[(size_t)(r0 + i2 + 1) * P.N] = (uint16_t)(pk >> 16);
@@ -613,7 +629,7 @@ int make_a_map(CUtensorMap* map, const uint16_t* a, int rows, int K, int box_row
 template <bool GU>
 int launch(mc_ctx* ctx, const uint16_t* a, int rows, const mc_qweights* w0, const mc_qweights* w1,
            int n_experts, uint16_t* out, const uint32_t* tiles, const uint32_t* n_tiles,
-           int max_tiles, uint32_t* status) {
+           int max_tiles, uint32_t* status, uint16_t* const* row_out = nullptr) {
   using C = Cfg<GU>;
   const int N = w0->out_features / n_experts, K = w0->in_features;
   TokenMaps tm;
@@ -622,7 +638,7 @@ int launch(mc_ctx* ctx, const uint16_t* a, int rows, const mc_qweights* w0, cons
       (rc = make_a_map(&tm.m256, a, rows, K, 256)))
     return rc;
   GemmParams P{*w0, GU ? *w1 : *w0, out, reinterpret_cast<const uint4*>(tiles), n_tiles, status,
-               N, K, rows, max_tiles, n_experts, mc_wait_limit(ctx, kTimeoutNs)};
+               N, K, rows, max_tiles, n_experts, mc_wait_limit(ctx, kTimeoutNs), row_out};
   MC_CUDA(cudaFuncSetAttribute(grouped_gemm_kernel<GU>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                C::SMEM));
   grouped_gemm_kernel<GU><<<ctx->num_sms, kThreads, C::SMEM, ctx->stream>>>(tm, P);
@@ -671,6 +687,19 @@ extern "C" int mc_gemm_q4_grouped(mc_ctx* ctx, const uint16_t* a, int rows, cons
   int rc = check_grouped(a, rows, w, n_experts, c, tiles, n_tiles, max_tiles, "gemm_q4_grouped");
   if (rc) return rc;
   return launch<false>(ctx, a, rows, w, nullptr, n_experts, c, tiles, n_tiles, max_tiles, status);
+}
+
+// The down GEMM of the expert-parallel step: mc_gemm_q4_grouped with each
+// output row stored through row_out (ep_prefill.cu).
+int mc_gemm_q4_grouped_rows(mc_ctx* ctx, const uint16_t* a, int rows, const mc_qweights* w,
+                            int n_experts, uint16_t* const* row_out, const uint32_t* tiles,
+                            const uint32_t* n_tiles, int max_tiles, uint32_t* status) {
+  MC_REQUIRE(ctx && row_out, "gemm_q4_grouped_rows: null context or row table");
+  int rc = check_grouped(a, rows, w, n_experts, a, tiles, n_tiles, max_tiles,
+                         "gemm_q4_grouped_rows");
+  if (rc) return rc;
+  return launch<false>(ctx, a, rows, w, nullptr, n_experts, nullptr, tiles, n_tiles, max_tiles,
+                       status, row_out);
 }
 
 extern "C" size_t mc_gemm_q4_workspace_words(int m) {

@@ -448,9 +448,10 @@ def moe_prefill_ep_emulated(ctx, xs, logits, gate, up, down, n_experts: int, pla
 
 # ------------------------------------------------- the C-ABI expert-parallel step
 # The whole step runs inside the library (mc_ep_moe_prefill): routing, slot
-# relabelling, sort, the NCCL all-gather of the counts, dispatch over NVLink,
-# device-side barriers, the grouped GEMMs, the return and the combine. Python
-# only bootstraps the NCCL unique id and loads each rank's slot weights.
+# relabelling, sort, the counts exchange and the dispatch over NVLink,
+# device-side barriers, the grouped GEMMs (the down GEMM returning its rows)
+# and the combine. Python only bootstraps the NCCL unique id and loads each
+# rank's slot weights.
 
 def place_slots(load, world: int, slots_per_rank: int):
     """Slot placement with hot-expert replication (mc_ep_place): load[s][e]
@@ -515,7 +516,7 @@ class EpPrefill:
         return int(v.value)
 
     def counts(self) -> np.ndarray:
-        """The last step's all-gathered pair counts [world][world * spr]."""
+        """The last step's pair counts of every rank [world][world * spr]."""
         import ctypes as C
         n = self.world * self.world * self.spr
         a = np.zeros(n, np.uint32)
@@ -525,8 +526,8 @@ class EpPrefill:
     def set_profile(self, on: bool) -> None:
         self.lib.call("mc_ep_set_profile", self.ctx.handle, 1 if on else 0)
 
-    PHASES = ("route_sort", "counts_allgather", "dispatch_barrier", "gemms", "return_barrier",
-              "combine")
+    PHASES = ("route_sort", "counts_exchange", "dispatch_barrier", "gemms_return",
+              "return_barrier", "combine")
 
     def phase_ms(self) -> dict:
         """The last profiled step's phase times (ms)."""
