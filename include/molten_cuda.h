@@ -284,8 +284,8 @@ int mc_moe_route_batch(mc_ctx* ctx, const float* logits, int m, int n_experts,
  * in two launches: counts[E], offsets[E] (exclusive scan), the stable
  * token-major, rank-major scatter ids_sorted[m*4] / slotpos[m*4], and the
  * row-tile list tiles[max_tiles] of uint4 {m0, m_end, expert, 0} with its
- * length in *n_tiles (device u32): experts by decreasing pair count (ties:
- * lower expert), each expert's full bm-row tiles then its partial one.
+ * length in *n_tiles (device u32): every full bm-row tile first, in expert
+ * order, then the partial tiles by decreasing height (ties: lower expert).
  * bm is the tile height (256 for the grouped GEMMs, at most 256 there);
  * max_tiles >= ceil(m*4/bm) + E. */
 int mc_moe_sort_map(mc_ctx* ctx, const uint32_t* ids, int m, int n_experts, int bm,
@@ -379,8 +379,8 @@ int mc_ipc_close(mc_ctx* ctx, void* ptr);
 int mc_ep_dispatch(mc_ctx* ctx, const uint16_t* x, int m, int hidden,
                    const uint32_t* ids_sorted, const uint32_t* counts_all, int rank, int world,
                    int n_experts, void* const* recv_bufs, size_t recv_cap_rows, uint32_t* status);
-/* Row-chunk list (uint4 {m0, m_end, local expert, 0}, <= bm rows, in the
- * order of mc_moe_sort_map's tile list) of this rank's receive buffer,
+/* Row-chunk list (uint4 {m0, m_end, local expert, 0}, <= bm rows, full chunks
+ * first then partial by decreasing height) of this rank's receive buffer,
  * its length in *n_tiles and the row count in *rows (nullable). */
 int mc_ep_tiles(mc_ctx* ctx, const uint32_t* counts_all, int rank, int world, int n_experts,
                 int bm, uint32_t* tiles, uint32_t* n_tiles, uint32_t* rows, int max_tiles);

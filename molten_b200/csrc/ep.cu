@@ -103,10 +103,9 @@ ep_return_kernel(const uint4* __restrict__ ed, uint32_t ed_rows, int h16,
   __threadfence_system();
 }
 
-// Row chunks of this rank's receive buffer for the grouped GEMMs: local
-// experts by decreasing received rows (ties: lower expert), each expert's
-// full bm-row chunks then its partial one (the order of mc_moe_sort_map's
-// tile list). One CTA; thread j = local expert j.
+// Row chunks of this rank's receive buffer for the grouped GEMMs: full
+// bm-row chunks first (local expert order), then the partial ones by
+// decreasing height (ties: lower expert). One CTA; thread j = local expert j.
 __global__ void __launch_bounds__(256)
 ep_tiles_kernel(const uint32_t* __restrict__ counts_all, int rank, int W, int E, int bm,
                 uint4* __restrict__ tiles, uint32_t* __restrict__ n_tiles, uint32_t* __restrict__ rows,
@@ -119,28 +118,37 @@ ep_tiles_kernel(const uint32_t* __restrict__ counts_all, int rank, int W, int E,
     total_s[j] = t;
   }
   __syncthreads();
-  uint32_t all_tiles = 0, all_rows = 0;
+  uint32_t full_all = 0, parts = 0, all_rows = 0;
   for (int jj = 0; jj < P; ++jj) {
-    all_tiles += (total_s[jj] + bm - 1) / bm;
+    full_all += total_s[jj] / bm;
+    parts += (total_s[jj] % bm) != 0;
     all_rows += total_s[jj];
   }
   if (threadIdx.x == 0) {
-    *n_tiles = all_tiles;
+    *n_tiles = full_all + parts;
     if (rows) *rows = all_rows;
   }
   for (int j = threadIdx.x; j < P; j += blockDim.x) {
-    const uint32_t tj = total_s[j];
-    uint32_t base = 0, first = 0;
+    const uint32_t tj = total_s[j], pj = tj % bm;
+    uint32_t base = 0, full_before = 0, rank_p = 0;
     for (int jj = 0; jj < P; ++jj) {
-      const uint32_t t = total_s[jj];
-      if (jj < j) base += t;
-      if (t > tj || (t == tj && jj < j)) first += (t + bm - 1) / bm;
+      const uint32_t t = total_s[jj], p = t % bm;
+      if (jj < j) {
+        base += t;
+        full_before += t / bm;
+      }
+      if (p && (p > pj || (p == pj && jj < j))) ++rank_p;
     }
-    const uint32_t nt = (tj + bm - 1) / bm;
-    for (uint32_t c = 0; c < nt; ++c) {
-      const uint32_t slot = first + c;
+    const uint32_t nfull = tj / bm;
+    for (uint32_t c = 0; c < nfull; ++c) {
+      const uint32_t slot = full_before + c;
       if (slot < (uint32_t)max_tiles)
-        tiles[slot] = make_uint4(base + c * bm, base + min(tj, (c + 1) * bm), (uint32_t)j, 0u);
+        tiles[slot] = make_uint4(base + c * bm, base + (c + 1) * bm, (uint32_t)j, 0u);
+    }
+    if (pj) {
+      const uint32_t slot = full_all + rank_p;
+      if (slot < (uint32_t)max_tiles)
+        tiles[slot] = make_uint4(base + nfull * bm, base + tj, (uint32_t)j, 0u);
     }
   }
 }

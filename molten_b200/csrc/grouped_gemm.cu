@@ -24,10 +24,8 @@
 //
 // Persistent kernel, one CTA per SM. Work items = (row chunk, 128-feature
 // block), chunk-major, dealt to CTAs in snake order; with the tile list from
-// mc_moe_sort_map (experts by decreasing rows, each expert's chunks
-// together) the CTAs working at one time share one or two experts' weight
-// tiles through L2, so each weight byte comes from HBM about once, and the
-// last items are the smallest chunks. Warp roles (320 threads):
+// mc_moe_sort_map (full chunks first, then partial ones by decreasing
+// height) every CTA gets a similar share. Warp roles (320 threads):
 //   warp 0      TMA of the token rows (128-byte swizzle) into the token ring
 //   warp 1      TMEM allocation (512 columns); lane 0 issues tcgen05.mma
 //               (M=128, N=chunk, K=16, bf16 x bf16 -> fp32) and commits
@@ -114,7 +112,8 @@ __device__ __forceinline__ Item item_info(const GemmParams& P, int item, int nbl
 }
 
 // The i-th work item of this CTA: items are dealt in snake order (0..G-1,
-// then G-1..0, ...) so that every CTA gets a similar total.
+// then G-1..0, ...) so that, with the tile list sorted by decreasing height,
+// every CTA gets a similar total.
 __device__ __forceinline__ int cta_item(int i) {
   const int G = (int)gridDim.x, b = (int)blockIdx.x;
   return i * G + ((i & 1) ? G - 1 - b : b);

@@ -8,8 +8,8 @@
 // the 4096-token chunk, so counts are deterministic). Launch 2 derives the
 // expert's offset and tile slots from the 64 counts, scans its pairs in
 // token-major, rank-major order (each thread a contiguous token range, block
-// exclusive scan), and writes ids_sorted / slotpos and its row tiles (experts
-// by decreasing pair count, each expert's full tiles then its partial one).
+// exclusive scan), and writes ids_sorted / slotpos and its row tiles (full
+// tiles first in expert order, then partial tiles by decreasing height).
 #include "mc_internal.cuh"
 
 namespace {
@@ -41,23 +41,28 @@ sort_scatter_kernel(const uint32_t* __restrict__ ids, int m, int E, int bm,
   const uint32_t e = blockIdx.x;
   const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
   if (t == 0) {
-    // Tile list order: experts by decreasing pair count (ties: lower expert
-    // first), each expert's tiles together, full tiles then its partial one.
-    // A consumer dealing tiles out in list order then works on one expert's
-    // tiles at a time (its weights are read from HBM once and shared through
-    // L2) and ends on the smallest tiles (its workers finish together).
-    const uint32_t ce = counts[e];
-    uint32_t off = 0, before = 0, all = 0;
+    // Tile list order: every full bm-row tile first (expert order), then the
+    // partial tiles by decreasing height (ties: lower expert first), so a
+    // consumer that deals tiles out in list order balances its workers.
+    const uint32_t ce = counts[e], pe = ce % (uint32_t)bm;
+    uint32_t off = 0, full_before = 0, full_all = 0, part_rank = 0, parts = 0;
     for (int j = 0; j < E; ++j) {
-      const uint32_t c = counts[j], nj = (c + bm - 1) / (uint32_t)bm;
-      if ((uint32_t)j < e) off += c;
-      if (c > ce || (c == ce && (uint32_t)j < e)) before += nj;
-      all += nj;
+      const uint32_t c = counts[j], pj = c % (uint32_t)bm;
+      if ((uint32_t)j < e) {
+        off += c;
+        full_before += c / bm;
+      }
+      full_all += c / bm;
+      if (pj) {
+        ++parts;
+        if (pj > pe || (pj == pe && (uint32_t)j < e)) ++part_rank;
+      }
     }
     base_s[0] = off;
-    base_s[1] = before;  // slot of this expert's first tile
+    base_s[1] = full_before;
+    base_s[2] = full_all + part_rank;  // slot of this expert's partial tile
     offsets[e] = off;
-    if (e == 0) *n_tiles = all;
+    if (e == 0) *n_tiles = full_all + parts;
   }
   // contiguous token range per thread
   const int per = (m + 255) / 256;
@@ -88,9 +93,9 @@ sort_scatter_kernel(const uint32_t* __restrict__ ids, int m, int E, int bm,
       }
   // row tiles of this expert
   const uint32_t n = counts[e];
-  const uint32_t nt = (n + bm - 1) / bm;
+  const uint32_t nt = (n + bm - 1) / bm, nfull = n / bm;
   for (uint32_t j = t; j < nt; j += 256) {
-    const uint32_t slot = base_s[1] + j;
+    const uint32_t slot = j < nfull ? base_s[1] + j : base_s[2];
     if (slot < (uint32_t)max_tiles) {
       const uint32_t m0 = base_s[0] + j * bm;
       tiles[slot] = make_uint4(m0, min(m0 + (uint32_t)bm, base_s[0] + n), e, 0u);

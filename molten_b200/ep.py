@@ -72,13 +72,13 @@ def plan_exchange(counts_all: np.ndarray, rank: int, chunk: int = CHUNK) -> Plan
             if n:
                 off = base[j] + counts_all[:peer, e0 + j].sum()
                 recv.append((peer, int(off), int(n)))
-    # experts by decreasing rows (ties: lower expert), each one's full
-    # chunks then its partial one (the order of mc_moe_sort_map's tile list)
-    tl = []
-    for j in sorted(range(per), key=lambda j: (-int(totals[j]), j)):
+    full, part = [], []
+    for j in range(per):
         for m0 in range(0, int(totals[j]), chunk):
-            tl.append((int(base[j] + m0), int(base[j] + min(m0 + chunk, totals[j])), j, 0))
-    tiles = np.array(tl, dtype=np.uint32).reshape(-1, 4)
+            t = (int(base[j] + m0), int(base[j] + min(m0 + chunk, totals[j])), j, 0)
+            (full if t[1] - t[0] == chunk else part).append(t)
+    part.sort(key=lambda t: (-(t[1] - t[0]), t[2]))
+    tiles = np.array(full + part, dtype=np.uint32).reshape(-1, 4)
     return Plan(rank, world, E, per, send, recv, int(totals.sum()),
                 totals.astype(np.uint32), base.astype(np.uint32), tiles)
 

@@ -47,15 +47,10 @@ def test_plan_invariants(world, E):
             assert p.local_offsets[j] <= m0 and m1 <= p.local_offsets[j] + p.local_counts[j]
             cov[m0:m1] += 1
         assert (cov == 1).all()
-        # experts by decreasing rows, each one's chunks together, full first
-        order = [int(t[2]) for t in p.tiles]
-        firsts = list(dict.fromkeys(order))
-        assert order == sorted(order, key=firsts.index), "one expert's chunks together"
-        rows = [int(p.local_counts[j]) for j in firsts]
-        assert rows == sorted(rows, reverse=True)
-        for j in firsts:
-            hs = [int(t[1] - t[0]) for t in p.tiles if t[2] == j]
-            assert all(h == ep.CHUNK for h in hs[:-1])
+        heights = [int(t[1] - t[0]) for t in p.tiles]
+        nfull = sum(h == ep.CHUNK for h in heights)
+        assert heights[:nfull] == [ep.CHUNK] * nfull
+        assert heights[nfull:] == sorted(heights[nfull:], reverse=True)
     # the i-th send from s to r pairs with the i-th receive at r from s
     for s in range(world):
         for r in range(world):

@@ -39,17 +39,18 @@ def test_route_batch_and_sort_map(cuda_ctx, m):
     assert np.array_equal(host_u32(bufs["offsets"]), offsets)
     assert np.array_equal(host_u32(bufs["ids_sorted"]), ids_sorted)
     assert np.array_equal(host_u32(bufs["slotpos"]), slotpos)
-    # tile list: every expert's rows covered once by <=128-row tiles; experts
-    # by decreasing pair count (ties: lower expert), each one's full tiles
-    # then its partial tile
+    # tile list: every expert's rows covered once by <=128-row tiles; full
+    # tiles first in expert order, then partial tiles by decreasing height
     nt = int(host_u32(bufs["n_tiles"])[0])
     tiles = host_u32(bufs["tiles"])[:nt]
-    want = []
-    for e in sorted(range(64), key=lambda e: (-int(counts[e]), e)):
+    full, part = [], []
+    for e in range(64):
         for j in range(0, int(counts[e]), 128):
             m0 = int(offsets[e]) + j
-            want.append((m0, min(m0 + 128, int(offsets[e] + counts[e])), e, 0))
-    assert [tuple(t) for t in tiles] == want
+            t = (m0, min(m0 + 128, int(offsets[e] + counts[e])), e, 0)
+            (full if t[1] - t[0] == 128 else part).append(t)
+    part.sort(key=lambda t: (-(t[1] - t[0]), t[2]))
+    assert [tuple(t) for t in tiles] == full + part
 
 
 def test_route_batch_sigmoid_mode(cuda_ctx):
