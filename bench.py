@@ -640,7 +640,10 @@ def bench_cfg3_ep(args, torch, ws, rank, local):
     lfm.moe_route_batch(ctx, logits, None, ids, gw, m)
     mine = torch.bincount(ids.view(-1).long(), minlength=E).to(torch.int64)
     loads = [torch.zeros_like(mine) for _ in range(ws)]
-    dist.all_gather(loads, mine)
+    if ws > 1:
+        dist.all_gather(loads, mine)
+    else:
+        loads = [mine]
     load = torch.stack(loads).cpu().numpy().astype(np.uint64)
     spr = E // ws + (args.ep_spare if args.ep_placement == "balanced" else 0)
     if args.ep_placement == "contiguous":
@@ -681,10 +684,13 @@ def bench_cfg3_ep(args, torch, ws, rank, local):
     step()
     phases = epp.phase_ms()
     epp.set_profile(False)
+    mine_rep = {"rank": rank, "rows_computed": recv_rows, "rows_sent_remote": sent_remote,
+                "phase_ms": {k: round(v, 4) for k, v in phases.items()}}
     per_rank = [None] * ws
-    dist.all_gather_object(per_rank, {"rank": rank, "rows_computed": recv_rows,
-                                      "rows_sent_remote": sent_remote,
-                                      "phase_ms": {k: round(v, 4) for k, v in phases.items()}})
+    if ws > 1:
+        dist.all_gather_object(per_rank, mine_rep)
+    else:
+        per_rank = [mine_rep]
     # e2e: host rows in, host rows out, through the same call
     hx, hl = x.cpu().pin_memory(), logits.cpu().pin_memory()
     hout = torch.empty((m, H), dtype=torch.bfloat16).pin_memory()
