@@ -162,3 +162,65 @@ def test_placement_balances_zipf_load(world):
     assert placed <= contiguous + 1e-12
     # a bound of greedy packing: within the heaviest expert of the ideal share
     assert placed <= load.sum() / world + load.max() + 1e-12
+
+
+def _failing_rank_main(rank, world, port, mode, q):
+    """Step 1 on both ranks; before step 2 rank 1 either raises (its process
+    ends) or stays away from the step; rank 0 must see its next collective
+    fail within the process group's short timeout instead of hanging."""
+    import datetime
+    import time as _t
+    try:
+        import torch.distributed as dist
+        os.environ["MASTER_ADDR"] = "127.0.0.1"
+        os.environ["MASTER_PORT"] = str(port)
+        dist.init_process_group("gloo", rank=rank, world_size=world,
+                                timeout=datetime.timedelta(seconds=5))
+        E, m, I, H = 8, 16, 128, 2048
+        g = synth.rng(920)
+        gate, up = synth.quant_weights_np(g, E * I, H), synth.quant_weights_np(g, E * I, H)
+        down = synth.quant_weights_np(g, E * H, I)
+        gr = synth.rng(930 + rank)
+        x, logits = synth.activations_np(gr, m, H), synth.zipf_logits_np(gr, m, E)
+        ops = OracleOps(gate, up, down, E, rank, world)
+        ep.moe_prefill_ep(ops, synth.bf16_tensor(x), torch.from_numpy(logits), rank, world)
+        if rank == 1:
+            if mode == "raise":
+                raise RuntimeError("injected failure between steps")
+            _t.sleep(20)          # alive, but never joins step 2
+            q.put((rank, True, "stayed away"))
+            return
+        t0 = _t.time()
+        try:
+            ep.moe_prefill_ep(ops, synth.bf16_tensor(x), torch.from_numpy(logits), rank, world)
+            q.put((rank, False, "step 2 completed without its peer"))
+        except Exception as exc:  # the collective with the missing rank fails
+            q.put((rank, True, f"{type(exc).__name__} after {_t.time() - t0:.1f} s"))
+    except Exception as exc:
+        q.put((rank, mode == "raise" and rank == 1, repr(exc)))
+
+
+@pytest.mark.parametrize("mode", ["raise", "absent"])
+def test_a_failed_rank_makes_the_others_fail_cleanly(mode):
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_failing_rank_main, args=(r, world, port, mode, q))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    try:
+        results = {}
+        for _ in range(world):
+            rank, ok, info = q.get(timeout=120)
+            results[rank] = (ok, info)
+    finally:
+        for p in procs:
+            p.join(timeout=30)
+            if p.is_alive():
+                p.kill()
+    ok0, info0 = results[0]
+    assert ok0, f"rank 0: {info0}"
+    secs = float(info0.split(" after ")[1].split(" s")[0])
+    assert secs < 60.0, f"rank 0 took {secs} s to notice"
