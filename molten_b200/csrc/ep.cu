@@ -20,6 +20,8 @@
 // once every sender's kernel has finished).
 #include <string.h>
 
+#include <algorithm>
+
 #include "mc_internal.cuh"
 
 namespace {
@@ -46,30 +48,47 @@ __device__ __forceinline__ void segment_bases(const uint32_t* counts_all, int W,
   *src_row = off;
 }
 
-// Rows of expert e from this rank -> owner's receive buffer. grid (E, Y);
-// one warp per row, 16 bytes per lane per step.
+// This rank's expert-sorted rows -> the owners' receive buffers. Every warp
+// takes rows across all experts (grid-stride over the sorted order), so a hot
+// expert's rows are spread over the whole grid; each CTA first lays out the
+// experts' starts (in the sorted order and in the owners' buffers) in shared
+// memory, then finds a row's expert by binary search. 16 bytes per lane per
+// step.
 __global__ void __launch_bounds__(256)
 ep_dispatch_kernel(const uint4* __restrict__ x, int m, int h16,
                    const uint32_t* __restrict__ ids_sorted, const uint32_t* __restrict__ counts_all,
                    int rank, int W, int E, PeerPtrs recv, uint32_t cap, uint32_t* status) {
-  const int e = blockIdx.x;
-  __shared__ uint32_t dst0, src0, n;
+  __shared__ uint32_t src0[kMaxExperts + 1], dst0[kMaxExperts];
+  for (int e = threadIdx.x; e < E; e += blockDim.x) {
+    uint32_t d, s;
+    segment_bases(counts_all, W, E, e, rank, &d, &s);
+    src0[e] = s;
+    dst0[e] = d;
+  }
   if (threadIdx.x == 0) {
-    segment_bases(counts_all, W, E, e, rank, &dst0, &src0);
-    n = counts_all[rank * E + e];
+    uint32_t t = 0;
+    for (int e = 0; e < E; ++e) t += counts_all[rank * E + e];
+    src0[E] = t;
   }
   __syncthreads();
-  const int owner = e / (E / W);
-  uint4* dst = reinterpret_cast<uint4*>(recv.p[owner]);
+  const uint32_t total = src0[E];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  for (uint32_t k = blockIdx.y * 8 + warp; k < n; k += gridDim.y * 8) {
-    const uint32_t tok = __ldg(ids_sorted + src0 + k);
-    if (dst0 + k >= cap || tok >= (uint32_t)m) {  // inconsistent counts: never write past a buffer
+  const int P = E / W;
+  for (uint32_t r = blockIdx.x * 8 + warp; r < total; r += gridDim.x * 8) {
+    int lo = 0, hi = E;  // src0[lo] <= r < src0[hi]
+    while (hi - lo > 1) {
+      const int mid = (lo + hi) >> 1;
+      if (src0[mid] <= r) lo = mid;
+      else hi = mid;
+    }
+    const uint32_t k = r - src0[lo];
+    const uint32_t tok = __ldg(ids_sorted + r);
+    if (dst0[lo] + k >= cap || tok >= (uint32_t)m) {  // inconsistent counts: never write past a buffer
       if (lane == 0 && status) atomicOr(status, 4u);
       continue;
     }
     const uint4* row = x + (size_t)tok * h16;
-    uint4* out = dst + (size_t)(dst0 + k) * h16;
+    uint4* out = reinterpret_cast<uint4*>(recv.p[lo / P]) + (size_t)(dst0[lo] + k) * h16;
     for (int c = lane; c < h16; c += 32) out[c] = __ldg(row + c);
   }
   __threadfence_system();
@@ -219,7 +238,8 @@ extern "C" int mc_ep_dispatch(mc_ctx* ctx, const uint16_t* x, int m, int hidden,
   if ((rc = fill_peers(&pp, recv_bufs, world, "ep_dispatch"))) return rc;
   MC_REQUIRE(m >= 1 && recv_cap_rows >= 1 && recv_cap_rows <= 0xffffffffu,
              "ep_dispatch: m %d / capacity %zu", m, recv_cap_rows);
-  ep_dispatch_kernel<<<dim3(n_experts, 8), 256, 0, ctx->stream>>>(
+  const int grid = std::max(1, std::min((4 * m + 7) / 8, ctx->num_sms * 8));
+  ep_dispatch_kernel<<<grid, 256, 0, ctx->stream>>>(
       reinterpret_cast<const uint4*>(x), m, hidden / 8, ids_sorted, counts_all, rank, world,
       n_experts, pp, (uint32_t)recv_cap_rows, status);
   return mc_after_launch("ep_dispatch_kernel");

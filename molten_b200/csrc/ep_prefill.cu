@@ -123,7 +123,7 @@ struct mc_ep_state {
   uint32_t *ids, *counts, *offsets, *ids_sorted, *slotpos, *sort_tiles, *sort_ntiles;
   uint32_t *counts_all, *tiles, *n_tiles, *rows, *status, *epoch;
   uint16_t *gw, *act, *ed;
-  uint16_t** row_out;  // return map: recv row -> its row in the source's home buffer
+  uint32_t *seg_row, *seg_home;  // return map (ep_segments_kernel)
   int sort_max_tiles = 0, max_tiles = 0;
   // phase timing (mc_ep_set_profile): events at the step's phase boundaries
   int profile = 0;
@@ -162,9 +162,7 @@ int nccl_settle(mc_ctx* ctx, ncclResult_t r, const char* what) {
 struct FlagPtrs {
   uint32_t* p[kMaxRanks];
 };
-struct PtrTable {
-  void* p[kMaxRanks];
-};
+
 
 __device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
   asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
@@ -220,32 +218,26 @@ ep_publish_counts_kernel(const uint32_t* __restrict__ counts, FlagPtrs tables, i
   if (threadIdx.x == 0) ep_barrier_thread(flags, epoch_word, rank, W, timeout_ns, status, test_skip);
 }
 
-// The return map: received row i (local slot j, source s, k-th of that
-// segment) -> row off_s[slot] + k of source s's home buffer. grid (W * spr).
+// The return map: for each local slot j and source s, the first received
+// row of that source's rows (seg_row[j][s]; seg_row[j][W] = the end of slot
+// j's rows) and the first row of them in the source's home buffer
+// (seg_home[j][s], the source's own sorted order). One CTA.
 __global__ void __launch_bounds__(256)
-ep_rowmap_kernel(const uint32_t* __restrict__ counts_all, int rank, int W, int E_slots, int H,
-                 PtrTable home, size_t home_cap, uint16_t** __restrict__ row_out,
-                 size_t recv_cap, uint32_t* status) {
+ep_segments_kernel(const uint32_t* __restrict__ counts_all, int rank, int W, int E_slots,
+                   uint32_t* __restrict__ seg_row, uint32_t* __restrict__ seg_home) {
   const int spr = E_slots / W;
-  const int src = blockIdx.x / spr, slot = rank * spr + blockIdx.x % spr;
-  uint32_t row0 = 0, slot0 = 0;
-  for (int j = rank * spr; j < slot; ++j)
-    for (int s = 0; s < W; ++s) row0 += counts_all[s * E_slots + j];
-  for (int s = 0; s < src; ++s) row0 += counts_all[s * E_slots + slot];
-  for (int e = 0; e < slot; ++e) slot0 += counts_all[src * E_slots + e];
-  const uint32_t n = counts_all[src * E_slots + slot];
-  uint16_t* base = static_cast<uint16_t*>(home.p[src]);
-  for (uint32_t k = threadIdx.x; k < n; k += blockDim.x) {
-    if (row0 + k >= recv_cap) {
-      if (status) atomicOr(status, 4u);
-      continue;
+  for (int t = threadIdx.x; t < spr * (W + 1); t += blockDim.x) {
+    const int j = t / (W + 1), s = t % (W + 1), slot = rank * spr + j;
+    uint32_t row = 0;
+    for (int jj = rank * spr; jj < slot; ++jj)
+      for (int q = 0; q < W; ++q) row += counts_all[q * E_slots + jj];
+    for (int q = 0; q < s; ++q) row += counts_all[q * E_slots + slot];
+    seg_row[j * (W + 1) + s] = row;
+    if (s < W) {
+      uint32_t h = 0;
+      for (int e = 0; e < slot; ++e) h += counts_all[s * E_slots + e];
+      seg_home[j * W + s] = h;
     }
-    if (slot0 + k >= home_cap) {
-      row_out[row0 + k] = nullptr;
-      if (status) atomicOr(status, 4u);
-      continue;
-    }
-    row_out[row0 + k] = base + (size_t)(slot0 + k) * H;
   }
 }
 
@@ -374,7 +366,8 @@ extern "C" int mc_ep_reserve(mc_ctx* ctx, int m_max, int n_experts, int slots_pe
   carve((void**)&ep->slotpos, S * 4);
   carve((void**)&ep->sort_tiles, (size_t)ep->sort_max_tiles * 16);
   carve((void**)&ep->sort_ntiles, 16);
-  carve((void**)&ep->row_out, ep->recv_cap * sizeof(uint16_t*));
+  carve((void**)&ep->seg_row, (size_t)slots_per_rank * (W + 1) * 4);
+  carve((void**)&ep->seg_home, (size_t)slots_per_rank * W * 4);
   carve((void**)&ep->tiles, (size_t)ep->max_tiles * 16);
   carve((void**)&ep->n_tiles, 16);
   carve((void**)&ep->rows, 16);
@@ -479,15 +472,9 @@ extern "C" int mc_ep_moe_prefill(mc_ctx* ctx, const uint16_t* x, const float* lo
   if ((rc = mc_ep_tiles(ctx, ep->counts_all, ep->rank, W, ep->E_slots, kChunk, ep->tiles,
                         ep->n_tiles, ep->rows, ep->max_tiles)))
     return rc;
-  {
-    PtrTable home;
-    for (int r = 0; r < kMaxRanks; ++r) home.p[r] = r < W ? ep->home_ptr[r] : nullptr;
-    ep_rowmap_kernel<<<W * ep->spr, 256, 0, ctx->stream>>>(ep->counts_all, ep->rank, W,
-                                                            ep->E_slots, ep->H, home,
-                                                            ep->home_cap, ep->row_out,
-                                                            ep->recv_cap, ep->status);
-    if ((rc = mc_after_launch("ep_rowmap_kernel"))) return rc;
-  }
+  ep_segments_kernel<<<1, 256, 0, ctx->stream>>>(ep->counts_all, ep->rank, W, ep->E_slots,
+                                                  ep->seg_row, ep->seg_home);
+  if ((rc = mc_after_launch("ep_segments_kernel"))) return rc;
   if ((rc = mc_ep_dispatch(ctx, x, m, ep->H, ep->ids_sorted, ep->counts_all, ep->rank, W,
                            ep->E_slots, ep->recv_ptr, ep->recv_cap, ep->status)))
     return rc;
@@ -499,8 +486,9 @@ extern "C" int mc_ep_moe_prefill(mc_ctx* ctx, const uint16_t* x, const float* lo
                                   ep->n_tiles, ep->max_tiles, ep->status)))
     return rc;
   // the down GEMM stores each expert row straight into its source's home row
-  if ((rc = mc_gemm_q4_grouped_rows(ctx, ep->act, rows, down, ep->spr, ep->row_out, ep->tiles,
-                                    ep->n_tiles, ep->max_tiles, ep->status)))
+  if ((rc = mc_gemm_q4_grouped_return(ctx, ep->act, rows, down, ep->spr, ep->seg_row,
+                                      ep->seg_home, ep->home_ptr, W, ep->home_cap, ep->tiles,
+                                      ep->n_tiles, ep->max_tiles, ep->status)))
     return rc;
   if ((rc = mark(4))) return rc;
   if ((rc = ep_barrier(ctx))) return rc;

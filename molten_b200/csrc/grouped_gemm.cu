@@ -74,6 +74,20 @@ struct Cfg {
 static_assert(Cfg<true>::SMEM + 512 <= 232448 && Cfg<false>::SMEM + 512 <= 232448,
               "shared memory budget");
 
+// Where the expert-parallel step's down GEMM stores its rows (set when
+// seg_row is not null): the rows of local expert j come from the W source
+// ranks in order, source s's from row seg_row[j][s] to seg_row[j][s+1], and
+// row r of that segment goes to row seg_home[j][s] + (r - seg_row[j][s]) of
+// source s's home buffer home[s] (local or another GPU's, H features).
+constexpr int kRetRanks = 8;
+struct ReturnMap {
+  const uint32_t* seg_row;   // [n_experts][W + 1]
+  const uint32_t* seg_home;  // [n_experts][W]
+  uint16_t* home[kRetRanks];
+  int W;
+  uint32_t home_cap;
+};
+
 struct GemmParams {
   mc_qweights w0, w1;
   uint16_t* out;
@@ -82,11 +96,7 @@ struct GemmParams {
   uint32_t* status;
   int N, K, rows, max_tiles, n_experts;
   unsigned long long timeout_ns;  // limit of every bounded wait (mc_set_wait_limit)
-  // when set, output row r goes to row_out[r] (a bf16 row of N features,
-  // local or another GPU's, null = dropped) instead of out + r * N: the
-  // expert-parallel step returns expert rows to their source ranks straight
-  // from this epilogue
-  uint16_t* const* row_out;
+  ReturnMap ret;
 };
 
 // One work item: token rows [m0, mend) of expert e against feature block nb.
@@ -532,7 +542,35 @@ grouped_gemm_kernel(const __grid_constant__ TokenMaps tm, const GemmParams P) {
       const int n16 = cur.n >> 4, split = (n16 + 1) >> 1;
       const int c_lo = grp ? split : 0, c_hi = grp ? n16 : split;
       const uint32_t lane_base = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(buf * C::ACC_COLS);
-      uint16_t* ocol = P.row_out ? nullptr : P.out + (size_t)cur.nb * BF + f;
+      const bool ret = !GU && P.ret.seg_row != nullptr;
+      uint16_t* ocol = ret ? nullptr : P.out + (size_t)cur.nb * BF + f;
+      uint32_t seg[kRetRanks + 1], segh[kRetRanks];
+      if (ret) {  // this expert's source segments (uniform over the warp)
+#pragma unroll
+        for (int k = 0; k <= kRetRanks; ++k)
+          seg[k] = k <= P.ret.W ? __ldg(P.ret.seg_row + (size_t)cur.e * (P.ret.W + 1) + k) : 0u;
+#pragma unroll
+        for (int k = 0; k < kRetRanks; ++k)
+          segh[k] = k < P.ret.W ? __ldg(P.ret.seg_home + (size_t)cur.e * P.ret.W + k) : 0u;
+      }
+      // source segment of output row r (-1: none) and its home row (or null)
+      auto seg_of = [&](uint32_t r) -> int {
+        int kk = -1;
+#pragma unroll
+        for (int k = 0; k < kRetRanks; ++k)
+          if (k < P.ret.W && r >= seg[k] && r < seg[k + 1]) kk = k;
+        return kk;
+      };
+      auto home_row = [&](uint32_t r) -> uint16_t* {
+        uint16_t* d = nullptr;
+#pragma unroll
+        for (int k = 0; k < kRetRanks; ++k)
+          if (k < P.ret.W && r >= seg[k] && r < seg[k + 1]) {
+            const uint32_t hr = segh[k] + (r - seg[k]);
+            d = hr < P.ret.home_cap ? P.ret.home[k] + (size_t)hr * P.N : nullptr;
+          }
+        return d;
+      };
 #pragma unroll 1
       for (int c = c_lo; c < c_hi; ++c) {
         uint32_t g[16], u[16];
@@ -540,6 +578,13 @@ grouped_gemm_kernel(const __grid_constant__ TokenMaps tm, const GemmParams P) {
         if (GU) tmem_ld16(lane_base + MAXN + 16 * c, u);
         tmem_wait_ld();
         const uint32_t r0 = cur.m0 + 16u * (uint32_t)c;
+        // a 16-row group inside one source segment gets one home base
+        uint16_t* gbase = nullptr;
+        if (ret) {
+          const uint32_t rl = min(r0 + 15u, cur.mend - 1u);
+          const int ka = seg_of(r0);
+          if (ka >= 0 && ka == seg_of(rl) && home_row(rl) != nullptr) gbase = home_row(r0);
+        }
 #pragma unroll
         for (int i2 = 0; i2 < 16; i2 += 2) {
           float o0, o1;
@@ -555,14 +600,15 @@ grouped_gemm_kernel(const __grid_constant__ TokenMaps tm, const GemmParams P) {
             o1 = __uint_as_float(g[i2 + 1]);
           }
           const uint32_t pk = pack_bf16x2(o0, o1);
-          if (P.row_out) {
+          if (ret) {
+            const size_t col = (size_t)cur.nb * BF + f;
             if (cur.ok && r0 + i2 < cur.mend) {
-              uint16_t* rp = P.row_out[r0 + i2];
-              if (rp) rp[(size_t)cur.nb * BF + f] = (uint16_t)pk;
+              uint16_t* rp = gbase ? gbase + (size_t)i2 * P.N : home_row(r0 + i2);
+              if (rp) rp[col] = (uint16_t)pk;
             }
             if (cur.ok && r0 + i2 + 1 < cur.mend) {
-              uint16_t* rp = P.row_out[r0 + i2 + 1];
-              if (rp) rp[(size_t)cur.nb * BF + f] = (uint16_t)(pk >> 16);
+              uint16_t* rp = gbase ? gbase + (size_t)(i2 + 1) * P.N : home_row(r0 + i2 + 1);
+              if (rp) rp[col] = (uint16_t)(pk >> 16);
             }
             continue;
           }
@@ -629,7 +675,7 @@ int make_a_map(CUtensorMap* map, const uint16_t* a, int rows, int K, int box_row
 template <bool GU>
 int launch(mc_ctx* ctx, const uint16_t* a, int rows, const mc_qweights* w0, const mc_qweights* w1,
            int n_experts, uint16_t* out, const uint32_t* tiles, const uint32_t* n_tiles,
-           int max_tiles, uint32_t* status, uint16_t* const* row_out = nullptr) {
+           int max_tiles, uint32_t* status, const ReturnMap* ret = nullptr) {
   using C = Cfg<GU>;
   const int N = w0->out_features / n_experts, K = w0->in_features;
   TokenMaps tm;
@@ -638,7 +684,8 @@ int launch(mc_ctx* ctx, const uint16_t* a, int rows, const mc_qweights* w0, cons
       (rc = make_a_map(&tm.m256, a, rows, K, 256)))
     return rc;
   GemmParams P{*w0, GU ? *w1 : *w0, out, reinterpret_cast<const uint4*>(tiles), n_tiles, status,
-               N, K, rows, max_tiles, n_experts, mc_wait_limit(ctx, kTimeoutNs), row_out};
+               N, K, rows, max_tiles, n_experts, mc_wait_limit(ctx, kTimeoutNs), {}};
+  if (ret) P.ret = *ret;
   MC_CUDA(cudaFuncSetAttribute(grouped_gemm_kernel<GU>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                C::SMEM));
   grouped_gemm_kernel<GU><<<ctx->num_sms, kThreads, C::SMEM, ctx->stream>>>(tm, P);
@@ -690,16 +737,28 @@ extern "C" int mc_gemm_q4_grouped(mc_ctx* ctx, const uint16_t* a, int rows, cons
 }
 
 // The down GEMM of the expert-parallel step: mc_gemm_q4_grouped with each
-// output row stored through row_out (ep_prefill.cu).
-int mc_gemm_q4_grouped_rows(mc_ctx* ctx, const uint16_t* a, int rows, const mc_qweights* w,
-                            int n_experts, uint16_t* const* row_out, const uint32_t* tiles,
-                            const uint32_t* n_tiles, int max_tiles, uint32_t* status) {
-  MC_REQUIRE(ctx && row_out, "gemm_q4_grouped_rows: null context or row table");
+// output row stored into its source rank's home buffer (ep_prefill.cu).
+int mc_gemm_q4_grouped_return(mc_ctx* ctx, const uint16_t* a, int rows, const mc_qweights* w,
+                              int n_experts, const uint32_t* seg_row, const uint32_t* seg_home,
+                              void* const* home, int world, size_t home_cap,
+                              const uint32_t* tiles, const uint32_t* n_tiles, int max_tiles,
+                              uint32_t* status) {
+  MC_REQUIRE(ctx && seg_row && seg_home && home, "gemm_q4_grouped_return: null pointer");
+  MC_REQUIRE(world >= 1 && world <= kRetRanks, "gemm_q4_grouped_return: world %d", world);
   int rc = check_grouped(a, rows, w, n_experts, a, tiles, n_tiles, max_tiles,
-                         "gemm_q4_grouped_rows");
+                         "gemm_q4_grouped_return");
   if (rc) return rc;
+  ReturnMap rm{};
+  rm.seg_row = seg_row;
+  rm.seg_home = seg_home;
+  for (int k = 0; k < world; ++k) {
+    MC_REQUIRE(home[k] && mc_aligned(home[k], 16), "gemm_q4_grouped_return: home buffer %d", k);
+    rm.home[k] = static_cast<uint16_t*>(home[k]);
+  }
+  rm.W = world;
+  rm.home_cap = (uint32_t)(home_cap < 0xffffffffu ? home_cap : 0xffffffffu);
   return launch<false>(ctx, a, rows, w, nullptr, n_experts, nullptr, tiles, n_tiles, max_tiles,
-                       status, row_out);
+                       status, &rm);
 }
 
 extern "C" size_t mc_gemm_q4_workspace_words(int m) {

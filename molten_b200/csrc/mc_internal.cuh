@@ -38,11 +38,15 @@ int mc_decode_layer_impl(mc_ctx* ctx, const uint16_t* h, const uint16_t* b,
                          const mc_qweights* gate, const mc_qweights* up, const mc_qweights* down,
                          int n_experts, uint16_t* out, uint32_t* sync, size_t ws_words, float eps,
                          float route_eps, bool noalloc, uint32_t* status_out);
-// Grouped GEMM (not gate/up) whose output row r is stored at row_out[r]
+// Grouped GEMM (not gate/up) storing each output row into its source
+// rank's home buffer: rows of expert j from source s are seg_row[j][s] ..
+// seg_row[j][s+1] and go to rows from seg_home[j][s] of home[s]
 // (grouped_gemm.cu).
-int mc_gemm_q4_grouped_rows(mc_ctx* ctx, const uint16_t* a, int rows, const mc_qweights* w,
-                            int n_experts, uint16_t* const* row_out, const uint32_t* tiles,
-                            const uint32_t* n_tiles, int max_tiles, uint32_t* status);
+int mc_gemm_q4_grouped_return(mc_ctx* ctx, const uint16_t* a, int rows, const mc_qweights* w,
+                              int n_experts, const uint32_t* seg_row, const uint32_t* seg_home,
+                              void* const* home, int world, size_t home_cap,
+                              const uint32_t* tiles, const uint32_t* n_tiles, int max_tiles,
+                              uint32_t* status);
 // Expert-parallel state (ep_prefill.cu): waits for the stream while watching
 // the communicator (mc_sync with a communicator); releases it on mc_destroy.
 int mc_ep_wait(mc_ctx* ctx);

@@ -28,8 +28,7 @@
 //   ws[2]            sticky error status bits: 1 logits wait gave up,
 //                    2 expert id out of range, 8 act wait, 16 a copy wait
 //   ws[3]            reserved (zero)
-//   ws[4]            router warps that published their logit (reset by the
-//                    last CTA to finish)
+//   ws[4]            reserved (zero; reset by the last CTA to finish)
 //   ws[5..8)         reserved (zero)
 //   ws[8..136)       64 tagged logits (u64: tag32 << 32 | f32 bits)
 //   ws[136..)        act values [slot][row], one tagged word each
@@ -263,9 +262,9 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(const Par
   __syncthreads();
   TRACE(1);
 
-  // ---- router logit of expert `cta` (warp 0), published epoch-tagged; the
-  // release add (which orders the store before it) counts the published
-  // logits, so readers poll one word instead of all E
+  // ---- router logit of expert `cta` (warp 0), published epoch-tagged: the
+  // tag and the value share one 64-bit word, so a reader that sees this
+  // launch's tag has the value (no fence, no counter)
   if (router_cta && warp == 0) {
     if (P.trace && t == 0) {  // profiling aid: when the router row arrives
       const uint4* w = reinterpret_cast<const uint4*>(rr.w);
@@ -282,32 +281,20 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(const Par
       P.logits[cta] = z;
       mc_st_publish_u64(logits64 + cta,
                         ((unsigned long long)tag32 << 32) | (unsigned long long)__float_as_uint(z));
-      mc_red_release_add(sync + 4, 1u);
     }
   }
   TRACE(2);
 
   // ---- gate/up activations prescaled once (all warps), meanwhile warp 0
-  // gathers the tagged logits
+  // gathers the tagged logits: lane l polls logits 2l, 2l+1 (one 16-byte
+  // load) until both carry this launch's tag
   float2 xs[32];
   const float xg = load_group_x<4, 2>(nbf, lane, xs);
   if (warp == 0) {
-    // lane 0 waits (backing off) until all E router warps have published;
-    // then lane l reads logits 2l, 2l+1 in one 16-byte load (tags checked)
     const unsigned long long deadline = mc_globaltimer() + P.timeout_ns;
     bool got = true;
-    if (lane == 0) {
-      while (mc_ld_acquire(sync + 4) < (uint32_t)P.E) {
-        if (mc_globaltimer() > deadline) {
-          got = false;
-          break;
-        }
-        __nanosleep(32);
-      }
-    }
     TRACE(14);
-    got = __shfl_sync(0xffffffffu, got ? 1 : 0, 0) != 0;
-    if (got && 2 * lane < P.E) {
+    if (2 * lane < P.E) {
       const int i = 2 * lane;
       unsigned long long v0, v1;
       for (;;) {
@@ -318,7 +305,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(const Par
           got = false;
           break;
         }
-        __nanosleep(64);
+        __nanosleep(32);
       }
       zs[i] = __uint_as_float((uint32_t)v0);
       if (i + 1 < P.E) zs[i + 1] = __uint_as_float((uint32_t)v1);
