@@ -35,6 +35,7 @@ struct PeerPtrs {
 
 // Segment starts for one expert e: where its rows from `src` land in the
 // owner's receive buffer, and where they sit in src's sorted order.
+// counts_all may be global or shared memory.
 __device__ __forceinline__ void segment_bases(const uint32_t* counts_all, int W, int E, int e,
                                               int src, uint32_t* recv_row, uint32_t* src_row) {
   const int P = E / W, owner = e / P, j0 = owner * P;
@@ -59,15 +60,18 @@ ep_dispatch_kernel(const uint4* __restrict__ x, int m, int h16,
                    const uint32_t* __restrict__ ids_sorted, const uint32_t* __restrict__ counts_all,
                    int rank, int W, int E, PeerPtrs recv, uint32_t cap, uint32_t* status) {
   __shared__ uint32_t src0[kMaxExperts + 1], dst0[kMaxExperts];
+  __shared__ uint32_t ca[kMaxRanks * kMaxExperts];  // the count table, staged once
+  for (int i = threadIdx.x; i < W * E; i += blockDim.x) ca[i] = counts_all[i];
+  __syncthreads();
   for (int e = threadIdx.x; e < E; e += blockDim.x) {
     uint32_t d, s;
-    segment_bases(counts_all, W, E, e, rank, &d, &s);
+    segment_bases(ca, W, E, e, rank, &d, &s);
     src0[e] = s;
     dst0[e] = d;
   }
   if (threadIdx.x == 0) {
     uint32_t t = 0;
-    for (int e = 0; e < E; ++e) t += counts_all[rank * E + e];
+    for (int e = 0; e < E; ++e) t += ca[rank * E + e];
     src0[E] = t;
   }
   __syncthreads();
@@ -131,9 +135,12 @@ ep_tiles_kernel(const uint32_t* __restrict__ counts_all, int rank, int W, int E,
                 int max_tiles) {
   const int P = E / W;
   __shared__ uint32_t total_s[kMaxExperts];
+  __shared__ uint32_t ca[kMaxRanks * kMaxExperts];  // the count table, staged once
+  for (int i = threadIdx.x; i < W * E; i += blockDim.x) ca[i] = counts_all[i];
+  __syncthreads();
   for (int j = threadIdx.x; j < P; j += blockDim.x) {
     uint32_t t = 0;
-    for (int s = 0; s < W; ++s) t += counts_all[s * E + rank * P + j];
+    for (int s = 0; s < W; ++s) t += ca[s * E + rank * P + j];
     total_s[j] = t;
   }
   __syncthreads();

@@ -223,8 +223,11 @@ ep_publish_counts_kernel(const uint32_t* __restrict__ counts, FlagPtrs tables, i
 // j's rows) and the first row of them in the source's home buffer
 // (seg_home[j][s], the source's own sorted order). One CTA.
 __global__ void __launch_bounds__(256)
-ep_segments_kernel(const uint32_t* __restrict__ counts_all, int rank, int W, int E_slots,
+ep_segments_kernel(const uint32_t* __restrict__ counts_all_g, int rank, int W, int E_slots,
                    uint32_t* __restrict__ seg_row, uint32_t* __restrict__ seg_home) {
+  __shared__ uint32_t counts_all[kMaxRanks * 256];  // the table, staged once
+  for (int i = threadIdx.x; i < W * E_slots; i += blockDim.x) counts_all[i] = counts_all_g[i];
+  __syncthreads();
   const int spr = E_slots / W;
   for (int t = threadIdx.x; t < spr * (W + 1); t += blockDim.x) {
     const int j = t / (W + 1), s = t % (W + 1), slot = rank * spr + j;

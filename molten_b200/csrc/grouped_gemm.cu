@@ -553,13 +553,24 @@ grouped_gemm_kernel(const __grid_constant__ TokenMaps tm, const GemmParams P) {
         for (int k = 0; k < kRetRanks; ++k)
           segh[k] = k < P.ret.W ? __ldg(P.ret.seg_home + (size_t)cur.e * P.ret.W + k) : 0u;
       }
-      // source segment of output row r (-1: none) and its home row (or null)
-      auto seg_of = [&](uint32_t r) -> int {
-        int kk = -1;
+      // the source segment holding the current rows: rows [s_lo, s_hi) go to
+      // home rows from s_base (null when the segment would pass the home
+      // buffer's end); looked up again only when a group leaves it
+      uint32_t s_lo = 1u, s_hi = 0u;
+      uint16_t* s_base = nullptr;
+      auto locate = [&](uint32_t r) {
+        s_lo = 1u;
+        s_hi = 0u;
+        s_base = nullptr;
 #pragma unroll
         for (int k = 0; k < kRetRanks; ++k)
-          if (k < P.ret.W && r >= seg[k] && r < seg[k + 1]) kk = k;
-        return kk;
+          if (k < P.ret.W && r >= seg[k] && r < seg[k + 1]) {
+            s_lo = seg[k];
+            s_hi = seg[k + 1];
+            s_base = segh[k] + (s_hi - s_lo) <= P.ret.home_cap
+                         ? P.ret.home[k] + (size_t)segh[k] * P.N
+                         : nullptr;
+          }
       };
       auto home_row = [&](uint32_t r) -> uint16_t* {
         uint16_t* d = nullptr;
@@ -582,8 +593,8 @@ grouped_gemm_kernel(const __grid_constant__ TokenMaps tm, const GemmParams P) {
         uint16_t* gbase = nullptr;
         if (ret) {
           const uint32_t rl = min(r0 + 15u, cur.mend - 1u);
-          const int ka = seg_of(r0);
-          if (ka >= 0 && ka == seg_of(rl) && home_row(rl) != nullptr) gbase = home_row(r0);
+          if (!(r0 >= s_lo && rl < s_hi)) locate(r0);
+          if (r0 >= s_lo && rl < s_hi && s_base) gbase = s_base + (size_t)(r0 - s_lo) * P.N;
         }
 #pragma unroll
         for (int i2 = 0; i2 < 16; i2 += 2) {
