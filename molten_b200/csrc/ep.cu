@@ -245,7 +245,7 @@ extern "C" int mc_ep_dispatch(mc_ctx* ctx, const uint16_t* x, int m, int hidden,
   if ((rc = fill_peers(&pp, recv_bufs, world, "ep_dispatch"))) return rc;
   MC_REQUIRE(m >= 1 && recv_cap_rows >= 1 && recv_cap_rows <= 0xffffffffu,
              "ep_dispatch: m %d / capacity %zu", m, recv_cap_rows);
-  const int grid = std::max(1, std::min((4 * m + 7) / 8, ctx->num_sms * 8));
+  const int grid = std::max(1, std::min((4 * m + 7) / 8, ctx->num_sms * 2));
   ep_dispatch_kernel<<<grid, 256, 0, ctx->stream>>>(
       reinterpret_cast<const uint4*>(x), m, hidden / 8, ids_sorted, counts_all, rank, world,
       n_experts, pp, (uint32_t)recv_cap_rows, status);

@@ -244,6 +244,43 @@ ep_segments_kernel(const uint32_t* __restrict__ counts_all_g, int rank, int W, i
   }
 }
 
+// The return without the fused epilogue: received expert rows ed[i] -> row
+// seg_home + (i - seg_row) of their source's home buffer, every warp taking
+// rows across all segments (grid-stride), the segment found by binary search
+// over the (slot, source) starts staged in shared memory.
+__global__ void __launch_bounds__(256)
+ep_return_rows_kernel(const uint4* __restrict__ ed, int h16, const uint32_t* __restrict__ seg_row,
+                      const uint32_t* __restrict__ seg_home, int spr, int W, FlagPtrs home,
+                      uint32_t home_cap, uint32_t* status) {
+  __shared__ uint32_t st[257], sh[256];
+  const int nseg = spr * W;
+  for (int k = threadIdx.x; k < nseg; k += blockDim.x) {
+    st[k] = seg_row[(k / W) * (W + 1) + k % W];
+    sh[k] = seg_home[k];
+  }
+  if (threadIdx.x == 0) st[nseg] = seg_row[(spr - 1) * (W + 1) + W];
+  __syncthreads();
+  const uint32_t total = st[nseg];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (uint32_t r = blockIdx.x * 8 + warp; r < total; r += gridDim.x * 8) {
+    int lo = 0, hi = nseg;  // st[lo] <= r < st[hi]
+    while (hi - lo > 1) {
+      const int mid = (lo + hi) >> 1;
+      if (st[mid] <= r) lo = mid;
+      else hi = mid;
+    }
+    const uint32_t hr = sh[lo] + (r - st[lo]);
+    if (hr >= home_cap) {
+      if (lane == 0 && status) atomicOr(status, 4u);
+      continue;
+    }
+    uint4* out = reinterpret_cast<uint4*>(home.p[lo % W]) + (size_t)hr * h16;
+    const uint4* row = ed + (size_t)r * h16;
+    for (int c = lane; c < h16; c += 32) out[c] = row[c];
+  }
+  __threadfence_system();
+}
+
 int ep_barrier(mc_ctx* ctx) {
   mc_ep_state* ep = ctx->ep;
   FlagPtrs f;
