@@ -573,9 +573,9 @@ CFG3_METRIC = "prefill grouped-GEMM tokens/s (cfg3: 4096-token MoE FFN, Zipf rou
 CFG3_WORKLOAD = ("cfg3: 4096 tokens per GPU x 2048, E=64 top-4 Zipf(s=1) routing, "
                  "SwiGLU 2048->1536->2048 Q4")
 # kernels one mc_ep_moe_prefill launches: route, relabel, sort (2), counts
-# exchange, row chunks, return map, dispatch, barrier, gate/up GEMM, down GEMM
-# (returning its rows), barrier, combine
-EP_STEP_LAUNCHES = 13
+# exchange, row chunks, return map, dispatch, barrier, gate/up GEMM, down GEMM,
+# return, barrier, combine
+EP_STEP_LAUNCHES = 14
 
 
 def prefill_flops(S):
@@ -726,10 +726,10 @@ def bench_cfg3_ep(args, torch, ws, rank, local):
                    "placement": ("greedy by the expert load of one routing pass, hot experts "
                                  "replicated in the spare slots (mc_ep_place)"
                                  if args.ep_placement == "balanced" else "contiguous ranges"),
-                   "exchange": "one library call per step (mc_ep_moe_prefill): counts and "
-                               "token rows stored into the other ranks' buffers over NVLink "
-                               "(CUDA IPC), expert rows returned by the down GEMM's epilogue, "
-                               "device-side bounded barriers, no host sync",
+                   "exchange": "one library call per step (mc_ep_moe_prefill): counts, "
+                               "token rows and expert rows stored into the other ranks' "
+                               "buffers over NVLink (CUDA IPC), device-side bounded barriers, "
+                               "no host sync",
                    "per_rank": per_rank,
                    "l2": "expert weights > L2, streamed every step"},
         "e2e": {"value": round(ws * m * n_e2e / (e2e_ms * 1e-3), 1), "unit": "tokens/s",

@@ -405,8 +405,8 @@ int mc_ep_return(mc_ctx* ctx, const uint16_t* ed, size_t ed_rows, int hidden,
  *           tables everywhere; the rank loads the weights of its slots
  *           (slot_expert[rank*spr ..]) stacked in slot order;
  *           mc_ep_moe_prefill(...) per step (collective; no host sync; the
- *           counts and rows move by peer stores, the down GEMM's epilogue
- *           returns each expert row to its source, bounded device barriers);
+ *           counts, token rows and expert rows move by peer stores between
+ *           bounded device barriers);
  *           mc_ep_status(ctx, &st) when it wants the step's status bits
  *           (1 a GEMM wait, 2 a malformed tile or expert id, 4 rows beyond a
  *           capacity, 8 a cross-rank barrier that gave up); mc_sync waits for
@@ -446,8 +446,8 @@ int mc_ep_finalize(mc_ctx* ctx);
 /* Profiling aid: with `on`, each step records events at its phase
  * boundaries; mc_ep_phase_ms waits and writes the last step's six phase
  * times in ms (route + relabel + sort, counts exchange + barrier, row chunks
- * + return map + dispatch + barrier, grouped GEMMs with the return, the
- * barrier after it, combine). */
+ * + return map + dispatch + barrier, grouped GEMMs + return, the barrier
+ * after it, combine). */
 int mc_ep_set_profile(mc_ctx* ctx, int on);
 int mc_ep_phase_ms(mc_ctx* ctx, float* out6);
 

@@ -8,9 +8,14 @@
 //   count table (peer stores) + barrier -> receive-side row chunks and the
 //   return map -> dispatch: rows stored straight into the owners' receive
 //   buffers over NVLink (CUDA IPC mappings) -> barrier -> grouped gate/up
-//   (+SwiGLU) GEMM -> down GEMM whose epilogue stores each expert row
-//   straight into its source's home buffer (the return overlaps the GEMM) ->
-//   barrier -> weighted combine at home.
+//   (+SwiGLU) and down GEMMs -> return: each expert row stored into its
+//   source's home buffer -> barrier -> weighted combine at home.
+//
+// (Returning the rows from the down GEMM's epilogue instead, so the NVLink
+// traffic overlaps the GEMM, measured slower on two B200s: 0.668 against
+// 0.640 ms per step. The epilogue runs on the dequantising warps, the
+// GEMM's critical resource, and paid more for the per-row destinations than
+// the separate copy costs. mc_gemm_q4_grouped_return keeps that variant.)
 //
 // Slots. E_slots = W * slots_per_rank; rank r owns slots [r*spr, (r+1)*spr)
 // and holds their weights stacked in slot order. With spr = E / W and an
@@ -49,8 +54,8 @@ constexpr int kChunk = 256;  // token rows per grouped-GEMM chunk
 constexpr unsigned long long kBarrierNs = 1000000000ull;  // default barrier limit: 1 s
 // Phases of a step timed by mc_ep_set_profile: route + relabel + sort, the
 // counts exchange (peer stores + barrier), row chunks + return map +
-// dispatch + barrier, the two grouped GEMMs (the down GEMM returning its
-// rows), the barrier after the return, combine.
+// dispatch + barrier, the two grouped GEMMs and the return, the barrier
+// after the return, combine.
 constexpr int kPhases = 6;
 constexpr size_t kCountsOff = 256;  // count table after the flag words in the control area
 
@@ -526,10 +531,19 @@ extern "C" int mc_ep_moe_prefill(mc_ctx* ctx, const uint16_t* x, const float* lo
                                   ep->n_tiles, ep->max_tiles, ep->status)))
     return rc;
   // the down GEMM stores each expert row straight into its source's home row
-  if ((rc = mc_gemm_q4_grouped_return(ctx, ep->act, rows, down, ep->spr, ep->seg_row,
-                                      ep->seg_home, ep->home_ptr, W, ep->home_cap, ep->tiles,
-                                      ep->n_tiles, ep->max_tiles, ep->status)))
+  if ((rc = mc_gemm_q4_grouped(ctx, ep->act, rows, down, ep->spr, ep->ed, ep->tiles, ep->n_tiles,
+                               ep->max_tiles, ep->status)))
     return rc;
+  {
+    FlagPtrs home;
+    for (int r = 0; r < kMaxRanks; ++r)
+      home.p[r] = r < W ? static_cast<uint32_t*>(ep->home_ptr[r]) : nullptr;
+    const int grid = ctx->num_sms * 2;
+    ep_return_rows_kernel<<<grid, 256, 0, ctx->stream>>>(
+        reinterpret_cast<const uint4*>(ep->ed), ep->H / 8, ep->seg_row, ep->seg_home, ep->spr, W,
+        home, (uint32_t)ep->home_cap, ep->status);
+    if ((rc = mc_after_launch("ep_return_rows_kernel"))) return rc;
+  }
   if ((rc = mark(4))) return rc;
   if ((rc = ep_barrier(ctx))) return rc;
   if ((rc = mark(5))) return rc;

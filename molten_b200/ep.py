@@ -449,8 +449,7 @@ def moe_prefill_ep_emulated(ctx, xs, logits, gate, up, down, n_experts: int, pla
 # ------------------------------------------------- the C-ABI expert-parallel step
 # The whole step runs inside the library (mc_ep_moe_prefill): routing, slot
 # relabelling, sort, the counts exchange and the dispatch over NVLink,
-# device-side barriers, the grouped GEMMs (the down GEMM returning its rows)
-# and the combine. Python only bootstraps the NCCL unique id and loads each
+# device-side barriers, the grouped GEMMs, the return and the combine. Python only bootstraps the NCCL unique id and loads each
 # rank's slot weights.
 
 def place_slots(load, world: int, slots_per_rank: int):
