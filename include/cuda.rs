@@ -258,11 +258,12 @@ extern "C" {
         seen: *const u32,
         s: *const McSampling,
         pos: u32,
+        pos_dev: *const u32,
         key: *mut u64,
         workspace: *mut c_void,
         ws_bytes: usize,
     ) -> c_int;
-    pub fn mc_sample_mark(ctx: *mut McCtx, tok: *const u32, seen: *mut u32, vocab: c_int) -> c_int;
+    pub fn mc_sample_mark(ctx: *mut McCtx, tok: *const u32, seen: *mut u32, vocab: c_int, pos_dev: *mut u32) -> c_int;
     pub fn mc_moe_route_batch(
         ctx: *mut McCtx,
         logits: *const f32,

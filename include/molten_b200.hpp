@@ -458,13 +458,14 @@ inline void sample_draw(Context& ctx, const Tensor& logits, const Tensor* seen,
   ensure(best.dtype == DType::U64 && best.numel() >= 1, "sampling key");
   ensure(s.repetition_penalty == 1.0f || seen, "a repetition penalty needs the seen set");
   check(mc_sample_draw(ctx.handle(), logits.as<const uint16_t>(), (int)logits.numel(),
-                       seen ? seen->as<const uint32_t>() : nullptr, &s, pos,
+                       seen ? seen->as<const uint32_t>() : nullptr, &s, pos, nullptr,
                        best.as<unsigned long long>(), workspace.data, workspace.nbytes()));
 }
 
 inline void sample_mark(Context& ctx, const Tensor& tok, const Tensor& seen, int vocab) {
   ensure(tok.numel() == 1 && tok.dtype == DType::U32, "sampled token slot");
-  check(mc_sample_mark(ctx.handle(), tok.as<const uint32_t>(), seen.as<uint32_t>(), vocab));
+  check(mc_sample_mark(ctx.handle(), tok.as<const uint32_t>(), seen.as<uint32_t>(), vocab,
+                       nullptr));
 }
 
 // Tensor::write_bytes / contents (tensor.rs:127-146, 165-200): stream-ordered

@@ -264,13 +264,18 @@ typedef struct mc_sampling {
  * words zero again; the rest is scratch); unused (may be NULL) when top_k
  * and top_p are both off. */
 size_t mc_sample_workspace_bytes(int vocab);
+/* pos_dev (nullable): read the position from this device word instead of
+ * `pos`, so a decode step captured once in a CUDA graph draws each replay at
+ * the next position (mc_sample_mark advances it). */
 int mc_sample_draw(mc_ctx* ctx, const uint16_t* logits, int vocab, const uint32_t* seen,
-                   const mc_sampling* s, uint32_t pos, unsigned long long* key,
-                   void* workspace, size_t ws_bytes);
+                   const mc_sampling* s, uint32_t pos, const uint32_t* pos_dev,
+                   unsigned long long* key, void* workspace, size_t ws_bytes);
 /* SampleScratch::encode_mark (lfm/sample.rs:340-353 -> lfm_sample_mark
  * lfm_sample.metal:922-931): after mc_token_tail wrote *tok, sets its bit in
- * `seen`. */
-int mc_sample_mark(mc_ctx* ctx, const uint32_t* tok, uint32_t* seen, int vocab);
+ * `seen` (nullable: no penalty) and, when pos_dev is set, advances the
+ * device position by one. */
+int mc_sample_mark(mc_ctx* ctx, const uint32_t* tok, uint32_t* seen, int vocab,
+                   uint32_t* pos_dev);
 
 /* ----------------------------------------------------------- prefill path */
 

@@ -111,8 +111,8 @@ SIGNATURES: dict[str, tuple] = {
     "mc_conv3_gemv": (I, [P, QP, P, P, P, P, P, I]),
     "mc_gemv_gu_act": (I, [P, QP, QP, P, P, I]),
     "mc_sample_workspace_bytes": (C.c_size_t, [I]),
-    "mc_sample_draw": (I, [P, P, I, P, C.POINTER(Sampling), C.c_uint32, P, P, C.c_size_t]),
-    "mc_sample_mark": (I, [P, P, P, I]),
+    "mc_sample_draw": (I, [P, P, I, P, C.POINTER(Sampling), C.c_uint32, P, P, P, C.c_size_t]),
+    "mc_sample_mark": (I, [P, P, P, I, P]),
     "mc_moe_route_batch": (I, [P, P, I, I, I, P, F, P, P]),
     "mc_moe_sort_map": (I, [P, P, I, I, I, P, P, P, P, P, P, I]),
     "mc_gather_rows_bf16": (I, [P, P, P, I, I, P]),

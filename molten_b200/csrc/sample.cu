@@ -53,9 +53,14 @@ struct Params {
   uint32_t top_k;        // 0 = off
   uint64_t p_fix;        // rint(top_p * 2^32); 2^32 = off
   uint32_t seed_lo, seed_hi, pos;
+  const uint32_t* pos_dev;  // when set, the position is read here (device feedback)
   int vocab;
   unsigned long long* key;
 };
+
+__device__ __forceinline__ uint32_t draw_pos(const Params& P) {
+  return P.pos_dev ? *P.pos_dev : P.pos;
+}
 
 // Workspace: the plan, the global histogram, then w[vocab].
 struct Plan {
@@ -343,7 +348,7 @@ __global__ void __launch_bounds__(kTG) sample_draw_kernel(const Params P, void* 
       const uint2 raw = *reinterpret_cast<const uint2*>(P.logits + i0);
       const uint16_t h[4] = {(uint16_t)raw.x, (uint16_t)(raw.x >> 16), (uint16_t)raw.y,
                              (uint16_t)(raw.y >> 16)};
-      uint32_t c[4] = {(uint32_t)i0 >> 2, P.pos, MC_SAMPLE_DOMAIN, 0u};
+      uint32_t c[4] = {(uint32_t)i0 >> 2, draw_pos(P), MC_SAMPLE_DOMAIN, 0u};
       mc_philox4x32_10(c, P.seed_lo, P.seed_hi);
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
@@ -365,7 +370,7 @@ __global__ void __launch_bounds__(kTG) sample_draw_kernel(const Params P, void* 
 #pragma unroll
     for (int j = 0; j < 4; ++j) any |= mc_fkey(wv[j]) >= tau;
     if (any) {
-      uint32_t c[4] = {(uint32_t)i0 >> 2, P.pos, MC_SAMPLE_DOMAIN, 0u};
+      uint32_t c[4] = {(uint32_t)i0 >> 2, draw_pos(P), MC_SAMPLE_DOMAIN, 0u};
       mc_philox4x32_10(c, P.seed_lo, P.seed_hi);
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
@@ -390,12 +395,14 @@ __global__ void __launch_bounds__(kTG) sample_draw_kernel(const Params P, void* 
   }
 }
 
-__global__ void sample_mark_kernel(const uint32_t* tok, uint32_t* seen, int vocab) {
+__global__ void sample_mark_kernel(const uint32_t* tok, uint32_t* seen, int vocab,
+                                   uint32_t* pos_dev) {
   mc_pdl_launch_dependents();
   mc_pdl_wait();
   if (threadIdx.x == 0) {
     const uint32_t t = *tok;
-    if (t < (uint32_t)vocab) seen[t >> 5] |= 1u << (t & 31u);
+    if (seen && t < (uint32_t)vocab) seen[t >> 5] |= 1u << (t & 31u);
+    if (pos_dev) *pos_dev += 1u;
   }
 }
 
@@ -412,8 +419,8 @@ extern "C" size_t mc_sample_workspace_bytes(int vocab) {
 }
 
 extern "C" int mc_sample_draw(mc_ctx* ctx, const uint16_t* logits, int vocab, const uint32_t* seen,
-                              const mc_sampling* s, uint32_t pos, unsigned long long* key,
-                              void* workspace, size_t ws_bytes) {
+                              const mc_sampling* s, uint32_t pos, const uint32_t* pos_dev,
+                              unsigned long long* key, void* workspace, size_t ws_bytes) {
   MC_REQUIRE(ctx, "sample_draw: null context");
   MC_REQUIRE(s, "sample_draw: null sampling parameters");
   MC_REQUIRE(logits && key, "sample_draw: null logits or key");
@@ -450,6 +457,7 @@ extern "C" int mc_sample_draw(mc_ctx* ctx, const uint16_t* logits, int vocab, co
   P.seed_lo = (uint32_t)s->seed;
   P.seed_hi = (uint32_t)(s->seed >> 32);
   P.pos = pos;
+  P.pos_dev = pos_dev;
   P.vocab = vocab;
   P.key = key;
   const int wide = (vocab + kTG * kTokPerThread - 1) / (kTG * kTokPerThread);
@@ -472,9 +480,11 @@ extern "C" int mc_sample_draw(mc_ctx* ctx, const uint16_t* logits, int vocab, co
   return launch(sample_draw_kernel<0>, wide, P, workspace, ctx, "sample_draw_kernel");
 }
 
-extern "C" int mc_sample_mark(mc_ctx* ctx, const uint32_t* tok, uint32_t* seen, int vocab) {
+extern "C" int mc_sample_mark(mc_ctx* ctx, const uint32_t* tok, uint32_t* seen, int vocab,
+                              uint32_t* pos_dev) {
   MC_REQUIRE(ctx, "sample_mark: null context");
-  MC_REQUIRE(tok && seen && vocab >= 1, "sample_mark: bad arguments");
-  MC_CUDA(mc_launch_pdl(sample_mark_kernel, dim3(1), dim3(32), 0, ctx->stream, tok, seen, vocab));
+  MC_REQUIRE(tok && (seen || pos_dev) && vocab >= 1, "sample_mark: bad arguments");
+  MC_CUDA(mc_launch_pdl(sample_mark_kernel, dim3(1), dim3(32), 0, ctx->stream, tok, seen, vocab,
+                        pos_dev));
   return mc_after_launch("sample_mark_kernel");
 }

@@ -97,19 +97,25 @@ class SampleScratch:
                 bits[t // 32] |= np.uint32(1 << (t % 32))
         self.seen.copy_(torch.from_numpy(bits.view(np.int32)))
 
-    def encode_draw(self, logits: torch.Tensor, best: torch.Tensor, s: Sampling, pos: int) -> None:
+    def encode_draw(self, logits: torch.Tensor, best: torch.Tensor, s: Sampling,
+                    pos: int | torch.Tensor) -> None:
         """Draws the token at absolute position ``pos`` from bf16 ``logits``
-        [vocab] into ``best`` (int64 [1], zero on entry)."""
+        [vocab] into ``best`` (int64 [1], zero on entry). ``pos`` may be a
+        device int32 [1] tensor (read on the device: a captured step draws at
+        the position ``encode_mark`` advanced)."""
         ensure(logits.numel() == self.vocab and logits.dtype == torch.bfloat16,
                "sampling logits row")
         ensure(best.dtype == torch.int64 and best.numel() >= 1, "sampling key")
-        ensure(0 <= pos < 2 ** 32, "position exceeds u32")
+        dev_pos = isinstance(pos, torch.Tensor)
+        ensure(dev_pos or 0 <= pos < 2 ** 32, "position exceeds u32")
         sp = s.c()
         _lib.call("mc_sample_draw", self.ctx.handle, _p(logits), self.vocab,
-                  _p(self.seen) if s.uses_penalty() else None, _lib.C.byref(sp), pos, _p(best),
+                  _p(self.seen) if s.uses_penalty() else None, _lib.C.byref(sp),
+                  0 if dev_pos else pos, _p(pos) if dev_pos else None, _p(best),
                   _p(self.ws), self.ws.numel())
 
-    def encode_mark(self, tok: torch.Tensor) -> None:
-        """After the token tail wrote ``tok`` (int32 [1]): adds it to the seen set."""
+    def encode_mark(self, tok: torch.Tensor, pos: torch.Tensor | None = None) -> None:
+        """After the token tail wrote ``tok`` (int32 [1]): adds it to the seen
+        set, and advances the device position ``pos`` (int32 [1]) when given."""
         ensure(tok.numel() == 1 and tok.dtype == torch.int32, "sampled token slot")
-        _lib.call("mc_sample_mark", self.ctx.handle, _p(tok), _p(self.seen), self.vocab)
+        _lib.call("mc_sample_mark", self.ctx.handle, _p(tok), _p(self.seen), self.vocab, _p(pos))

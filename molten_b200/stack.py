@@ -30,6 +30,13 @@ residual stream. The expert part runs one of three ways (``moe_path``):
 
 The token feeds back on the device, so a step can be captured once in a CUDA
 graph and replayed.
+
+With ``sampling`` (batch 1, the reference's temperature > 0 path,
+lfm/sample.rs), the head stores its bf16 logits (gemv_quant) and the draw
+(mc_sample_draw) folds the sampled token into the same key the greedy head
+writes; the token tail then runs unchanged and mc_sample_mark adds the token
+to the seen set and advances the device position, so the sampled step is
+graph-capturable too.
 """
 from __future__ import annotations
 
@@ -40,8 +47,10 @@ from molten_b200 import lfm
 
 class DecodeStack:
     def __init__(self, ctx: lfm.Context, layers: list[dict], head, embed: torch.Tensor,
-                 batch: int, n_experts: int = 64, moe_path: str | None = None):
+                 batch: int, n_experts: int = 64, moe_path: str | None = None, sampling=None):
         self.ctx, self.layers, self.head, self.embed = ctx, layers, head, embed
+        self.sampling = sampling
+        lfm.ensure(sampling is None or batch == 1, "sampling decodes one sequence")
         self.B, self.E = batch, n_experts
         # measured on B200 (40 layers): batch 8 runs faster on the per-token
         # GEMVs, batch 32 on the grouped expert GEMMs
@@ -72,10 +81,21 @@ class DecodeStack:
         if self.path == "grouped":
             nb = lfm.moe_prefill_workspace_size(batch, n_experts, H, I)
             self.pws = torch.zeros(nb, dtype=torch.uint8, device=dev)
+        self.sample = None
+        if sampling is not None:
+            from molten_b200.sample import SampleScratch
+            self.sample = SampleScratch(ctx, head.out_features)
+            self.head_logits = bf(head.out_features)
+            self.pos = torch.zeros(1, dtype=torch.int32, device=dev)
 
-    def start(self, tokens: torch.Tensor) -> None:
-        """Loads the embedding rows of the first tokens (int32 [B])."""
+    def start(self, tokens: torch.Tensor, pos: int = 0, seen=()) -> None:
+        """Loads the embedding rows of the first tokens (int32 [B]); with
+        sampling, ``pos`` is the absolute position of the token the next step
+        draws and ``seen`` the sequence's token ids so far."""
         self.x.copy_(self.embed[tokens.long()])
+        if self.sample is not None:
+            self.pos.fill_(pos)
+            self.sample.upload_seen(list(seen) + [int(t) for t in tokens.cpu()])
 
     def step(self) -> None:
         ctx, cur = self.ctx, self.x
@@ -102,9 +122,15 @@ class DecodeStack:
                     lfm.gemv_gather_down_combine4(ctx, L["down"], self.act, self.ids[l],
                                                   self.wts[l], nxt, n_experts=self.E)
             cur = nxt
-        lfm.gemv_head_argmax(ctx, self.head, cur, self.keys)
+        if self.sample is None:
+            lfm.gemv_head_argmax(ctx, self.head, cur, self.keys)
+        else:
+            lfm.gemv_quant(ctx, self.head, cur, self.head_logits)
+            self.sample.encode_draw(self.head_logits, self.keys, self.sampling, self.pos)
         lfm.token_tail(ctx, self.keys, self.tokens,
                        (self.embed, self.tail_norm_w, self.x, self.tail_normed))
+        if self.sample is not None:
+            self.sample.encode_mark(self.tokens, self.pos)
 
     def status_words(self) -> list[torch.Tensor]:
         """The device status words this stack's kernels report into (the
@@ -131,4 +157,10 @@ class DecodeStack:
 
     def launches_per_step(self) -> int:
         per_layer = {"fused": 2, "gemv": 4, "grouped": 2 + lfm.MOE_PREFILL_LAUNCHES}[self.path]
-        return len(self.layers) * per_layer + 2
+        tail = 2
+        if self.sampling is not None:
+            s = self.sampling
+            full = (s.top_k == 0 or s.top_k >= self.head.out_features) and s.top_p >= 1.0
+            draw = 1 if full else 2 + 3 * ((s.top_k > 0) + (s.top_p < 1.0))
+            tail = 1 + draw + 1 + 1
+        return len(self.layers) * per_layer + tail

@@ -109,3 +109,57 @@ def test_stacked_decode_grouped_path(cuda_ctx):
             assert 0.0 <= gap <= 2e-2 * float(np.abs(v).max()), f"step {s} row {r}: gap {gap}"
         toks = stacks["gemv"].tokens.clone()
     assert stacks["grouped"].launches_per_step() == L * 9 + 2
+
+
+def test_stacked_decode_with_sampling_matches_oracle(cuda_ctx):
+    """The sampled decode loop (batch 1, top-k + top-p + repetition penalty):
+    every step's token equals the oracle's draw on the oracle's head logits,
+    eagerly and when one step is captured in a CUDA graph and replayed (the
+    position and the seen set advance on the device)."""
+    from molten_b200.sample import Sampling
+    L, E, I, V, steps = 2, 8, 512, 4096, 3
+    layers, head, embed = make_stack(97, L, E, I, V)
+    dl = [dict(proj=dev_qw(*l["proj"]), norm_w=dev_bf16(l["norm_w"]), router=dev_bf16(l["router"]),
+               gate=dev_qw(*l["gate"]), up=dev_qw(*l["up"]), down=dev_qw(*l["down"])) for l in layers]
+    s = Sampling(temperature=0.8, top_k=40, top_p=0.9, repetition_penalty=1.3, seed=2024)
+    st = DecodeStack(cuda_ctx, dl, dev_qw(*head, bits=6), dev_bf16(embed), 1, n_experts=E,
+                     moe_path="fused", sampling=s)
+    tok, pos, seen = 123, 17, [5, 99, 123]
+    st.start(torch.tensor([tok], dtype=torch.int32).cuda(), pos=pos, seen=seen[:-1])
+    seen_bits = np.zeros(V // 32, np.uint32)
+    for t in seen:
+        seen_bits[t >> 5] |= np.uint32(1 << (t & 31))
+
+    def oracle_next(tok, pos):
+        x = embed[[tok]]
+        for Lw in layers:
+            p = oracle.gemv_quant(*Lw["proj"], 4, x)
+            _, normed, _, ids, wts = oracle.router_addnorm_route(x, p, Lw["norm_w"], Lw["router"],
+                                                                 0, None, 0)
+            act = oracle.gemv_gather_act(Lw["gate"], Lw["up"], normed, ids, n_experts=E)
+            x = oracle.gemv_gather_down_combine4(Lw["down"], act, ids, wts, n_experts=E)
+        logits = oracle.gemv_quant(*head, 6, x)[0]
+        key, _ = oracle.sample_draw(logits, seen_bits, 0.8, 40, 0.9, 1.3, 2024, pos)
+        return (~key) & 0xffffffff
+
+    g = None
+    for s_i in range(2 * steps):
+        want = oracle_next(tok, pos)
+        if s_i < steps:
+            st.step()
+        else:
+            if g is None:
+                g = torch.cuda.CUDAGraph()
+                stream = torch.cuda.Stream()
+                stream.wait_stream(torch.cuda.current_stream())
+                with torch.cuda.stream(stream):
+                    with torch.cuda.graph(g, stream=stream):
+                        st.step()
+                torch.cuda.current_stream().wait_stream(stream)
+            g.replay()
+        torch.cuda.synchronize()
+        got = int(st.read_tokens().numpy().view(np.uint32)[0])
+        assert got == want, f"step {s_i}: {got} != {want}"
+        tok, pos = got, pos + 1
+        seen_bits[tok >> 5] |= np.uint32(1 << (tok & 31))
+        assert int(st.pos.cpu()[0]) == pos
