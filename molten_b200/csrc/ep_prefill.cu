@@ -671,31 +671,32 @@ extern "C" int mc_ep_finalize(mc_ctx* ctx) {
 
 // ------------------------------------------------------------ placement
 
-// Skew-aware placement of E experts on W ranks of spr slots each (host
-// only). load[s][e]: pairs of source rank s routed to expert e (one routing
-// pass). Every expert gets one replica, the spare slots go one by one to
-// the expert with the largest load per replica (a replica count never
-// exceeds W); replicas are placed largest first on the least loaded rank
-// with a free slot that holds no replica of that expert yet (ties: lower
-// rank); the (source, expert) pairs of a replicated expert then go,
-// heaviest first, to the replica whose rank carries the least so far (ties:
-// the source's own rank, then the lower rank). tables[s][e] = the slot
-// source s sends expert e's rows to; slot_expert[slot] = the expert a slot
-// holds. Deterministic: every rank computes the same placement.
-extern "C" int mc_ep_place(const unsigned long long* load, int world, int n_experts,
-                           int slots_per_rank, uint32_t* tables, int32_t* slot_expert) {
-  MC_REQUIRE(load && tables && slot_expert, "ep_place: null pointer");
-  MC_REQUIRE(world >= 1 && world <= kMaxRanks, "ep_place: world %d", world);
-  MC_REQUIRE(n_experts >= 1 && slots_per_rank >= 1 && (long)world * slots_per_rank >= n_experts &&
-                 world * slots_per_rank <= 256,
-             "ep_place: %d slots per rank x %d ranks for %d experts", slots_per_rank, world,
-             n_experts);
-  const int W = world, E = n_experts, T = W * slots_per_rank;
+namespace {
+
+// One candidate placement: slot_expert[T], tables[W][E], and the rank loads.
+struct Placement {
+  std::vector<int32_t> slot_expert;
+  std::vector<uint32_t> tables;
+  std::vector<double> rank_load;
+  double max_load() const { return *std::max_element(rank_load.begin(), rank_load.end()); }
+};
+
+// Builds a placement with `spare` of the W * spr - E spare slots used for
+// replicas (the rest stay empty): replica counts by largest load per
+// replica, replicas placed largest first on the least-loaded rank holding
+// none of that expert, (source, expert) pairs of replicated experts sent,
+// heaviest first, to the replica on the least-loaded rank (ties: the
+// source's own rank, then the lower rank). Then a local search lowers the
+// heaviest rank's load while it can: moving one (source, expert) pair to
+// another replica of the expert, or moving an expert with one replica to
+// another rank's free slot or swapping it with one there.
+Placement build_placement(const unsigned long long* load, int W, int E, int spr, int spare) {
+  const int T = W * spr;
   std::vector<double> L(E, 0.0);
   for (int s = 0; s < W; ++s)
     for (int e = 0; e < E; ++e) L[e] += (double)load[(size_t)s * E + e];
   std::vector<int> rep(E, 1);
-  for (int x = E; x < T; ++x) {
+  for (int x = 0; x < spare; ++x) {
     int best = -1;
     for (int e = 0; e < E; ++e)
       if (rep[e] < W && (best < 0 || L[e] / rep[e] > L[best] / rep[best])) best = e;
@@ -710,62 +711,148 @@ extern "C" int mc_ep_place(const unsigned long long* load, int world, int n_expe
     if (a.w != b.w) return a.w > b.w;
     return a.e != b.e ? a.e < b.e : a.j < b.j;
   });
-  std::vector<double> rank_load(W, 0.0);
+  Placement pl;
+  pl.slot_expert.assign(T, -1);
+  pl.tables.assign((size_t)W * E, 0u);
+  std::vector<double> est(W, 0.0);
   std::vector<int> used(W, 0);
-  std::vector<std::vector<int>> rank_of(E);   // ranks holding a replica of e
-  std::vector<std::vector<int>> slot_of(E);   // their slots
-  for (int t = 0; t < T; ++t) slot_expert[t] = -1;
+  std::vector<std::vector<int>> slot_of(E);
+  auto holds = [&](int e, int r) {
+    for (int sl : slot_of[e])
+      if (sl / spr == r) return true;
+    return false;
+  };
   for (const Unit& u : units) {
     int pick = -1;
     for (int pass = 0; pass < 2 && pick < 0; ++pass)
       for (int r = 0; r < W; ++r) {
-        if (used[r] >= slots_per_rank) continue;
-        const bool holds =
-            std::find(rank_of[u.e].begin(), rank_of[u.e].end(), r) != rank_of[u.e].end();
-        if (pass == 0 && holds) continue;
-        if (pick < 0 || rank_load[r] < rank_load[pick]) pick = r;
+        if (used[r] >= spr || (pass == 0 && holds(u.e, r))) continue;
+        if (pick < 0 || est[r] < est[pick]) pick = r;
       }
     if (pick < 0) break;
-    const int slot = pick * slots_per_rank + used[pick]++;
-    rank_load[pick] += u.w;
-    rank_of[u.e].push_back(pick);
+    const int slot = pick * spr + used[pick]++;
+    est[pick] += u.w;
     slot_of[u.e].push_back(slot);
-    slot_expert[slot] = u.e;
+    pl.slot_expert[slot] = u.e;
   }
-  // sources to replicas: an expert with one replica sends everything there;
-  // the (source, expert) pairs of replicated experts then go, heaviest
-  // first, to the replica whose rank carries the least so far (ties: the
-  // source's own rank, then the lower rank)
-  std::vector<double> total(W, 0.0);
+  pl.rank_load.assign(W, 0.0);
   struct Pair { int s, e; double w; };
   std::vector<Pair> pairs;
-  for (int e = 0; e < E; ++e) {
-    MC_REQUIRE(!slot_of[e].empty(), "ep_place: expert %d got no slot", e);
+  for (int e = 0; e < E; ++e)
     for (int s = 0; s < W; ++s) {
       const double w = (double)load[(size_t)s * E + e];
       if (slot_of[e].size() == 1) {
-        tables[(size_t)s * E + e] = (uint32_t)slot_of[e][0];
-        total[rank_of[e][0]] += w;
+        pl.tables[(size_t)s * E + e] = (uint32_t)slot_of[e][0];
+        pl.rank_load[slot_of[e][0] / spr] += w;
       } else {
         pairs.push_back({s, e, w});
       }
     }
-  }
   std::stable_sort(pairs.begin(), pairs.end(), [](const Pair& a, const Pair& b) {
     if (a.w != b.w) return a.w > b.w;
     return a.e != b.e ? a.e < b.e : a.s < b.s;
   });
-  for (const Pair& pr : pairs) {
+  for (const Pair& p : pairs) {
     int j = 0;
-    for (int c = 1; c < (int)slot_of[pr.e].size(); ++c) {
-      const int rc = rank_of[pr.e][c], rj = rank_of[pr.e][j];
-      if (total[rc] < total[rj] ||
-          (total[rc] == total[rj] && (rc == pr.s || (rj != pr.s && rc < rj))))
-        j = c;
+    for (int c = 1; c < (int)slot_of[p.e].size(); ++c) {
+      const int rc = slot_of[p.e][c] / spr, rj = slot_of[p.e][j] / spr;
+      const double lc = pl.rank_load[rc], lj = pl.rank_load[rj];
+      if (lc < lj || (lc == lj && (rc == p.s || (rj != p.s && rc < rj)))) j = c;
     }
-    tables[(size_t)pr.s * E + pr.e] = (uint32_t)slot_of[pr.e][j];
-    total[rank_of[pr.e][j]] += pr.w;
+    pl.tables[(size_t)p.s * E + p.e] = (uint32_t)slot_of[p.e][j];
+    pl.rank_load[slot_of[p.e][j] / spr] += p.w;
   }
+  // ---- local search on the heaviest rank
+  auto wl = [&](int s, int e) { return (double)load[(size_t)s * E + e]; };
+  for (int iter = 0; iter < 4096; ++iter) {
+    const int rm = (int)(std::max_element(pl.rank_load.begin(), pl.rank_load.end()) -
+                         pl.rank_load.begin());
+    const double cur = pl.rank_load[rm];
+    double best = cur;
+    int kind = -1, a0 = 0, a1 = 0, a2 = 0;
+    // (a) one pair of a replicated expert to its replica on another rank
+    for (int s = 0; s < W; ++s)
+      for (int e = 0; e < E; ++e) {
+        if (slot_of[e].size() < 2 || (int)pl.tables[(size_t)s * E + e] / spr != rm) continue;
+        const double w = wl(s, e);
+        for (int sl : slot_of[e]) {
+          const int r2 = sl / spr;
+          if (r2 == rm) continue;
+          const double m = std::max(cur - w, pl.rank_load[r2] + w);
+          if (m < best) { best = m; kind = 0; a0 = s; a1 = e; a2 = sl; }
+        }
+      }
+    // (b) an expert with one replica on rm to a free slot or swapped with
+    // a one-replica expert on another rank
+    for (int sa = rm * spr; sa < (rm + 1) * spr; ++sa) {
+      const int ea = pl.slot_expert[sa];
+      if (ea < 0 || slot_of[ea].size() != 1) continue;
+      const double la = L[ea];
+      for (int sb = 0; sb < T; ++sb) {
+        const int r2 = sb / spr;
+        if (r2 == rm) continue;
+        const int eb = pl.slot_expert[sb];
+        if (eb >= 0 && slot_of[eb].size() != 1) continue;
+        const double lb = eb >= 0 ? L[eb] : 0.0;
+        const double m = std::max(cur - la + lb, pl.rank_load[r2] + la - lb);
+        if (m < best) { best = m; kind = 1; a0 = sa; a1 = sb; }
+      }
+    }
+    if (kind < 0 || best >= cur - 1e-9) break;
+    if (kind == 0) {
+      const double w = wl(a0, a1);
+      pl.rank_load[rm] -= w;
+      pl.rank_load[a2 / spr] += w;
+      pl.tables[(size_t)a0 * E + a1] = (uint32_t)a2;
+    } else {
+      const int ea = pl.slot_expert[a0], eb = pl.slot_expert[a1];
+      const double lb = eb >= 0 ? L[eb] : 0.0;
+      pl.rank_load[rm] += lb - L[ea];
+      pl.rank_load[a1 / spr] += L[ea] - lb;
+      pl.slot_expert[a0] = eb;
+      pl.slot_expert[a1] = ea;
+      slot_of[ea][0] = a1;
+      for (int s = 0; s < W; ++s) pl.tables[(size_t)s * E + ea] = (uint32_t)a1;
+      if (eb >= 0) {
+        slot_of[eb][0] = a0;
+        for (int s = 0; s < W; ++s) pl.tables[(size_t)s * E + eb] = (uint32_t)a0;
+      }
+    }
+  }
+  return pl;
+}
+
+}  // namespace
+
+// Skew-aware placement of E experts on W ranks of spr slots each (host
+// only). load[s][e]: pairs of source rank s routed to expert e (one routing
+// pass). Candidates use 0, 1, ... of the spare slots for replicas of the
+// hottest experts (build_placement); the one whose heaviest rank carries the
+// least wins (ties: fewer replicas), so spare slots never make it worse.
+// tables[s][e] = the slot source s sends expert e's rows to;
+// slot_expert[slot] = the expert a slot holds (-1: empty). Deterministic:
+// every rank computes the same placement.
+extern "C" int mc_ep_place(const unsigned long long* load, int world, int n_experts,
+                           int slots_per_rank, uint32_t* tables, int32_t* slot_expert) {
+  MC_REQUIRE(load && tables && slot_expert, "ep_place: null pointer");
+  MC_REQUIRE(world >= 1 && world <= kMaxRanks, "ep_place: world %d", world);
+  MC_REQUIRE(n_experts >= 1 && slots_per_rank >= 1 && (long)world * slots_per_rank >= n_experts &&
+                 world * slots_per_rank <= 256,
+             "ep_place: %d slots per rank x %d ranks for %d experts", slots_per_rank, world,
+             n_experts);
+  const int spare = world * slots_per_rank - n_experts;
+  Placement best;
+  for (int x = 0; x <= spare; ++x) {
+    Placement p = build_placement(load, world, n_experts, slots_per_rank, x);
+    if (best.rank_load.empty() || p.max_load() < best.max_load() - 1e-9) best = std::move(p);
+  }
+  for (int e = 0; e < n_experts; ++e) {
+    bool placed = false;
+    for (int32_t v : best.slot_expert) placed |= v == e;
+    MC_REQUIRE(placed, "ep_place: expert %d got no slot", e);
+  }
+  std::copy(best.slot_expert.begin(), best.slot_expert.end(), slot_expert);
+  std::copy(best.tables.begin(), best.tables.end(), tables);
   return MC_OK;
 }
 
