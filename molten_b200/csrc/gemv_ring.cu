@@ -23,18 +23,22 @@
 namespace {
 
 constexpr int kK = 2048;
-constexpr int kRows = 16;                  // rows per stage, one per compute warp
-constexpr int kComputeWarps = kRows;
-constexpr int kThreads = (kComputeWarps + 1) * 32;  // + the producer warp
 constexpr int kMaxStages = 8;
+constexpr uint32_t kRingBudget = 196608;                 // shared-memory ring, bytes
 constexpr unsigned long long kTimeoutNs = 200000000ull;  // default limit per wait: 200 ms
 
-template <int BITS>
+// CW compute warps take RPW rows each per stage (rows w, w + CW, ...): a
+// stage is CW * RPW rows of codes, then their scales, then their biases.
+template <int BITS, int CW, int RPW, uint32_t BUDGET = kRingBudget>
 struct RingShape {
+  static constexpr int kRows = CW * RPW;
+  static constexpr int kThreads = (CW + 1) * 32;                 // + the producer warp
   static constexpr uint32_t kCode = kK * BITS / 8;               // code bytes per row
   static constexpr uint32_t kStage = kRows * (kCode + 2 * 64);   // codes + scales + biases
-  static constexpr int kStages = BITS == 6 ? 6 : 8;              // ~160 / ~150 KB
+  static constexpr int kStages =
+      BUDGET / kStage < kMaxStages ? (int)(BUDGET / kStage) : kMaxStages;
   static constexpr uint32_t kSmem = kStages * kStage;
+  static_assert(kStages >= 2, "ring needs two stages");
 };
 
 __device__ __forceinline__ bool ring_wait(uint64_t* bar, uint32_t parity,
@@ -46,17 +50,18 @@ __device__ __forceinline__ bool ring_wait(uint64_t* bar, uint32_t parity,
 
 // MODE 0: y[n] = bf16(row n . x). MODE 1: keys[0] = max over rows of the
 // argmax key of the bf16-rounded row values (the key must be zero on entry).
-template <int BITS, int MODE>
-__global__ void __launch_bounds__(kThreads, 1)
+template <int BITS, int MODE, int CW, int RPW, uint32_t BUDGET>
+__global__ void __launch_bounds__(RingShape<BITS, CW, RPW, BUDGET>::kThreads, 1)
 gemv_ring_kernel(const uint8_t* __restrict__ codes, const uint16_t* __restrict__ scales,
                  const uint16_t* __restrict__ biases, const uint16_t* __restrict__ x,
                  uint16_t* __restrict__ y, unsigned long long* __restrict__ keys, int N,
                  unsigned int* __restrict__ status, unsigned long long timeout_ns) {
-  using S = RingShape<BITS>;
+  using S = RingShape<BITS, CW, RPW, BUDGET>;
+  constexpr int kRows = S::kRows;
   extern __shared__ __align__(128) uint8_t sm[];
   __shared__ __align__(8) uint64_t full[kMaxStages], empty[kMaxStages];
-  __shared__ float bv_s[kComputeWarps];
-  __shared__ uint32_t bi_s[kComputeWarps];
+  __shared__ float bv_s[CW];
+  __shared__ uint32_t bi_s[CW];
   const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
   const int G = gridDim.x, cta = blockIdx.x;
   const int r0 = (int)(((long)cta * N) / G), r1 = (int)(((long)(cta + 1) * N) / G);
@@ -64,7 +69,7 @@ gemv_ring_kernel(const uint8_t* __restrict__ codes, const uint16_t* __restrict__
   if (t == 0) {
     for (int s = 0; s < S::kStages; ++s) {
       mc_mbar_init(full + s, 1);
-      mc_mbar_init(empty + s, kComputeWarps);
+      mc_mbar_init(empty + s, CW);
     }
     mc_fence_barrier_init();
   }
@@ -72,7 +77,7 @@ gemv_ring_kernel(const uint8_t* __restrict__ codes, const uint16_t* __restrict__
   mc_pdl_launch_dependents();
   const unsigned long long deadline = mc_globaltimer() + timeout_ns;
 
-  if (warp == kComputeWarps) {
+  if (warp == CW) {
     // ---- producer: stage s goes to slot s % kStages once the compute warps
     // have released the slot's previous use
     bool ok = true;
@@ -112,50 +117,94 @@ gemv_ring_kernel(const uint8_t* __restrict__ codes, const uint16_t* __restrict__
   uint32_t best_i = 0;
   for (int s = 0; s < nst; ++s) {
     const int slot = s % S::kStages;
-    if (!ring_wait(full + slot, (s / S::kStages) & 1, deadline)) {
+    // warp-uniform answer: the shuffles below need every lane
+    if (!__all_sync(0xffffffffu, ring_wait(full + slot, (s / S::kStages) & 1, deadline))) {
       if (lane == 0) atomicOr(status, 2u);
       break;
     }
     const int n0 = r0 + s * kRows, nr = min(kRows, r1 - n0);
     const uint8_t* st = sm + (uint32_t)slot * S::kStage;
-    float sum = 0.0f;
-    if (warp < nr) {
-      const uint16_t* sc = reinterpret_cast<const uint16_t*>(st + kRows * S::kCode);
-      const uint16_t* bi = reinterpret_cast<const uint16_t*>(st + kRows * (S::kCode + 64u));
-      const float sv = mc_bf16_to_f32(sc[warp * 32 + lane]);
-      const float bv = mc_bf16_to_f32(bi[warp * 32 + lane]);
+    const uint16_t* sc = reinterpret_cast<const uint16_t*>(st + kRows * S::kCode);
+    const uint16_t* bi = reinterpret_cast<const uint16_t*>(st + kRows * (S::kCode + 64u));
+    // all RPW rows are computed unconditionally, so their chains interleave;
+    // a row past the end of a short last stage reads stale bytes of its own
+    // stage slot and its result is dropped
+    float sum[RPW];
+#pragma unroll
+    for (int j = 0; j < RPW; ++j) {
+      const int r = warp + j * CW;
+      const float sv = mc_bf16_to_f32(sc[r * 32 + lane]);
+      const float bv = mc_bf16_to_f32(bi[r * 32 + lane]);
       QGroup<BITS> q;
-      const uint4* p = reinterpret_cast<const uint4*>(st + warp * S::kCode + lane * (BITS * 8));
+      const uint4* p = reinterpret_cast<const uint4*>(st + r * S::kCode + lane * (BITS * 8));
 #pragma unroll
       for (int c = 0; c < BITS / 2; ++c) q.v[c] = p[c];
-      const float acc = __fadd_rn(0.0f, __fmaf_rn(sv, q.qx(xs), __fmul_rn(bv, xg)));
-      sum = mc_warp_butterfly(acc);
+      sum[j] = __fadd_rn(0.0f, __fmaf_rn(sv, q.qx(xs), __fmul_rn(bv, xg)));
+    }
+    // the canonical 32-lane butterfly of each row, as a reduce-scatter: the
+    // first log2(RPW) steps hand each half (quarter) of the warp one row and
+    // exchange one value per lane instead of one per row; every lane still
+    // forms the same tree nodes (IEEE addition commutes), so the row sums are
+    // bit-identical to mc_warp_butterfly's
+    int jr = 0;
+    float v;
+    if constexpr (RPW == 2) {
+      const bool h = lane & 16;
+      v = __fadd_rn(h ? sum[1] : sum[0], __shfl_xor_sync(0xffffffffu, h ? sum[0] : sum[1], 16));
+      jr = h;
+#pragma unroll
+      for (int m = 8; m >= 1; m >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, m));
+    } else if constexpr (RPW == 4) {
+      const bool h = lane & 16, q = lane & 8;
+      const float k0 = __fadd_rn(h ? sum[2] : sum[0],
+                                 __shfl_xor_sync(0xffffffffu, h ? sum[0] : sum[2], 16));
+      const float k1 = __fadd_rn(h ? sum[3] : sum[1],
+                                 __shfl_xor_sync(0xffffffffu, h ? sum[1] : sum[3], 16));
+      v = __fadd_rn(q ? k1 : k0, __shfl_xor_sync(0xffffffffu, q ? k0 : k1, 8));
+      jr = (h ? 2 : 0) + (q ? 1 : 0);
+#pragma unroll
+      for (int m = 4; m >= 1; m >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, m));
+    } else {
+      static_assert(RPW == 1, "rows per warp: 1, 2 or 4");
+      v = mc_warp_butterfly(sum[0]);
     }
     __syncwarp();
     if (lane == 0) mc_mbar_arrive(empty + slot);
-    if (warp < nr) {
-      const int n = n0 + warp;
+    // lane jr * 32 / RPW holds row jr (every lane of its group has it)
+    const int r = warp + jr * CW;
+    if (r < nr) {
+      const int n = n0 + r;
       if (MODE == 0) {
-        if (lane == 0) y[n] = mc_f32_to_bf16(sum);
+        if ((lane & (32 / RPW - 1)) == 0) y[n] = mc_f32_to_bf16(v);
       } else {
-        const float v = mc_round_bf16(sum);
-        if (mc_better(v, (uint32_t)n, best_v, best_i)) {
-          best_v = v;
+        const float vr = mc_round_bf16(v);
+        if (mc_better(vr, (uint32_t)n, best_v, best_i)) {
+          best_v = vr;
           best_i = (uint32_t)n;
         }
       }
     }
   }
   if (MODE == 1) {
+    // the lane groups held different rows: fold their bests into lane 0
+#pragma unroll
+    for (int m = 16; m >= 32 / RPW; m >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, best_v, m);
+      const uint32_t oi = __shfl_xor_sync(0xffffffffu, best_i, m);
+      if (mc_better(ov, oi, best_v, best_i)) {
+        best_v = ov;
+        best_i = oi;
+      }
+    }
     if (lane == 0) {
       bv_s[warp] = best_v;
       bi_s[warp] = best_i;
     }
-    asm volatile("bar.sync 1, %0;" ::"n"(kComputeWarps * 32));
+    asm volatile("bar.sync 1, %0;" ::"n"(CW * 32));
     if (t == 0) {
       float v = bv_s[0];
       uint32_t i = bi_s[0];
-      for (int w = 1; w < kComputeWarps; ++w)
+      for (int w = 1; w < CW; ++w)
         if (mc_better(bv_s[w], bi_s[w], v, i)) {
           v = bv_s[w];
           i = bi_s[w];
@@ -167,26 +216,31 @@ gemv_ring_kernel(const uint8_t* __restrict__ codes, const uint16_t* __restrict__
 
 __device__ unsigned int g_ring_status;
 
-template <int BITS, int MODE>
+template <int BITS, int MODE, int CW, int RPW, uint32_t BUDGET = kRingBudget>
 int launch_ring(mc_ctx* ctx, const mc_qweights* w, const uint16_t* x, uint16_t* y,
                 unsigned long long* keys) {
-  using S = RingShape<BITS>;
-  auto fn = gemv_ring_kernel<BITS, MODE>;
+  using S = RingShape<BITS, CW, RPW, BUDGET>;
+  auto fn = gemv_ring_kernel<BITS, MODE, CW, RPW, BUDGET>;
   // per device: the shared-memory limit raised once, the status word's address
   static std::atomic<bool> ready[64];
   static unsigned int* status_of[64];
   const int dev = ctx->device & 63;
+  if ((int)S::kSmem + 4096 > ctx->max_smem_optin) return 1;
   if (!ready[dev].load()) {
     MC_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kSmem));
     MC_CUDA(cudaGetSymbolAddress((void**)&status_of[dev], g_ring_status));
     ready[dev].store(true);
   }
   unsigned int* status = status_of[dev];
-  MC_CUDA(mc_launch_pdl(fn, dim3(ctx->num_sms), dim3(kThreads), S::kSmem, ctx->stream,
+  MC_CUDA(mc_launch_pdl(fn, dim3(ctx->num_sms), dim3(S::kThreads), S::kSmem, ctx->stream,
                         reinterpret_cast<const uint8_t*>(w->codes), w->scales, w->biases, x, y,
                         keys, w->out_features, status, mc_wait_limit(ctx, kTimeoutNs)));
   return mc_after_launch("gemv_ring_kernel");
 }
+
+// The configuration per bit width: compute warps, rows per warp and stage.
+constexpr int kCW4 = 8, kRPW4 = 4;
+constexpr int kCW6 = 8, kRPW6 = 4;
 
 }  // namespace
 
@@ -196,12 +250,13 @@ int launch_ring(mc_ctx* ctx, const mc_qweights* w, const uint16_t* x, uint16_t* 
 int mc_gemv_ring(mc_ctx* ctx, const mc_qweights* w, const uint16_t* x, uint16_t* y,
                  unsigned long long* keys, int batch, int mode) {
   if (batch != 1 || w->in_features != kK || w->group_size != 64) return 1;
-  if (w->out_features < ctx->num_sms * 2 * kRows) return 1;
-  const uint32_t smem = w->bits == 6 ? RingShape<6>::kSmem : RingShape<4>::kSmem;
-  if ((int)smem + 4096 > ctx->max_smem_optin) return 1;
+  const int rows = w->bits == 6 ? kCW6 * kRPW6 : kCW4 * kRPW4;
+  if (w->out_features < ctx->num_sms * 2 * rows) return 1;
   if (!mc_aligned(w->codes, 16) || !mc_aligned(w->scales, 16) || !mc_aligned(w->biases, 16))
     return 1;
   if (w->bits == 6)
-    return mode ? launch_ring<6, 1>(ctx, w, x, y, keys) : launch_ring<6, 0>(ctx, w, x, y, keys);
-  return mode ? launch_ring<4, 1>(ctx, w, x, y, keys) : launch_ring<4, 0>(ctx, w, x, y, keys);
+    return mode ? launch_ring<6, 1, kCW6, kRPW6>(ctx, w, x, y, keys)
+                : launch_ring<6, 0, kCW6, kRPW6>(ctx, w, x, y, keys);
+  return mode ? launch_ring<4, 1, kCW4, kRPW4>(ctx, w, x, y, keys)
+              : launch_ring<4, 0, kCW4, kRPW4>(ctx, w, x, y, keys);
 }
