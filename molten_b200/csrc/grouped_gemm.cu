@@ -30,8 +30,8 @@
 //   warp 1      TMEM allocation (512 columns); lane 0 issues tcgen05.mma
 //               (M=128, N=chunk, K=16, bf16 x bf16 -> fp32) and commits
 //   warps 2..9  dequantise the weight tiles straight into the UMMA K-major
-//               128-byte-swizzled layout (w = bf16(fma(s, q, b)), MLX's
-//               dequantize): gate/up: warps 2-5 the gate tile, 6-9 the up
+//               128-byte-swizzled layout (w = bf16(s*q + b) in bf16x2
+//               arithmetic, MLX's dequantize): gate/up: warps 2-5 the gate tile, 6-9 the up
 //               tile; down: warps 2-5 the first 32 K of every row, 6-9 the
 //               second. Then the epilogue from TMEM, half the columns each.
 // Two rings: token rows (bfull: TMA tx, bempty: tcgen05.commit) and weight
@@ -245,51 +245,35 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
 }
 
 // ---- dequantisation of Q4 words into the UMMA layout -------------------------
-// NP word pairs (16 codes each, k = 16m + j in the order of the word pairs)
-// -> 16*NP bf16 values in natural k order, stored as 16-byte chunks
-// c0 + 2m, c0 + 2m + 1 at row_base + ((c ^ swz) * 16): the UMMA K-major
-// 128B-swizzle layout. w = bf16(fma(s, q, b)) with s*q exact (MLX
-// dequantize, quant_nax.metal:2947).
-template <int NP>
-__device__ __forceinline__ void dequant_words(const uint32_t* W, float s, float bias,
+// NW Q4 words (8 codes each, code j of word i at bits 4j is k = 8i + j) ->
+// 8*NW bf16 values in natural k order, word i stored as the 16-byte chunk
+// c0 + i at row_base + ((c ^ swz) * 16): the UMMA K-major 128B-swizzle
+// layout. In bf16x2 arithmetic, per code pair (k, k+1): one prmt gathers the
+// pair's byte from w and w >> 4, one lop3 keeps the two nibbles and ORs the
+// exponent of 128 into both halves (bf16 128 + q, exact for q < 16), one
+// sub.bf16x2 takes 128 off (exact) and one fma.bf16x2 gives
+// w = bf16(s*q + b) rounded once from the exact value (MLX dequantize,
+// quant_nax.metal:2948-2951, computes s*q + b in fp32 and then rounds to
+// bf16; the two agree except where that double rounding lands on a bf16
+// tie, which stays inside the prefill tolerance).
+template <int NW>
+__device__ __forceinline__ void dequant_words(const uint32_t* W, uint32_t s2, uint32_t b2,
                                               uint8_t* row_base, int swz, int c0) {
-  const float2 neg = make_float2(-MC_MAGIC_F, -MC_MAGIC_F);
-  const float2 bb = make_float2(bias, bias);
-  float se[8];
+  const uint32_t M = 0x43004300u;  // (128, 128) in bf16
 #pragma unroll
-  for (int j = 0; j < 8; ++j) se[j] = __fmul_rn(s, mc_pow2_neg(j < 5 ? 4 * j : 4 * (j - 3)));
-  // lane .x of pair j is k = 16m + j, lane .y is k = 16m + 8 + j, so each word
-  // pair completes two 16-byte chunks, stored at once
-#pragma unroll
-  for (int m = 0; m < NP; ++m) {
-    const uint32_t wa = W[2 * m], wb = W[2 * m + 1];
-    const uint64_t Wd = ((uint64_t)wb << 32) | wa;
-    const uint64_t Sd = ((uint64_t)(wb >> 12) << 32) | (wa >> 12);
-    const uint64_t MAG = 0x4B0000004B000000ull;
-    const uint64_t masked[8] = {Wd & 0x0000000F0000000Full, Wd & 0x000000F0000000F0ull,
-                                Wd & 0x00000F0000000F00ull, Wd & 0x0000F0000000F000ull,
-                                Wd & 0x000F0000000F0000ull, Sd & 0x00000F0000000F00ull,
-                                Sd & 0x0000F0000000F000ull, Sd & 0x000F0000000F0000ull};
-    float2 w[8];
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const uint64_t qb = masked[j] | MAG;
-      float2 q = make_float2(__uint_as_float((uint32_t)qb), __uint_as_float((uint32_t)(qb >> 32)));
-      q = __fadd2_rn(q, neg);                               // (q_k, q_{k+8}) * 2^e, exact
-      w[j] = __ffma2_rn(q, make_float2(se[j], se[j]), bb);  // s*q + b, one rounding
-    }
-    uint32_t lo[4], hi[4];
+  for (int i = 0; i < NW; ++i) {
+    const uint32_t w = W[i], wo = w >> 4;
+    uint32_t o[4];
 #pragma unroll
     for (int h = 0; h < 4; ++h) {
-      const __nv_bfloat162 tl = __floats2bfloat162_rn(w[2 * h].x, w[2 * h + 1].x);
-      const __nv_bfloat162 th = __floats2bfloat162_rn(w[2 * h].y, w[2 * h + 1].y);
-      lo[h] = *reinterpret_cast<const uint32_t*>(&tl);
-      hi[h] = *reinterpret_cast<const uint32_t*>(&th);
+      uint32_t p, q;
+      const uint32_t sel = h | (h << 4) | ((h + 4) << 8) | ((h + 4) << 12);
+      asm("prmt.b32 %0, %1, %2, %3;" : "=r"(p) : "r"(w), "r"(wo), "r"(sel));
+      asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(p) : "r"(p), "n"(0x000F000F), "r"(M));
+      asm("sub.rn.bf16x2 %0, %1, %2;" : "=r"(q) : "r"(p), "r"(M));
+      asm("fma.rn.bf16x2 %0, %1, %2, %3;" : "=r"(o[h]) : "r"(s2), "r"(q), "r"(b2));
     }
-    const int c = c0 + 2 * m;
-    *reinterpret_cast<uint4*>(row_base + ((c ^ swz) << 4)) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
-    *reinterpret_cast<uint4*>(row_base + (((c + 1) ^ swz) << 4)) =
-        make_uint4(hi[0], hi[1], hi[2], hi[3]);
+    *reinterpret_cast<uint4*>(row_base + (((c0 + i) ^ swz) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
   }
 }
 
@@ -478,7 +462,7 @@ grouped_gemm_kernel(const __grid_constant__ TokenMaps tm, const GemmParams P) {
       return w;
     };
     // dequantise the slice held in c (K step kk) into stage itk
-    auto do_slice = [&](const uint4* c, uint32_t itk, float sc, float bi) -> bool {
+    auto do_slice = [&](const uint4* c, uint32_t itk, uint32_t sc, uint32_t bi) -> bool {
       const int s = itk % C::ASTAGES;
       const uint32_t ph = (itk / C::ASTAGES) & 1;
       if (!warp_wait(&aempty[s], ph ^ 1, &abort_s, P.timeout_ns)) return false;
@@ -491,7 +475,7 @@ grouped_gemm_kernel(const __grid_constant__ TokenMaps tm, const GemmParams P) {
         W[4 * u + 2] = c[u].z;
         W[4 * u + 3] = c[u].w;
       }
-      dequant_words<2 * NU>(W, sc, bi, row, d & 7, GU ? 0 : 4 * grp);
+      dequant_words<4 * NU>(W, sc, bi, row, d & 7, GU ? 0 : 4 * grp);
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       __syncwarp();
       if (lane == 0) mc_mbar_arrive(&afull[s]);
@@ -510,15 +494,15 @@ grouped_gemm_kernel(const __grid_constant__ TokenMaps tm, const GemmParams P) {
 #pragma unroll
         for (int u = 0; u < NU; ++u) x[u] = c0[u];
         load_codes(c0, kk + 2);
-        if (!do_slice(x, it + kk, mc_bf16_to_f32((uint16_t)sw), mc_bf16_to_f32((uint16_t)bw))) {
+        // the K step's bf16 scale and bias, each in both halves
+        if (!do_slice(x, it + kk, __byte_perm(sw, 0, 0x1010), __byte_perm(bw, 0, 0x1010))) {
           ok = false;
           break;
         }
 #pragma unroll
         for (int u = 0; u < NU; ++u) x[u] = c1[u];
         load_codes(c1, kk + 3);
-        if (!do_slice(x, it + kk + 1, mc_bf16_to_f32((uint16_t)(sw >> 16)),
-                      mc_bf16_to_f32((uint16_t)(bw >> 16)))) {
+        if (!do_slice(x, it + kk + 1, __byte_perm(sw, 0, 0x3232), __byte_perm(bw, 0, 0x3232))) {
           ok = false;
           break;
         }
