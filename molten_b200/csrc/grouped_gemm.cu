@@ -55,6 +55,7 @@ constexpr int MAXN = 256;  // token rows per chunk (the MMA's N, rounded up to 1
 constexpr int kDeqThreads = 256;
 constexpr int kThreads = 64 + kDeqThreads;
 constexpr unsigned long long kTimeoutNs = 1000000000ull;  // default limit per wait: 1 s
+constexpr int kCodePrefetch = 4;  // K steps of codes each dequant thread has in flight (even)
 
 template <bool GU>
 struct Cfg {
@@ -62,11 +63,16 @@ struct Cfg {
   static constexpr int B_BYTES = MAXN * BK * 2;        // 32 KB of token rows per K step
   static constexpr int A_BYTES = BF * BK * 2;          // 16 KB per weight tile
   static constexpr int A_STAGE = NMAT * A_BYTES;
-  // Ring depths measured best on B200 (deeper token rings were slower: more
-  // TMA traffic in flight delays the dequant warps' weight loads in L2).
-  static constexpr int BSTAGES = GU ? 2 : 4;
-  static constexpr int ASTAGES = GU ? 2 : 4;
-  static constexpr int SMEM = BSTAGES * B_BYTES + ASTAGES * A_STAGE + 1024;
+  // Ring depths measured best on B200. Shared memory and L1 share each SM's
+  // 256 KB, and the dequant threads' code loads in flight live in L1: the
+  // down GEMM at 4 + 4 stages plus the epilogue tiles (201 KB) ran at 254 us
+  // on the cfg3 workload, at 3 + 3 stages (161 KB) at 160 us.
+  static constexpr int BSTAGES = GU ? 2 : 3;
+  static constexpr int ASTAGES = GU ? 2 : 3;
+  // per epilogue warp a [16 tokens][32 features] bf16 tile: the warp's
+  // outputs leave as 16-byte row vectors instead of one 2-byte store each
+  static constexpr int EPI_BYTES = (kDeqThreads / 32) * 16 * 64;
+  static constexpr int SMEM = BSTAGES * B_BYTES + ASTAGES * A_STAGE + EPI_BYTES + 1024;
   static constexpr int TMEM_COLS = 512;
   static constexpr int ACC_COLS = NMAT * MAXN;         // accumulator columns per item
   static constexpr int NBUF = TMEM_COLS / ACC_COLS;    // gate/up: 1, down: 2
@@ -291,6 +297,7 @@ grouped_gemm_kernel(const __grid_constant__ TokenMaps tm, const GemmParams P) {
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
   uint8_t* a_ring = smem + C::BSTAGES * C::B_BYTES;
+  uint8_t* epi_ring = a_ring + C::ASTAGES * C::A_STAGE;
   const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
 
   if (t == 0) {
@@ -428,26 +435,32 @@ grouped_gemm_kernel(const __grid_constant__ TokenMaps tm, const GemmParams P) {
     const uint16_t* wscales = (GU && grp) ? P.w1.scales : P.w0.scales;
     const uint16_t* wbiases = (GU && grp) ? P.w1.biases : P.w0.biases;
     const int half_off = GU ? 0 : 16 * grp;  // byte offset of this thread's codes in a slice
-    // Code slices two K steps ahead in two slots (even / odd K step); the
-    // scale and bias of a K-step pair as one 32-bit word each, one pair ahead
-    // (raw until use: converting at load time would wait for the load there).
-    // The next item's first loads are issued before this item's epilogue.
-    uint4 c0[NU], c1[NU];
-    uint32_t sw_n = 0, bw_n = 0;
+    // Code slices kPF K steps ahead in a register ring (slot k % kPF); the
+    // scale and bias of a K-step pair as one 32-bit word each, kPF / 2 pairs
+    // ahead (raw until use: converting at load time would wait for the load
+    // there). The next item's first loads are issued before this item's
+    // epilogue.
+    constexpr int kPF = kCodePrefetch;
+    uint4 cr[kPF][NU];
+    uint32_t swr[kPF / 2], bwr[kPF / 2];
     const uint8_t* crow = nullptr;
     const uint32_t *srow = nullptr, *brow = nullptr;
 #pragma unroll
-    for (int u = 0; u < NU; ++u) c0[u] = c1[u] = make_uint4(0, 0, 0, 0);
+    for (int p = 0; p < kPF; ++p)
+#pragma unroll
+      for (int u = 0; u < NU; ++u) cr[p][u] = make_uint4(0, 0, 0, 0);
+#pragma unroll
+    for (int p = 0; p < kPF / 2; ++p) swr[p] = bwr[p] = 0u;
     auto load_codes = [&](uint4* c, int kk) {
       if (kk < ksteps) {
 #pragma unroll
         for (int u = 0; u < NU; ++u) c[u] = mc_ldg_stream(crow + kk * 32 + half_off + 16 * u);
       }
     };
-    auto load_sb = [&](int pair) {
+    auto load_sb = [&](int slot, int pair) {
       if (2 * pair < ksteps) {
-        sw_n = __ldg(srow + pair);
-        bw_n = __ldg(brow + pair);
+        swr[slot] = __ldg(srow + pair);
+        bwr[slot] = __ldg(brow + pair);
       }
     };
     auto start_item = [&](int item) -> Item {
@@ -456,9 +469,10 @@ grouped_gemm_kernel(const __grid_constant__ TokenMaps tm, const GemmParams P) {
       crow = reinterpret_cast<const uint8_t*>(wcodes) + wrow * (P.K / 2);
       srow = reinterpret_cast<const uint32_t*>(wscales + wrow * (P.K / 64));
       brow = reinterpret_cast<const uint32_t*>(wbiases + wrow * (P.K / 64));
-      load_codes(c0, 0);
-      load_codes(c1, 1);
-      load_sb(0);
+#pragma unroll
+      for (int p = 0; p < kPF; ++p) load_codes(cr[p], p);
+#pragma unroll
+      for (int p = 0; p < kPF / 2; ++p) load_sb(p, p);
       return w;
     };
     // dequantise the slice held in c (K step kk) into stage itk
@@ -487,24 +501,23 @@ grouped_gemm_kernel(const __grid_constant__ TokenMaps tm, const GemmParams P) {
       if (__any_sync(0xffffffffu, abort_s != 0)) break;
       if (!w.ok && dt == 0 && P.status) atomicOr(P.status, 2u);
       bool ok = true;
-      for (int kk = 0; kk < ksteps; kk += 2) {
-        const uint32_t sw = sw_n, bw = bw_n;
-        load_sb(kk / 2 + 1);
-        uint4 x[NU];
+      for (int kk = 0; kk < ksteps && ok; kk += kPF) {
 #pragma unroll
-        for (int u = 0; u < NU; ++u) x[u] = c0[u];
-        load_codes(c0, kk + 2);
-        // the K step's bf16 scale and bias, each in both halves
-        if (!do_slice(x, it + kk, __byte_perm(sw, 0, 0x1010), __byte_perm(bw, 0, 0x1010))) {
-          ok = false;
-          break;
-        }
+        for (int p = 0; p < kPF; ++p) {
+          const int k = kk + p;
+          if (k >= ksteps) break;
+          // the K step's bf16 scale and bias, each in both halves
+          const uint32_t sel = (p & 1) ? 0x3232u : 0x1010u;
+          const uint32_t sc = __byte_perm(swr[p / 2], 0, sel), bi = __byte_perm(bwr[p / 2], 0, sel);
+          if (p & 1) load_sb(p / 2, k / 2 + kPF / 2);
+          uint4 x[NU];
 #pragma unroll
-        for (int u = 0; u < NU; ++u) x[u] = c1[u];
-        load_codes(c1, kk + 3);
-        if (!do_slice(x, it + kk + 1, __byte_perm(sw, 0, 0x3232), __byte_perm(bw, 0, 0x3232))) {
-          ok = false;
-          break;
+          for (int u = 0; u < NU; ++u) x[u] = cr[p][u];
+          load_codes(cr[p], k + kPF);
+          if (!do_slice(x, it + k, sc, bi)) {
+            ok = false;
+            break;
+          }
         }
       }
       if (!ok) {
@@ -522,12 +535,10 @@ grouped_gemm_kernel(const __grid_constant__ TokenMaps tm, const GemmParams P) {
         break;
       }
       tc_fence_after();
-      const int f = 32 * q + lane;  // feature row of D this thread reads
       const int n16 = cur.n >> 4, split = (n16 + 1) >> 1;
       const int c_lo = grp ? split : 0, c_hi = grp ? n16 : split;
       const uint32_t lane_base = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(buf * C::ACC_COLS);
       const bool ret = !GU && P.ret.seg_row != nullptr;
-      uint16_t* ocol = ret ? nullptr : P.out + (size_t)cur.nb * BF + f;
       uint32_t seg[kRetRanks + 1], segh[kRetRanks];
       if (ret) {  // this expert's source segments (uniform over the warp)
 #pragma unroll
@@ -566,50 +577,69 @@ grouped_gemm_kernel(const __grid_constant__ TokenMaps tm, const GemmParams P) {
           }
         return d;
       };
+      // two 16-column groups per TMEM wait: their loads and the two groups'
+      // independent arithmetic overlap (one group per wait left the epilogue
+      // latency-bound)
 #pragma unroll 1
-      for (int c = c_lo; c < c_hi; ++c) {
-        uint32_t g[16], u[16];
-        tmem_ld16(lane_base + 16 * c, g);
-        if (GU) tmem_ld16(lane_base + MAXN + 16 * c, u);
-        tmem_wait_ld();
-        const uint32_t r0 = cur.m0 + 16u * (uint32_t)c;
-        // a 16-row group inside one source segment gets one home base
-        uint16_t* gbase = nullptr;
-        if (ret) {
-          const uint32_t rl = min(r0 + 15u, cur.mend - 1u);
-          if (!(r0 >= s_lo && rl < s_hi)) locate(r0);
-          if (r0 >= s_lo && rl < s_hi && s_base) gbase = s_base + (size_t)(r0 - s_lo) * P.N;
+      for (int c2 = c_lo; c2 < c_hi; c2 += 2) {
+        const bool two = c2 + 1 < c_hi;  // warp-uniform
+        uint32_t gg[2][16], uu[2][16];
+        tmem_ld16(lane_base + 16 * c2, gg[0]);
+        if (GU) tmem_ld16(lane_base + MAXN + 16 * c2, uu[0]);
+        if (two) {
+          tmem_ld16(lane_base + 16 * (c2 + 1), gg[1]);
+          if (GU) tmem_ld16(lane_base + MAXN + 16 * (c2 + 1), uu[1]);
         }
+        tmem_wait_ld();
 #pragma unroll
-        for (int i2 = 0; i2 < 16; i2 += 2) {
-          float o0, o1;
-          if (GU) {
-            const float g0 = bf16_round(__uint_as_float(g[i2]));
-            const float g1 = bf16_round(__uint_as_float(g[i2 + 1]));
-            const float u0 = bf16_round(__uint_as_float(u[i2]));
-            const float u1 = bf16_round(__uint_as_float(u[i2 + 1]));
-            o0 = __fmul_rn(bf16_round(silu_fast(g0)), u0);
-            o1 = __fmul_rn(bf16_round(silu_fast(g1)), u1);
-          } else {
-            o0 = __uint_as_float(g[i2]);
-            o1 = __uint_as_float(g[i2 + 1]);
-          }
-          const uint32_t pk = pack_bf16x2(o0, o1);
+        for (int h = 0; h < 2; ++h) {
+          if (h == 1 && !two) break;
+          const int c = c2 + h;
+          const uint32_t* g = gg[h];
+          const uint32_t* u = uu[h];
+          const uint32_t r0 = cur.m0 + 16u * (uint32_t)c;
+          // a 16-row group inside one source segment gets one home base
+          uint16_t* gbase = nullptr;
           if (ret) {
-            const size_t col = (size_t)cur.nb * BF + f;
-            if (cur.ok && r0 + i2 < cur.mend) {
-              uint16_t* rp = gbase ? gbase + (size_t)i2 * P.N : home_row(r0 + i2);
-              if (rp) rp[col] = (uint16_t)pk;
-            }
-            if (cur.ok && r0 + i2 + 1 < cur.mend) {
-              uint16_t* rp = gbase ? gbase + (size_t)(i2 + 1) * P.N : home_row(r0 + i2 + 1);
-              if (rp) rp[col] = (uint16_t)(pk >> 16);
-            }
-            continue;
+            const uint32_t rl = min(r0 + 15u, cur.mend - 1u);
+            if (!(r0 >= s_lo && rl < s_hi)) locate(r0);
+            if (r0 >= s_lo && rl < s_hi && s_base) gbase = s_base + (size_t)(r0 - s_lo) * P.N;
           }
-          if (cur.ok && r0 + i2 < cur.mend) ocol[(size_t)(r0 + i2) * P.N] = (uint16_t)pk;
-          if (cur.ok && r0 + i2 + 1 < cur.mend)
-            ocol[(size_t)(r0 + i2 + 1) * P.N] = (uint16_t)(pk >> 16);
+          // this group's 16 tokens x the warp's 32 features through the warp's
+          // shared tile, then one 16-byte vector per (token, 8 features)
+          uint8_t* tb = epi_ring + (dt >> 5) * 1024;
+#pragma unroll
+          for (int i2 = 0; i2 < 16; i2 += 2) {
+            float o0, o1;
+            if (GU) {
+              const float g0 = bf16_round(__uint_as_float(g[i2]));
+              const float g1 = bf16_round(__uint_as_float(g[i2 + 1]));
+              const float u0 = bf16_round(__uint_as_float(u[i2]));
+              const float u1 = bf16_round(__uint_as_float(u[i2 + 1]));
+              o0 = __fmul_rn(bf16_round(silu_fast(g0)), u0);
+              o1 = __fmul_rn(bf16_round(silu_fast(g1)), u1);
+            } else {
+              o0 = __uint_as_float(g[i2]);
+              o1 = __uint_as_float(g[i2 + 1]);
+            }
+            const uint32_t pk = pack_bf16x2(o0, o1);
+            *reinterpret_cast<uint16_t*>(tb + i2 * 64 + lane * 2) = (uint16_t)pk;
+            *reinterpret_cast<uint16_t*>(tb + (i2 + 1) * 64 + lane * 2) = (uint16_t)(pk >> 16);
+          }
+          __syncwarp();
+          const size_t col = (size_t)cur.nb * BF + 32 * q + 8 * (lane & 3);
+#pragma unroll
+          for (int hh = 0; hh < 2; ++hh) {
+            const int rr = (lane >> 2) + 8 * hh;
+            const uint4 v = *reinterpret_cast<const uint4*>(tb + rr * 64 + (lane & 3) * 16);
+            const uint32_t row = r0 + (uint32_t)rr;
+            if (cur.ok && row < cur.mend) {
+              uint16_t* rp = ret ? (gbase ? gbase + (size_t)rr * P.N : home_row(row))
+                                 : P.out + (size_t)row * P.N;
+              if (rp) *reinterpret_cast<uint4*>(rp + col) = v;
+            }
+          }
+          __syncwarp();
         }
       }
       tc_fence_before();
