@@ -53,9 +53,9 @@ constexpr int BF = 128;    // weight features per work item (the MMA's M)
 constexpr int BK = 64;     // K per stage
 constexpr int MAXN = 256;  // token rows per chunk (the MMA's N, rounded up to 16)
 constexpr int kDeqThreads = 256;
-constexpr int kThreads = 64 + kDeqThreads;
+constexpr int kCodeWarp = (64 + kDeqThreads) / 32;  // the code-tile TMA warp
+constexpr int kThreads = 64 + kDeqThreads + 32;
 constexpr unsigned long long kTimeoutNs = 1000000000ull;  // default limit per wait: 1 s
-constexpr int kCodePrefetch = 4;  // K steps of codes each dequant thread has in flight (even)
 
 template <bool GU>
 struct Cfg {
@@ -72,7 +72,12 @@ struct Cfg {
   // per epilogue warp a [16 tokens][32 features] bf16 tile: the warp's
   // outputs leave as 16-byte row vectors instead of one 2-byte store each
   static constexpr int EPI_BYTES = (kDeqThreads / 32) * 16 * 64;
-  static constexpr int SMEM = BSTAGES * B_BYTES + ASTAGES * A_STAGE + EPI_BYTES + 1024;
+  // Q4 code tiles: per stage two K steps (64 bytes) of the block's 128 rows
+  // per weight matrix, brought in by TMA ahead of the dequant warps
+  static constexpr int C_STAGE = NMAT * BF * 64;
+  static constexpr int CSTAGES = 4;
+  static constexpr int SMEM =
+      BSTAGES * B_BYTES + ASTAGES * A_STAGE + EPI_BYTES + CSTAGES * C_STAGE + 1024;
   static constexpr int TMEM_COLS = 512;
   static constexpr int ACC_COLS = NMAT * MAXN;         // accumulator columns per item
   static constexpr int NBUF = TMEM_COLS / ACC_COLS;    // gate/up: 1, down: 2
@@ -140,6 +145,7 @@ __device__ __forceinline__ int cta_item(int i) {
 // stage beats several small ones).
 struct TokenMaps {
   CUtensorMap m64, m128, m256;
+  CUtensorMap c0, c1;  // Q4 codes of w0 / w1 as bytes [E*N rows][K/2], 64-byte swizzle
 };
 
 // ---- PTX wrappers -----------------------------------------------------------
@@ -290,6 +296,7 @@ grouped_gemm_kernel(const __grid_constant__ TokenMaps tm, const GemmParams P) {
   extern __shared__ uint8_t smem_raw[];
   __shared__ __align__(8) uint64_t bfull[C::BSTAGES], bempty[C::BSTAGES];
   __shared__ __align__(8) uint64_t afull[C::ASTAGES], aempty[C::ASTAGES];
+  __shared__ __align__(8) uint64_t cfull[C::CSTAGES], cempty[C::CSTAGES];
   __shared__ __align__(8) uint64_t acc_full[2], acc_empty[2], drain_bar;
   __shared__ uint32_t tmem_base_s;
   __shared__ volatile uint32_t abort_s;
@@ -298,6 +305,7 @@ grouped_gemm_kernel(const __grid_constant__ TokenMaps tm, const GemmParams P) {
                                              ~uintptr_t(1023));
   uint8_t* a_ring = smem + C::BSTAGES * C::B_BYTES;
   uint8_t* epi_ring = a_ring + C::ASTAGES * C::A_STAGE;
+  uint8_t* c_ring = epi_ring + C::EPI_BYTES;
   const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
 
   if (t == 0) {
@@ -308,6 +316,10 @@ grouped_gemm_kernel(const __grid_constant__ TokenMaps tm, const GemmParams P) {
     for (int s = 0; s < C::ASTAGES; ++s) {
       mc_mbar_init(&afull[s], kDeqThreads / 32);
       mc_mbar_init(&aempty[s], 1);
+    }
+    for (int s = 0; s < C::CSTAGES; ++s) {
+      mc_mbar_init(&cfull[s], 1);
+      mc_mbar_init(&cempty[s], kDeqThreads / 32);
     }
     for (int b = 0; b < 2; ++b) {
       mc_mbar_init(&acc_full[b], 1);
@@ -422,6 +434,41 @@ grouped_gemm_kernel(const __grid_constant__ TokenMaps tm, const GemmParams P) {
       __syncwarp();
     }
     __syncwarp();
+  } else if (warp == kCodeWarp) {
+    // ------------------------------------------------------- code-tile TMA
+    // per item and K-step pair one 64-byte x 128-row box of each weight
+    // matrix's codes; runs ahead of the dequant warps by the ring's depth,
+    // across item boundaries too
+    uint32_t cs = 0;
+    const int npairs = ksteps / 2;
+    for (int i = 0, item = cta_item(0); item < total; item = cta_item(++i)) {
+      if (__any_sync(0xffffffffu, abort_s != 0)) break;
+      const Item w = item_info(P, item, nblk);
+      const int row0 = (int)(w.e * (uint32_t)P.N) + w.nb * BF;
+      bool ok = true;
+      for (int pr = 0; pr < npairs; ++pr, ++cs) {
+        const int s = (int)(cs % C::CSTAGES);
+        const uint32_t ph = (cs / C::CSTAGES) & 1;
+        if (!warp_wait(&cempty[s], ph ^ 1, &abort_s, P.timeout_ns)) {
+          ok = false;
+          break;
+        }
+        if (elect_one()) {
+          mc_mbar_expect_tx(&cfull[s], C::C_STAGE);
+          tma_load_2d(c_ring + s * C::C_STAGE, &tm.c0, pr * 64, row0, &cfull[s]);
+          if (GU) tma_load_2d(c_ring + s * C::C_STAGE + BF * 64, &tm.c1, pr * 64, row0, &cfull[s]);
+        }
+        __syncwarp();
+      }
+      if (!ok) {
+        if (lane == 0) abort_s = 1;
+        break;
+      }
+    }
+    __syncwarp();
+    if (abort_s) {
+      for (int k = 0; k < 200; ++k) __nanosleep(1000);
+    }
   } else {
     // ------------------------------------------ dequant producers + epilogue
     // gate/up: group g = matrix, each thread one 64-code row slice per K
@@ -431,32 +478,20 @@ grouped_gemm_kernel(const __grid_constant__ TokenMaps tm, const GemmParams P) {
     const int grp = dt >> 7;
     const int d = dt & 127;           // weight row within the feature block
     const int q = warp & 3;           // TMEM lane quarter this warp may access
-    const uint32_t* wcodes = (GU && grp) ? P.w1.codes : P.w0.codes;
     const uint16_t* wscales = (GU && grp) ? P.w1.scales : P.w0.scales;
     const uint16_t* wbiases = (GU && grp) ? P.w1.biases : P.w0.biases;
-    const int half_off = GU ? 0 : 16 * grp;  // byte offset of this thread's codes in a slice
-    // Code slices kPF K steps ahead in a register ring (slot k % kPF); the
-    // scale and bias of a K-step pair as one 32-bit word each, kPF / 2 pairs
-    // ahead (raw until use: converting at load time would wait for the load
-    // there). The next item's first loads are issued before this item's
-    // epilogue.
-    constexpr int kPF = kCodePrefetch;
-    uint4 cr[kPF][NU];
-    uint32_t swr[kPF / 2], bwr[kPF / 2];
-    const uint8_t* crow = nullptr;
+    // Codes come from the TMA ring (cfull / cempty, one stage per K-step
+    // pair; row d's 64 bytes have their 16-byte chunks at c ^ ((d >> 1) & 3),
+    // the 64-byte swizzle, so eight consecutive rows' chunk c hit eight
+    // different bank groups). The scale and bias of a K-step pair are one
+    // 32-bit word each, kSB pairs ahead (raw until use: converting at load
+    // time would wait for the load there); the next item's first words are
+    // requested before this item's epilogue.
+    constexpr int kSB = 2;
+    uint32_t swr[kSB], bwr[kSB];
     const uint32_t *srow = nullptr, *brow = nullptr;
 #pragma unroll
-    for (int p = 0; p < kPF; ++p)
-#pragma unroll
-      for (int u = 0; u < NU; ++u) cr[p][u] = make_uint4(0, 0, 0, 0);
-#pragma unroll
-    for (int p = 0; p < kPF / 2; ++p) swr[p] = bwr[p] = 0u;
-    auto load_codes = [&](uint4* c, int kk) {
-      if (kk < ksteps) {
-#pragma unroll
-        for (int u = 0; u < NU; ++u) c[u] = mc_ldg_stream(crow + kk * 32 + half_off + 16 * u);
-      }
-    };
+    for (int p = 0; p < kSB; ++p) swr[p] = bwr[p] = 0u;
     auto load_sb = [&](int slot, int pair) {
       if (2 * pair < ksteps) {
         swr[slot] = __ldg(srow + pair);
@@ -466,13 +501,10 @@ grouped_gemm_kernel(const __grid_constant__ TokenMaps tm, const GemmParams P) {
     auto start_item = [&](int item) -> Item {
       const Item w = item_info(P, item, nblk);
       const size_t wrow = (size_t)w.e * P.N + (size_t)w.nb * BF + d;
-      crow = reinterpret_cast<const uint8_t*>(wcodes) + wrow * (P.K / 2);
       srow = reinterpret_cast<const uint32_t*>(wscales + wrow * (P.K / 64));
       brow = reinterpret_cast<const uint32_t*>(wbiases + wrow * (P.K / 64));
 #pragma unroll
-      for (int p = 0; p < kPF; ++p) load_codes(cr[p], p);
-#pragma unroll
-      for (int p = 0; p < kPF / 2; ++p) load_sb(p, p);
+      for (int p = 0; p < kSB; ++p) load_sb(p, p);
       return w;
     };
     // dequantise the slice held in c (K step kk) into stage itk
@@ -495,30 +527,42 @@ grouped_gemm_kernel(const __grid_constant__ TokenMaps tm, const GemmParams P) {
       if (lane == 0) mc_mbar_arrive(&afull[s]);
       return true;
     };
-    uint32_t it = 0, j = 0;
+    const int csw = (d >> 1) & 3;
+    const uint32_t c_off = (GU ? (uint32_t)grp * BF * 64u : 0u) + (uint32_t)d * 64u;
+    uint32_t it = 0, j = 0, cs = 0;
     Item w = start_item(cta_item(0) < total ? cta_item(0) : 0);
     for (int i = 0, item = cta_item(0); item < total; item = cta_item(++i), ++j) {
       if (__any_sync(0xffffffffu, abort_s != 0)) break;
       if (!w.ok && dt == 0 && P.status) atomicOr(P.status, 2u);
       bool ok = true;
-      for (int kk = 0; kk < ksteps && ok; kk += kPF) {
+      for (int kk = 0; kk < ksteps && ok; kk += 2, ++cs) {
+        const int cst = (int)(cs % C::CSTAGES);
+        if (!warp_wait(&cfull[cst], (cs / C::CSTAGES) & 1, &abort_s, P.timeout_ns)) {
+          ok = false;
+          break;
+        }
+        const uint8_t* cb = c_ring + cst * C::C_STAGE + c_off;
+        const int slot = (kk / 2) % kSB;
+        const uint32_t sw = swr[slot], bw = bwr[slot];
+        load_sb(slot, kk / 2 + kSB);
 #pragma unroll
-        for (int p = 0; p < kPF; ++p) {
-          const int k = kk + p;
-          if (k >= ksteps) break;
-          // the K step's bf16 scale and bias, each in both halves
-          const uint32_t sel = (p & 1) ? 0x3232u : 0x1010u;
-          const uint32_t sc = __byte_perm(swr[p / 2], 0, sel), bi = __byte_perm(bwr[p / 2], 0, sel);
-          if (p & 1) load_sb(p / 2, k / 2 + kPF / 2);
+        for (int h = 0; h < 2; ++h) {
           uint4 x[NU];
 #pragma unroll
-          for (int u = 0; u < NU; ++u) x[u] = cr[p][u];
-          load_codes(cr[p], k + kPF);
-          if (!do_slice(x, it + k, sc, bi)) {
+          for (int u = 0; u < NU; ++u) {
+            const int c = 2 * h + (GU ? u : grp);
+            x[u] = *reinterpret_cast<const uint4*>(cb + ((c ^ csw) << 4));
+          }
+          // the K step's bf16 scale and bias, each in both halves
+          const uint32_t sel = h ? 0x3232u : 0x1010u;
+          if (!do_slice(x, it + kk + h, __byte_perm(sw, 0, sel), __byte_perm(bw, 0, sel))) {
             ok = false;
             break;
           }
         }
+        // both K steps of the stage are read: the code stage is free
+        __syncwarp();
+        if (ok && lane == 0) mc_mbar_arrive(&cempty[cst]);
       }
       if (!ok) {
         abort_s = 1;
@@ -697,6 +741,22 @@ int make_a_map(CUtensorMap* map, const uint16_t* a, int rows, int K, int box_row
   return MC_OK;
 }
 
+// The Q4 codes of a stacked [rows][K] matrix as bytes [rows][K/2]; box =
+// two K steps (64 bytes) x 128 rows, 64-byte swizzle.
+int make_code_map(CUtensorMap* map, const void* codes, int rows, int K) {
+  auto enc = get_encode();
+  if (!enc) return mc_fail(MC_ECUDA, "cuTensorMapEncodeTiled unavailable");
+  const cuuint64_t dims[2] = {(cuuint64_t)K / 2, (cuuint64_t)rows};
+  const cuuint64_t strides[1] = {(cuuint64_t)K / 2};
+  const cuuint32_t box[2] = {64, (cuuint32_t)BF};
+  const cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(codes), dims, strides,
+                   box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return mc_fail(MC_ECUDA, "cuTensorMapEncodeTiled (codes) failed (%d)", (int)r);
+  return MC_OK;
+}
+
 template <bool GU>
 int launch(mc_ctx* ctx, const uint16_t* a, int rows, const mc_qweights* w0, const mc_qweights* w1,
            int n_experts, uint16_t* out, const uint32_t* tiles, const uint32_t* n_tiles,
@@ -706,7 +766,9 @@ int launch(mc_ctx* ctx, const uint16_t* a, int rows, const mc_qweights* w0, cons
   TokenMaps tm;
   int rc;
   if ((rc = make_a_map(&tm.m64, a, rows, K, 64)) || (rc = make_a_map(&tm.m128, a, rows, K, 128)) ||
-      (rc = make_a_map(&tm.m256, a, rows, K, 256)))
+      (rc = make_a_map(&tm.m256, a, rows, K, 256)) ||
+      (rc = make_code_map(&tm.c0, w0->codes, w0->out_features, K)) ||
+      (rc = make_code_map(&tm.c1, GU ? w1->codes : w0->codes, w0->out_features, K)))
     return rc;
   GemmParams P{*w0, GU ? *w1 : *w0, out, reinterpret_cast<const uint4*>(tiles), n_tiles, status,
                N, K, rows, max_tiles, n_experts, mc_wait_limit(ctx, kTimeoutNs), {}};
@@ -743,6 +805,7 @@ int check_grouped(const uint16_t* a, int rows, const mc_qweights* w, int n_exper
              w->in_features, 2 * BK);
   MC_REQUIRE(mc_aligned(w->scales, 4) && mc_aligned(w->biases, 4),
              "%s: scales/biases must be 4-byte aligned", what);
+  MC_REQUIRE(mc_aligned(w->codes, 16), "%s: codes must be 16-byte aligned", what);
   MC_REQUIRE(rows >= 1, "%s: rows %d", what, rows);
   MC_REQUIRE(a && out && tiles && n_tiles && max_tiles >= 1, "%s: null pointer", what);
   MC_REQUIRE(mc_aligned(a, 16) && mc_aligned(out, 16) && mc_aligned(tiles, 16),
