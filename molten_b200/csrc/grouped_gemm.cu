@@ -63,11 +63,14 @@ struct Cfg {
   static constexpr int B_BYTES = MAXN * BK * 2;        // 32 KB of token rows per K step
   static constexpr int A_BYTES = BF * BK * 2;          // 16 KB per weight tile
   static constexpr int A_STAGE = NMAT * A_BYTES;
-  // Ring depths measured best on B200. Shared memory and L1 share each SM's
-  // 256 KB, and the dequant threads' code loads in flight live in L1: the
-  // down GEMM at 4 + 4 stages plus the epilogue tiles (201 KB) ran at 254 us
-  // on the cfg3 workload, at 3 + 3 stages (161 KB) at 160 us.
-  static constexpr int BSTAGES = GU ? 2 : 3;
+  // Ring depths measured best on B200 (cfg3 workload). While the dequant
+  // threads still loaded their codes themselves, those loads in flight lived
+  // in L1, which shares each SM's 256 KB with shared memory, and deeper rings
+  // were slower (down at 4 + 4 stages: 254 us, at 3 + 3: 160 us). With the
+  // codes brought by TMA the token rings can be deeper: gate/up 3 token +
+  // 2 weight + 2 code stages 247 us (2 + 2 + 4: 262 us), down 4 + 3 + 2
+  // 157 us.
+  static constexpr int BSTAGES = GU ? 3 : 4;
   static constexpr int ASTAGES = GU ? 2 : 3;
   // per epilogue warp a [16 tokens][32 features] bf16 tile: the warp's
   // outputs leave as 16-byte row vectors instead of one 2-byte store each
@@ -75,7 +78,7 @@ struct Cfg {
   // Q4 code tiles: per stage two K steps (64 bytes) of the block's 128 rows
   // per weight matrix, brought in by TMA ahead of the dequant warps
   static constexpr int C_STAGE = NMAT * BF * 64;
-  static constexpr int CSTAGES = 4;
+  static constexpr int CSTAGES = 2;
   static constexpr int SMEM =
       BSTAGES * B_BYTES + ASTAGES * A_STAGE + EPI_BYTES + CSTAGES * C_STAGE + 1024;
   static constexpr int TMEM_COLS = 512;
