@@ -573,9 +573,9 @@ CFG3_METRIC = "prefill grouped-GEMM tokens/s (cfg3: 4096-token MoE FFN, Zipf rou
 CFG3_WORKLOAD = ("cfg3: 4096 tokens per GPU x 2048, E=64 top-4 Zipf(s=1) routing, "
                  "SwiGLU 2048->1536->2048 Q4")
 # kernels one mc_ep_moe_prefill launches: route, relabel, sort (2), counts
-# exchange, row chunks, return map, dispatch, barrier, gate/up GEMM, down GEMM,
-# return, barrier, combine
-EP_STEP_LAUNCHES = 14
+# exchange, row chunks, return map, dispatch, barrier, gate/up GEMM, down GEMM
+# (which also returns the expert rows), barrier, combine
+EP_STEP_LAUNCHES = 13
 
 
 def prefill_flops(S):

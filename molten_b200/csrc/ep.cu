@@ -93,7 +93,7 @@ ep_dispatch_kernel(const uint4* __restrict__ x, int m, int h16,
     }
     const uint4* row = x + (size_t)tok * h16;
     uint4* out = reinterpret_cast<uint4*>(recv.p[lo / P]) + (size_t)(dst0[lo] + k) * h16;
-    for (int c = lane; c < h16; c += 32) out[c] = __ldg(row + c);
+    mc_copy_row16(out, row, h16, lane);
   }
   __threadfence_system();
 }
@@ -121,7 +121,7 @@ ep_return_kernel(const uint4* __restrict__ ed, uint32_t ed_rows, int h16,
     }
     const uint4* row = ed + (size_t)(row0 + k) * h16;
     uint4* out = dst + (size_t)(slot0 + k) * h16;
-    for (int c = lane; c < h16; c += 32) out[c] = __ldg(row + c);
+    mc_copy_row16(out, row, h16, lane);
   }
   __threadfence_system();
 }

@@ -8,14 +8,15 @@
 //   count table (peer stores) + barrier -> receive-side row chunks and the
 //   return map -> dispatch: rows stored straight into the owners' receive
 //   buffers over NVLink (CUDA IPC mappings) -> barrier -> grouped gate/up
-//   (+SwiGLU) and down GEMMs -> return: each expert row stored into its
-//   source's home buffer -> barrier -> weighted combine at home.
+//   (+SwiGLU) and down GEMMs, the down GEMM's epilogue storing each expert
+//   row straight into its source's home buffer -> barrier -> weighted
+//   combine at home.
 //
-// (Returning the rows from the down GEMM's epilogue instead, so the NVLink
-// traffic overlaps the GEMM, measured slower on two B200s: 0.668 against
-// 0.640 ms per step. The epilogue runs on the dequantising warps, the
-// GEMM's critical resource, and paid more for the per-row destinations than
-// the separate copy costs. mc_gemm_q4_grouped_return keeps that variant.)
+// (The return from the epilogue overlaps the NVLink traffic with the GEMM.
+// While the epilogue stored one 2-byte value per thread and row it lost to a
+// separate grid-stride copy after the GEMM (0.668 against 0.640 ms per step
+// on two B200s); with the outputs staged in shared memory and stored as
+// 16-byte rows it wins: 0.566 against 0.605 ms.)
 //
 // Slots. E_slots = W * slots_per_rank; rank r owns slots [r*spr, (r+1)*spr)
 // and holds their weights stacked in slot order. With spr = E / W and an
@@ -127,7 +128,7 @@ struct mc_ep_state {
   uint8_t* scratch = nullptr;
   uint32_t *ids, *counts, *offsets, *ids_sorted, *slotpos, *sort_tiles, *sort_ntiles;
   uint32_t *counts_all, *tiles, *n_tiles, *rows, *status, *epoch;
-  uint16_t *gw, *act, *ed;
+  uint16_t *gw, *act;
   uint32_t *seg_row, *seg_home;  // return map (ep_segments_kernel)
   int sort_max_tiles = 0, max_tiles = 0;
   // phase timing (mc_ep_set_profile): events at the step's phase boundaries
@@ -247,43 +248,6 @@ ep_segments_kernel(const uint32_t* __restrict__ counts_all_g, int rank, int W, i
       seg_home[j * W + s] = h;
     }
   }
-}
-
-// The return without the fused epilogue: received expert rows ed[i] -> row
-// seg_home + (i - seg_row) of their source's home buffer, every warp taking
-// rows across all segments (grid-stride), the segment found by binary search
-// over the (slot, source) starts staged in shared memory.
-__global__ void __launch_bounds__(256)
-ep_return_rows_kernel(const uint4* __restrict__ ed, int h16, const uint32_t* __restrict__ seg_row,
-                      const uint32_t* __restrict__ seg_home, int spr, int W, FlagPtrs home,
-                      uint32_t home_cap, uint32_t* status) {
-  __shared__ uint32_t st[257], sh[256];
-  const int nseg = spr * W;
-  for (int k = threadIdx.x; k < nseg; k += blockDim.x) {
-    st[k] = seg_row[(k / W) * (W + 1) + k % W];
-    sh[k] = seg_home[k];
-  }
-  if (threadIdx.x == 0) st[nseg] = seg_row[(spr - 1) * (W + 1) + W];
-  __syncthreads();
-  const uint32_t total = st[nseg];
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  for (uint32_t r = blockIdx.x * 8 + warp; r < total; r += gridDim.x * 8) {
-    int lo = 0, hi = nseg;  // st[lo] <= r < st[hi]
-    while (hi - lo > 1) {
-      const int mid = (lo + hi) >> 1;
-      if (st[mid] <= r) lo = mid;
-      else hi = mid;
-    }
-    const uint32_t hr = sh[lo] + (r - st[lo]);
-    if (hr >= home_cap) {
-      if (lane == 0 && status) atomicOr(status, 4u);
-      continue;
-    }
-    uint4* out = reinterpret_cast<uint4*>(home.p[lo % W]) + (size_t)hr * h16;
-    const uint4* row = ed + (size_t)r * h16;
-    for (int c = lane; c < h16; c += 32) out[c] = row[c];
-  }
-  __threadfence_system();
 }
 
 int ep_barrier(mc_ctx* ctx) {
@@ -419,7 +383,6 @@ extern "C" int mc_ep_reserve(mc_ctx* ctx, int m_max, int n_experts, int slots_pe
   carve((void**)&ep->status, 16);
   carve((void**)&ep->epoch, 16);
   carve((void**)&ep->act, ep->recv_cap * moe_inter * 2);
-  carve((void**)&ep->ed, ep->recv_cap * hidden * 2);
   void* q = nullptr;
   cudaError_t e = cudaMalloc(&q, o);
   if (e != cudaSuccess) {
@@ -531,19 +494,10 @@ extern "C" int mc_ep_moe_prefill(mc_ctx* ctx, const uint16_t* x, const float* lo
                                   ep->n_tiles, ep->max_tiles, ep->status)))
     return rc;
   // the down GEMM stores each expert row straight into its source's home row
-  if ((rc = mc_gemm_q4_grouped(ctx, ep->act, rows, down, ep->spr, ep->ed, ep->tiles, ep->n_tiles,
-                               ep->max_tiles, ep->status)))
+  if ((rc = mc_gemm_q4_grouped_return(ctx, ep->act, rows, down, ep->spr, ep->seg_row, ep->seg_home,
+                                       ep->home_ptr, W, ep->home_cap, ep->tiles, ep->n_tiles,
+                                       ep->max_tiles, ep->status)))
     return rc;
-  {
-    FlagPtrs home;
-    for (int r = 0; r < kMaxRanks; ++r)
-      home.p[r] = r < W ? static_cast<uint32_t*>(ep->home_ptr[r]) : nullptr;
-    const int grid = ctx->num_sms * 2;
-    ep_return_rows_kernel<<<grid, 256, 0, ctx->stream>>>(
-        reinterpret_cast<const uint4*>(ep->ed), ep->H / 8, ep->seg_row, ep->seg_home, ep->spr, W,
-        home, (uint32_t)ep->home_cap, ep->status);
-    if ((rc = mc_after_launch("ep_return_rows_kernel"))) return rc;
-  }
   if ((rc = mark(4))) return rc;
   if ((rc = ep_barrier(ctx))) return rc;
   if ((rc = mark(5))) return rc;

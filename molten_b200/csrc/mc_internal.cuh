@@ -114,6 +114,27 @@ __device__ __forceinline__ uint4 mc_ldg_stream(const void* p) {
   return r;
 }
 
+// One row of h16 16-byte words copied by a warp: eight loads per lane in
+// flight before their stores (a load-store pair per step left the NVLink row
+// copies latency-bound). `in` is read through the read-only path: it must
+// not be written during the kernel.
+__device__ __forceinline__ void mc_copy_row16(uint4* __restrict__ out,
+                                              const uint4* __restrict__ in, int h16, int lane) {
+  for (int c0 = 0; c0 < h16; c0 += 256) {
+    uint4 v[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int c = c0 + lane + 32 * i;
+      if (c < h16) v[i] = __ldg(in + c);
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int c = c0 + lane + 32 * i;
+      if (c < h16) out[c] = v[i];
+    }
+  }
+}
+
 __device__ __forceinline__ float mc_warp_butterfly(float v) {
 #pragma unroll
   for (int m = 16; m >= 1; m >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, m));
