@@ -972,7 +972,8 @@ def bench_cfg4(args, torch, ws, rank, local):
         "config": {"workload": f"cfg4: {L} layers x (Q4 2048x2048 + E=64 top-4 SwiGLU 2048->1536"
                                f"->2048) + Q6 65536x2048 head + bf16 embedding gather, batch {B}, "
                                "one step per CUDA-graph replay",
-                   "batch": B, "moe_path": st.path, "gbs": round(gbs, 1),
+                   "batch": B, "moe_path": st.path, "fused_projection": st.fuse_proj,
+                   "gbs": round(gbs, 1),
                    "bytes_per_step": step_bytes,
                    "distinct_experts_per_layer_mean": round(sum(U) / L, 2),
                    "l2": f"inputs > L2: {L} layers of weights ({L * 0.342:.1f} GB) streamed per step",

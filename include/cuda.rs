@@ -220,6 +220,32 @@ extern "C" {
         eps: f32,
         route_eps: f32,
     ) -> c_int;
+    pub fn mc_moe_decode_proj_workspace_words(moe_inter: c_int) -> usize;
+    pub fn mc_moe_decode_layer_proj(
+        ctx: *mut McCtx,
+        h: *const u16,
+        proj: *const McQweights,
+        p_out: *mut u16,
+        norm_w: *const u16,
+        h_out: *mut u16,
+        normed: *mut u16,
+        router_w: *const c_void,
+        router_dtype: c_int,
+        expert_bias: *const f32,
+        route_mode: c_int,
+        logits: *mut f32,
+        ids: *mut u32,
+        weights: *mut u16,
+        gate: *const McQweights,
+        up: *const McQweights,
+        down: *const McQweights,
+        n_experts: c_int,
+        out: *mut u16,
+        workspace: *mut u32,
+        ws_words: usize,
+        eps: f32,
+        route_eps: f32,
+    ) -> c_int;
     pub fn mc_proj3_gemv_scatter(
         ctx: *mut McCtx,
         q: *const McQweights,

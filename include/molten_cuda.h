@@ -205,6 +205,29 @@ int mc_moe_decode_layer_noalloc(mc_ctx* ctx, const uint16_t* h, const uint16_t* 
                                 const mc_qweights* up, const mc_qweights* down, int n_experts,
                                 uint16_t* out, uint32_t* status, float eps, float route_eps);
 
+/* gemv_quant(proj, h) -> b (kernels/lfm.rs:112-149) followed by
+ * mc_moe_decode_layer(h, b, ...) in ONE launch: every CTA computes its slice
+ * of b = bf16(proj . h) (proj: Q4 2048 x 2048, group 64) in the canonical
+ * GEMV order, the slices are exchanged as epoch-tagged words and the layer
+ * proceeds as mc_moe_decode_layer, so every output is bit-identical to the
+ * two calls. The pairing is the decode step of BASELINE cfg4 (a Q4
+ * projection of the layer input feeding the MoE layer's residual add); the
+ * reference issues the two ops separately, and the saving is the kernel
+ * boundary between them. `workspace` holds mc_moe_decode_proj_workspace_words(I)
+ * words (mc_moe_decode_workspace_words(I) + 2048; b's tagged words follow
+ * the act words); `p_out` (may be NULL) receives b; status bit 32 in
+ * workspace[2] reports a projection wait that gave up. Other rules as
+ * mc_moe_decode_layer. */
+size_t mc_moe_decode_proj_workspace_words(int moe_inter);
+int mc_moe_decode_layer_proj(mc_ctx* ctx, const uint16_t* h, const mc_qweights* proj,
+                             uint16_t* p_out, const uint16_t* norm_w, uint16_t* h_out,
+                             uint16_t* normed, const void* router_w, int router_dtype,
+                             const float* expert_bias, int route_mode, float* logits,
+                             uint32_t* ids, uint16_t* weights, const mc_qweights* gate,
+                             const mc_qweights* up, const mc_qweights* down, int n_experts,
+                             uint16_t* out, uint32_t* workspace, size_t ws_words, float eps,
+                             float route_eps);
+
 /* ------------------------------------------------ decode neighbours */
 
 /* proj3_gemv_scatter (kernels/lfm.rs:150-205 -> lfm_proj3_gemv_scatter_bf16

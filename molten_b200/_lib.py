@@ -107,6 +107,9 @@ SIGNATURES: dict[str, tuple] = {
     "mc_ep_return": (I, [P, P, C.c_size_t, I, P, I, I, I, P, C.c_size_t, P]),
     "mc_moe_decode_layer_noalloc": (I, [P, P, P, P, P, P, P, I, P, I, P, P, P, QP, QP, QP, I, P,
                                         P, F, F]),
+    "mc_moe_decode_proj_workspace_words": (C.c_size_t, [I]),
+    "mc_moe_decode_layer_proj": (I, [P, P, QP, P, P, P, P, P, I, P, I, P, P, P, QP, QP, QP, I, P,
+                                     P, C.c_size_t, F, F]),
     "mc_proj3_gemv_scatter": (I, [P, QP, QP, QP, P, P, P, P, I, I]),
     "mc_conv3_gemv": (I, [P, QP, P, P, P, P, P, I]),
     "mc_gemv_gu_act": (I, [P, QP, QP, P, P, I]),

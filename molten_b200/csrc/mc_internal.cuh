@@ -29,15 +29,17 @@ static inline unsigned long long mc_wait_limit(const mc_ctx* ctx, unsigned long 
   return ctx->wait_limit_ns ? ctx->wait_limit_ns : dflt;
 }
 
-// The fused decode layer behind mc_moe_decode_layer and
-// mc_moe_decode_layer_noalloc (moe_decode_fused.cu).
+// The fused decode layer behind mc_moe_decode_layer, _noalloc and _proj
+// (moe_decode_fused.cu). With `proj`, b is computed in the launch as
+// bf16(proj . h) (b must be null) and copied to p_out when that is given.
 int mc_decode_layer_impl(mc_ctx* ctx, const uint16_t* h, const uint16_t* b,
                          const uint16_t* norm_w, uint16_t* h_out, uint16_t* normed,
                          const void* router_w, int router_dtype, const float* expert_bias,
                          int route_mode, float* logits, uint32_t* ids, uint16_t* weights,
                          const mc_qweights* gate, const mc_qweights* up, const mc_qweights* down,
                          int n_experts, uint16_t* out, uint32_t* sync, size_t ws_words, float eps,
-                         float route_eps, bool noalloc, uint32_t* status_out);
+                         float route_eps, bool noalloc, uint32_t* status_out,
+                         const mc_qweights* proj, uint16_t* p_out);
 // Grouped GEMM (not gate/up) storing each output row into its source
 // rank's home buffer: rows of expert j from source s are seg_row[j][s] ..
 // seg_row[j][s+1] and go to rows from seg_home[j][s] of home[s]

@@ -26,13 +26,17 @@
 //   ws[0]            epoch (advanced by the last CTA to finish)
 //   ws[1]            CTAs finished (reset by the last one)
 //   ws[2]            sticky error status bits: 1 logits wait gave up,
-//                    2 expert id out of range, 8 act wait, 16 a copy wait
+//                    2 expert id out of range, 8 act wait, 16 a copy wait,
+//                    32 projection wait
 //   ws[3]            reserved (zero)
-//   ws[4]            reserved (zero; reset by the last CTA to finish)
+//   ws[4]            CTAs whose projection rows are stored (fused
+//                    projection only; reset by the last CTA to finish)
 //   ws[5..8)         reserved (zero)
 //   ws[8..136)       64 tagged logits (u64: tag32 << 32 | f32 bits)
 //   ws[136..)        act values [slot][row], one tagged word each
 //                    (tag16 << 16 | bf16 bits, tag16 = tag32 % 65535 + 1)
+//   ws[136 + 4I..)   with the fused projection: its 2048 bf16 outputs
+//                    (4 KB; 2048 words reserved)
 // Every wait is bounded by a %globaltimer deadline; a CTA whose copies did
 // not all land waits for them (bounded again) before it exits.
 //
@@ -71,10 +75,12 @@ __host__ __device__ inline int chunk_count(int np) {
 
 struct Layout {
   int np_max, nr_max, nchunk_max;
-  uint32_t uc, sb, dn, pro, total;
+  uint32_t uc, sb, dn, pro, pj, total;
 };
 
-__host__ __device__ inline Layout make_layout(int I, int G) {
+// With `proj` the layout ends with this CTA's projection rows: nr_max rows of
+// Q4 codes (1024 B each), then their scales, then their biases (64 B each).
+__host__ __device__ inline Layout make_layout(int I, int G, bool proj = false) {
   Layout L;
   L.np_max = (4 * I + G - 1) / G;
   L.nr_max = (H + G - 1) / G;
@@ -85,6 +91,8 @@ __host__ __device__ inline Layout make_layout(int I, int G) {
   L.pro = L.dn + 4u * (uint32_t)L.nr_max * (uint32_t)(I / 2);
   const uint32_t act_bytes = 8u * (uint32_t)I;  // 4 x I bf16, reuses the prologue area
   L.total = L.pro + (act_bytes > kPrologueBytes ? act_bytes : kPrologueBytes);
+  L.pj = L.total;
+  if (proj) L.total += (uint32_t)L.nr_max * (H / 2 + 128u);
   return L;
 }
 
@@ -114,6 +122,11 @@ struct Params {
   uint32_t* status_out;
   int report_status;
   int skip_publish;  // test aid (mc_set_test_flags): router warps publish nothing
+  // fused projection (mc_moe_decode_layer_proj): b = bf16(proj . h) computed
+  // here, row slice [i0, i1) per CTA, exchanged as tagged words; p_out
+  // (nullable) receives b
+  mc_qweights proj;
+  uint16_t* p_out;
 };
 
 constexpr int kTraceSlots = 32;  // per-CTA phase timestamps (mc_set_trace)
@@ -138,7 +151,7 @@ __device__ __forceinline__ float smem_group_qx(const uint8_t* p, const float2* x
   return q4_group_qx(q[0], q[1], xs);
 }
 
-template <int DT>
+template <int DT, bool PROJ>
 __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(const Params P,
                                                                       const Layout L) {
   extern __shared__ __align__(128) uint8_t sm[];
@@ -149,7 +162,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(const Par
   __shared__ float p_s[4][32];
   __shared__ float gu_s[2][256];  // bf16-rounded gate and up sums per local pair
   __shared__ uint32_t flag_s;
-  __shared__ __align__(8) uint64_t bar_sb, bar_dn, bar_gu[kMaxChunks];
+  __shared__ __align__(8) uint64_t bar_sb, bar_dn, bar_gu[kMaxChunks], bar_pj;
 
   const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
   const int G = gridDim.x, cta = blockIdx.x;
@@ -178,7 +191,20 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(const Par
     mc_mbar_init(&bar_sb, 1);
     mc_mbar_init(&bar_dn, 1);
     for (int c = 0; c < kMaxChunks; ++c) mc_mbar_init(bar_gu + c, 1);
+    mc_mbar_init(&bar_pj, 1);
     mc_fence_barrier_init();
+    // this CTA's projection rows (weights: never written by earlier kernels,
+    // so they stream in before the programmatic-dependent-launch wait)
+    if (PROJ && nr > 0) {
+      const uint64_t pol = mc_policy_evict_first();
+      mc_mbar_expect_tx(&bar_pj, (uint32_t)nr * (H / 2 + 128u));
+      mc_bulk_g2s(sm + L.pj, reinterpret_cast<const uint8_t*>(P.proj.codes) + (size_t)i0 * (H / 2),
+                  (uint32_t)nr * (H / 2), &bar_pj, pol);
+      mc_bulk_g2s(sm + L.pj + (uint32_t)L.nr_max * (H / 2), P.proj.scales + (size_t)i0 * 32,
+                  (uint32_t)nr * 64u, &bar_pj, pol);
+      mc_bulk_g2s(sm + L.pj + (uint32_t)L.nr_max * (H / 2 + 64u), P.proj.biases + (size_t)i0 * 32,
+                  (uint32_t)nr * 64u, &bar_pj, pol);
+    }
   }
   RouterRow<DT> rr;
   if (router_cta && warp == 0) {
@@ -218,6 +244,59 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(const Par
   const uint32_t tag32 = epoch == 0xffffffffu ? 1u : epoch + 1u;
   const uint32_t tag16 = tag32 % 65535u + 1u;  // never 0, differs from the last launch's
 
+  // ---- fused projection: warp 1 + j computes row i0 + j of b = proj . h in
+  // the canonical GEMV order (gemv_kernel, K = 2048: lane l owns group l,
+  // term = fma(s, qx, b * xg), 32-lane butterfly), bit-identical to
+  // gemv_quant, and stores it (bf16) into the workspace; once a CTA's rows
+  // are stored (a barrier over the projection warps), one release increment
+  // of ws[4] counts the CTA, and the CTAs read b once ws[4] reaches the grid
+  // size. (Epoch-tagged
+  // words polled by every thread, as the act rows are, measured far slower
+  // here: 148 x 256 pollers over the same 8 KB of lines delayed the stores
+  // they waited for by up to 12 us.)
+  uint16_t* pw16 = reinterpret_cast<uint16_t*>(sync + kActWord + 4 * I);
+  if (PROJ && warp >= 1 && warp <= nr) {
+    const int j = warp - 1;
+    float2 xsh[32];
+    const float xgh = load_group_x<4>(P.h, lane, xsh);
+    if (wait_copies(&bar_pj, mc_globaltimer() + P.timeout_ns)) {
+      const uint16_t* psb = reinterpret_cast<const uint16_t*>(sm + L.pj + (uint32_t)L.nr_max * (H / 2));
+      const float s = mc_bf16_to_f32(psb[j * 32 + lane]);
+      const float bb = mc_bf16_to_f32(psb[L.nr_max * 32 + j * 32 + lane]);
+      const float acc = __fadd_rn(
+          0.0f, __fmaf_rn(s, smem_group_qx(sm + L.pj + (uint32_t)j * (H / 2) + 32 * lane, xsh),
+                          __fmul_rn(bb, xgh)));
+      const float sum = mc_warp_butterfly(acc);
+      if (lane == 0) {
+        const uint16_t v = (uint16_t)mc_f32_to_bf16(sum);
+        __stcg(pw16 + i0 + j, v);
+        if (P.p_out) P.p_out[i0 + j] = v;
+        // profiling aid: when this CTA's first projection row is stored
+        if (P.trace && j == 0) P.trace[kTraceSlots * blockIdx.x + 5] = mc_globaltimer();
+      }
+    } else if (lane == 0) {
+      record_error(sync, 32u);
+    }
+    asm volatile("bar.sync 1, %0;" ::"r"(nr * 32) : "memory");
+    if (warp == 1 && lane == 0) mc_red_release_add(sync + 4, 1u);
+  }
+  if (PROJ && t < 256) {
+    if (t == 0) {
+      const unsigned long long deadline = mc_globaltimer() + P.timeout_ns;
+      while (mc_ld_acquire(sync + 4) < (uint32_t)G) {
+        if (mc_globaltimer() > deadline) {
+          record_error(sync, 32u);
+          break;
+        }
+        __nanosleep(64);
+      }
+    }
+    asm volatile("bar.sync 2, 256;" ::: "memory");
+    bv = __ldcg(reinterpret_cast<const uint4*>(pw16) + t);
+    TRACE(8);
+  }
+  const bool has_b = P.badd != nullptr || PROJ;
+
   // ---- add + RMSNorm (canonical order of addnorm_row_2048)
   float hp[8];
   if (t < 256) {
@@ -227,7 +306,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(const Par
     for (int i = 0; i < 8; ++i) {
       const float hf = mc_bf16_to_f32((uint16_t)(hw[i >> 1] >> (16 * (i & 1))));
       float v = hf;
-      if (P.badd) v = __fadd_rn(hf, mc_bf16_to_f32((uint16_t)(bw[i >> 1] >> (16 * (i & 1)))));
+      if (has_b) v = __fadd_rn(hf, mc_bf16_to_f32((uint16_t)(bw[i >> 1] >> (16 * (i & 1)))));
       hp[i] = mc_round_bf16(v);
       acc = __fmaf_rn(hp[i], hp[i], acc);
     }
@@ -597,6 +676,9 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_fused_kernel(const Par
     for (int c = 0; issued && c < nchunk; ++c) all = wait_copies(bar_gu + c, deadline) && all;
     if (!all) record_error(sync, 16u);
   }
+  if (t == 0 && PROJ && nr > 0 &&
+      !wait_copies(&bar_pj, mc_globaltimer() + P.timeout_ns))
+    record_error(sync, 16u);
 
   // ---- the last CTA to finish resets the counters and advances the epoch
   TRACE(7);
@@ -623,6 +705,10 @@ extern "C" size_t mc_moe_decode_workspace_words(int moe_inter) {
   return (size_t)kActWord + 4 * (size_t)(moe_inter > 0 ? moe_inter : 0);
 }
 
+extern "C" size_t mc_moe_decode_proj_workspace_words(int moe_inter) {
+  return mc_moe_decode_workspace_words(moe_inter) + H;
+}
+
 // The fused decode layer behind both entry points. With `noalloc` the
 // workspace arguments are ignored: every argument is checked first, then the
 // library's built-in scratch is fetched (its first use on a device sets it
@@ -633,9 +719,20 @@ int mc_decode_layer_impl(mc_ctx* ctx, const uint16_t* h, const uint16_t* b,
                          int route_mode, float* logits, uint32_t* ids, uint16_t* weights,
                          const mc_qweights* gate, const mc_qweights* up, const mc_qweights* down,
                          int n_experts, uint16_t* out, uint32_t* sync, size_t ws_words, float eps,
-                         float route_eps, bool noalloc, uint32_t* status_out) {
+                         float route_eps, bool noalloc, uint32_t* status_out,
+                         const mc_qweights* proj, uint16_t* p_out) {
   MC_REQUIRE(ctx, "moe_decode_layer: null context");
   int rc;
+  if (proj) {
+    if ((rc = mc_check_gemv_weights(proj, "moe_decode_layer_proj proj"))) return rc;
+    MC_REQUIRE(proj->bits == 4 && proj->in_features == H && proj->out_features == H &&
+                   proj->group_size == 64,
+               "moe_decode_layer_proj: proj must be Q4 2048 x 2048, group 64");
+    MC_REQUIRE(mc_aligned(proj->codes, 16) && mc_aligned(proj->scales, 16) &&
+                   mc_aligned(proj->biases, 16),
+               "moe_decode_layer_proj: proj buffers must be 16-byte aligned");
+    MC_REQUIRE(!b && !noalloc, "moe_decode_layer_proj: b is computed, not passed");
+  }
   if ((rc = mc_check_gemv_weights(gate, "moe_decode_layer gate"))) return rc;
   if ((rc = mc_check_gemv_weights(up, "moe_decode_layer up"))) return rc;
   if ((rc = mc_check_gemv_weights(down, "moe_decode_layer down"))) return rc;
@@ -650,9 +747,10 @@ int mc_decode_layer_impl(mc_ctx* ctx, const uint16_t* h, const uint16_t* b,
   MC_REQUIRE(I % 64 == 0 && I <= 2048 && 4 * I <= 4 * 2048 && down->in_features == I &&
                  down->out_features == n_experts * H,
              "moe_decode_layer: expert shapes (I=%d)", I);
-  MC_REQUIRE(noalloc || ws_words >= mc_moe_decode_workspace_words(I),
-             "moe_decode_layer: workspace of %zu words < %zu", ws_words,
-             mc_moe_decode_workspace_words(I));
+  const size_t need = proj ? mc_moe_decode_proj_workspace_words(I)
+                           : mc_moe_decode_workspace_words(I);
+  MC_REQUIRE(noalloc || ws_words >= need, "moe_decode_layer: workspace of %zu words < %zu",
+             ws_words, need);
   MC_REQUIRE(h && norm_w && h_out && normed && router_w && logits && ids && weights && out &&
                  (noalloc || sync),
              "moe_decode_layer: null pointer");
@@ -671,11 +769,13 @@ int mc_decode_layer_impl(mc_ctx* ctx, const uint16_t* h, const uint16_t* b,
   MC_REQUIRE((const void*)h_out != (const void*)h && (const void*)h_out != (const void*)b &&
                  (const void*)normed != (const void*)h && (const void*)normed != (const void*)b,
              "moe_decode_layer: h_out/normed must not alias h or b");
+  MC_REQUIRE(!p_out || ((const void*)p_out != (const void*)h && (const void*)p_out != (const void*)out),
+             "moe_decode_layer_proj: p_out must not alias h or out");
   const int G = ctx->num_sms;
   // each CTA: <= 16 down rows (4 warps x kDnRows per expert), <= kMaxChunks
   // chunks of gate/up pairs, one router row per expert among the CTAs, and
   // its whole slice of expert rows in shared memory
-  const Layout L = make_layout(I, G);
+  const Layout L = make_layout(I, G, proj != nullptr);
   MC_REQUIRE(L.nr_max <= 4 * kDnRows && L.nchunk_max <= kMaxChunks && G >= n_experts,
              "moe_decode_layer: too few SMs (%d)", G);
   MC_REQUIRE((int)L.total + 4096 <= ctx->max_smem_optin,
@@ -696,7 +796,9 @@ int mc_decode_layer_impl(mc_ctx* ctx, const uint16_t* h, const uint16_t* b,
            ctx->wait_limit_ns ? ctx->wait_limit_ns : kTimeoutNs,
            status_out,
            noalloc ? 1 : 0,
-           (ctx->test_flags & MC_TEST_SKIP_LOGIT_PUBLISH) ? 1 : 0};
+           (ctx->test_flags & MC_TEST_SKIP_LOGIT_PUBLISH) ? 1 : 0,
+           proj ? *proj : mc_qweights{},
+           p_out};
   for (int r = 0; r < 2; ++r) {
     if (!ctx->pf_ptr[r]) continue;
     // whole 128-byte lines covering the range
@@ -707,11 +809,15 @@ int mc_decode_layer_impl(mc_ctx* ctx, const uint16_t* h, const uint16_t* b,
     ctx->pf_ptr[r] = nullptr;
     ctx->pf_bytes[r] = 0;
   }
-  void* fn = router_dtype == MC_DTYPE_BF16 ? (void*)moe_decode_fused_kernel<MC_DTYPE_BF16>
-                                           : (void*)moe_decode_fused_kernel<MC_DTYPE_F32>;
+  void* fn = router_dtype == MC_DTYPE_BF16
+                 ? (proj ? (void*)moe_decode_fused_kernel<MC_DTYPE_BF16, true>
+                         : (void*)moe_decode_fused_kernel<MC_DTYPE_BF16, false>)
+                 : (proj ? (void*)moe_decode_fused_kernel<MC_DTYPE_F32, true>
+                         : (void*)moe_decode_fused_kernel<MC_DTYPE_F32, false>);
   // the dynamic shared memory limit is raised once per device and kernel
-  static std::atomic<int> smem_set[2][64];
-  std::atomic<int>& cur = smem_set[router_dtype == MC_DTYPE_BF16 ? 0 : 1][ctx->device & 63];
+  static std::atomic<int> smem_set[4][64];
+  std::atomic<int>& cur =
+      smem_set[(router_dtype == MC_DTYPE_BF16 ? 0 : 1) + (proj ? 2 : 0)][ctx->device & 63];
   if (cur.load() < (int)L.total) {
     MC_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  ctx->max_smem_optin - 4096));
@@ -750,5 +856,23 @@ extern "C" int mc_moe_decode_layer(mc_ctx* ctx, const uint16_t* h, const uint16_
                                    float route_eps) {
   return mc_decode_layer_impl(ctx, h, b, norm_w, h_out, normed, router_w, router_dtype,
                               expert_bias, route_mode, logits, ids, weights, gate, up, down,
-                              n_experts, out, sync, ws_words, eps, route_eps, false, nullptr);
+                              n_experts, out, sync, ws_words, eps, route_eps, false, nullptr,
+                              nullptr, nullptr);
+}
+
+// gemv_quant(proj, h) -> b followed by moe_decode (kernels/lfm.rs:112-149,
+// lfm.rs:967-1011) in one launch; see the header.
+extern "C" int mc_moe_decode_layer_proj(mc_ctx* ctx, const uint16_t* h, const mc_qweights* proj,
+                                        uint16_t* p_out, const uint16_t* norm_w, uint16_t* h_out,
+                                        uint16_t* normed, const void* router_w, int router_dtype,
+                                        const float* expert_bias, int route_mode, float* logits,
+                                        uint32_t* ids, uint16_t* weights, const mc_qweights* gate,
+                                        const mc_qweights* up, const mc_qweights* down,
+                                        int n_experts, uint16_t* out, uint32_t* sync,
+                                        size_t ws_words, float eps, float route_eps) {
+  MC_REQUIRE(proj, "moe_decode_layer_proj: null proj");
+  return mc_decode_layer_impl(ctx, h, nullptr, norm_w, h_out, normed, router_w, router_dtype,
+                              expert_bias, route_mode, logits, ids, weights, gate, up, down,
+                              n_experts, out, sync, ws_words, eps, route_eps, false, nullptr, proj,
+                              p_out);
 }

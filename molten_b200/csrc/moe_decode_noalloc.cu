@@ -108,5 +108,6 @@ extern "C" int mc_moe_decode_layer_noalloc(
   // the remaining checks, then the scratch set-up, then the one launch
   return mc_decode_layer_impl(ctx, h, b, norm_w, h_out, normed, router_w, router_dtype,
                               expert_bias, route_mode, logits, ids, weights, gate, up, down,
-                              n_experts, out, nullptr, 0, eps, route_eps, true, status);
+                              n_experts, out, nullptr, 0, eps, route_eps, true, status,
+                              nullptr, nullptr);
 }

@@ -80,7 +80,8 @@ class Context:
     def prefetch_next(self, *tensors) -> None:
         """Cross-layer prefetch hint (mc_set_l2_prefetch, no reference
         counterpart): the next moe_decode_layer on this context pulls up to two
-        tensors (the next layer's router and RMSNorm weights) into L2."""
+        tensors (e.g. the next layer's router and RMSNorm weights, or its
+        router and projection codes) into L2."""
         ts = [t for t in tensors if t is not None][:2] + [None, None]
         args = []
         for t in ts[:2]:
@@ -388,6 +389,42 @@ def moe_decode_layer_noalloc(ctx: Context, h, b, nw, hout, normed, router, logit
               n_experts, _p(out), _p(status), eps, route_eps)
     if check:
         raise_on_status(status, "moe_decode_layer_noalloc")
+
+
+def moe_decode_proj_workspace_words(moe_inter: int = FIXED_MOE_INTER) -> int:
+    """u32 words of workspace moe_decode_layer_proj needs (zero it once)."""
+    return int(_lib.lib().mc_moe_decode_proj_workspace_words(moe_inter))
+
+
+def moe_decode_layer_proj(ctx: Context, h, proj: QuantWeights, nw, hout, normed, router, logits,
+                          bias, ids, weights, gate: QuantWeights, up: QuantWeights,
+                          down: QuantWeights, out, workspace, p_out=None, eps: float = 1e-5,
+                          route_mode: int = ROUTE_SOFTMAX_RENORM, route_eps: float = 1e-6,
+                          n_experts: int = 64, check: bool = False) -> None:
+    """gemv_quant(proj, h) -> b (kernels/lfm.rs:112-149) and moe_decode_layer(h,
+    b, ...) in one launch, bit-identical to the two calls. ``workspace``:
+    int32 [moe_decode_proj_workspace_words(I)], zeroed once, owned by one
+    chain of calls; ``p_out`` (optional bf16 [2048]) receives b."""
+    for w in (proj, gate, up, down):
+        check_quant(w)
+    ensure(proj.bits == 4 and proj.in_features == FIXED_HIDDEN and
+           proj.out_features == FIXED_HIDDEN, "proj must be Q4 2048 x 2048")
+    e, k = router.shape
+    ensure(e == n_experts and k == FIXED_HIDDEN, "router shape")
+    ensure(h.numel() == k and out.numel() == k, "moe_decode_layer_proj is batch 1")
+    ensure(p_out is None or p_out.numel() == k, "p_out shape")
+    _bf16(h, nw, hout, normed, weights, out)
+    if p_out is not None:
+        _bf16(p_out)
+    _u32(ids, workspace)
+    dt = _lib.DTYPE_BF16 if router.dtype == torch.bfloat16 else _lib.DTYPE_F32
+    _lib.call("mc_moe_decode_layer_proj", ctx.handle, _p(h), _lib.C.byref(proj.qw()),
+              _p(p_out), _p(nw), _p(hout), _p(normed), _p(router), dt, _p(bias), route_mode,
+              _p(logits), _p(ids), _p(weights), _lib.C.byref(gate.qw()), _lib.C.byref(up.qw()),
+              _lib.C.byref(down.qw()), n_experts, _p(out), _p(workspace), workspace.numel(), eps,
+              route_eps)
+    if check:
+        raise_on_status(workspace[2:3], "moe_decode_layer_proj")
 
 
 def decode_workspace_act(workspace: torch.Tensor, moe_inter: int = FIXED_MOE_INTER):

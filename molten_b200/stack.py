@@ -15,8 +15,10 @@ The MoE layer normalises its input (RMSNorm of h + b) before the router and
 the experts, so activations stay bounded over the stack without a separate
 residual stream. The expert part runs one of three ways (``moe_path``):
 
-  "fused"    B = 1: the one-launch fused layer (moe_decode_layer), the
-             default at batch 1;
+  "fused"    B = 1: the one-launch fused layer, the default at batch 1;
+             with ``fuse_proj`` (the default) the layer's projection runs
+             inside the same launch (moe_decode_layer_proj: one launch per
+             layer, bit-identical to gemv_quant + moe_decode_layer);
   "grouped"  B > 1: router_addnorm_route for the B rows, then the prefill
              MoE FFN (moe_prefill: route, sort, gather, tensor-core grouped
              GEMMs, combine), so each routed expert's rows are read and
@@ -47,7 +49,8 @@ from molten_b200 import lfm
 
 class DecodeStack:
     def __init__(self, ctx: lfm.Context, layers: list[dict], head, embed: torch.Tensor,
-                 batch: int, n_experts: int = 64, moe_path: str | None = None, sampling=None):
+                 batch: int, n_experts: int = 64, moe_path: str | None = None, sampling=None,
+                 fuse_proj: bool = True):
         self.ctx, self.layers, self.head, self.embed = ctx, layers, head, embed
         self.sampling = sampling
         lfm.ensure(sampling is None or batch == 1, "sampling decodes one sequence")
@@ -57,6 +60,7 @@ class DecodeStack:
         self.path = moe_path or ("fused" if batch == 1 else "gemv" if batch <= 16 else "grouped")
         lfm.ensure(self.path in ("fused", "grouped", "gemv"), f"moe_path {self.path!r}")
         lfm.ensure(self.path != "fused" or batch == 1, "the fused layer is batch 1")
+        self.fuse_proj = fuse_proj and self.path == "fused"
         H = embed.shape[1]
         I = layers[0]["gate"].out_features // n_experts
         dev = embed.device
@@ -76,7 +80,9 @@ class DecodeStack:
         self.tail_normed = bf(batch, H)
         self.ws = None
         if self.path == "fused":
-            self.ws = torch.zeros(lfm.moe_decode_workspace_words(I), dtype=torch.int32, device=dev)
+            words = (lfm.moe_decode_proj_workspace_words(I) if self.fuse_proj
+                     else lfm.moe_decode_workspace_words(I))
+            self.ws = torch.zeros(words, dtype=torch.int32, device=dev)
         self.pws = None
         if self.path == "grouped":
             nb = lfm.moe_prefill_workspace_size(batch, n_experts, H, I)
@@ -100,8 +106,20 @@ class DecodeStack:
     def step(self) -> None:
         ctx, cur = self.ctx, self.x
         for l, L in enumerate(self.layers):
-            lfm.gemv_quant(ctx, L["proj"], cur, self.p)
             nxt = self.outs[l % 2]
+            if self.fuse_proj:
+                # the next layer's router rows and projection codes into L2
+                # while this layer exchanges its act rows (its norm weights
+                # are read before the launch's dependency wait anyway)
+                following = self.layers[(l + 1) % len(self.layers)]
+                ctx.prefetch_next(following["router"], following["proj"].codes)
+                lfm.moe_decode_layer_proj(ctx, cur, L["proj"], L["norm_w"], self.hout, self.normed,
+                                          L["router"], self.logits, None, self.ids[l],
+                                          self.wts[l], L["gate"], L["up"], L["down"], nxt,
+                                          self.ws, n_experts=self.E)
+                cur = nxt
+                continue
+            lfm.gemv_quant(ctx, L["proj"], cur, self.p)
             if self.path == "fused":
                 following = self.layers[(l + 1) % len(self.layers)]
                 ctx.prefetch_next(following["router"], following["norm_w"])
@@ -156,7 +174,8 @@ class DecodeStack:
         return self.tokens.cpu()
 
     def launches_per_step(self) -> int:
-        per_layer = {"fused": 2, "gemv": 4, "grouped": 2 + lfm.MOE_PREFILL_LAUNCHES}[self.path]
+        per_layer = {"fused": 1 if self.fuse_proj else 2, "gemv": 4,
+                     "grouped": 2 + lfm.MOE_PREFILL_LAUNCHES}[self.path]
         tail = 2
         if self.sampling is not None:
             s = self.sampling

@@ -315,6 +315,44 @@ def test_fused_moe_decode_layer(cuda_ctx, moe_layer, mode, seed):
         assert_bits_equal(host_bits(out), out_o, "out")
 
 
+@pytest.mark.parametrize("mode,seed", [(0, 0), (1, 1)])
+def test_fused_proj_moe_decode_layer(cuda_ctx, moe_layer, mode, seed):
+    """mc_moe_decode_layer_proj: b = bf16(proj . h), computed inside the
+    launch and exchanged between the CTAs, equals the oracle's Q4 GEMV bit for
+    bit, and every layer output equals the oracle's (so gemv_quant followed by
+    moe_decode_layer) on consecutive calls sharing one workspace."""
+    g = synth.rng(2100 + seed)
+    D = moe_layer["dev"]
+    pc, ps, pb = synth.quant_weights_np(g, 2048, 2048)
+    proj = dev_qw(pc, ps, pb)
+    ebias = g.normal(0, 0.1, 64).astype(np.float32)
+    ws = zeros_u32(lfm.moe_decode_proj_workspace_words())
+    hout, normed = empty_bf16(1, 2048), empty_bf16(1, 2048)
+    logits = torch.empty((1, 64), dtype=torch.float32, device="cuda")
+    ids, wts = zeros_u32(1, 4), empty_bf16(1, 4)
+    out, p_out = empty_bf16(1, 2048), empty_bf16(1, 2048)
+    for it in range(3):
+        h = synth.activations_np(g, 1, 2048)
+        lfm.moe_decode_layer_proj(cuda_ctx, dev_bf16(h), proj, D["norm_w"], hout, normed,
+                                  D["router"], logits, dev_f32(ebias), ids, wts, D["gate"],
+                                  D["up"], D["down"], out, ws, p_out=p_out, route_mode=mode)
+        torch.cuda.synchronize()
+        ctl = host_u32(ws[:4])
+        assert ctl[0] == it + 1 and ctl[1] == 0 and ctl[2] == 0 and ctl[3] == 0, ctl
+        p_o = oracle.gemv_quant(pc, ps, pb, 4, h)
+        assert_bits_equal(host_bits(p_out), p_o, "projection b")
+        ho, no, lo, io, wo = oracle.router_addnorm_route(h, p_o, moe_layer["norm_w"],
+                                                         moe_layer["router"], 0, ebias, mode)
+        assert np.array_equal(host_u32(ids), io), "top-4 ids"
+        assert_bits_equal(host_bits(wts), wo, "weights")
+        assert_bits_equal(host_bits(hout), ho, "h_out")
+        assert_bits_equal(host_bits(normed), no, "normed")
+        assert np.array_equal(logits.cpu().numpy().view(np.uint32), lo.view(np.uint32))
+        act_o = oracle.gemv_gather_act(moe_layer["gate"], moe_layer["up"], no, io)
+        out_o = oracle.gemv_gather_down_combine4(moe_layer["down"], act_o, io, wo)
+        assert_bits_equal(host_bits(out), out_o, "out")
+
+
 def test_copy_async_host_device(cuda_ctx):
     """mc_copy_async: pinned host -> device and back through the copy kernel
     (16-byte multiples), an odd byte count through the cudaMemcpyAsync path,
