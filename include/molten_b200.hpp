@@ -280,6 +280,41 @@ inline void moe_decode_layer(Context& ctx, const Tensor& h, const Tensor* b, con
       (size_t)workspace.numel(), eps, 1e-6f));
 }
 
+// gemv_quant(proj, h) -> b (kernels/lfm.rs:112-149) and moe_decode_layer(h, b,
+// ...) in one launch, bit-identical to the two calls; proj Q4 2048 x 2048;
+// workspace: U32 [mc_moe_decode_proj_workspace_words(I)], zeroed once;
+// p_out (optional) receives b.
+inline void moe_decode_layer_proj(Context& ctx, const Tensor& h, const QuantWeights& proj,
+                                  const Tensor* p_out, const Tensor& nw, const Tensor& hout,
+                                  const Tensor& normed, const Tensor& router,
+                                  const Tensor& logits, const Tensor* bias, const Tensor& ids,
+                                  const Tensor& weights, const QuantWeights& gate,
+                                  const QuantWeights& up, const QuantWeights& down,
+                                  const Tensor& out, const Tensor& workspace, int n_experts = 64,
+                                  float eps = 1e-5f, int route_mode = MC_ROUTE_SOFTMAX_RENORM) {
+  check_quant(proj);
+  check_quant(gate);
+  check_quant(up);
+  check_quant(down);
+  ensure(proj.bits == 4 && proj.in_features() == 2048 && proj.out_features() == 2048,
+         "projection must be Q4 2048 x 2048");
+  ensure(router.dtype == DType::F32 || router.dtype == DType::BF16, "router weight dtype");
+  ensure(workspace.dtype == DType::U32 &&
+             (size_t)workspace.numel() >=
+                 mc_moe_decode_proj_workspace_words(gate.out_features() / n_experts),
+         "decode workspace too small");
+  ensure(out.numel() == h.numel() && hout.numel() == h.numel(), "decode row shapes");
+  ensure(!p_out || p_out->numel() == h.numel(), "projection output shape");
+  const mc_qweights pj = proj.abi(), g = gate.abi(), u = up.abi(), d = down.abi();
+  check(mc_moe_decode_layer_proj(
+      ctx.handle(), h.as<const uint16_t>(), &pj, p_out ? p_out->as<uint16_t>() : nullptr,
+      nw.as<const uint16_t>(), hout.as<uint16_t>(), normed.as<uint16_t>(), router.data,
+      router.dtype == DType::F32 ? MC_DTYPE_F32 : MC_DTYPE_BF16,
+      bias ? bias->as<const float>() : nullptr, route_mode, logits.as<float>(), ids.as<uint32_t>(),
+      weights.as<uint16_t>(), &g, &u, &d, n_experts, out.as<uint16_t>(), workspace.as<uint32_t>(),
+      (size_t)workspace.numel(), eps, 1e-6f));
+}
+
 // gemm_q4_grouped_mlx (quant.rs:223-266): c rows of each row tile of `tiles`
 // (uint4 {m0, m_end, expert, 0}, n_tiles entries) against that expert.
 inline void gemm_q4_grouped_mlx(Context& ctx, const Tensor& a, const QuantWeights& w,
