@@ -10,8 +10,9 @@
 // The scratch is the same layout mc_moe_decode_layer documents for its
 // caller-owned workspace: word 0 epoch, word 1 exit counter, word 2 status
 // (moved to the caller's `status` and cleared by the launch's last CTA, so it
-// reports that call only), word 3 reserved, word 4 router counter, words
-// 8..135 tagged router logits, then the bf16 act rows. It serves expert
+// reports that call only), words 3 and 4 reserved (zero; word 4 counts
+// projection rows only in mc_moe_decode_layer_proj, which this entry point
+// does not run), words 8..135 tagged router logits, then the bf16 act rows. It serves expert
 // widths up to kNoallocMaxInter; wider layers are rejected with MC_EINVAL
 // before anything is launched.
 //
