@@ -25,16 +25,22 @@
 // Persistent kernel, one CTA per SM. Work items = (row chunk, 128-feature
 // block), chunk-major, dealt to CTAs in snake order; with the tile list from
 // mc_moe_sort_map (full chunks first, then partial ones by decreasing
-// height) every CTA gets a similar share. Warp roles (320 threads):
+// height) every CTA gets a similar share. Warp roles (352 threads):
 //   warp 0      TMA of the token rows (128-byte swizzle) into the token ring
 //   warp 1      TMEM allocation (512 columns); lane 0 issues tcgen05.mma
 //               (M=128, N=chunk, K=16, bf16 x bf16 -> fp32) and commits
 //   warps 2..9  dequantise the weight tiles straight into the UMMA K-major
 //               128-byte-swizzled layout (w = bf16(s*q + b) in bf16x2
-//               arithmetic, MLX's dequantize): gate/up: warps 2-5 the gate tile, 6-9 the up
-//               tile; down: warps 2-5 the first 32 K of every row, 6-9 the
-//               second. Then the epilogue from TMEM, half the columns each.
-// Two rings: token rows (bfull: TMA tx, bempty: tcgen05.commit) and weight
+//               arithmetic, MLX's dequantize): gate/up: warps 2-5 the gate
+//               tile, 6-9 the up tile; down: warps 2-5 the first 32 K of
+//               every row, 6-9 the second. Then the epilogue from TMEM, half
+//               the columns each, staged per warp in shared memory and
+//               stored as 16-byte rows (or, for the expert-parallel step,
+//               into each row's home buffer on its source rank)
+//   warp 10     TMA of the Q4 code tiles (64-byte swizzle, two K steps per
+//               stage) into the code ring, ahead of the dequant warps
+// Three rings: token rows (bfull: TMA tx, bempty: tcgen05.commit), code
+// tiles (cfull: TMA tx, cempty: one arrival per dequant warp) and weight
 // tiles (afull: one arrival per dequant warp, aempty: tcgen05.commit). The
 // TMA and MMA roles run on whole warps with one elected lane issuing, and
 // every wait a warp takes gives all its lanes one answer.
