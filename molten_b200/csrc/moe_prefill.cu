@@ -38,16 +38,19 @@ sort_scatter_kernel(const uint32_t* __restrict__ ids, int m, int E, int bm,
                     uint4* __restrict__ tiles, uint32_t* __restrict__ n_tiles, int max_tiles) {
   __shared__ uint32_t warp_tot[8];
   __shared__ uint32_t base_s[3];
+  __shared__ uint32_t cnt_s[1024];  // the E counts, staged once
   const uint32_t e = blockIdx.x;
   const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
+  for (int j = t; j < E; j += 256) cnt_s[j] = counts[j];
+  __syncthreads();
   if (t == 0) {
     // Tile list order: every full bm-row tile first (expert order), then the
     // partial tiles by decreasing height (ties: lower expert first), so a
     // consumer that deals tiles out in list order balances its workers.
-    const uint32_t ce = counts[e], pe = ce % (uint32_t)bm;
+    const uint32_t ce = cnt_s[e], pe = ce % (uint32_t)bm;
     uint32_t off = 0, full_before = 0, full_all = 0, part_rank = 0, parts = 0;
     for (int j = 0; j < E; ++j) {
-      const uint32_t c = counts[j], pj = c % (uint32_t)bm;
+      const uint32_t c = cnt_s[j], pj = c % (uint32_t)bm;
       if ((uint32_t)j < e) {
         off += c;
         full_before += c / bm;
@@ -64,13 +67,28 @@ sort_scatter_kernel(const uint32_t* __restrict__ ids, int m, int E, int bm,
     offsets[e] = off;
     if (e == 0) *n_tiles = full_all + parts;
   }
-  // contiguous token range per thread
+  // contiguous token range per thread; a token's 4 ids are one 16-byte row,
+  // read 8 rows at a time so their loads are in flight together (one scalar
+  // load after another left the kernel latency-bound)
   const int per = (m + 255) / 256;
   const int t0 = min(m, t * per), t1 = min(m, t0 + per);
+  const bool vec = (reinterpret_cast<uintptr_t>(ids) & 15) == 0;
+  const uint4* ids4 = reinterpret_cast<const uint4*>(ids);
+  auto row_ids = [&](int tok) -> uint4 {
+    if (vec) return __ldg(ids4 + tok);
+    return make_uint4(__ldg(ids + 4 * (size_t)tok), __ldg(ids + 4 * (size_t)tok + 1),
+                      __ldg(ids + 4 * (size_t)tok + 2), __ldg(ids + 4 * (size_t)tok + 3));
+  };
   uint32_t c = 0;
-  for (int tok = t0; tok < t1; ++tok)
+  for (int b0 = t0; b0 < t1; b0 += 8) {
+    uint4 v[8];
 #pragma unroll
-    for (int r = 0; r < 4; ++r) c += (__ldg(ids + 4 * (size_t)tok + r) == e);
+    for (int j = 0; j < 8; ++j)
+      if (b0 + j < t1) v[j] = row_ids(b0 + j);
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      if (b0 + j < t1) c += (v[j].x == e) + (v[j].y == e) + (v[j].z == e) + (v[j].w == e);
+  }
   // block exclusive scan of c
   uint32_t incl = c;
 #pragma unroll
@@ -83,16 +101,27 @@ sort_scatter_kernel(const uint32_t* __restrict__ ids, int m, int E, int bm,
   uint32_t wbase = 0;
   for (int w = 0; w < warp; ++w) wbase += warp_tot[w];
   uint32_t pos = base_s[0] + wbase + incl - c;
-  for (int tok = t0; tok < t1; ++tok)
+  for (int b0 = t0; b0 < t1; b0 += 8) {
+    uint4 v[8];
 #pragma unroll
-    for (int r = 0; r < 4; ++r)
-      if (__ldg(ids + 4 * (size_t)tok + r) == e) {
-        ids_sorted[pos] = (uint32_t)tok;
-        slotpos[4 * (size_t)tok + r] = pos;
-        ++pos;
-      }
+    for (int j = 0; j < 8; ++j)
+      if (b0 + j < t1) v[j] = row_ids(b0 + j);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      if (b0 + j >= t1) break;
+      const int tok = b0 + j;
+      const uint32_t r4[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
+#pragma unroll
+      for (int r = 0; r < 4; ++r)
+        if (r4[r] == e) {
+          ids_sorted[pos] = (uint32_t)tok;
+          slotpos[4 * (size_t)tok + r] = pos;
+          ++pos;
+        }
+    }
+  }
   // row tiles of this expert
-  const uint32_t n = counts[e];
+  const uint32_t n = cnt_s[e];
   const uint32_t nt = (n + bm - 1) / bm, nfull = n / bm;
   for (uint32_t j = t; j < nt; j += 256) {
     const uint32_t slot = j < nfull ? base_s[1] + j : base_s[2];
@@ -148,6 +177,27 @@ combine_kernel(const uint16_t* __restrict__ ed, const uint32_t* __restrict__ slo
   float s[8];
 #pragma unroll
   for (int j = 0; j < 8; ++j) s[j] = 0.0f;
+  if (topk == 4 && (reinterpret_cast<uintptr_t>(slotpos) & 15) == 0 &&
+      (reinterpret_cast<uintptr_t>(gw) & 7) == 0) {
+    // the token's four slots and weights in one load each, the four expert
+    // rows' loads in flight together, summed in rank order as below
+    const uint4 pp = __ldg(reinterpret_cast<const uint4*>(slotpos) + t);
+    const uint2 ww = __ldg(reinterpret_cast<const uint2*>(gw) + t);
+    const uint32_t pr[4] = {pp.x, pp.y, pp.z, pp.w};
+    const uint32_t wr[4] = {ww.x & 0xffffu, ww.x >> 16, ww.y & 0xffffu, ww.y >> 16};
+    uint4 v[4];
+#pragma unroll
+    for (int r = 0; r < 4; ++r) v[r] = __ldg(reinterpret_cast<const uint4*>(ed + (size_t)pr[r] * h8 * 8) + c);
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      const float w = mc_bf16_to_f32((uint16_t)wr[r]);
+      const uint32_t vw[4] = {v[r].x, v[r].y, v[r].z, v[r].w};
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        s[j] = __fadd_rn(s[j], mc_round_bf16(__fmul_rn(
+                                   w, mc_bf16_to_f32((uint16_t)(vw[j >> 1] >> (16 * (j & 1)))))));
+    }
+  } else
   for (int r = 0; r < topk; ++r) {
     const uint32_t p = __ldg(slotpos + t * topk + r);
     const float w = mc_bf16_to_f32(__ldg(gw + t * topk + r));
