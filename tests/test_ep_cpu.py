@@ -128,8 +128,11 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def test_two_rank_gloo_matches_one_device_oracle():
-    world, E, m, I = 2, 8, 48, 256
+@pytest.mark.parametrize("world", [2, 4])
+def test_multi_rank_gloo_matches_one_device_oracle(world):
+    """The host-side expert-parallel step on `world` gloo ranks (CPU, oracle
+    arithmetic per rank) equals the one-device oracle."""
+    E, m, I = 8, 48, 256
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
