@@ -490,7 +490,7 @@ extern "C" {
     pub fn mc_ep_counts(ctx: *mut McCtx, out: *mut u32, n: usize) -> c_int;
     pub fn mc_ep_finalize(ctx: *mut McCtx) -> c_int;
     pub fn mc_ep_set_profile(ctx: *mut McCtx, on: c_int) -> c_int;
-    pub fn mc_ep_phase_ms(ctx: *mut McCtx, out6: *mut f32) -> c_int;
+    pub fn mc_ep_phase_ms(ctx: *mut McCtx, out7: *mut f32) -> c_int;
     pub fn mc_set_l2_prefetch(
         ctx: *mut McCtx,
         p0: *const c_void,

@@ -472,12 +472,12 @@ int mc_ep_status(mc_ctx* ctx, uint32_t* out);
 int mc_ep_counts(mc_ctx* ctx, uint32_t* out, size_t n);
 int mc_ep_finalize(mc_ctx* ctx);
 /* Profiling aid: with `on`, each step records events at its phase
- * boundaries; mc_ep_phase_ms waits and writes the last step's six phase
+ * boundaries; mc_ep_phase_ms waits and writes the last step's seven phase
  * times in ms (route + relabel + sort, counts exchange + barrier, row chunks
- * + return map + dispatch + barrier, grouped GEMMs + return, the barrier
- * after it, combine). */
+ * + return map + dispatch, the barrier after the dispatch, grouped GEMMs +
+ * return, the barrier after them, combine). */
 int mc_ep_set_profile(mc_ctx* ctx, int on);
-int mc_ep_phase_ms(mc_ctx* ctx, float* out6);
+int mc_ep_phase_ms(mc_ctx* ctx, float* out7);
 
 /* Cross-layer prefetch hint (no reference counterpart): the next
  * mc_moe_decode_layer (or _noalloc) launched on ctx prefetches the byte

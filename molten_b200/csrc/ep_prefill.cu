@@ -57,7 +57,7 @@ constexpr unsigned long long kBarrierNs = 1000000000ull;  // default barrier lim
 // counts exchange (peer stores + barrier), row chunks + return map +
 // dispatch + barrier, the two grouped GEMMs and the return, the barrier
 // after the return, combine.
-constexpr int kPhases = 6;
+constexpr int kPhases = 7;
 constexpr size_t kCountsOff = 256;  // count table after the flag words in the control area
 
 // ------------------------------------------------------------ NCCL at run time
@@ -486,8 +486,9 @@ extern "C" int mc_ep_moe_prefill(mc_ctx* ctx, const uint16_t* x, const float* lo
   if ((rc = mc_ep_dispatch(ctx, x, m, ep->H, ep->ids_sorted, ep->counts_all, ep->rank, W,
                            ep->E_slots, ep->recv_ptr, ep->recv_cap, ep->status)))
     return rc;
-  if ((rc = ep_barrier(ctx))) return rc;
   if ((rc = mark(3))) return rc;
+  if ((rc = ep_barrier(ctx))) return rc;
+  if ((rc = mark(4))) return rc;
   uint16_t* recv = static_cast<uint16_t*>(ep->recv_ptr[ep->rank]);
   const int rows = (int)ep->recv_cap;
   if ((rc = mc_gemm_q4_grouped_gu(ctx, recv, rows, gate, up, ep->spr, ep->act, ep->tiles,
@@ -498,13 +499,13 @@ extern "C" int mc_ep_moe_prefill(mc_ctx* ctx, const uint16_t* x, const float* lo
                                        ep->home_ptr, W, ep->home_cap, ep->tiles, ep->n_tiles,
                                        ep->max_tiles, ep->status)))
     return rc;
-  if ((rc = mark(4))) return rc;
-  if ((rc = ep_barrier(ctx))) return rc;
   if ((rc = mark(5))) return rc;
+  if ((rc = ep_barrier(ctx))) return rc;
+  if ((rc = mark(6))) return rc;
   if ((rc = mc_moe_combine_rows(ctx, static_cast<uint16_t*>(ep->home_ptr[ep->rank]), ep->slotpos,
                                 ep->gw, out, m, 4, ep->H)))
     return rc;
-  return mark(6);
+  return mark(7);
 }
 
 extern "C" int mc_ep_set_profile(mc_ctx* ctx, int on) {

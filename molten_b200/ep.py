@@ -525,13 +525,13 @@ class EpPrefill:
     def set_profile(self, on: bool) -> None:
         self.lib.call("mc_ep_set_profile", self.ctx.handle, 1 if on else 0)
 
-    PHASES = ("route_sort", "counts_exchange", "dispatch_barrier", "gemms_return",
+    PHASES = ("route_sort", "counts_exchange", "dispatch", "dispatch_barrier", "gemms_return",
               "return_barrier", "combine")
 
     def phase_ms(self) -> dict:
         """The last profiled step's phase times (ms)."""
         import ctypes as C
-        a = (C.c_float * 6)()
+        a = (C.c_float * len(self.PHASES))()
         self.lib.call("mc_ep_phase_ms", self.ctx.handle, a)
         return {k: float(v) for k, v in zip(self.PHASES, a)}
 
