@@ -49,6 +49,90 @@ __device__ __forceinline__ void segment_bases(const uint32_t* counts_all, int W,
   *src_row = off;
 }
 
+// Row chunks of this rank's receive buffer for the grouped GEMMs, from the
+// count table ca (shared memory, W x E): full bm-row chunks first (local
+// expert order), then the partial ones by decreasing height (ties: lower
+// expert). Run by a whole CTA (it synchronises); total_s: P words of shared
+// scratch.
+__device__ void tiles_body(const uint32_t* ca, int rank, int W, int E, int bm, uint4* tiles,
+                           uint32_t* n_tiles, uint32_t* rows, int max_tiles, uint32_t* total_s) {
+  const int P = E / W;
+  for (int j = threadIdx.x; j < P; j += blockDim.x) {
+    uint32_t t = 0;
+    for (int s = 0; s < W; ++s) t += ca[s * E + rank * P + j];
+    total_s[j] = t;
+  }
+  __syncthreads();
+  uint32_t full_all = 0, parts = 0, all_rows = 0;
+  for (int jj = 0; jj < P; ++jj) {
+    full_all += total_s[jj] / bm;
+    parts += (total_s[jj] % bm) != 0;
+    all_rows += total_s[jj];
+  }
+  if (threadIdx.x == 0) {
+    *n_tiles = full_all + parts;
+    if (rows) *rows = all_rows;
+  }
+  for (int j = threadIdx.x; j < P; j += blockDim.x) {
+    const uint32_t tj = total_s[j], pj = tj % bm;
+    uint32_t base = 0, full_before = 0, rank_p = 0;
+    for (int jj = 0; jj < P; ++jj) {
+      const uint32_t t = total_s[jj], p = t % bm;
+      if (jj < j) {
+        base += t;
+        full_before += t / bm;
+      }
+      if (p && (p > pj || (p == pj && jj < j))) ++rank_p;
+    }
+    const uint32_t nfull = tj / bm;
+    for (uint32_t c = 0; c < nfull; ++c) {
+      const uint32_t slot = full_before + c;
+      if (slot < (uint32_t)max_tiles)
+        tiles[slot] = make_uint4(base + c * bm, base + (c + 1) * bm, (uint32_t)j, 0u);
+    }
+    if (pj) {
+      const uint32_t slot = full_all + rank_p;
+      if (slot < (uint32_t)max_tiles)
+        tiles[slot] = make_uint4(base + nfull * bm, base + tj, (uint32_t)j, 0u);
+    }
+  }
+}
+
+// The return map of this rank's local slots from the count table ca: the
+// rows of local slot j from source s are seg_row[j][s] .. seg_row[j][s+1] of
+// the receive buffer and go to rows from seg_home[j][s] of s's home buffer
+// (s's own sorted order).
+__device__ void segments_body(const uint32_t* ca, int rank, int W, int E, uint32_t* seg_row,
+                              uint32_t* seg_home) {
+  const int spr = E / W;
+  for (int t = threadIdx.x; t < spr * (W + 1); t += blockDim.x) {
+    const int j = t / (W + 1), s = t % (W + 1), slot = rank * spr + j;
+    uint32_t row = 0;
+    for (int jj = rank * spr; jj < slot; ++jj)
+      for (int q = 0; q < W; ++q) row += ca[q * E + jj];
+    for (int q = 0; q < s; ++q) row += ca[q * E + slot];
+    seg_row[j * (W + 1) + s] = row;
+    if (s < W) {
+      uint32_t h = 0;
+      for (int e = 0; e < slot; ++e) h += ca[s * E + e];
+      seg_home[j * W + s] = h;
+    }
+  }
+}
+
+// What the expert-parallel step also wants from the dispatch launch (all null
+// for mc_ep_dispatch): the receive side's row chunks and the return map,
+// built by the last CTA from the count table it has staged anyway, so they
+// cost no launch of their own.
+struct Plan {
+  uint4* tiles;
+  uint32_t* n_tiles;
+  uint32_t* rows;
+  uint32_t* seg_row;
+  uint32_t* seg_home;
+  int bm, max_tiles;
+};
+
 // This rank's expert-sorted rows -> the owners' receive buffers. Every warp
 // takes rows across all experts (grid-stride over the sorted order), so a hot
 // expert's rows are spread over the whole grid; each CTA first lays out the
@@ -58,11 +142,18 @@ __device__ __forceinline__ void segment_bases(const uint32_t* counts_all, int W,
 __global__ void __launch_bounds__(256)
 ep_dispatch_kernel(const uint4* __restrict__ x, int m, int h16,
                    const uint32_t* __restrict__ ids_sorted, const uint32_t* __restrict__ counts_all,
-                   int rank, int W, int E, PeerPtrs recv, uint32_t cap, uint32_t* status) {
+                   int rank, int W, int E, PeerPtrs recv, uint32_t cap, uint32_t* status,
+                   const Plan plan) {
   __shared__ uint32_t src0[kMaxExperts + 1], dst0[kMaxExperts];
   __shared__ uint32_t ca[kMaxRanks * kMaxExperts];  // the count table, staged once
   for (int i = threadIdx.x; i < W * E; i += blockDim.x) ca[i] = counts_all[i];
   __syncthreads();
+  if (plan.tiles && blockIdx.x == gridDim.x - 1) {  // uniform over the CTA
+    tiles_body(ca, rank, W, E, plan.bm, plan.tiles, plan.n_tiles, plan.rows, plan.max_tiles,
+               dst0);
+    segments_body(ca, rank, W, E, plan.seg_row, plan.seg_home);
+    __syncthreads();  // dst0 is reused below
+  }
   for (int e = threadIdx.x; e < E; e += blockDim.x) {
     uint32_t d, s;
     segment_bases(ca, W, E, e, rank, &d, &s);
@@ -126,57 +217,17 @@ ep_return_kernel(const uint4* __restrict__ ed, uint32_t ed_rows, int h16,
   __threadfence_system();
 }
 
-// Row chunks of this rank's receive buffer for the grouped GEMMs: full
-// bm-row chunks first (local expert order), then the partial ones by
-// decreasing height (ties: lower expert). One CTA; thread j = local expert j.
+// Row chunks of this rank's receive buffer for the grouped GEMMs (see
+// tiles_body). One CTA.
 __global__ void __launch_bounds__(256)
 ep_tiles_kernel(const uint32_t* __restrict__ counts_all, int rank, int W, int E, int bm,
                 uint4* __restrict__ tiles, uint32_t* __restrict__ n_tiles, uint32_t* __restrict__ rows,
                 int max_tiles) {
-  const int P = E / W;
   __shared__ uint32_t total_s[kMaxExperts];
   __shared__ uint32_t ca[kMaxRanks * kMaxExperts];  // the count table, staged once
   for (int i = threadIdx.x; i < W * E; i += blockDim.x) ca[i] = counts_all[i];
   __syncthreads();
-  for (int j = threadIdx.x; j < P; j += blockDim.x) {
-    uint32_t t = 0;
-    for (int s = 0; s < W; ++s) t += ca[s * E + rank * P + j];
-    total_s[j] = t;
-  }
-  __syncthreads();
-  uint32_t full_all = 0, parts = 0, all_rows = 0;
-  for (int jj = 0; jj < P; ++jj) {
-    full_all += total_s[jj] / bm;
-    parts += (total_s[jj] % bm) != 0;
-    all_rows += total_s[jj];
-  }
-  if (threadIdx.x == 0) {
-    *n_tiles = full_all + parts;
-    if (rows) *rows = all_rows;
-  }
-  for (int j = threadIdx.x; j < P; j += blockDim.x) {
-    const uint32_t tj = total_s[j], pj = tj % bm;
-    uint32_t base = 0, full_before = 0, rank_p = 0;
-    for (int jj = 0; jj < P; ++jj) {
-      const uint32_t t = total_s[jj], p = t % bm;
-      if (jj < j) {
-        base += t;
-        full_before += t / bm;
-      }
-      if (p && (p > pj || (p == pj && jj < j))) ++rank_p;
-    }
-    const uint32_t nfull = tj / bm;
-    for (uint32_t c = 0; c < nfull; ++c) {
-      const uint32_t slot = full_before + c;
-      if (slot < (uint32_t)max_tiles)
-        tiles[slot] = make_uint4(base + c * bm, base + (c + 1) * bm, (uint32_t)j, 0u);
-    }
-    if (pj) {
-      const uint32_t slot = full_all + rank_p;
-      if (slot < (uint32_t)max_tiles)
-        tiles[slot] = make_uint4(base + nfull * bm, base + tj, (uint32_t)j, 0u);
-    }
-  }
+  tiles_body(ca, rank, W, E, bm, tiles, n_tiles, rows, max_tiles, total_s);
 }
 
 int check_ranks(int rank, int W, int E, const char* what) {
@@ -248,7 +299,31 @@ extern "C" int mc_ep_dispatch(mc_ctx* ctx, const uint16_t* x, int m, int hidden,
   const int grid = std::max(1, std::min((4 * m + 7) / 8, ctx->num_sms * 2));
   ep_dispatch_kernel<<<grid, 256, 0, ctx->stream>>>(
       reinterpret_cast<const uint4*>(x), m, hidden / 8, ids_sorted, counts_all, rank, world,
-      n_experts, pp, (uint32_t)recv_cap_rows, status);
+      n_experts, pp, (uint32_t)recv_cap_rows, status, Plan{});
+  return mc_after_launch("ep_dispatch_kernel");
+}
+
+int mc_ep_dispatch_plan(mc_ctx* ctx, const uint16_t* x, int m, int hidden,
+                        const uint32_t* ids_sorted, const uint32_t* counts_all, int rank,
+                        int world, int n_experts, void* const* recv_bufs, size_t recv_cap_rows,
+                        uint32_t* status, int bm, uint32_t* tiles, uint32_t* n_tiles,
+                        uint32_t* rows, int max_tiles, uint32_t* seg_row, uint32_t* seg_home) {
+  MC_REQUIRE(ctx && x && ids_sorted && counts_all && tiles && n_tiles && seg_row && seg_home,
+             "ep_dispatch_plan: null pointer");
+  int rc;
+  if ((rc = check_ranks(rank, world, n_experts, "ep_dispatch_plan"))) return rc;
+  MC_REQUIRE(hidden > 0 && hidden % 8 == 0 && mc_aligned(x, 16), "ep_dispatch_plan: rows");
+  MC_REQUIRE(bm >= 1 && bm <= 4096 && max_tiles >= 1 && mc_aligned(tiles, 16),
+             "ep_dispatch_plan: bm %d / max_tiles %d", bm, max_tiles);
+  PeerPtrs pp;
+  if ((rc = fill_peers(&pp, recv_bufs, world, "ep_dispatch_plan"))) return rc;
+  MC_REQUIRE(m >= 1 && recv_cap_rows >= 1 && recv_cap_rows <= 0xffffffffu,
+             "ep_dispatch_plan: m %d / capacity %zu", m, recv_cap_rows);
+  Plan plan{reinterpret_cast<uint4*>(tiles), n_tiles, rows, seg_row, seg_home, bm, max_tiles};
+  const int grid = std::max(1, std::min((4 * m + 7) / 8, ctx->num_sms * 2));
+  ep_dispatch_kernel<<<grid, 256, 0, ctx->stream>>>(
+      reinterpret_cast<const uint4*>(x), m, hidden / 8, ids_sorted, counts_all, rank, world,
+      n_experts, pp, (uint32_t)recv_cap_rows, status, plan);
   return mc_after_launch("ep_dispatch_kernel");
 }
 

@@ -5,9 +5,10 @@
 //
 //   route (top-4) -> relabel model experts to slots (this rank's table) ->
 //   sort by slot -> publish the per-slot pair counts into every rank's
-//   count table (peer stores) + barrier -> receive-side row chunks and the
-//   return map -> dispatch: rows stored straight into the owners' receive
-//   buffers over NVLink (CUDA IPC mappings) -> barrier -> grouped gate/up
+//   count table (peer stores) + barrier -> dispatch: rows stored straight
+//   into the owners' receive buffers over NVLink (CUDA IPC mappings), the
+//   launch's last CTA also building the receive-side row chunks and the
+//   return map -> barrier -> grouped gate/up
 //   (+SwiGLU) and down GEMMs, the down GEMM's epilogue storing each expert
 //   row straight into its source's home buffer -> barrier -> weighted
 //   combine at home.
@@ -129,7 +130,7 @@ struct mc_ep_state {
   uint32_t *ids, *counts, *offsets, *ids_sorted, *slotpos, *sort_tiles, *sort_ntiles;
   uint32_t *counts_all, *tiles, *n_tiles, *rows, *status, *epoch;
   uint16_t *gw, *act;
-  uint32_t *seg_row, *seg_home;  // return map (ep_segments_kernel)
+  uint32_t *seg_row, *seg_home;  // return map (built by the dispatch launch)
   int sort_max_tiles = 0, max_tiles = 0;
   // phase timing (mc_ep_set_profile): events at the step's phase boundaries
   int profile = 0;
@@ -224,31 +225,6 @@ ep_publish_counts_kernel(const uint32_t* __restrict__ counts, FlagPtrs tables, i
   if (threadIdx.x == 0) ep_barrier_thread(flags, epoch_word, rank, W, timeout_ns, status, test_skip);
 }
 
-// The return map: for each local slot j and source s, the first received
-// row of that source's rows (seg_row[j][s]; seg_row[j][W] = the end of slot
-// j's rows) and the first row of them in the source's home buffer
-// (seg_home[j][s], the source's own sorted order). One CTA.
-__global__ void __launch_bounds__(256)
-ep_segments_kernel(const uint32_t* __restrict__ counts_all_g, int rank, int W, int E_slots,
-                   uint32_t* __restrict__ seg_row, uint32_t* __restrict__ seg_home) {
-  __shared__ uint32_t counts_all[kMaxRanks * 256];  // the table, staged once
-  for (int i = threadIdx.x; i < W * E_slots; i += blockDim.x) counts_all[i] = counts_all_g[i];
-  __syncthreads();
-  const int spr = E_slots / W;
-  for (int t = threadIdx.x; t < spr * (W + 1); t += blockDim.x) {
-    const int j = t / (W + 1), s = t % (W + 1), slot = rank * spr + j;
-    uint32_t row = 0;
-    for (int jj = rank * spr; jj < slot; ++jj)
-      for (int q = 0; q < W; ++q) row += counts_all[q * E_slots + jj];
-    for (int q = 0; q < s; ++q) row += counts_all[q * E_slots + slot];
-    seg_row[j * (W + 1) + s] = row;
-    if (s < W) {
-      uint32_t h = 0;
-      for (int e = 0; e < slot; ++e) h += counts_all[s * E_slots + e];
-      seg_home[j * W + s] = h;
-    }
-  }
-}
 
 int ep_barrier(mc_ctx* ctx) {
   mc_ep_state* ep = ctx->ep;
@@ -477,14 +453,13 @@ extern "C" int mc_ep_moe_prefill(mc_ctx* ctx, const uint16_t* x, const float* lo
     if ((rc = mc_after_launch("ep_publish_counts_kernel"))) return rc;
   }
   if ((rc = mark(2))) return rc;
-  if ((rc = mc_ep_tiles(ctx, ep->counts_all, ep->rank, W, ep->E_slots, kChunk, ep->tiles,
-                        ep->n_tiles, ep->rows, ep->max_tiles)))
-    return rc;
-  ep_segments_kernel<<<1, 256, 0, ctx->stream>>>(ep->counts_all, ep->rank, W, ep->E_slots,
-                                                  ep->seg_row, ep->seg_home);
-  if ((rc = mc_after_launch("ep_segments_kernel"))) return rc;
-  if ((rc = mc_ep_dispatch(ctx, x, m, ep->H, ep->ids_sorted, ep->counts_all, ep->rank, W,
-                           ep->E_slots, ep->recv_ptr, ep->recv_cap, ep->status)))
+  // the dispatch; its last CTA also builds the receive side's row chunks and
+  // the return map (two single-CTA launches of their own cost ~20 us a step
+  // on the critical path)
+  if ((rc = mc_ep_dispatch_plan(ctx, x, m, ep->H, ep->ids_sorted, ep->counts_all, ep->rank, W,
+                                ep->E_slots, ep->recv_ptr, ep->recv_cap, ep->status, kChunk,
+                                ep->tiles, ep->n_tiles, ep->rows,
+                                ep->max_tiles, ep->seg_row, ep->seg_home)))
     return rc;
   if ((rc = mark(3))) return rc;
   if ((rc = ep_barrier(ctx))) return rc;

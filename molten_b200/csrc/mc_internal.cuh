@@ -44,6 +44,15 @@ int mc_decode_layer_impl(mc_ctx* ctx, const uint16_t* h, const uint16_t* b,
 // rank's home buffer: rows of expert j from source s are seg_row[j][s] ..
 // seg_row[j][s+1] and go to rows from seg_home[j][s] of home[s]
 // (grouped_gemm.cu).
+// mc_ep_dispatch whose last CTA also writes the receive side's row chunks
+// (as mc_ep_tiles) and the return map of the local slots: rows of local slot
+// j from source s are seg_row[j][s] .. seg_row[j][s+1] and go to rows from
+// seg_home[j][s] of s's home buffer (ep.cu).
+int mc_ep_dispatch_plan(mc_ctx* ctx, const uint16_t* x, int m, int hidden,
+                        const uint32_t* ids_sorted, const uint32_t* counts_all, int rank,
+                        int world, int n_experts, void* const* recv_bufs, size_t recv_cap_rows,
+                        uint32_t* status, int bm, uint32_t* tiles, uint32_t* n_tiles,
+                        uint32_t* rows, int max_tiles, uint32_t* seg_row, uint32_t* seg_home);
 int mc_gemm_q4_grouped_return(mc_ctx* ctx, const uint16_t* a, int rows, const mc_qweights* w,
                               int n_experts, const uint32_t* seg_row, const uint32_t* seg_home,
                               void* const* home, int world, size_t home_cap,
