@@ -169,7 +169,14 @@ ep_dispatch_kernel(const uint4* __restrict__ x, int m, int h16,
   const uint32_t total = src0[E];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int P = E / W;
-  for (uint32_t r = blockIdx.x * 8 + warp; r < total; r += gridDim.x * 8) {
+  // The sorted rows are grouped by owner rank; walked in that order by every
+  // source, all ranks would write into rank 0 first, then all into rank 1,
+  // ..., one destination's inbound link at a time. Source s starts at the
+  // rows for rank s + 1 instead (a rotation of the same rows).
+  const uint32_t rot = W > 1 ? src0[((rank + 1) % W) * P] : 0u;
+  for (uint32_t i = blockIdx.x * 8 + warp; i < total; i += gridDim.x * 8) {
+    uint32_t r = i + rot;
+    if (r >= total) r -= total;
     int lo = 0, hi = E;  // src0[lo] <= r < src0[hi]
     while (hi - lo > 1) {
       const int mid = (lo + hi) >> 1;
