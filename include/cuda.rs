@@ -6,8 +6,8 @@
 //! values travel as u16 bit patterns; every call returns 0 or a negative
 //! MC_E* code with the message in mc_last_error(). The op-level wrappers with
 //! the reference's `ensure!` checks follow the pattern `check(unsafe {
-//! mc_gemv_quant(...) })` shown in INTEGRATION.md; tests/test_rust_binding.py
-//! checks every declaration below against the C header.
+//! mc_gemv_quant(...) })`; tests/test_rust_binding.py checks every
+//! declaration below against the C header.
 #![allow(non_camel_case_types, dead_code)]
 
 use std::ffi::CStr;

@@ -1,4 +1,4 @@
-// Sampling draw on the logits: repetition penalty,
+// Sampling draw on the logits (the temperature > 0 token step): repetition penalty,
 // temperature, top-k, top-p and the Gumbel-max draw, all on the device, the
 // token folded into the same 64-bit key the greedy head writes so the token
 // tail (mc_token_tail) serves both paths. Contract of the reference

@@ -424,7 +424,7 @@ void or_gemv_gather_down_combine4(const void* dc, const uint16_t* ds, const uint
   free(xf); free(xs); free(xg);
 }
 
-/* --------------------------------------------- decode neighbours */
+/* ---------------------------- decode neighbours of the MoE block (Q/K/V, conv, dense FFN) */
 
 /* proj3_gemv_scatter (kernels/lfm.rs:150-205 -> lfm_proj3_gemv_scatter_bf16
  * lfm.metal:1020-1068): the Q, K and V GEMVs of one row x (K = 2048) in the
@@ -485,7 +485,7 @@ void or_gemv_gu_act(const void* gc, const uint16_t* gs, const uint16_t* gb, cons
   free(g); free(u);
 }
 
-/* ------------------------------------------------- sampling
+/* ------------------------------------------------- sampling draw
  * Contract: docs/PROTOCOL.md:48-75 and lfm_sample.metal:1-27 (w = pen(v)/T;
  * kept set {w >= tau}: top-k ties kept, then the smallest top-p prefix with
  * its boundary tie group; Gumbel-max draw with Philox4x32-10, counter
