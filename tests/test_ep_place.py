@@ -73,3 +73,31 @@ def test_ties_prefer_the_sources_own_replica():
     assert (slot_expert == 0).sum() == 2, slot_expert
     for s in range(world):
         assert tables[s, 0] // spr == s
+
+
+@pytest.mark.parametrize("seed", range(12))
+def test_placement_properties_on_random_loads(seed):
+    """Random world sizes, slot counts and (skewed or flat) loads: the
+    placement is valid, and its heaviest rank never carries more than the
+    placement with one slot per expert."""
+    g = np.random.default_rng(9000 + seed)
+    world = int(g.choice([2, 3, 4, 8]))
+    E = world * int(g.integers(2, 9))
+    spr = E // world + int(g.integers(0, 4))
+    if g.random() < 0.5:
+        load = g.integers(0, 500, size=(world, E)).astype(np.uint64)
+    else:
+        load = zipf_load(g, world, E).astype(np.uint64)
+    tables, slot_expert = ep.place_slots(load, world, spr)
+    assert set(slot_expert[slot_expert >= 0].tolist()) == set(range(E))
+    for r in range(world):
+        held = slot_expert[r * spr:(r + 1) * spr]
+        held = held[held >= 0]
+        assert len(set(held.tolist())) == len(held)
+    for s in range(world):
+        for e in range(E):
+            assert slot_expert[tables[s, e]] == e
+    loads = rank_loads(load, tables, world, spr)
+    assert loads.sum() == load.sum()
+    base_t, _ = ep.place_slots(load, world, E // world)
+    assert loads.max() <= rank_loads(load, base_t, world, E // world).max() + 1e-9
