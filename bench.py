@@ -573,9 +573,10 @@ CFG3_METRIC = "prefill grouped-GEMM tokens/s (cfg3: 4096-token MoE FFN, Zipf rou
 CFG3_WORKLOAD = ("cfg3: 4096 tokens per GPU x 2048, E=64 top-4 Zipf(s=1) routing, "
                  "SwiGLU 2048->1536->2048 Q4")
 # kernels one mc_ep_moe_prefill launches: route, relabel, sort (2), counts
-# exchange, row chunks, return map, dispatch, barrier, gate/up GEMM, down GEMM
+# exchange, dispatch (which also builds the row chunks and the return map and
+# arrives at the barrier after it), gate/up GEMM (which waits there), down GEMM
 # (which also returns the expert rows), barrier, combine
-EP_STEP_LAUNCHES = 13
+EP_STEP_LAUNCHES = 10
 
 
 def prefill_flops(S):

@@ -131,6 +131,14 @@ struct Plan {
   uint32_t* seg_row;
   uint32_t* seg_home;
   int bm, max_tiles;
+  // arrival (set when done is not null): once every CTA's rows are written,
+  // the last CTA advances the rank's epoch word and stores it into this
+  // rank's slot of every rank's flag words -- the arrival half of the
+  // barrier after the dispatch (the consumer's GEMM does the waiting)
+  uint32_t* flag_p[kMaxRanks];
+  uint32_t* epoch;
+  uint32_t* done;
+  int skip;  // test aid: do not arrive
 };
 
 // This rank's expert-sorted rows -> the owners' receive buffers. Every warp
@@ -194,6 +202,19 @@ ep_dispatch_kernel(const uint4* __restrict__ x, int m, int h16,
     mc_copy_row16(out, row, h16, lane);
   }
   __threadfence_system();
+  if (plan.done) {  // uniform over the grid
+    __syncthreads();
+    if (threadIdx.x == 0 && atomicAdd(plan.done, 1u) == gridDim.x - 1) {
+      *plan.done = 0u;
+      const uint32_t ep = *plan.epoch + 1u;
+      *plan.epoch = ep;
+      __threadfence_system();
+      if (!plan.skip)
+        for (int p = 0; p < W; ++p)
+          asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(plan.flag_p[p] + rank), "r"(ep)
+                       : "memory");
+    }
+  }
 }
 
 // Expert outputs of this rank's received rows -> each source's slot.
@@ -314,9 +335,11 @@ int mc_ep_dispatch_plan(mc_ctx* ctx, const uint16_t* x, int m, int hidden,
                         const uint32_t* ids_sorted, const uint32_t* counts_all, int rank,
                         int world, int n_experts, void* const* recv_bufs, size_t recv_cap_rows,
                         uint32_t* status, int bm, uint32_t* tiles, uint32_t* n_tiles,
-                        uint32_t* rows, int max_tiles, uint32_t* seg_row, uint32_t* seg_home) {
+                        uint32_t* rows, int max_tiles, uint32_t* seg_row, uint32_t* seg_home,
+                        uint32_t* const* flag_ptrs, uint32_t* epoch, uint32_t* done, int skip) {
   MC_REQUIRE(ctx && x && ids_sorted && counts_all && tiles && n_tiles && seg_row && seg_home,
              "ep_dispatch_plan: null pointer");
+  MC_REQUIRE(!done || (flag_ptrs && epoch), "ep_dispatch_plan: arrival needs flags and epoch");
   int rc;
   if ((rc = check_ranks(rank, world, n_experts, "ep_dispatch_plan"))) return rc;
   MC_REQUIRE(hidden > 0 && hidden % 8 == 0 && mc_aligned(x, 16), "ep_dispatch_plan: rows");
@@ -326,7 +349,13 @@ int mc_ep_dispatch_plan(mc_ctx* ctx, const uint16_t* x, int m, int hidden,
   if ((rc = fill_peers(&pp, recv_bufs, world, "ep_dispatch_plan"))) return rc;
   MC_REQUIRE(m >= 1 && recv_cap_rows >= 1 && recv_cap_rows <= 0xffffffffu,
              "ep_dispatch_plan: m %d / capacity %zu", m, recv_cap_rows);
-  Plan plan{reinterpret_cast<uint4*>(tiles), n_tiles, rows, seg_row, seg_home, bm, max_tiles};
+  Plan plan{reinterpret_cast<uint4*>(tiles), n_tiles, rows, seg_row, seg_home, bm, max_tiles,
+            {}, epoch, done, skip};
+  if (done)
+    for (int r = 0; r < world; ++r) {
+      MC_REQUIRE(flag_ptrs[r], "ep_dispatch_plan: flag words of rank %d", r);
+      plan.flag_p[r] = flag_ptrs[r];
+    }
   const int grid = std::max(1, std::min((4 * m + 7) / 8, ctx->num_sms * 2));
   ep_dispatch_kernel<<<grid, 256, 0, ctx->stream>>>(
       reinterpret_cast<const uint4*>(x), m, hidden / 8, ids_sorted, counts_all, rank, world,

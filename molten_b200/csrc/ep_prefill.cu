@@ -128,7 +128,7 @@ struct mc_ep_state {
   // local device scratch
   uint8_t* scratch = nullptr;
   uint32_t *ids, *counts, *offsets, *ids_sorted, *slotpos, *sort_tiles, *sort_ntiles;
-  uint32_t *counts_all, *tiles, *n_tiles, *rows, *status, *epoch;
+  uint32_t *counts_all, *tiles, *n_tiles, *rows, *status, *epoch, *done;
   uint16_t *gw, *act;
   uint32_t *seg_row, *seg_home;  // return map (built by the dispatch launch)
   int sort_max_tiles = 0, max_tiles = 0;
@@ -358,6 +358,7 @@ extern "C" int mc_ep_reserve(mc_ctx* ctx, int m_max, int n_experts, int slots_pe
   carve((void**)&ep->rows, 16);
   carve((void**)&ep->status, 16);
   carve((void**)&ep->epoch, 16);
+  carve((void**)&ep->done, 16);
   carve((void**)&ep->act, ep->recv_cap * moe_inter * 2);
   void* q = nullptr;
   cudaError_t e = cudaMalloc(&q, o);
@@ -459,15 +460,21 @@ extern "C" int mc_ep_moe_prefill(mc_ctx* ctx, const uint16_t* x, const float* lo
   if ((rc = mc_ep_dispatch_plan(ctx, x, m, ep->H, ep->ids_sorted, ep->counts_all, ep->rank, W,
                                 ep->E_slots, ep->recv_ptr, ep->recv_cap, ep->status, kChunk,
                                 ep->tiles, ep->n_tiles, ep->rows,
-                                ep->max_tiles, ep->seg_row, ep->seg_home)))
+                                ep->max_tiles, ep->seg_row, ep->seg_home, ep->flag_ptr,
+                                ep->epoch, ep->done,
+                                (ctx->test_flags & MC_TEST_SKIP_BARRIER_ARRIVE) ? 1 : 0)))
     return rc;
   if ((rc = mark(3))) return rc;
-  if ((rc = ep_barrier(ctx))) return rc;
+  // the barrier after the dispatch: the dispatch launch arrives (its last
+  // CTA stores the epoch into every rank's flag slot) and the gate/up GEMM
+  // waits before its first token load, its set-up and first weight stages
+  // overlapping the wait (a barrier launch of its own sat between them)
   if ((rc = mark(4))) return rc;
   uint16_t* recv = static_cast<uint16_t*>(ep->recv_ptr[ep->rank]);
   const int rows = (int)ep->recv_cap;
-  if ((rc = mc_gemm_q4_grouped_gu(ctx, recv, rows, gate, up, ep->spr, ep->act, ep->tiles,
-                                  ep->n_tiles, ep->max_tiles, ep->status)))
+  if ((rc = mc_gemm_q4_grouped_gu_after(ctx, recv, rows, gate, up, ep->spr, ep->act, ep->tiles,
+                                        ep->n_tiles, ep->max_tiles, ep->status,
+                                        ep->flag_ptr[ep->rank], ep->epoch, W)))
     return rc;
   // the down GEMM stores each expert row straight into its source's home row
   if ((rc = mc_gemm_q4_grouped_return(ctx, ep->act, rows, down, ep->spr, ep->seg_row, ep->seg_home,

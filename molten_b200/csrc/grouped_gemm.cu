@@ -108,6 +108,18 @@ struct ReturnMap {
   uint32_t home_cap;
 };
 
+// The expert-parallel step's arrival check (set when flags is not null):
+// before its first token load the GEMM waits until every rank's slot of this
+// rank's flag words has reached *epoch, the epoch the ranks' dispatch
+// launches stored after their rows (into this GEMM's token buffer) were
+// written -- the barrier after the dispatch, inside the GEMM, so the GEMM's
+// set-up and first weight stages overlap the wait.
+struct ArrivalWait {
+  const uint32_t* flags;  // this rank's flag words [W]
+  const uint32_t* epoch;  // this rank's epoch word
+  int W;
+};
+
 struct GemmParams {
   mc_qweights w0, w1;
   uint16_t* out;
@@ -117,6 +129,7 @@ struct GemmParams {
   int N, K, rows, max_tiles, n_experts;
   unsigned long long timeout_ns;  // limit of every bounded wait (mc_set_wait_limit)
   ReturnMap ret;
+  ArrivalWait arrive;
 };
 
 // One work item: token rows [m0, mend) of expert e against feature block nb.
@@ -362,6 +375,35 @@ grouped_gemm_kernel(const __grid_constant__ TokenMaps tm, const GemmParams P) {
     // descriptors are warp-uniform) and one elected lane issues: a lone lane
     // in a divergent branch issued tcgen05.mma at about half the rate the
     // tensor pipe takes them while the dequant warps kept its sub-partition busy.
+    if (P.arrive.flags) {
+      // every rank's rows are in the token buffer once its flag slot holds
+      // this step's epoch (bounded; the async-proxy fence then orders the
+      // TMA reads after what the acquire loads observed)
+      bool arrived = true;
+      if (lane == 0) {
+        uint32_t ep;
+        asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(ep) : "l"(P.arrive.epoch) : "memory");
+        const unsigned long long dl = mc_globaltimer() + P.timeout_ns;
+        for (int q = 0; q < P.arrive.W && arrived; ++q) {
+          for (;;) {
+            uint32_t v;
+            asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(P.arrive.flags + q) : "memory");
+            if ((int)(v - ep) >= 0) break;
+            if (mc_globaltimer() > dl) {
+              arrived = false;
+              break;
+            }
+            __nanosleep(200);
+          }
+        }
+        asm volatile("fence.proxy.async.global;" ::: "memory");
+        if (!arrived) {
+          if (P.status) atomicOr(P.status, 8u);
+          abort_s = 1;
+        }
+      }
+      __syncwarp();
+    }
     uint32_t it = 0;
     for (int i = 0, item = cta_item(0); item < total; item = cta_item(++i)) {
       if (__any_sync(0xffffffffu, abort_s != 0)) break;
@@ -769,7 +811,8 @@ int make_code_map(CUtensorMap* map, const void* codes, int rows, int K) {
 template <bool GU>
 int launch(mc_ctx* ctx, const uint16_t* a, int rows, const mc_qweights* w0, const mc_qweights* w1,
            int n_experts, uint16_t* out, const uint32_t* tiles, const uint32_t* n_tiles,
-           int max_tiles, uint32_t* status, const ReturnMap* ret = nullptr) {
+           int max_tiles, uint32_t* status, const ReturnMap* ret = nullptr,
+           const ArrivalWait* arrive = nullptr) {
   using C = Cfg<GU>;
   const int N = w0->out_features / n_experts, K = w0->in_features;
   TokenMaps tm;
@@ -782,6 +825,7 @@ int launch(mc_ctx* ctx, const uint16_t* a, int rows, const mc_qweights* w0, cons
   GemmParams P{*w0, GU ? *w1 : *w0, out, reinterpret_cast<const uint4*>(tiles), n_tiles, status,
                N, K, rows, max_tiles, n_experts, mc_wait_limit(ctx, kTimeoutNs), {}};
   if (ret) P.ret = *ret;
+  if (arrive) P.arrive = *arrive;
   MC_CUDA(cudaFuncSetAttribute(grouped_gemm_kernel<GU>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                C::SMEM));
   grouped_gemm_kernel<GU><<<ctx->num_sms, kThreads, C::SMEM, ctx->stream>>>(tm, P);
@@ -877,6 +921,26 @@ extern "C" int mc_gemm_q4(mc_ctx* ctx, const uint16_t* a, int m, const mc_qweigh
                                                               n_tiles, m);
   if ((rc = mc_after_launch("dense_tiles_kernel"))) return rc;
   return launch<false>(ctx, a, m, w, nullptr, 1, c, tiles, n_tiles, T, status);
+}
+
+int mc_gemm_q4_grouped_gu_after(mc_ctx* ctx, const uint16_t* a, int rows,
+                                const mc_qweights* gate, const mc_qweights* up, int n_experts,
+                                uint16_t* act, const uint32_t* tiles, const uint32_t* n_tiles,
+                                int max_tiles, uint32_t* status, const uint32_t* flags,
+                                const uint32_t* epoch, int world) {
+  MC_REQUIRE(ctx && flags && epoch, "gemm_q4_grouped_gu_after: null pointer");
+  MC_REQUIRE(world >= 1 && world <= kRetRanks, "gemm_q4_grouped_gu_after: world %d", world);
+  int rc = check_grouped(a, rows, gate, n_experts, act, tiles, n_tiles, max_tiles,
+                         "gemm_q4_grouped_gu_after gate");
+  if (rc) return rc;
+  rc = check_grouped(a, rows, up, n_experts, act, tiles, n_tiles, max_tiles,
+                     "gemm_q4_grouped_gu_after up");
+  if (rc) return rc;
+  MC_REQUIRE(gate->out_features == up->out_features && gate->in_features == up->in_features,
+             "gemm_q4_grouped_gu_after: gate/up shapes differ");
+  const ArrivalWait aw{flags, epoch, world};
+  return launch<true>(ctx, a, rows, gate, up, n_experts, act, tiles, n_tiles, max_tiles, status,
+                      nullptr, &aw);
 }
 
 extern "C" int mc_gemm_q4_grouped_gu(mc_ctx* ctx, const uint16_t* a, int rows,

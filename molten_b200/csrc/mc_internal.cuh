@@ -52,7 +52,15 @@ int mc_ep_dispatch_plan(mc_ctx* ctx, const uint16_t* x, int m, int hidden,
                         const uint32_t* ids_sorted, const uint32_t* counts_all, int rank,
                         int world, int n_experts, void* const* recv_bufs, size_t recv_cap_rows,
                         uint32_t* status, int bm, uint32_t* tiles, uint32_t* n_tiles,
-                        uint32_t* rows, int max_tiles, uint32_t* seg_row, uint32_t* seg_home);
+                        uint32_t* rows, int max_tiles, uint32_t* seg_row, uint32_t* seg_home,
+                        uint32_t* const* flag_ptrs, uint32_t* epoch, uint32_t* done, int skip);
+// mc_gemm_q4_grouped_gu whose token loads first wait (bounded) until every
+// slot of `flags` [world] has reached *epoch (grouped_gemm.cu).
+int mc_gemm_q4_grouped_gu_after(mc_ctx* ctx, const uint16_t* a, int rows,
+                                const mc_qweights* gate, const mc_qweights* up, int n_experts,
+                                uint16_t* act, const uint32_t* tiles, const uint32_t* n_tiles,
+                                int max_tiles, uint32_t* status, const uint32_t* flags,
+                                const uint32_t* epoch, int world);
 int mc_gemm_q4_grouped_return(mc_ctx* ctx, const uint16_t* a, int rows, const mc_qweights* w,
                               int n_experts, const uint32_t* seg_row, const uint32_t* seg_home,
                               void* const* home, int world, size_t home_cap,
