@@ -473,9 +473,10 @@ int mc_ep_counts(mc_ctx* ctx, uint32_t* out, size_t n);
 int mc_ep_finalize(mc_ctx* ctx);
 /* Profiling aid: with `on`, each step records events at its phase
  * boundaries; mc_ep_phase_ms waits and writes the last step's seven phase
- * times in ms (route + relabel + sort, counts exchange + barrier, row chunks
- * + return map + dispatch, the barrier after the dispatch, grouped GEMMs +
- * return, the barrier after them, combine). */
+ * times in ms (route + relabel + sort, counts exchange + barrier, dispatch
+ * with the row chunks and the return map, a slot kept for the barrier after
+ * the dispatch -- its wait now runs inside the gate/up GEMM, so the slot is
+ * ~0 --, grouped GEMMs + return, the barrier after them, combine). */
 int mc_ep_set_profile(mc_ctx* ctx, int on);
 int mc_ep_phase_ms(mc_ctx* ctx, float* out7);
 
